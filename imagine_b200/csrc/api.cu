@@ -1,0 +1,260 @@
+// extern "C" entry points of libw8a8 (declared in include/w8a8.h): argument
+// validation, error reporting and dispatch to the kernels.
+//
+// Error mapping follows the reference bridge (inference/native/bridge.cpp,
+// `protect`): invalid arguments -> W8A8_ERR_VALUE (-20), out-of-range indices
+// -> W8A8_ERR_INDEX (-21), CUDA failures -> W8A8_ERR_ACCELERATOR (-10) with the
+// cudaError_t kept for w8a8_last_accelerator_code().  No call allocates device
+// memory and no call synchronises the stream except w8a8_device_error.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "w8a8_internal.h"
+
+namespace w8a8 {
+namespace {
+thread_local char g_last_error[512] = "";
+thread_local int g_last_accel = 0;
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int device_sm_count() {
+  static int cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < 64) {
+    if (cache[dev] == 0) {
+      int n = 0;
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+      cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+  }
+  return 148;
+}
+
+namespace {
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+// Converts a pending CUDA error (if any) into the accelerator code.
+int finish(int rc) {
+  if (rc == W8A8_ERR_ACCELERATOR) {
+    g_last_accel = static_cast<int>(cudaPeekAtLastError());
+  }
+  if (rc == 0) g_last_error[0] = '\0';
+  return rc;
+}
+
+bool is_float_dtype(int d) { return d == W8A8_F32 || d == W8A8_F16 || d == W8A8_BF16; }
+
+int check_epilogue(const w8a8_epilogue_t* epi, int64_t N, bool need_ws) {
+  if (!epi) return fail(W8A8_ERR_VALUE, "epilogue descriptor is NULL");
+  if (need_ws) {
+    if (!epi->ws) return fail(W8A8_ERR_VALUE, "weight scale pointer is NULL");
+    if (epi->ws_numel != 1 && epi->ws_numel != N) {
+      return fail(W8A8_ERR_VALUE,
+                  "INT8 weight scale must be scalar or per-output-channel, got %lld for N=%lld",
+                  static_cast<long long>(epi->ws_numel), static_cast<long long>(N));
+    }
+  }
+  if (epi->residual && !epi->residual_scale) {
+    return fail(W8A8_ERR_VALUE, "int8_linear: residual requires residual_scale");
+  }
+  if (epi->residual && epi->ldr < N) {
+    return fail(W8A8_ERR_VALUE, "residual row stride %lld < N=%lld",
+                static_cast<long long>(epi->ldr), static_cast<long long>(N));
+  }
+  if (epi->dequant_order < W8A8_DQ_EAGER || epi->dequant_order > W8A8_DQ_CHAINED) {
+    return fail(W8A8_ERR_VALUE, "unknown dequant order %d", epi->dequant_order);
+  }
+  if (epi->activation != W8A8_ACT_NONE && epi->activation != W8A8_ACT_GELU_TANH) {
+    return fail(W8A8_ERR_VALUE, "unknown output activation %d", epi->activation);
+  }
+  return 0;
+}
+
+}  // namespace
+}  // namespace w8a8
+
+using namespace w8a8;
+
+extern "C" {
+
+const char* w8a8_last_error(void) { return g_last_error; }
+
+int w8a8_last_accelerator_code(void) { return g_last_accel; }
+
+int w8a8_abi_version(void) { return 100; }
+
+int w8a8_device_error(void* stream) {
+  int v = 0;
+  const int rc = read_and_clear_device_error(static_cast<cudaStream_t>(stream), &v);
+  if (rc != 0) {
+    g_last_accel = rc;
+    return fail(W8A8_ERR_ACCELERATOR, "reading the device error word failed: %s",
+                cudaGetErrorString(static_cast<cudaError_t>(rc)));
+  }
+  return v;
+}
+
+int w8a8_quantize_rowwise(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
+                          int8_t* q, int64_t ldq, float* scale, int scale_mode, int stochastic,
+                          uint64_t seed, void* stream) {
+  if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
+  if (scale_mode != W8A8_SCALE_EAGER && scale_mode != W8A8_SCALE_KITCHEN) {
+    return fail(W8A8_ERR_VALUE, "unknown scale mode %d", scale_mode);
+  }
+  if (rows == 0 || cols == 0) return finish(0);
+  if (!x || !q || !scale) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldx < cols || ldq < cols) return fail(W8A8_ERR_VALUE, "row stride smaller than cols");
+  if (cols > 0x7fffffffLL || rows > 0x7fffffffLL) {
+    return fail(W8A8_ERR_VALUE, "quantize_int8_rowwise only supports rows, K <= INT_MAX");
+  }
+  return finish(quantize_rowwise_launch(x, x_dtype, rows, cols, ldx, q, ldq, scale, scale_mode,
+                                        stochastic, seed, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_gemm_dequant(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* xs,
+                      const w8a8_epilogue_t* epi, void* out, int out_dtype, int64_t ldo, int64_t M,
+                      int64_t N, int64_t K, const w8a8_gemm_config_t* cfg, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (M == 0 || N == 0) return finish(0);
+  if (!q || !w || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldq < K || ldw < K || ldo < N) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  GemmArgs g{};
+  g.kind = 0;
+  g.a = q;
+  g.lda = ldq;
+  g.b = w;
+  g.ldb = ldw;
+  g.xs = xs;
+  g.epi = epi;
+  g.out = out;
+  g.out_dtype = out_dtype;
+  g.ldo = ldo;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.cfg = cfg;
+  return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_gemm_s32(const int8_t* q, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
+                  const w8a8_gemm_config_t* cfg, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (M == 0 || N == 0) return finish(0);
+  if (!q || !w || !acc) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  GemmArgs g{};
+  g.kind = 0;
+  g.a = q;
+  g.lda = K;
+  g.b = w;
+  g.ldb = K;
+  g.out = acc;
+  g.out_dtype = W8A8_S32;
+  g.ldo = N;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.cfg = cfg;
+  return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_dequantize_linear(const int32_t* acc, const float* xs, const w8a8_epilogue_t* epi,
+                           void* out, int out_dtype, int64_t M, int64_t N, void* stream) {
+  if (M < 0 || N < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (M == 0 || N == 0) return finish(0);
+  if (!acc || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  return finish(dequant_launch(acc, xs, epi, out, out_dtype, M, N, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_gemv_dequant(const int8_t* q, const int8_t* w, const float* xs,
+                      const w8a8_epilogue_t* epi, void* out, int out_dtype, int64_t M, int64_t N,
+                      int64_t K, void* stream) {
+  if (M != 1 && M != 2) return fail(W8A8_ERR_VALUE, "GEMV supports M in {1, 2}, got %lld", static_cast<long long>(M));
+  if (N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (N == 0) return finish(0);
+  if (!q || !w || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  return finish(gemv_launch(q, w, xs, epi, out, out_dtype, M, N, K, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_linear_small(const void* x, int x_dtype, const int8_t* w, const w8a8_epilogue_t* epi,
+                      int scale_mode, int8_t* q_out, float* xs_out, void* out, int out_dtype,
+                      int64_t M, int64_t N, int64_t K, void* stream) {
+  if (M != 1 && M != 2) return fail(W8A8_ERR_VALUE, "small linear supports M in {1, 2}, got %lld", static_cast<long long>(M));
+  if (N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (scale_mode != W8A8_SCALE_EAGER && scale_mode != W8A8_SCALE_KITCHEN) {
+    return fail(W8A8_ERR_VALUE, "unknown scale mode %d", scale_mode);
+  }
+  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (N == 0) return finish(0);
+  if (!x || !w || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  return finish(linear_small_launch(x, x_dtype, w, epi, scale_mode, q_out, xs_out, out, out_dtype,
+                                    M, N, K, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_quantize_fp8_tensor(const void* x, int x_dtype, int64_t numel, const float* scale,
+                             uint8_t* out, void* stream) {
+  if (numel < 0) return fail(W8A8_ERR_VALUE, "negative size");
+  if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
+  if (numel == 0) return finish(0);
+  if (!x || !scale || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  return finish(quantize_fp8_tensor_launch(x, x_dtype, numel, scale, out, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_fp8_gemm(const uint8_t* a, const uint8_t* b, const float* sa, const float* sb,
+                  const void* bias, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                  const w8a8_gemm_config_t* cfg, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (M == 0 || N == 0) return finish(0);
+  if (!a || !b || !sa || !sb || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  w8a8_epilogue_t epi{};
+  epi.ws_numel = 1;
+  epi.bias = bias;
+  epi.dequant_order = W8A8_DQ_CHAINED;
+  GemmArgs g{};
+  g.kind = 1;
+  g.a = a;
+  g.lda = K;
+  g.b = b;
+  g.ldb = K;
+  g.sa = sa;
+  g.sb = sb;
+  g.epi = &epi;
+  g.out = out;
+  g.out_dtype = out_dtype;
+  g.ldo = N;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.cfg = cfg;
+  return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,108 @@
+// Dequantisation epilogue shared by the tcgen05 GEMM, the GEMV and the
+// stand-alone dequant kernel.  The arithmetic of each order is spelled with
+// explicit-rounding intrinsics (__fmul_rn/__fmaf_rn/__fadd_rn) so that the
+// compiler cannot re-associate or contract it differently from the reference.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace w8a8 {
+
+// Dequant orders found in the reference (see oracle/eager.py):
+//   kDqEager        inference/src/int8_linear.rs:244-268
+//                   y = T(acc * (xs*ws)); y = T(y + bias)         (two roundings)
+//   kDqScaleProduct KSRC backends/triton/quantization.py:861-1018
+//                   y = T(fma(acc, xs*ws, bias))                  (one rounding)
+//   kDqChained      native/comfy-port/kitchen/int8_linear.cu:517-545, 585-708
+//                   y = T(fma(acc*xs, ws, bias))                  (one rounding)
+enum DequantOrder : int { kDqEager = 0, kDqScaleProduct = 1, kDqChained = 2 };
+enum OutputAct : int { kActNone = 0, kActGeluTanh = 1 };
+
+template <typename T>
+struct OutTraits;
+template <>
+struct OutTraits<float> {
+  static __device__ __forceinline__ float round(float v) { return v; }
+  static __device__ __forceinline__ float load(const void* p, int64_t i) {
+    return static_cast<const float*>(p)[i];
+  }
+};
+template <>
+struct OutTraits<__nv_bfloat16> {
+  static __device__ __forceinline__ float round(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+  }
+  static __device__ __forceinline__ float load(const void* p, int64_t i) {
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  }
+};
+template <>
+struct OutTraits<__half> {
+  static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
+  static __device__ __forceinline__ float load(const void* p, int64_t i) {
+    return __half2float(static_cast<const __half*>(p)[i]);
+  }
+};
+
+// GELU with the tanh approximation, evaluated in fp32 on a value already
+// rounded to the output dtype (the reference applies gelu to the stored
+// tensor).  tanh comes from the hardware approximation instruction.
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float k1 = 0.044715f;
+  const float inner = k0 * (x + k1 * x * x * x);
+  return 0.5f * x * (1.0f + tanh_fast(inner));
+}
+
+struct EpilogueParams {
+  const float* xs;         // [M] per-row activation scales (int8 path)
+  const float* ws;         // [N] per-channel weight scales, or [1]
+  int ws_scalar;           // 1 if ws has one element
+  const float* sa;         // fp8 path: per-tensor activation scale (device scalar)
+  const float* sb;         // fp8 path: per-tensor weight scale (device scalar)
+  const void* bias;        // [N] in the output dtype, or nullptr
+  const void* residual;    // [M, ldr] in the output dtype, or nullptr
+  int64_t ldr;             // residual row stride (elements)
+  const void* rscale;      // [N] in the output dtype (required with residual)
+  int dq_order;            // DequantOrder
+  int act;                 // OutputAct
+  int vec_ws;              // 1 if ws is 16-byte aligned (vector loads allowed)
+  int vec_bias;            // 1 if bias is 16-byte aligned
+  int vec_rscale;          // 1 if rscale is 16-byte aligned
+};
+
+// Value of one output element before the optional residual, already rounded
+// to OutT's precision (returned as float).  `a` is the accumulator as fp32
+// (int32 converted with round-to-nearest, or the fp8 path's fp32 sum).
+template <typename OutT>
+__device__ __forceinline__ float dequant_one(float a, float xs_row, float ws_col, float bias_col,
+                                             bool has_bias, int order) {
+  float y;
+  if (order == kDqEager) {
+    y = OutTraits<OutT>::round(__fmul_rn(a, __fmul_rn(xs_row, ws_col)));
+    if (has_bias) y = OutTraits<OutT>::round(__fadd_rn(y, bias_col));
+  } else if (order == kDqScaleProduct) {
+    const float s = __fmul_rn(xs_row, ws_col);
+    y = OutTraits<OutT>::round(has_bias ? __fmaf_rn(a, s, bias_col) : __fmul_rn(a, s));
+  } else {
+    const float t = __fmul_rn(a, xs_row);
+    y = OutTraits<OutT>::round(has_bias ? __fmaf_rn(t, ws_col, bias_col) : __fmul_rn(t, ws_col));
+  }
+  return y;
+}
+
+template <typename OutT>
+__device__ __forceinline__ float finish_one(float y, float resid, float rs, bool has_resid, int act) {
+  if (act == kActGeluTanh) y = OutTraits<OutT>::round(gelu_tanh(y));
+  if (has_resid) y = OutTraits<OutT>::round(__fmaf_rn(y, rs, resid));
+  return y;
+}
+
+}  // namespace w8a8

@@ -1,0 +1,623 @@
+// Persistent, warp-specialised tcgen05 GEMM for the W8A8 / FP8 linear family.
+//
+// Replaces the reference's CUTLASS 2.x Sm80 INT8 GEMM with EVT dequant
+// epilogue (KSRC backends/cuda/ops/cutlass_gemm_int8.cu:66-420), its cuBLASLt
+// int32 GEMM + separate dequant pass (KSRC backends/cuda/ops/cublas_gemm_int8.cu,
+// native/comfy-port/kitchen/int8_linear.cu:517-583) and the cuBLASLt
+// per-tensor FP8 `_scaled_mm` (inference/native/bridge.cpp:401-413).
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 4      TMA producer: A[128 x 128B] and B[BN x 128B] K-slices into a
+//               kStages-deep shared-memory ring (128B swizzle), one mbarrier
+//               pair (full/empty) per stage.
+//   warp 5      TMEM owner + MMA issuer: one elected thread issues
+//               tcgen05.mma (kind::i8 -> s32, or kind::f8f6f4 -> f32),
+//               128 x BN x 32 per instruction, into one of two TMEM
+//               accumulators (2 x BN columns), and tcgen05.commit's the stage
+//               back to the producer / the accumulator to the epilogue.
+//   warps 0-3   epilogue: tcgen05.ld 32 lanes x 32 columns, dequant
+//               (three reference orders), bias, GELU-tanh, residual, convert,
+//               write a swizzled 32x32 staging tile, TMA store.  The double
+//               buffered accumulator lets tile i's epilogue overlap tile i+1's
+//               main loop.
+// Tiles are visited persistently (tile = blockIdx.x + i * gridDim.x) in
+// grouped-M order so concurrently running CTAs share A and B panels in L2.
+//
+// Every mbarrier wait is bounded (sm100_ptx.cuh); on a timeout the kernel
+// records an error in g_w8a8_device_error, every role falls through, and TMEM
+// is released.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+
+#include "epilogue.cuh"
+#include "sm100_ptx.cuh"
+#include "w8a8_internal.h"
+
+namespace w8a8 {
+
+__device__ int g_w8a8_device_error;
+
+int read_and_clear_device_error(cudaStream_t stream, int* value) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_w8a8_device_error, sizeof(int), 0,
+                                            cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_w8a8_device_error, &zero, sizeof(int), 0,
+                                cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return static_cast<int>(e);
+  }
+  *value = v;
+  return 0;
+}
+
+namespace {
+
+constexpr int kBM = 128;          // rows per tile (TMEM lanes)
+constexpr int kBK = 128;          // K bytes per pipeline stage (one 128B swizzle row)
+constexpr int kUmmaK = 32;        // K per tcgen05.mma for 8-bit operand kinds
+constexpr int kEpiWarps = 4;
+constexpr int kProducerWarp = kEpiWarps;
+constexpr int kMmaWarp = kEpiWarps + 1;
+constexpr int kThreads = (kEpiWarps + 2) * 32;
+constexpr int kMaxSmem = 232448;  // 227 KB opt-in per CTA on sm_100
+
+template <int BN, typename OutT>
+struct Cfg {
+  static constexpr int kABytes = kBM * kBK;
+  static constexpr int kBBytes = BN * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStageD = 32 * 32 * static_cast<int>(sizeof(OutT));  // one warp's tile
+  static constexpr int kDBytes = kEpiWarps * 2 * kStageD;
+  static constexpr int kBarBytes = 256;
+  static constexpr int kFixed = 1024 + kDBytes + kBarBytes;
+  static constexpr int kStagesRaw = (kMaxSmem - kFixed) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr int kSmemBytes = kFixed + kStages * kStageBytes;
+  static constexpr uint32_t kTmemCols = (2 * BN <= 256) ? 256u : 512u;
+  static_assert(kStages >= 2, "pipeline needs at least two stages");
+  static_assert(kSmemBytes <= kMaxSmem, "shared memory budget exceeded");
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group_m, int& mb,
+                                            int& nb) {
+  const int per_group = group_m * num_n;
+  const int g = tile / per_group;
+  const int first_m = g * group_m;
+  const int gsize = min(num_m - first_m, group_m);
+  const int r = tile - g * per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+// 32 consecutive per-column values starting at col0 as fp32.  Every lane of a
+// warp reads the same addresses (broadcast); vector loads when the whole
+// chunk is in range and the base is 16-byte aligned.
+template <typename T>
+__device__ __forceinline__ void load_cols32(const void* p, int col0, int N, bool vec_ok,
+                                            float (&v)[32]) {
+  if (vec_ok && col0 + 32 <= N) {
+    if constexpr (sizeof(T) == 4) {
+      const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + col0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 t = __ldg(q + i);
+        v[4 * i] = t.x;
+        v[4 * i + 1] = t.y;
+        v[4 * i + 2] = t.z;
+        v[4 * i + 3] = t.w;
+      }
+    } else {
+      const uint4* q = reinterpret_cast<const uint4*>(static_cast<const T*>(p) + col0);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 t = __ldg(q + i);
+        const T* e = reinterpret_cast<const T*>(&t);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[8 * i + j] = OutTraits<T>::load(e, j);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = col0 + j < N ? OutTraits<T>::load(p, col0 + j) : 0.0f;
+  }
+}
+
+__device__ __forceinline__ void spin_ns(uint64_t ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < ns) {
+  }
+}
+
+template <typename OutT>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int KIND, int BN, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmD, int M, int N, int K, int num_m_tiles,
+                      int num_n_tiles, int group_m, EpilogueParams ep) {
+  using C = Cfg<BN, OutT>;
+  constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::kStages * C::kABytes;
+  uint8_t* sD = smem + C::kStages * C::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sD + C::kDBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* tfull = empty + C::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  volatile int* abortv = abort_flag;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int num_tiles = num_m_tiles * num_n_tiles;
+  const int num_kb = (K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], kEpiWarps * 32);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == kProducerWarp && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if constexpr (!kRaw) tma_prefetch_desc(&tmD);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc<C::kTmemCols>(tmem_slot);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = static_cast<int>(it % C::kStages);
+          const uint32_t ph = (it / C::kStages) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, abortv, &g_w8a8_device_error, kDevTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+          tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kBK, mb * kBM);
+          tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kBK, nb * BN);
+        }
+      }
+      if (!ok) spin_ns(1000000);  // let TMA loads already in flight land (bounded)
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc<KIND>(kBM, BN);
+      uint32_t it = 0;
+      uint32_t tl = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++tl) {
+        const uint32_t acc = tl & 1u;
+        const uint32_t use = tl >> 1;
+        if (!mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abortv, &g_w8a8_device_error,
+                       kDevTimeoutTmemEmpty)) {
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = static_cast<int>(it % C::kStages);
+          const uint32_t ph = (it / C::kStages) & 1u;
+          if (!mbar_wait(&full[s], ph, abortv, &g_w8a8_device_error, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * C::kABytes);
+          const uint32_t b0 = smem_u32(sB + s * C::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            umma_ss<KIND>(d_tmem, smem_desc_k_sw128(a0 + k * kUmmaK),
+                          smem_desc_k_sw128(b0 + k * kUmmaK), idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    uint8_t* stage0 = sD + warp * 2 * C::kStageD;
+    const bool has_bias = ep.bias != nullptr;
+    const bool has_resid = ep.residual != nullptr;
+    float fp8_scale = 0.0f;
+    if constexpr (KIND == 1) fp8_scale = __fmul_rn(__ldg(ep.sa), __ldg(ep.sb));
+    uint32_t tl = 0;
+    uint32_t chunk_ctr = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tl) {
+      int mb, nb;
+      tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
+      const uint32_t acc = tl & 1u;
+      const uint32_t use = tl >> 1;
+      const int col_base = nb * BN;
+      if (!mbar_wait(&tfull[acc], use & 1u, abortv, &g_w8a8_device_error, kDevTimeoutTmemFull)) {
+        break;
+      }
+      tc_fence_after();
+      const int row0 = mb * kBM + warp * 32;
+      const int grow = row0 + lane;
+      float xs_row = 0.0f;
+      if constexpr (KIND == 0 && !kRaw) xs_row = grow < M ? __ldg(ep.xs + grow) : 0.0f;
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = col_base + c * 32;
+        if (col0 >= N) break;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + c * 32, r);
+        tmem_ld_wait();
+        float wsv[32], bv[32], rsv[32];
+        if constexpr (!kRaw) {
+          if constexpr (KIND == 0) {
+            if (ep.ws_scalar) {
+              const float w0 = __ldg(ep.ws);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) wsv[j] = w0;
+            } else {
+              load_cols32<float>(ep.ws, col0, N, ep.vec_ws, wsv);
+            }
+          }
+          if (has_bias) load_cols32<OutT>(ep.bias, col0, N, ep.vec_bias, bv);
+          if (has_resid) load_cols32<OutT>(ep.rscale, col0, N, ep.vec_rscale, rsv);
+        }
+        uint8_t* st = stage0 + (chunk_ctr & 1u) * C::kStageD;
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+        if constexpr (sizeof(OutT) == 4) {
+          // 32 x 4-byte values = 8 chunks of 16 B; 128B swizzle: chunk ^= row & 7.
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int j = cc * 4 + e;
+              if constexpr (kRaw) {
+                w4[e] = r[j];
+              } else {
+                const float a = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(r[j]))
+                                            : __uint_as_float(r[j]);
+                float y;
+                if constexpr (KIND == 0) {
+                  y = dequant_one<OutT>(a, xs_row, wsv[j], (has_bias ? bv[j] : 0.0f), has_bias,
+                                        ep.dq_order);
+                } else {
+                  y = dequant_one<OutT>(a, fp8_scale, 1.0f, (has_bias ? bv[j] : 0.0f), has_bias,
+                                        kDqChained);
+                }
+                float res = 0.0f;
+                if (has_resid && grow < M && col0 + j < N) {
+                  res = OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(grow) * ep.ldr +
+                                                               col0 + j);
+                }
+                y = finish_one<OutT>(y, res, (has_resid ? rsv[j] : 0.0f), has_resid, ep.act);
+                w4[e] = __float_as_uint(y);
+              }
+            }
+            const int phys = cc ^ (lane & 7);
+            *reinterpret_cast<uint4*>(st + lane * 128 + phys * 16) =
+                make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+        } else {
+          // 32 x 2-byte values = 4 chunks of 16 B; 64B swizzle: chunk ^= (row >> 1) & 3.
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float y2[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int j = cc * 8 + e * 2 + h;
+                const float a = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(r[j]))
+                                            : __uint_as_float(r[j]);
+                float y;
+                if constexpr (KIND == 0) {
+                  y = dequant_one<OutT>(a, xs_row, wsv[j], (has_bias ? bv[j] : 0.0f), has_bias,
+                                        ep.dq_order);
+                } else {
+                  y = dequant_one<OutT>(a, fp8_scale, 1.0f, (has_bias ? bv[j] : 0.0f), has_bias,
+                                        kDqChained);
+                }
+                float res = 0.0f;
+                if (has_resid && grow < M && col0 + j < N) {
+                  res = OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(grow) * ep.ldr +
+                                                               col0 + j);
+                }
+                y2[h] = finish_one<OutT>(y, res, (has_resid ? rsv[j] : 0.0f), has_resid, ep.act);
+              }
+              w4[e] = pack2<OutT>(y2[0], y2[1]);
+            }
+            const int phys = cc ^ ((lane >> 1) & 3);
+            *reinterpret_cast<uint4*>(st + lane * 64 + phys * 16) =
+                make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && row0 < M) {
+          tma_store_2d(&tmD, st, col0, row0);
+          tma_store_commit();
+        }
+        ++chunk_ctr;
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+  }
+
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc<C::kTmemCols>(tmem_base);
+  }
+}
+
+// ---------------------------------------------------------------- CUDA-core path
+// For shapes the TMA path cannot address (K % 16 != 0, unaligned rows, K == 0).
+// One thread per output element; the A row is broadcast across the block.
+template <int KIND, typename OutT>
+__global__ void __launch_bounds__(128) gemm_simt_kernel(const uint8_t* __restrict__ a, int64_t lda,
+                                                        const uint8_t* __restrict__ b, int64_t ldb,
+                                                        void* __restrict__ out, int64_t ldo, int M,
+                                                        int N, int K, EpilogueParams ep) {
+  constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
+  const int m = blockIdx.y;
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  const uint8_t* ar = a + static_cast<int64_t>(m) * lda;
+  const uint8_t* br = b + static_cast<int64_t>(n) * ldb;
+  float af = 0.0f;
+  int32_t ai = 0;
+  for (int k = 0; k < K; ++k) {
+    if constexpr (KIND == 0) {
+      ai += static_cast<int32_t>(static_cast<int8_t>(ar[k])) *
+            static_cast<int32_t>(static_cast<int8_t>(br[k]));
+    } else {
+      __nv_fp8_e4m3 x, y;
+      x.__x = ar[k];
+      y.__x = br[k];
+      af = __fmaf_rn(static_cast<float>(x), static_cast<float>(y), af);
+    }
+  }
+  const int64_t o = static_cast<int64_t>(m) * ldo + n;
+  if constexpr (kRaw) {
+    static_cast<int32_t*>(out)[o] = ai;
+  } else {
+    const bool has_bias = ep.bias != nullptr;
+    const float bias = has_bias ? OutTraits<OutT>::load(ep.bias, n) : 0.0f;
+    float y;
+    if constexpr (KIND == 0) {
+      y = dequant_one<OutT>(static_cast<float>(ai), __ldg(ep.xs + m),
+                            __ldg(ep.ws + (ep.ws_scalar ? 0 : n)), bias, has_bias, ep.dq_order);
+    } else {
+      y = dequant_one<OutT>(af, __fmul_rn(__ldg(ep.sa), __ldg(ep.sb)), 1.0f, bias, has_bias,
+                            kDqChained);
+    }
+    const bool has_resid = ep.residual != nullptr;
+    const float res = has_resid ? OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(m) * ep.ldr + n) : 0.0f;
+    const float rs = has_resid ? OutTraits<OutT>::load(ep.rscale, n) : 0.0f;
+    y = finish_one<OutT>(y, res, rs, has_resid, ep.act);
+    if constexpr (std::is_same<OutT, float>::value) {
+      static_cast<float*>(out)[o] = y;
+    } else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+      static_cast<__nv_bfloat16*>(out)[o] = __float2bfloat16_rn(y);
+    } else {
+      static_cast<__half*>(out)[o] = __float2half_rn(y);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  return fn;
+}
+
+bool make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, int elem_bytes, const void* base,
+                 uint64_t inner, uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner,
+                 uint32_t box_outer, CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * static_cast<uint64_t>(elem_bytes)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+EpilogueParams to_params(const GemmArgs& g) {
+  EpilogueParams ep{};
+  ep.xs = g.xs;
+  ep.sa = g.sa;
+  ep.sb = g.sb;
+  if (g.epi) {
+    ep.ws = g.epi->ws;
+    ep.ws_scalar = g.epi->ws_numel == 1 ? 1 : 0;
+    ep.bias = g.epi->bias;
+    ep.residual = g.epi->residual;
+    ep.ldr = g.epi->ldr;
+    ep.rscale = g.epi->residual_scale;
+    ep.dq_order = g.epi->dequant_order;
+    ep.act = g.epi->activation;
+  }
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  ep.vec_ws = ep.ws && a16(ep.ws);
+  ep.vec_bias = ep.bias && a16(ep.bias);
+  ep.vec_rscale = ep.rscale && a16(ep.rscale);
+  return ep;
+}
+
+template <int KIND, int BN, typename OutT>
+int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
+              int group_m, int max_ctas, cudaStream_t stream) {
+  using C = Cfg<BN, OutT>;
+  auto kern = gemm_sm100_kernel<KIND, BN, OutT>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute failed: %s", cudaGetErrorString(e));
+      return W8A8_ERR_ACCELERATOR;
+    }
+    attr_set[dev] = true;
+  }
+  const int num_m = static_cast<int>((g.M + kBM - 1) / kBM);
+  const int num_n = static_cast<int>((g.N + BN - 1) / BN);
+  const int tiles = num_m * num_n;
+  const int sms = device_sm_count();
+  int grid = std::min(tiles, max_ctas > 0 ? max_ctas : sms);
+  if (grid < 1) grid = 1;
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ma, mb, md, static_cast<int>(g.M),
+                                                 static_cast<int>(g.N), static_cast<int>(g.K),
+                                                 num_m, num_n, group_m, to_params(g));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("tcgen05 GEMM launch failed: %s", cudaGetErrorString(e));
+    return W8A8_ERR_ACCELERATOR;
+  }
+  return 0;
+}
+
+template <int KIND, typename OutT>
+int launch_simt(const GemmArgs& g, cudaStream_t stream) {
+  if (g.M == 0 || g.N == 0) return 0;
+  dim3 grid(static_cast<unsigned>((g.N + 127) / 128), static_cast<unsigned>(g.M));
+  gemm_simt_kernel<KIND, OutT><<<grid, 128, 0, stream>>>(
+      static_cast<const uint8_t*>(g.a), g.lda, static_cast<const uint8_t*>(g.b), g.ldb, g.out,
+      g.ldo, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), to_params(g));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("CUDA-core GEMM launch failed: %s", cudaGetErrorString(e));
+    return W8A8_ERR_ACCELERATOR;
+  }
+  return 0;
+}
+
+template <int KIND, typename OutT>
+int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_ctas,
+                 cudaStream_t stream) {
+  if (!tc_ok) return launch_simt<KIND, OutT>(g, stream);
+  CUtensorMap ma, mb, md;
+  bool ok = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.a, g.K, g.M, g.lda, kBK, kBM,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  ok = ok && make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.b, g.K, g.N, g.ldb, kBK,
+                         static_cast<uint32_t>(bn), CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMapDataType dt;
+  if constexpr (std::is_same<OutT, float>::value) dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  else if constexpr (std::is_same<OutT, int32_t>::value) dt = CU_TENSOR_MAP_DATA_TYPE_INT32;
+  else if constexpr (std::is_same<OutT, __half>::value) dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  else dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  ok = ok && make_map_2d(&md, dt, static_cast<int>(sizeof(OutT)), g.out, g.N, g.M, g.ldo, 32, 32,
+                         sizeof(OutT) == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  if (!ok) {
+    set_error("cuTensorMapEncodeTiled rejected the operands (M=%lld N=%lld K=%lld)",
+              static_cast<long long>(g.M), static_cast<long long>(g.N), static_cast<long long>(g.K));
+    return W8A8_ERR_RUNTIME;
+  }
+  if (bn == 128) return launch_tc<KIND, 128, OutT>(g, ma, mb, md, group_m, max_ctas, stream);
+  return launch_tc<KIND, 256, OutT>(g, ma, mb, md, group_m, max_ctas, stream);
+}
+
+}  // namespace
+
+int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
+  if (g.M == 0 || g.N == 0) return 0;
+  const int out_bytes = g.out_dtype == W8A8_F32 || g.out_dtype == W8A8_S32 ? 4 : 2;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool tc_ok = g.K > 0 && g.K % 16 == 0 && g.lda % 16 == 0 && g.ldb % 16 == 0 &&
+                     a16(g.a) && a16(g.b) && a16(g.out) && (g.ldo * out_bytes) % 16 == 0 &&
+                     g.M < (1ll << 31) && g.N < (1ll << 31) && g.K < (1ll << 31);
+  int bn = g.cfg && g.cfg->block_n ? g.cfg->block_n : 0;
+  if (bn != 0 && bn != 128 && bn != 256) {
+    set_error("block_n must be 128 or 256, got %d", bn);
+    return W8A8_ERR_VALUE;
+  }
+  if (bn == 0) {
+    const int sms = device_sm_count();
+    const long long tiles256 = ((g.M + kBM - 1) / kBM) * ((g.N + 255) / 256);
+    bn = (tiles256 >= sms || g.N % 256 == 0) && g.N >= 256 ? 256 : 128;
+  }
+  const int group_m = g.cfg && g.cfg->group_m > 0 ? g.cfg->group_m : 8;
+  const int max_ctas = g.cfg ? g.cfg->max_ctas : 0;
+  if (g.kind == 0) {
+    switch (g.out_dtype) {
+      case W8A8_BF16: return dispatch_out<0, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, stream);
+      case W8A8_F16: return dispatch_out<0, __half>(g, tc_ok, bn, group_m, max_ctas, stream);
+      case W8A8_F32: return dispatch_out<0, float>(g, tc_ok, bn, group_m, max_ctas, stream);
+      case W8A8_S32: return dispatch_out<0, int32_t>(g, tc_ok, bn, group_m, max_ctas, stream);
+      default: break;
+    }
+  } else {
+    switch (g.out_dtype) {
+      case W8A8_BF16: return dispatch_out<1, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, stream);
+      case W8A8_F16: return dispatch_out<1, __half>(g, tc_ok, bn, group_m, max_ctas, stream);
+      case W8A8_F32: return dispatch_out<1, float>(g, tc_ok, bn, group_m, max_ctas, stream);
+      default: break;
+    }
+  }
+  set_error("unsupported output dtype code %d", g.out_dtype);
+  return W8A8_ERR_VALUE;
+}
+
+}  // namespace w8a8

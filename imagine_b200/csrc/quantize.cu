@@ -1,0 +1,250 @@
+// Per-token (row-wise) dynamic INT8 quantiser, bf16/f16/f32 -> int8 + fp32
+// row scale.  Replaces the reference's quantize_int8_rowwise_kernel
+// (native/comfy-port/kitchen/int8_linear.cu:184-227, launcher :1322-1371) and
+// its Triton twin (KSRC backends/triton/quantization.py:771-816), with the
+// numerics of the eager path (inference/src/eager.rs:159-171) by default.
+//
+// Layout: a group of WPR warps owns one row.  Each thread loads up to kMaxVec
+// 16-byte vectors of the row into registers (one HBM read of x), the group
+// reduces |x| with shuffles (+ shared memory across warps), and the same
+// registers are scaled, rounded and written as int8.  Rows whose byte length or
+// base are not 16-byte aligned, or that do not fit in registers, take a
+// scalar two-pass path (second pass hits L2).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "epilogue.cuh"
+#include "w8a8_internal.h"
+
+namespace w8a8 {
+namespace {
+
+constexpr int kMaxVec = 16;          // 16-byte vectors per thread (64 registers)
+constexpr int kQuantThreads = 256;   // threads per CTA
+
+template <typename T>
+struct InTraits;
+template <>
+struct InTraits<float> {
+  static constexpr int kPerVec = 4;
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float round_t(float v) { return v; }
+  static constexpr float kFiniteMax = 3.4028234663852886e38f;
+  static constexpr float kTiny = 1.1754943508222875e-38f;
+};
+template <>
+struct InTraits<__nv_bfloat16> {
+  static constexpr int kPerVec = 8;
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ float round_t(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+  }
+  static constexpr float kFiniteMax = 3.3895313892515355e38f;
+  static constexpr float kTiny = 1.1754943508222875e-38f;
+};
+template <>
+struct InTraits<__half> {
+  static constexpr int kPerVec = 8;
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ float round_t(float v) { return __half2float(__float2half_rn(v)); }
+  static constexpr float kFiniteMax = 65504.0f;
+  static constexpr float kTiny = 6.103515625e-05f;
+};
+
+// Row scale from the row's absmax.
+//   eager   (inference/src/eager.rs:163-166):       max(amax / 127, 1e-30)
+//   kitchen (native/.../int8_linear.cu:206-208):    max(min(amax, finite) * (1/127), 1e-30)
+template <typename T>
+__device__ __forceinline__ float row_scale(float amax, int mode) {
+  if (mode == W8A8_SCALE_KITCHEN) {
+    return fmaxf(__fmul_rn(fminf(amax, InTraits<T>::kFiniteMax), 1.0f / 127.0f), 1.0e-30f);
+  }
+  return fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-30f);
+}
+
+// The divisor actually used for the elements: the scale rounded to T, with an
+// exact zero replaced by T's smallest normal (inference/src/eager.rs:94-109).
+template <typename T>
+__device__ __forceinline__ float scale_divisor(float scale) {
+  const float s = InTraits<T>::round_t(scale);
+  return s == 0.0f ? InTraits<T>::kTiny : s;
+}
+
+// PCG-hash stochastic rounding noise of the reference's CUDA quantiser
+// (native/comfy-port/kitchen/int8_linear.cu:82-95): uniform in [0,1) with 24
+// bits, rounded to T.
+__device__ __forceinline__ uint32_t pcg_hash(uint32_t x) {
+  const uint32_t state = x * 747796405u + 2891336453u;
+  const uint32_t word = ((state >> ((state >> 28u) + 4u)) ^ state) * 277803737u;
+  return (word >> 22u) ^ word;
+}
+
+template <typename T>
+__device__ __forceinline__ float quant_elem(float xv, float div, bool stochastic, int64_t idx,
+                                            uint64_t seed) {
+  const float scaled = InTraits<T>::round_t(__fdiv_rn(xv, div));
+  float r;
+  if (stochastic) {
+    const uint64_t key = static_cast<uint64_t>(idx) + seed;
+    const uint32_t folded = static_cast<uint32_t>(key) ^ static_cast<uint32_t>(key >> 32);
+    const float noise = InTraits<T>::round_t(static_cast<float>(pcg_hash(folded) >> 8) * 0x1.0p-24f);
+    r = floorf(InTraits<T>::round_t(__fadd_rn(scaled, noise)));
+  } else {
+    r = rintf(scaled);
+  }
+  return fminf(127.0f, fmaxf(-128.0f, r));
+}
+
+template <typename T, int WPR>
+__global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
+    const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q, int64_t ldq,
+    float* __restrict__ scales, int rows, int cols, int scale_mode, int stochastic, uint64_t seed) {
+  constexpr int kPer = InTraits<T>::kPerVec;
+  constexpr int kGroupThreads = WPR * 32;
+  constexpr int kRowsPerCta = kQuantThreads / kGroupThreads;
+  __shared__ float red[kQuantThreads / 32];
+
+  const int group = threadIdx.x / kGroupThreads;
+  const int gt = threadIdx.x % kGroupThreads;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int row = blockIdx.x * kRowsPerCta + group;
+  const bool live = row < rows;
+  const int nvec = cols / kPer;
+
+  const uint4* xrow = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(live ? row : 0) * ldx);
+  uint4 v[kMaxVec];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int vi = gt + i * kGroupThreads;
+    if (live && vi < nvec) {
+      v[i] = __ldg(xrow + vi);
+      const T* e = reinterpret_cast<const T*>(&v[i]);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) amax = fmaxf(amax, fabsf(InTraits<T>::to_f(e[j])));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if constexpr (WPR > 1) {
+    if (lane == 0) red[warp] = amax;
+    __syncthreads();
+    amax = red[group * WPR];
+#pragma unroll
+    for (int w = 1; w < WPR; ++w) amax = fmaxf(amax, red[group * WPR + w]);
+  }
+  if (!live) return;
+  const float scale = row_scale<T>(amax, scale_mode);
+  if (gt == 0) scales[row] = scale;
+  const float div = scale_divisor<T>(scale);
+  int8_t* qrow = q + static_cast<int64_t>(row) * ldq;
+  const int64_t base_idx = static_cast<int64_t>(row) * cols;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int vi = gt + i * kGroupThreads;
+    if (vi < nvec) {
+      const T* e = reinterpret_cast<const T*>(&v[i]);
+      uint32_t packed[kPer / 4];
+#pragma unroll
+      for (int w = 0; w < kPer / 4; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = vi * kPer + w * 4 + j;
+          const float qv = quant_elem<T>(InTraits<T>::to_f(e[w * 4 + j]), div, stochastic != 0,
+                                         base_idx + c, seed);
+          word |= (static_cast<uint32_t>(static_cast<int>(qv)) & 0xFFu) << (8 * j);
+        }
+        packed[w] = word;
+      }
+      if constexpr (kPer == 8) {
+        reinterpret_cast<uint2*>(qrow)[vi] = make_uint2(packed[0], packed[1]);
+      } else {
+        reinterpret_cast<uint32_t*>(qrow)[vi] = packed[0];
+      }
+    }
+  }
+}
+
+// Scalar two-pass fallback: one CTA per row.
+template <typename T>
+__global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_scalar_kernel(
+    const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q, int64_t ldq,
+    float* __restrict__ scales, int rows, int cols, int scale_mode, int stochastic, uint64_t seed) {
+  __shared__ float red[kQuantThreads / 32];
+  const int row = blockIdx.x;
+  const T* xr = x + static_cast<int64_t>(row) * ldx;
+  float amax = 0.0f;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) amax = fmaxf(amax, fabsf(InTraits<T>::to_f(xr[c])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+  for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+  const float scale = row_scale<T>(amax, scale_mode);
+  if (threadIdx.x == 0) scales[row] = scale;
+  const float div = scale_divisor<T>(scale);
+  int8_t* qr = q + static_cast<int64_t>(row) * ldq;
+  const int64_t base_idx = static_cast<int64_t>(row) * cols;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    qr[c] = static_cast<int8_t>(static_cast<int>(
+        quant_elem<T>(InTraits<T>::to_f(xr[c]), div, stochastic != 0, base_idx + c, seed)));
+  }
+}
+
+template <typename T>
+int launch_quant(const void* x, int64_t ldx, int8_t* q, int64_t ldq, float* scales, int rows,
+                 int cols, int scale_mode, int stochastic, uint64_t seed, cudaStream_t stream) {
+  constexpr int kPer = InTraits<T>::kPerVec;
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (cols % kPer == 0) &&
+                       ((ldx * static_cast<int64_t>(sizeof(T))) % 16 == 0) && (ldq % 8 == 0);
+  const int nvec = cols / kPer;
+  int wpr = 0;
+  if (aligned) {
+    for (int w : {1, 2, 4, 8}) {
+      if (nvec <= w * 32 * kMaxVec) {
+        wpr = w;
+        break;
+      }
+    }
+  }
+  auto go = [&](auto kernel, int rows_per_cta) {
+    const int grid = (rows + rows_per_cta - 1) / rows_per_cta;
+    kernel<<<grid, kQuantThreads, 0, stream>>>(static_cast<const T*>(x), ldx, q, ldq, scales, rows,
+                                               cols, scale_mode, stochastic, seed);
+  };
+  switch (wpr) {
+    case 1: go(quantize_rowwise_vec_kernel<T, 1>, 8); break;
+    case 2: go(quantize_rowwise_vec_kernel<T, 2>, 4); break;
+    case 4: go(quantize_rowwise_vec_kernel<T, 4>, 2); break;
+    case 8: go(quantize_rowwise_vec_kernel<T, 8>, 1); break;
+    default: go(quantize_rowwise_scalar_kernel<T>, 1); break;
+  }
+  return 0;
+}
+
+}  // namespace
+
+int quantize_rowwise_launch(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
+                            int8_t* q, int64_t ldq, float* scales, int scale_mode, int stochastic,
+                            uint64_t seed, cudaStream_t stream) {
+  switch (x_dtype) {
+    case W8A8_BF16:
+      return launch_quant<__nv_bfloat16>(x, ldx, q, ldq, scales, (int)rows, (int)cols, scale_mode,
+                                         stochastic, seed, stream);
+    case W8A8_F16:
+      return launch_quant<__half>(x, ldx, q, ldq, scales, (int)rows, (int)cols, scale_mode,
+                                  stochastic, seed, stream);
+    case W8A8_F32:
+      return launch_quant<float>(x, ldx, q, ldq, scales, (int)rows, (int)cols, scale_mode,
+                                 stochastic, seed, stream);
+    default:
+      return -1;
+  }
+}
+
+}  // namespace w8a8

@@ -1,0 +1,56 @@
+// Internal declarations shared by the libw8a8 translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../../include/w8a8.h"
+
+namespace w8a8 {
+
+// Device-side error word (one per device, module-scope __device__ variable).
+int read_and_clear_device_error(cudaStream_t stream, int* value);
+
+int quantize_rowwise_launch(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
+                            int8_t* q, int64_t ldq, float* scales, int scale_mode, int stochastic,
+                            uint64_t seed, cudaStream_t stream);
+
+// kind 0: int8 x int8 (s32 accumulate); kind 1: e4m3 x e4m3 (f32 accumulate).
+// Returns 0 on success, a W8A8_ERR_* code otherwise (message via set_error).
+struct GemmArgs {
+  int kind;
+  const void* a;
+  int64_t lda;  // elements (bytes)
+  const void* b;
+  int64_t ldb;
+  const float* xs;    // int8: [M] row scales
+  const float* sa;    // fp8: device scalar
+  const float* sb;    // fp8: device scalar
+  const w8a8_epilogue_t* epi;  // may be null for raw s32
+  void* out;
+  int out_dtype;      // W8A8_F32/F16/BF16/S32
+  int64_t ldo;
+  int64_t M, N, K;
+  const w8a8_gemm_config_t* cfg;
+};
+int gemm_launch(const GemmArgs& args, cudaStream_t stream);
+
+int dequant_launch(const int32_t* acc, const float* xs, const w8a8_epilogue_t* epi, void* out,
+                   int out_dtype, int64_t M, int64_t N, cudaStream_t stream);
+
+int gemv_launch(const int8_t* q, const int8_t* w, const float* xs, const w8a8_epilogue_t* epi,
+                void* out, int out_dtype, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+
+int linear_small_launch(const void* x, int x_dtype, const int8_t* w, const w8a8_epilogue_t* epi,
+                        int scale_mode, int8_t* q_out, float* xs_out, void* out, int out_dtype,
+                        int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+
+int quantize_fp8_tensor_launch(const void* x, int x_dtype, int64_t numel, const float* scale,
+                               uint8_t* out, cudaStream_t stream);
+
+// Error reporting (thread-local), implemented in api.cu.
+void set_error(const char* fmt, ...);
+
+// Number of SMs on the current device (cached per device).
+int device_sm_count();
+
+}  // namespace w8a8

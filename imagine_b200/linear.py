@@ -1,0 +1,321 @@
+"""Host-side mirror of the reference's W8A8 linear-family operators.
+
+The functions keep the names, argument meaning and error behaviour of the
+reference's registry operators (inference/src/backend_signatures.rs:445-460,
+KSRC comfy_kitchen/__init__.py) so a caller written against them can switch
+over unchanged; every numeric step runs in libw8a8 (include/w8a8.h) through the
+C ABI -- there is no CPU or PyTorch fallback for the linear itself.  PyTorch is
+used for device memory, streams and the ATen steps the reference's own CUDA
+route also delegates to ATen (input activations that are not fused,
+ConvRot rotation: inference/src/cuda_linear.rs:452-475, 586-600).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+DTYPE_CODE = {torch.float32: N.F32, torch.float16: N.F16, torch.bfloat16: N.BF16}
+DEQUANT = {"eager": N.DQ_EAGER, "scale_product": N.DQ_SCALE_PRODUCT, "chained": N.DQ_CHAINED}
+SCALE_MODE = {"eager": N.SCALE_EAGER, "kitchen": N.SCALE_KITCHEN}
+OUTPUT_ACT = {None: N.ACT_NONE, "none": N.ACT_NONE, "gelu_tanh": N.ACT_GELU_TANH}
+
+
+def _vp(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _cuda(name: str, t: torch.Tensor, device: Optional[torch.device] = None) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (libw8a8 has no CPU path)")
+    if device is not None and t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    return t
+
+
+def _code(dtype: torch.dtype) -> int:
+    if dtype not in DTYPE_CODE:
+        raise ValueError(f"unsupported floating dtype {dtype}")
+    return DTYPE_CODE[dtype]
+
+
+def _config(config) -> Optional[N.GemmConfig]:
+    if config is None:
+        return None
+    if isinstance(config, N.GemmConfig):
+        return config
+    bn, gm, ctas = (tuple(config) + (0, 0, 0))[:3]
+    return N.GemmConfig(int(bn), int(gm), int(ctas), 0)
+
+
+def _cfg_ptr(cfg):
+    return ctypes.byref(cfg) if cfg is not None else None
+
+
+# --------------------------------------------------------------------------
+# a1 / a12
+# --------------------------------------------------------------------------
+def quantize_int8_rowwise(x: torch.Tensor, stochastic_rounding: int = 0, *,
+                          scale_mode: str = "eager"):
+    """Per-row INT8 quantisation (Kitchen ``quantize_int8_rowwise(x,
+    stochastic_rounding)``, inference/src/eager.rs:159-171).
+
+    Returns ``(q int8 [..., K], scale fp32 [..., 1])``.  ``stochastic_rounding > 0``
+    selects the reference CUDA kernel's PCG-hash stochastic rounding with that
+    seed (native/comfy-port/kitchen/int8_linear.cu:82-95)."""
+    _cuda("x", x)
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+    seed = int(stochastic_rounding or 0)
+    N.check(N.LIB.w8a8_quantize_rowwise(
+        _vp(x2), _code(x2.dtype), m, k, x2.stride(0) if m > 0 else k, _vp(q), k, _vp(s),
+        SCALE_MODE[scale_mode], 1 if seed > 0 else 0, max(seed, 0), _stream(x.device)))
+    return q.reshape(x.shape), s.reshape(*x.shape[:-1], 1)
+
+
+def quantize_weight(weight: torch.Tensor):
+    """Offline per-output-channel weight quantisation
+    (inference/src/layout_complete.rs:119-159 TensorWiseINT8Layout.from_float):
+    returns ``(w_q int8 [N, K], ws fp32 [N])``."""
+    q, s = quantize_int8_rowwise(weight)
+    return q, s.reshape(-1)
+
+
+# --------------------------------------------------------------------------
+# a3 / a4 / a5 / a6
+# --------------------------------------------------------------------------
+def _epilogue(weight_scale, bias, residual, residual_scale, dequant, output_act, n, ldr):
+    ep = N.Epilogue()
+    ep.ws = weight_scale.data_ptr()
+    ep.ws_numel = weight_scale.numel()
+    ep.bias = bias.data_ptr() if bias is not None else None
+    ep.residual = residual.data_ptr() if residual is not None else None
+    ep.ldr = ldr if residual is not None else 0
+    ep.residual_scale = residual_scale.data_ptr() if residual_scale is not None else None
+    if dequant not in DEQUANT:
+        raise ValueError(f"unknown dequant order {dequant!r}")
+    ep.dequant_order = DEQUANT[dequant]
+    if output_act not in OUTPUT_ACT:
+        raise ValueError(f"unknown output activation {output_act!r}")
+    ep.activation = OUTPUT_ACT[output_act]
+    return ep
+
+
+def _apply_input(x, input_act, weight, eps):
+    """inference/src/int8_linear.rs:37-97 on the device (ATen, as the reference's
+    CUDA route does for activations it does not fuse)."""
+    if input_act is None or input_act == "none":
+        return x
+    if input_act == "gelu_tanh":
+        return torch.nn.functional.gelu(x, approximate="tanh")
+    if input_act == "swiglu":
+        gate, up = x.chunk(2, dim=-1)
+        return torch.nn.functional.silu(gate).mul_(up)
+    if input_act == "rms_norm":
+        if weight is None:
+            raise ValueError("input_act 'rms_norm' requires act_weight")
+        return torch.nn.functional.rms_norm(x, (x.shape[-1],), weight.to(x.dtype), eps or None)
+    raise ValueError(f"unknown input_act {input_act!r}")
+
+
+_HADAMARD: dict = {}
+
+
+def _hadamard(size: int, device, dtype) -> torch.Tensor:
+    """inference/src/int8_utils.rs:21-58 (cached per device/dtype)."""
+    key = (size, device, dtype)
+    if key not in _HADAMARD:
+        if size < 4 or size & (size - 1) or (size.bit_length() - 1) % 2:
+            raise ValueError(f"Regular Hadamard size must be a power of 4, got {size}")
+        h4 = torch.tensor([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]],
+                          dtype=torch.int64).to(dtype)
+        h = h4
+        while h.shape[0] < size:
+            h = torch.kron(h, h4)
+        _HADAMARD[key] = (h / (size ** 0.5)).to(device)
+    return _HADAMARD[key]
+
+
+def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
+                bias: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                convrot: bool = False, convrot_groupsize: int = 256,
+                input_act: Optional[str] = None, input_act_weight: Optional[torch.Tensor] = None,
+                input_act_eps: float = 0.0, residual: Optional[torch.Tensor] = None,
+                residual_scale: Optional[torch.Tensor] = None, *, dequant: str = "eager",
+                scale_mode: str = "eager", output_act: Optional[str] = None, config=None):
+    """The registry operator ``int8_linear`` (inference/src/backend_signatures.rs:445-460;
+    eager body inference/src/int8_linear.rs:198-277; CUDA route
+    inference/src/cuda_linear.rs:419-824).
+
+    ``dequant`` / ``scale_mode`` choose which of the reference routes' numerics
+    to reproduce (default: the eager route, bit-exact); ``output_act`` applies
+    GELU-tanh in the epilogue (the MLP-up fusion).  ``config`` is an optional
+    ``(block_n, group_m, max_ctas)`` tile configuration.
+    """
+    _cuda("x", x)
+    dev = x.device
+    _cuda("weight", weight, dev)
+    if residual is not None and residual_scale is None:
+        raise ValueError("int8_linear: residual requires residual_scale")
+    out_dtype = out_dtype or x.dtype
+    x = _apply_input(x, input_act, input_act_weight, input_act_eps)
+    k = x.shape[-1]
+    if weight.dim() != 2 or weight.dtype != torch.int8:
+        raise ValueError("weight must be a 2-D int8 tensor [N, K]")
+    if k != weight.shape[-1]:
+        raise ValueError(f"Input and weight inner dimensions must match, got {k} and {weight.shape[-1]}")
+    n = weight.shape[0]
+    ws = weight_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    if ws.numel() not in (1, n):
+        raise ValueError(f"INT8 weight scale must be scalar or per-output-channel, got "
+                         f"{tuple(weight_scale.shape)} for weight shape {tuple(weight.shape)}")
+    if convrot:
+        if convrot_groupsize == 0:
+            raise ZeroDivisionError("integer modulo by zero")
+        if k % convrot_groupsize:
+            raise ValueError(f"ConvRot group size {convrot_groupsize} does not divide input "
+                             f"features {k}")
+        h = _hadamard(convrot_groupsize, dev, x.dtype)
+        shape = x.shape
+        x = torch.matmul(x.reshape(-1, k // convrot_groupsize, convrot_groupsize), h).reshape(shape)
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, k)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    w = weight if weight.is_contiguous() else weight.contiguous()
+    b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
+    r = rs = None
+    if residual is not None:
+        r = residual.to(device=dev, dtype=out_dtype).reshape(m, n).contiguous()
+        rs = residual_scale.to(device=dev, dtype=out_dtype).reshape(-1).contiguous()
+        if rs.numel() != n:
+            raise ValueError("residual_scale must have N elements")
+    out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    ep = _epilogue(ws, b, r, rs, dequant, output_act, n, n)
+    stream = _stream(dev)
+    if 1 <= m <= 2 and k > 0 and m * k <= 32768:
+        # a5: the AdaLN-modulation shape -- quantise and GEMV in one launch.
+        N.check(N.LIB.w8a8_linear_small(_vp(x2), _code(x2.dtype), _vp(w), ctypes.byref(ep),
+                                        SCALE_MODE[scale_mode], None, None, _vp(out),
+                                        _code(out_dtype), m, n, k, stream))
+    else:
+        q = torch.empty((m, k), dtype=torch.int8, device=dev)
+        xs = torch.empty((m,), dtype=torch.float32, device=dev)
+        if m > 0 and k > 0:
+            N.check(N.LIB.w8a8_quantize_rowwise(_vp(x2), _code(x2.dtype), m, k, k, _vp(q), k,
+                                                _vp(xs), SCALE_MODE[scale_mode], 0, 0, stream))
+        cfg = _config(config)
+        N.check(N.LIB.w8a8_gemm_dequant(_vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep), _vp(out),
+                                        _code(out_dtype), n, m, n, k, _cfg_ptr(cfg), stream))
+    return out.reshape(*lead, n)
+
+
+def int8_gemm_s32(q: torch.Tensor, w: torch.Tensor, config=None) -> torch.Tensor:
+    """``cublas_gemm_int8`` replacement: exact int32 q[M,K] . w[N,K]^T."""
+    _cuda("q", q)
+    _cuda("w", w, q.device)
+    m, k = q.shape
+    n = w.shape[0]
+    acc = torch.empty((m, n), dtype=torch.int32, device=q.device)
+    cfg = _config(config)
+    N.check(N.LIB.w8a8_gemm_s32(_vp(q.contiguous()), _vp(w.contiguous()), _vp(acc), m, n, k,
+                                _cfg_ptr(cfg), _stream(q.device)))
+    return acc
+
+
+def dequantize_int8_linear(acc, x_scale, weight_scale, bias=None, out_dtype=torch.bfloat16, *,
+                           dequant="chained"):
+    """``dequantize_int8_linear`` replacement (native/comfy-port/kitchen/int8_linear.cu:517-583)."""
+    _cuda("acc", acc)
+    dev = acc.device
+    m, n = acc.shape
+    ws = weight_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    xs = x_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
+    out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    ep = _epilogue(ws, b, None, None, dequant, None, n, n)
+    N.check(N.LIB.w8a8_dequantize_linear(_vp(acc.contiguous()), _vp(xs), ctypes.byref(ep), _vp(out),
+                                         _code(out_dtype), m, n, _stream(dev)))
+    return out
+
+
+def int8_gemv(q, w, x_scale, weight_scale, bias=None, out_dtype=torch.bfloat16, residual=None,
+              residual_scale=None, *, dequant="chained"):
+    """``int8_gemv_dequant`` replacement (M in {1, 2};
+    native/comfy-port/kitchen/int8_linear.cu:585-708)."""
+    _cuda("q", q)
+    dev = q.device
+    m, k = q.shape
+    n = w.shape[0]
+    ws = weight_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    xs = x_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
+    r = residual.to(device=dev, dtype=out_dtype).reshape(m, n).contiguous() if residual is not None else None
+    rs = residual_scale.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if residual is not None else None
+    out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    ep = _epilogue(ws, b, r, rs, dequant, None, n, n)
+    N.check(N.LIB.w8a8_gemv_dequant(_vp(q.contiguous()), _vp(w.contiguous()), _vp(xs),
+                                    ctypes.byref(ep), _vp(out), _code(out_dtype), m, n, k,
+                                    _stream(dev)))
+    return out
+
+
+# --------------------------------------------------------------------------
+# a9: FP8 e4m3 per-tensor
+# --------------------------------------------------------------------------
+def quantize_per_tensor_fp8(x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """Kitchen ``quantize_per_tensor_fp8(x, scale)`` with the eager numerics
+    (inference/src/eager.rs:74-88).  Returns float8_e4m3fn of x's shape."""
+    _cuda("x", x)
+    s = scale.to(device=x.device, dtype=torch.float32).reshape(-1)[:1].contiguous()
+    xc = x.contiguous()
+    out = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device)
+    N.check(N.LIB.w8a8_quantize_fp8_tensor(_vp(xc), _code(xc.dtype), xc.numel(), _vp(s),
+                                           _vp(out), _stream(x.device)))
+    return out
+
+
+def fp8_linear(a: torch.Tensor, scale_a: torch.Tensor, w: torch.Tensor, scale_w: torch.Tensor,
+               bias: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.bfloat16,
+               config=None) -> torch.Tensor:
+    """Per-tensor FP8 linear: (a . w^T) * (scale_a * scale_w) + bias on tcgen05
+    kind::f8f6f4 (replaces ``_scaled_mm`` TensorWise, inference/src/fp8_ops.rs:81-121)."""
+    _cuda("a", a)
+    dev = a.device
+    _cuda("w", w, dev)
+    if a.dtype != torch.float8_e4m3fn or w.dtype != torch.float8_e4m3fn:
+        raise ValueError("fp8_linear expects float8_e4m3fn operands")
+    lead = a.shape[:-1]
+    a2 = a.reshape(-1, a.shape[-1]).contiguous()
+    m, k = a2.shape
+    n = w.shape[0]
+    sa = scale_a.to(device=dev, dtype=torch.float32).reshape(-1)[:1].contiguous()
+    sw = scale_w.to(device=dev, dtype=torch.float32).reshape(-1)[:1].contiguous()
+    b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
+    out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    cfg = _config(config)
+    N.check(N.LIB.w8a8_fp8_gemm(_vp(a2), _vp(w.contiguous()), _vp(sa), _vp(sw), _vp(b), _vp(out),
+                                _code(out_dtype), m, n, k, _cfg_ptr(cfg), _stream(dev)))
+    return out.reshape(*lead, n)
+
+
+def device_error(device=None) -> int:
+    """Read-and-clear the device-side error word (nonzero: a bounded wait in a
+    tcgen05 kernel gave up)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    return N.LIB.w8a8_device_error(_stream(dev))

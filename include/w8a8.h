@@ -1,0 +1,184 @@
+/*
+ * libw8a8 -- B200 (sm_100a) W8A8 / FP8 / MXFP8 linear family, plain C ABI.
+ *
+ * Drop-in boundary for the reference's Kitchen INT8/FP8 kernels as the Rust
+ * inference crate binds them (reference: inference/native/bridge.hpp:29
+ * `imagine_kitchen_call`, dispatching to the launchers of
+ * native/comfy-port/kitchen/int8_linear.cu and the Kitchen CUDA ops).  Every
+ * entry point takes raw device pointers, element counts/strides and a
+ * cudaStream_t passed as `void*`; no framework types cross the boundary.
+ *
+ * Conventions shared by all entry points:
+ *  - The caller owns every buffer (inference/src/cuda_linear.rs:603-605, 638,
+ *    681 allocate q, scale and out before each call).  The library allocates
+ *    no device memory on any call path.
+ *  - Work is enqueued asynchronously on `stream` (the caller's current stream,
+ *    inference/src/cuda_linear.rs:448) on the calling thread's current device.
+ *  - Return codes follow the reference bridge's exception mapping
+ *    (inference/native/bridge.cpp `protect`): 0 ok, -1 runtime, -9 out of
+ *    memory, -10 accelerator error, -20 ValueError, -21 IndexError.  The
+ *    message is in the thread-local w8a8_last_error().
+ *  - Row-major tensors; `ld*` arguments are row strides in elements.
+ */
+#ifndef IMAGINE_B200_W8A8_H
+#define IMAGINE_B200_W8A8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (inference/native/bridge.hpp:14-16, bridge.cpp protect) */
+#define W8A8_OK 0
+#define W8A8_ERR_RUNTIME (-1)
+#define W8A8_ERR_OOM (-9)
+#define W8A8_ERR_ACCELERATOR (-10)
+#define W8A8_ERR_VALUE (-20)
+#define W8A8_ERR_INDEX (-21)
+
+/* ---- dtype codes.  0/1/2 are the reference's output codes
+ * (inference/src/cuda_linear.rs:488-497). */
+#define W8A8_F32 0
+#define W8A8_F16 1
+#define W8A8_BF16 2
+#define W8A8_S32 3
+#define W8A8_S8 4
+#define W8A8_E4M3 5
+
+/* ---- row-scale semantics of the INT8 quantiser.
+ * EAGER:   max(amax / 127, 1e-30), IEEE divide (inference/src/eager.rs:163-166)
+ * KITCHEN: max(min(amax, finite_max) * (1/127), 1e-30), the reference's CUDA
+ *          and Triton routes (native/comfy-port/kitchen/int8_linear.cu:206-208) */
+#define W8A8_SCALE_EAGER 0
+#define W8A8_SCALE_KITCHEN 1
+
+/* ---- dequant orders of the INT8 linear epilogue.
+ * EAGER:         y = T(acc*(xs*ws)); y = T(y + bias)   (inference/src/int8_linear.rs:244-268)
+ * SCALE_PRODUCT: y = T(fma(acc, xs*ws, bias))          (KSRC triton/quantization.py:861-1018)
+ * CHAINED:       y = T(fma(acc*xs, ws, bias))          (native/.../int8_linear.cu:517-545) */
+#define W8A8_DQ_EAGER 0
+#define W8A8_DQ_SCALE_PRODUCT 1
+#define W8A8_DQ_CHAINED 2
+
+/* ---- output activation applied after bias, before the residual */
+#define W8A8_ACT_NONE 0
+#define W8A8_ACT_GELU_TANH 1
+
+/* Epilogue description shared by the GEMM, GEMV and dequant entry points. */
+typedef struct w8a8_epilogue {
+  const float* ws;            /* [N] per-output-channel weight scales, or [1] */
+  int64_t ws_numel;           /* N or 1 */
+  const void* bias;           /* [N] in the output dtype, or NULL */
+  const void* residual;       /* [M, ldr] in the output dtype, or NULL */
+  int64_t ldr;                /* residual row stride (elements) */
+  const void* residual_scale; /* [N] in the output dtype; required with residual */
+  int32_t dequant_order;      /* W8A8_DQ_* */
+  int32_t activation;         /* W8A8_ACT_* */
+} w8a8_epilogue_t;
+
+/* Optional GEMM launch configuration (what the autotuner selects).  A NULL
+ * pointer, or zero fields, select the built-in heuristic. */
+typedef struct w8a8_gemm_config {
+  int32_t block_n;  /* 128 or 256 output columns per CTA tile */
+  int32_t group_m;  /* M tiles per rasterisation group (L2 reuse) */
+  int32_t max_ctas; /* persistent CTAs (0 = one per SM) */
+  int32_t reserved;
+} w8a8_gemm_config_t;
+
+/* ---- library state ---------------------------------------------------- */
+/* Thread-local message of the last failing call on this thread
+ * (inference/native/bridge.hpp:14 imagine_last_error). */
+const char* w8a8_last_error(void);
+/* cudaError_t of the last accelerator failure on this thread
+ * (inference/native/bridge.hpp:15 imagine_last_accelerator_code). */
+int w8a8_last_accelerator_code(void);
+/* ABI version of this library (major*100 + minor). */
+int w8a8_abi_version(void);
+/* Reads, then clears, the device-side error word of the current device after
+ * synchronising `stream`.  Nonzero means a kernel's bounded wait gave up
+ * (1..4: which barrier).  No reference counterpart: the reference's kernels
+ * have no device-side waits. */
+int w8a8_device_error(void* stream);
+
+/* ---- a1 / a12: per-row INT8 quantiser ------------------------------------
+ * Replaces `quantize_int8_rowwise(x, q, scale, stochastic, seed, stream)`
+ * (call site inference/src/cuda_linear.rs:605-616; kernel
+ * native/comfy-port/kitchen/int8_linear.cu:184-227, launcher :1322-1371).
+ * x [rows, cols] (x_dtype F32/F16/BF16, row stride ldx) -> q int8 [rows, cols]
+ * (row stride ldq) and scale fp32 [rows].  stochastic != 0 uses the
+ * reference CUDA kernel's PCG-hash noise keyed by (row*cols + col + seed). */
+int w8a8_quantize_rowwise(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
+                          int8_t* q, int64_t ldq, float* scale, int scale_mode, int stochastic,
+                          uint64_t seed, void* stream);
+
+/* ---- a3 / a4 / a6: INT8 GEMM with fused dequant epilogue -----------------
+ * Replaces `cutlass_int8_dequant(q, w, xs, ws, bias, out, out_code, stream)`
+ * and `cutlass_int8_dequant_residual(...)` (call sites
+ * inference/src/cuda_linear.rs:724-764; kernels KSRC
+ * backends/cuda/ops/cutlass_gemm_int8.cu:348-420).  Unlike the reference, the
+ * call never declines: it returns 0 for every valid shape (tcgen05 path when
+ * K % 16 == 0 and rows are 16-byte aligned, else a CUDA-core path).
+ * out[m, n] = epilogue(sum_k q[m,k] * w[n,k]) with q int8 [M, K] (stride ldq),
+ * w int8 [N, K] (stride ldw), xs fp32 [M]. */
+int w8a8_gemm_dequant(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* xs,
+                      const w8a8_epilogue_t* epi, void* out, int out_dtype, int64_t ldo, int64_t M,
+                      int64_t N, int64_t K, const w8a8_gemm_config_t* cfg, void* stream);
+
+/* Raw int32 accumulators acc[M, N] = q[M,K] . w[N,K]^T.  Replaces
+ * `cublas_gemm_int8(q, w, acc_i32, workspace, stream)` (call site
+ * inference/src/cuda_linear.rs:769-780; KSRC backends/cuda/ops/cublas_gemm_int8.cu:89-230);
+ * needs no workspace. */
+int w8a8_gemm_s32(const int8_t* q, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
+                  const w8a8_gemm_config_t* cfg, void* stream);
+
+/* Stand-alone dequant of int32 accumulators.  Replaces
+ * `dequantize_int8_linear(acc, xs, ws, bias, out, code, stream)` (call site
+ * inference/src/cuda_linear.rs:782-795; kernel
+ * native/comfy-port/kitchen/int8_linear.cu:517-583, launcher :1721-1798). */
+int w8a8_dequantize_linear(const int32_t* acc, const float* xs, const w8a8_epilogue_t* epi,
+                           void* out, int out_dtype, int64_t M, int64_t N, void* stream);
+
+/* ---- a5: M <= 2 GEMV ---------------------------------------------------------
+ * Replaces `int8_gemv_dequant(q, w, xs, ws, bias, out, out_code, stream,
+ * [resid], [rscale])` (call site inference/src/cuda_linear.rs:657-677;
+ * kernels native/comfy-port/kitchen/int8_linear.cu:585-708, launcher
+ * :1800-1929).  M in {1, 2}; K % 16 == 0 and 16-byte aligned q/w rows use the
+ * vector path, anything else a scalar path. */
+int w8a8_gemv_dequant(const int8_t* q, const int8_t* w, const float* xs,
+                      const w8a8_epilogue_t* epi, void* out, int out_dtype, int64_t M, int64_t N,
+                      int64_t K, void* stream);
+
+/* Fused quantise + GEMV for M <= 2 in one launch.  Replaces
+ * `int8_linear_m1(x, q, xs, w, ws, bias, out, out_code, convrot=false, ...)`
+ * (call site inference/src/cuda_linear.rs:557-583; KSRC
+ * backends/cuda/dlpack_bindings.cpp:3594-3690) and extends it to two rows (the
+ * AdaLN modulation linear).  q_out [M, K] / xs_out [M] receive the codes and
+ * scales (either may be NULL). */
+int w8a8_linear_small(const void* x, int x_dtype, const int8_t* w, const w8a8_epilogue_t* epi,
+                      int scale_mode, int8_t* q_out, float* xs_out, void* out, int out_dtype,
+                      int64_t M, int64_t N, int64_t K, void* stream);
+
+/* ---- a9: FP8 e4m3, per-tensor scales ---------------------------------------
+ * Replaces `quantize_per_tensor_fp8(x, scale, out)` (call site
+ * inference/src/models/qwen_image21/layers.rs:124-151; kernel KSRC
+ * backends/cuda/ops/per_tensor_quantize.cu:39-72) with the eager numerics of
+ * inference/src/eager.rs:74-88: out = e4m3(clamp(x * T(1/scale), +-448)).
+ * `scale` is a device fp32 scalar. */
+int w8a8_quantize_fp8_tensor(const void* x, int x_dtype, int64_t numel, const float* scale,
+                             uint8_t* out, void* stream);
+
+/* Per-tensor FP8 GEMM on tcgen05 kind::f8f6f4: out = (a . b^T) * (sa*sb) + bias.
+ * Replaces `imagine_fp8_scaled_mm` -> at::_scaled_mm_v2 TensorWise
+ * (inference/native/bridge.cpp:401-413).  a e4m3 [M, K], b e4m3 [N, K],
+ * sa / sb device fp32 scalars, bias [N] in the output dtype or NULL. */
+int w8a8_fp8_gemm(const uint8_t* a, const uint8_t* b, const float* sa, const float* sb,
+                  const void* bias, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
+                  const w8a8_gemm_config_t* cfg, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IMAGINE_B200_W8A8_H */

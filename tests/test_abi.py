@@ -1,0 +1,91 @@
+"""The C-ABI library loads, exports every symbol include/w8a8.h declares, and
+rejects bad arguments on the host before touching a GPU (no compute calls)."""
+import ctypes
+import os
+import subprocess
+
+import pytest
+
+from imagine_b200 import _native as N
+
+
+def test_library_exports_every_declared_symbol():
+    declared = N.header_symbols()
+    assert len(declared) >= 10
+    for name in declared:
+        assert hasattr(N.LIB, name), f"{name} declared in include/w8a8.h but not exported"
+    assert set(declared) == set(N.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_abi_version():
+    assert N.LIB.w8a8_abi_version() == 100
+
+
+def test_header_compiles_as_c():
+    src = os.path.join(os.path.dirname(N.HEADER), "w8a8.h")
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-fsyntax-only", "-x", "c", src],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
+def _err():
+    return N.LIB.w8a8_last_error().decode()
+
+
+def test_quantize_rejects_bad_arguments():
+    rc = N.LIB.w8a8_quantize_rowwise(None, N.BF16, -1, 4, 4, None, 4, None, 0, 0, 0, None)
+    assert rc == N.ERR_VALUE and "negative" in _err()
+    rc = N.LIB.w8a8_quantize_rowwise(None, 7, 1, 4, 4, None, 4, None, 0, 0, 0, None)
+    assert rc == N.ERR_VALUE and "dtype" in _err()
+    rc = N.LIB.w8a8_quantize_rowwise(None, N.BF16, 1, 4, 4, None, 4, None, 9, 0, 0, None)
+    assert rc == N.ERR_VALUE and "scale mode" in _err()
+    rc = N.LIB.w8a8_quantize_rowwise(None, N.BF16, 1, 4, 4, None, 4, None, 0, 0, 0, None)
+    assert rc == N.ERR_VALUE and "NULL" in _err()
+    # empty input is a no-op success, like the reference launcher's early return
+    assert N.LIB.w8a8_quantize_rowwise(None, N.BF16, 0, 4, 4, None, 4, None, 0, 0, 0, None) == 0
+
+
+def test_gemm_rejects_bad_epilogue():
+    ep = N.Epilogue()
+    ep.ws = None
+    rc = N.LIB.w8a8_gemm_dequant(None, 16, None, 16, None, ctypes.byref(ep), None, N.BF16, 8, 4, 8,
+                                 16, None, None)
+    assert rc == N.ERR_VALUE and "weight scale" in _err()
+    ep.ws = 16  # any non-null address; never dereferenced on this path
+    ep.ws_numel = 3
+    rc = N.LIB.w8a8_gemm_dequant(None, 16, None, 16, None, ctypes.byref(ep), None, N.BF16, 8, 4, 8,
+                                 16, None, None)
+    assert rc == N.ERR_VALUE and "scalar or per-output-channel" in _err()
+    ep.ws_numel = 1
+    ep.residual = 16
+    rc = N.LIB.w8a8_gemm_dequant(None, 16, None, 16, None, ctypes.byref(ep), None, N.BF16, 8, 4, 8,
+                                 16, None, None)
+    assert rc == N.ERR_VALUE and "residual requires residual_scale" in _err()
+    ep.residual = None
+    ep.dequant_order = 7
+    rc = N.LIB.w8a8_gemm_dequant(None, 16, None, 16, None, ctypes.byref(ep), None, N.BF16, 8, 4, 8,
+                                 16, None, None)
+    assert rc == N.ERR_VALUE and "dequant order" in _err()
+    ep.dequant_order = 0
+    rc = N.LIB.w8a8_gemm_dequant(None, 16, None, 16, None, ctypes.byref(ep), None, N.S8, 8, 4, 8,
+                                 16, None, None)
+    assert rc == N.ERR_VALUE
+
+
+def test_gemv_rejects_large_m():
+    ep = N.Epilogue()
+    ep.ws = 16
+    ep.ws_numel = 1
+    rc = N.LIB.w8a8_gemv_dequant(None, None, None, ctypes.byref(ep), None, N.BF16, 3, 8, 16, None)
+    assert rc == N.ERR_VALUE and "M in {1, 2}" in _err()
+
+
+def test_python_errors_map_to_exceptions():
+    with pytest.raises(ValueError):
+        N.check(N.ERR_VALUE)
+    with pytest.raises(IndexError):
+        N.check(N.ERR_INDEX)
+    with pytest.raises(MemoryError):
+        N.check(N.ERR_OOM)
+    with pytest.raises(N.W8A8Error):
+        N.check(N.ERR_ACCELERATOR)

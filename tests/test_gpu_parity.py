@@ -1,0 +1,321 @@
+"""GPU parity of libw8a8 (called through its C ABI) against the CPU oracle and
+the reference's golden vectors.
+
+Bars: int8 codes, row scales and int32 accumulators are
+bit-exact; bf16/f16/f32 outputs of the dequant orders that the oracle restates
+exactly are bit-exact too, and everything involving transcendental functions
+or a different summation order is held to max-abs-error <= 1% of output RMS.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import eager as O
+from tests import _golden as G
+
+pytestmark = pytest.mark.gpu
+
+RMS_TOL = 0.01  # max |y - ref| <= 1% of rms(ref)
+
+
+def W():
+    import imagine_b200
+
+    return imagine_b200
+
+
+def cuda():
+    return torch.device("cuda", 0)
+
+
+def _b(t):
+    return O.as_bytes(t.cpu())
+
+
+def assert_rms_close(y, ref, tol=RMS_TOL):
+    y = y.float().cpu()
+    ref = ref.float().cpu()
+    rms = ref.pow(2).mean().sqrt().item()
+    err = (y - ref).abs().max().item()
+    assert err <= tol * max(rms, 1e-12), f"max abs err {err} > {tol} * rms {rms}"
+
+
+def no_device_error():
+    assert W().device_error() == 0
+
+
+# ---------------------------------------------------------------- quantiser
+KE = G.load("kitchen_eager")
+MAN = G.manifest()
+
+
+@pytest.mark.parametrize("name", [n for n in MAN["kitchen_eager"] if n.startswith("quant/")])
+def test_quantize_rowwise_golden(name):
+    dt = G.DT[name.split("/")[-1]]
+    x = G.tensor(KE[name + "/x"], dt).to(cuda())
+    q, s = W().quantize_int8_rowwise(x)
+    assert np.array_equal(_b(q), KE[name + "/q"].view(np.uint8).reshape(-1))
+    assert np.array_equal(_b(s), KE[name + "/s"].view(np.uint8).reshape(-1))
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("shape", [(5600, 3072), (256, 12288), (3, 40000), (7, 1001), (1, 8), (130, 24)])
+def test_quantize_rowwise_random(dt, shape):
+    g = torch.Generator().manual_seed(sum(shape))
+    x = (torch.randn(*shape, generator=g) * 4).to(dt)
+    x[0, : min(5, shape[1])] = 0
+    if shape[0] > 2:
+        x[1] = 0
+    qg, sg = W().quantize_int8_rowwise(x.to(cuda()))
+    qo, so = O.quantize_int8_rowwise(x)
+    assert torch.equal(qg.cpu(), qo)
+    assert torch.equal(sg.cpu(), so)
+    qk, sk = W().quantize_int8_rowwise(x.to(cuda()), scale_mode="kitchen")
+    qko, sko = O.quantize_int8_rowwise_kitchen(x)
+    assert torch.equal(qk.cpu(), qko)
+    assert torch.equal(sk.cpu(), sko)
+
+
+def test_quantize_3d_input_and_strided_rows():
+    x = torch.randn(2, 37, 512, dtype=torch.bfloat16)
+    q, s = W().quantize_int8_rowwise(x.to(cuda()))
+    qo, so = O.quantize_int8_rowwise(x)
+    assert q.shape == (2, 37, 512) and s.shape == (2, 37, 1)
+    assert torch.equal(q.cpu(), qo) and torch.equal(s.cpu(), so)
+
+
+# ---------------------------------------------------------------- int8 GEMM
+GEMM_SHAPES = [
+    (128, 128, 256),     # one tile
+    (300, 3072, 1024),   # M tail, several K blocks
+    (130, 160, 264),     # N tail (not a multiple of 256 or 128), K tail inside a block
+    (17, 48, 40),        # tiny
+    (5600, 3072, 512),   # the image-stream M
+    (33, 100, 24),       # K % 16 != 0 -> CUDA-core path
+    (4, 0, 16),          # K == 0
+]
+
+
+def _rand_i8(g, *shape):
+    return torch.randint(-128, 128, shape, generator=g, dtype=torch.int8)
+
+
+@pytest.mark.parametrize("m,k,n", GEMM_SHAPES)
+@pytest.mark.parametrize("bn", [0, 128, 256])
+def test_gemm_s32_exact(m, k, n, bn):
+    g = torch.Generator().manual_seed(m * 7 + k * 3 + n)
+    q = _rand_i8(g, m, k)
+    w = _rand_i8(g, n, k)
+    acc = W().int8_gemm_s32(q.to(cuda()), w.to(cuda()), config=(bn, 8, 0))
+    torch.cuda.synchronize()
+    no_device_error()
+    assert torch.equal(acc.cpu(), O.int8_accumulate(q, w))
+
+
+@pytest.mark.parametrize("m,k,n", GEMM_SHAPES[:-1])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_int8_linear_eager_order_bit_exact(m, k, n, out_dtype):
+    g = torch.Generator().manual_seed(m + k + n)
+    x = torch.randn(m, k, generator=g).to(out_dtype)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(out_dtype)
+    wq, ws = O.quantize_weight(w)
+    b = (torch.randn(n, generator=g) * 0.02).to(out_dtype)
+    y = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda()), out_dtype=out_dtype)
+    ref = O.int8_linear(x, wq, ws, b, out_dtype=out_dtype)
+    no_device_error()
+    assert np.array_equal(_b(y), _b(ref))
+
+
+@pytest.mark.parametrize("name", [n for n in MAN["kitchen_eager"] if n.startswith("linear/")
+                                  and "input_act" not in n and "convrot" not in n])
+def test_int8_linear_golden(name):
+    dn = [p for p in name.split("_") if p in G.DT][0]
+    dt = G.DT[dn]
+    x = G.tensor(KE[name + "/x"], dt).to(cuda())
+    wq = G.tensor(KE[name + "/wq"], torch.int8).to(cuda())
+    ws = G.tensor(KE[name + "/ws"], torch.float32).to(cuda())
+    b = G.tensor(KE[name + "/bias"], dt).to(cuda()) if name + "/bias" in KE else None
+    kw = {}
+    if name + "/residual" in KE:
+        kw.update(residual=G.tensor(KE[name + "/residual"], dt).to(cuda()),
+                  residual_scale=G.tensor(KE[name + "/residual_scale"], dt).to(cuda()))
+    y = W().int8_linear(x, wq, ws, b, out_dtype=dt, **kw)
+    ref = G.tensor(KE[name + "/y"], dt)
+    if "residual" in name:
+        assert_rms_close(y, ref)  # addcmul on the CPU vs one fma on the GPU
+        # the linear part before the residual is bit-exact
+        y0 = W().int8_linear(x, wq, ws, b, out_dtype=dt)
+        r0 = O.int8_linear(x.cpu(), wq.cpu(), ws.cpu(), b.cpu() if b is not None else None, out_dtype=dt)
+        assert np.array_equal(_b(y0), _b(r0))
+    else:
+        assert np.array_equal(_b(y), KE[name + "/y"].view(np.uint8).reshape(-1))
+    acc = W().int8_gemm_s32(G.tensor(KE[name + "/xq"], torch.int8).to(cuda()), wq)
+    assert np.array_equal(acc.cpu().numpy(), KE[name + "/acc"])
+
+
+@pytest.mark.parametrize("name", [n for n in MAN["kitchen_eager"] if n.startswith("linear/")
+                                  and ("input_act" in n or "convrot" in n)])
+def test_int8_linear_golden_input_act_and_convrot(name):
+    """Input activations / ConvRot run as device ATen ops before the quantiser
+    (as the reference's CUDA route does when it does not fuse them); their
+    results may differ from the CPU by an ulp, so the output is held to the
+    tolerance bar."""
+    dn = [p for p in name.split("_") if p in G.DT][0]
+    dt = G.DT[dn]
+    x = G.tensor(KE[name + "/x"], dt).to(cuda())
+    wq = G.tensor(KE[name + "/wq"], torch.int8).to(cuda())
+    ws = G.tensor(KE[name + "/ws"], torch.float32).to(cuda())
+    b = G.tensor(KE[name + "/bias"], dt).to(cuda()) if name + "/bias" in KE else None
+    kw = {}
+    k = wq.shape[1]
+    if "input_act" in name:
+        if name + "/act_w" in KE:
+            kw.update(input_act="rms_norm", input_act_weight=G.tensor(KE[name + "/act_w"], dt).to(cuda()),
+                      input_act_eps=1e-6)
+        elif x.shape[1] == 2 * k:
+            kw.update(input_act="swiglu")
+        else:
+            kw.update(input_act="gelu_tanh")
+    if "convrot" in name:
+        kw.update(convrot=True, convrot_groupsize=256)
+    y = W().int8_linear(x, wq, ws, b, out_dtype=dt, **kw)
+    assert_rms_close(y, G.tensor(KE[name + "/y"], dt))
+
+
+PROBE = G.load("triton_probe")
+
+
+@pytest.mark.parametrize("case", MAN["triton_probe"], ids=lambda c: c["name"])
+def test_triton_probe_bytes(case):
+    """The reference's recorded Triton-route outputs, reproduced by the tcgen05
+    GEMM (or the M<=2 GEMV) with kitchen scales and the scale-product epilogue."""
+    x, w, ws, b, dt = G.probe_inputs(case)
+    y = W().int8_linear(x.to(cuda()), w.to(cuda()), ws.to(cuda()), b.to(cuda()) if b is not None else None,
+                        out_dtype=dt, dequant="scale_product", scale_mode="kitchen")
+    q, s = W().quantize_int8_rowwise(x.to(cuda()), scale_mode="kitchen")
+    assert np.array_equal(_b(q), PROBE[case["name"] + "/q"])
+    assert np.array_equal(_b(s), PROBE[case["name"] + "/s"])
+    assert np.array_equal(_b(y), PROBE[case["name"] + "/y"])
+
+
+@pytest.mark.parametrize("order", ["scale_product", "chained"])
+@pytest.mark.parametrize("m,k,n", [(300, 3072, 1024), (130, 160, 264), (1, 256, 72), (2, 3072, 520)])
+def test_dequant_orders_bit_exact(order, m, k, n):
+    g = torch.Generator().manual_seed(11 + m)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    wq = _rand_i8(g, n, k)
+    ws = torch.rand(n, generator=g) * 1e-3 + 1e-4
+    b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
+    y = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda()), dequant=order)
+    ref = O.int8_linear(x, wq, ws, b, out_dtype=torch.bfloat16, dequant=order)
+    assert np.array_equal(_b(y), _b(ref))
+
+
+@pytest.mark.parametrize("m,k,n", [(300, 3072, 1024), (5600, 3072, 256)])
+def test_gelu_epilogue(m, k, n):
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    wq, ws = O.quantize_weight(w)
+    b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
+    y = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda()), output_act="gelu_tanh")
+    ref = O.int8_linear(x, wq, ws, b, out_dtype=torch.bfloat16, output_act="gelu_tanh")
+    assert_rms_close(y, ref)
+
+
+def test_residual_epilogue():
+    g = torch.Generator().manual_seed(9)
+    m, k, n = 257, 512, 384
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    wq = _rand_i8(g, n, k)
+    ws = torch.rand(n, generator=g) * 1e-3
+    r = torch.randn(m, n, generator=g).to(torch.bfloat16)
+    rs = torch.rand(n, generator=g).to(torch.bfloat16)
+    y = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), None, residual=r.to(cuda()),
+                        residual_scale=rs.to(cuda()))
+    ref = O.int8_linear(x, wq, ws, None, out_dtype=torch.bfloat16, residual=r, residual_scale=rs)
+    assert_rms_close(y, ref)
+
+
+def test_headline_shape_properties():
+    """5600 x 3072 -> 12288 (the MLP-up headline): exact int32 row checksums over
+    the whole output, exact rows on a random sample, and the GELU epilogue on
+    the sampled rows."""
+    g = torch.Generator().manual_seed(0)
+    m, k, n = 5600, 3072, 12288
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    wq, ws = O.quantize_weight(w)
+    xd = x.to(cuda())
+    qd, sd = W().quantize_int8_rowwise(xd)
+    acc = W().int8_gemm_s32(qd, wq.to(cuda()))
+    q = qd.cpu()
+    # checksum of checksums: sum_n acc[m, n] == q[m, :] . colsum(w)
+    colsum = wq.to(torch.int64).sum(dim=0)
+    want = (q.to(torch.int64) * colsum).sum(dim=1)
+    got = acc.to(torch.int64).sum(dim=1).cpu()
+    assert torch.equal(got, want)
+    rows = torch.randperm(m, generator=g)[:48]
+    assert torch.equal(acc[rows.to(cuda())].cpu(), O.int8_accumulate(q[rows], wq))
+    y = W().int8_linear(xd, wq.to(cuda()), ws.to(cuda()), None, output_act="gelu_tanh")
+    ref = O.int8_linear(x[rows], wq, ws, None, out_dtype=torch.bfloat16, output_act="gelu_tanh")
+    assert_rms_close(y[rows.to(cuda())], ref)
+    no_device_error()
+
+
+# ---------------------------------------------------------------- GEMV (M <= 2)
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("k,n", [(3072, 18432), (64, 24), (48, 40), (100, 36)])
+def test_gemv_exact(m, k, n):
+    g = torch.Generator().manual_seed(m * 1000 + k + n)
+    q = _rand_i8(g, m, k)
+    wq = _rand_i8(g, n, k)
+    xs = torch.rand(m, generator=g) * 0.01
+    ws = torch.rand(n, generator=g) * 1e-3
+    b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
+    y = W().int8_gemv(q.to(cuda()), wq.to(cuda()), xs.to(cuda()), ws.to(cuda()), b.to(cuda()))
+    ref = O.int8_gemv(q, wq, xs, ws, b, torch.bfloat16)
+    assert np.array_equal(_b(y), _b(ref))
+
+
+@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("k,n", [(3072, 18432), (64, 24), (100, 36)])
+def test_fused_small_linear_matches_eager(m, dt, k, n):
+    """a5: SiLU(temb) [2, 3072] -> 18432 through one fused quantise+GEMV launch."""
+    g = torch.Generator().manual_seed(m + k + n)
+    x = torch.nn.functional.silu(torch.randn(m, k, generator=g)).to(dt)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(dt)
+    wq, ws = O.quantize_weight(w)
+    b = (torch.randn(n, generator=g) * 0.02).to(dt)
+    y = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda()), out_dtype=dt)
+    ref = O.int8_linear(x, wq, ws, b, out_dtype=dt)
+    assert np.array_equal(_b(y), _b(ref))
+
+
+# ---------------------------------------------------------------- FP8
+@pytest.mark.parametrize("name", [n for n in MAN["kitchen_eager"] if n.startswith("fp8")])
+def test_fp8_quantize_golden(name):
+    dt = G.DT[name.split("/")[-1]]
+    x = G.tensor(KE[name + "/x"], dt).to(cuda())
+    s = G.tensor(KE[name + "/scale"], torch.float32).to(cuda())
+    q = W().quantize_per_tensor_fp8(x, s)
+    assert np.array_equal(_b(q), KE[name + "/q"].reshape(-1))
+
+
+@pytest.mark.parametrize("m,k,n", [(300, 3072, 1024), (5600, 3072, 512), (130, 160, 264), (33, 100, 24)])
+def test_fp8_linear(m, k, n):
+    g = torch.Generator().manual_seed(m + n)
+    x = torch.randn(m, k, generator=g)
+    x = torch.where(torch.rand(m, k, generator=g) < 0.01, x * 20, x).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    sa = (x.abs().max().float() / 448).reshape(1)
+    sw = (w.abs().max().float() / 448).reshape(1)
+    b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
+    aq = W().quantize_per_tensor_fp8(x.to(cuda()), sa.to(cuda()))
+    wq = W().quantize_per_tensor_fp8(w.to(cuda()), sw.to(cuda()))
+    assert np.array_equal(_b(aq), _b(O.quantize_fp8(x, sa)))
+    y = W().fp8_linear(aq, sa.to(cuda()), wq, sw.to(cuda()), b.to(cuda()))
+    no_device_error()
+    assert_rms_close(y, O.fp8_linear_exact(aq.cpu(), sa, wq.cpu(), sw, b))
+    assert_rms_close(y, O.fp8_linear(aq.cpu(), sa, wq.cpu(), sw, b))
