@@ -1,0 +1,330 @@
+"""Benchmark of the W8A8 linear hot path (BASELINE metric: W8A8 linear TOPS).
+
+One step = one pass of the reference's ``int8_linear`` operator over one batch
+of synthetic input, on the headline shape of the BASELINE sweep: the MMDiT
+MLP-up linear, X bf16 [5600, 3072] -> per-token INT8 quantiser -> tcgen05 INT8
+GEMM with dequant + bias + GELU-tanh epilogue -> Y bf16 [5600, 12288].
+Inputs are seeded synthetic tensors with the BASELINE distributions (X ~ N(0,1),
+W ~ N(0, 0.02) quantised per output channel, bias ~ N(0, 0.02)).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU; every rank runs its own linear
+(independent CFG branches / seeds: weak scaling, no data-path collective) and
+the job's value is the sum of all ranks' work over the slowest rank's time.
+``--impl reference`` times the reference's LibTorch CPU path (the oracle's
+restatement of inference/src/int8_linear.rs:198-277) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M, K, N = 5600, 3072, 12288
+OPS = 2.0 * M * N * K
+WORKLOAD = {"workload": "mmdit_mlp_up_w8a8_linear", "M": M, "K": K, "N": N,
+            "x": "bf16 N(0,1)", "w": "int8 per-channel from bf16 N(0,0.02)",
+            "epilogue": "per-token x per-channel dequant + bias + gelu_tanh -> bf16",
+            "quantiser": "per-token dynamic absmax (eager numerics)",
+            "l2": "flushed (256 MiB write) before every timed step"}
+METRIC = "W8A8 linear TOPS (% int8 peak)"
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while active."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(device, seed=0):
+    from imagine_b200 import quantize_weight
+
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=torch.Generator().manual_seed(seed + 1)) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, generator=torch.Generator().manual_seed(seed + 2)) * 0.02).to(torch.bfloat16)
+    wq, ws = quantize_weight(w.to(device))
+    return x, wq, ws, b.to(device)
+
+
+def traffic_per_launch():
+    """DRAM bytes per GEMM launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get("gemm_dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+def run_ours(args, rank, world, local_rank):
+    import ctypes
+
+    import imagine_b200 as W
+    from imagine_b200 import _native as NAT
+    from imagine_b200.linear import _epilogue, _stream, _vp
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    x_host, wq, ws, bias = make_inputs(dev, seed=rank * 10)
+    x = x_host.to(dev)
+    q = torch.empty((M, K), dtype=torch.int8, device=dev)
+    xs = torch.empty((M,), dtype=torch.float32, device=dev)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    ep = _epilogue(ws, bias, None, None, "eager", "gelu_tanh", N, N)
+    stream = torch.cuda.current_stream(dev)
+    sp = _stream(dev)
+
+    def quant():
+        NAT.check(NAT.LIB.w8a8_quantize_rowwise(_vp(x), NAT.BF16, M, K, K, _vp(q), K, _vp(xs),
+                                                NAT.SCALE_EAGER, 0, 0, sp))
+
+    def gemm():
+        NAT.check(NAT.LIB.w8a8_gemm_dequant(_vp(q), K, _vp(wq), K, _vp(xs), ctypes.byref(ep),
+                                            _vp(y), NAT.BF16, N, M, N, K, None, sp))
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        quant()
+        gemm()
+    torch.cuda.synchronize()
+    if W.device_error() != 0:
+        raise RuntimeError("device error during warm-up")
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record(stream)
+        quant()
+        ev[i][1].record(stream)
+        gemm()
+        ev[i][2].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    step_ms = [ev[i][0].elapsed_time(ev[i][2]) for i in range(args.steps)]
+    quant_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(args.steps)]
+    gemm_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps)]
+    total_ms = sum(step_ms)
+
+    # ---- e2e through the public operator with host buffers (H2D of X, D2H of Y)
+    x_pin = x_host.pin_memory()
+    y_pin = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        yd = W.int8_linear(x_pin.to(dev, non_blocking=True), wq, ws, bias, output_act="gelu_tanh")
+        y_pin.copy_(yd, non_blocking=True)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        yd = W.int8_linear(x_pin.to(dev, non_blocking=True), wq, ws, bias, output_act="gelu_tanh")
+        y_pin.copy_(yd, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms, e2e_ms = float(t[0]), float(t[1])
+    if W.device_error() != 0:
+        raise RuntimeError("device error during timing")
+    return dict(total_ms=total_ms, step_ms=step_ms, quant_ms=quant_ms, gemm_ms=gemm_ms,
+                e2e_ms=e2e_ms, clocks=clocks, x_host=x_host, wq=wq, ws=ws, bias=bias)
+
+
+def cpu_baseline(rows: int = 256, reps: int = 3):
+    """The reference's LibTorch CPU path (oracle restatement of
+    inference/src/int8_linear.rs:198-277) on a bounded sample: `rows` of the
+    5600 tokens through the full 3072 -> 12288 linear, all host threads."""
+    from oracle import eager as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(rows, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=torch.Generator().manual_seed(1)) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, generator=torch.Generator().manual_seed(2)) * 0.02).to(torch.bfloat16)
+    wq, ws = O.quantize_weight(w)
+    O.int8_linear(x[:16], wq, ws, b, output_act="gelu_tanh")  # warm-up
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.int8_linear(x, wq, ws, b, output_act="gelu_tanh")
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    return {"value": 2.0 * rows * N * K / sec / 1e12, "unit": "TOPS",
+            "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{rows} of {M} rows through the full {K}->{N} linear (quantise, int32 "
+                      f"_int_mm, dequant, bias, gelu), median of {reps}",
+            "seconds_per_sample": sec}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        steps = []
+        base = None
+        for _ in range(args.warmup + args.steps):
+            base = cpu_baseline(rows=64, reps=1)
+            steps.append(base["seconds_per_sample"])
+        sec = statistics.median(steps[args.warmup:])
+        value = 2.0 * 64 * N * K / sec / 1e12
+        line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic", "config": WORKLOAD, "impl": "reference",
+                "cpu_baseline": {"value": value, "unit": "TOPS", "cores": base["cores"],
+                                 "kind": "port",
+                                 "sample": "64 of 5600 rows per step through the full linear"},
+                "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    if world > 1:
+        torch.distributed.init_process_group(
+            "nccl", device_id=torch.device("cuda", local_rank),
+            timeout=__import__("datetime").timedelta(seconds=120))
+    r = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    hbm, bf16, src = peaks()
+    int8_peak = 2.0 * bf16  # dense int8 rate is twice dense bf16 on B200
+    avg_gemm_ms = statistics.mean(r["gemm_ms"])
+    avg_quant_ms = statistics.mean(r["quant_ms"])
+    gemm_tops = OPS / (avg_gemm_ms * 1e-3) / 1e12
+    quant_bytes = M * K * 3 + 4 * M
+    quant_gbs = quant_bytes / (avg_quant_ms * 1e-3) / 1e9
+    value = world * OPS * args.steps / (r["total_ms"] * 1e-3) / 1e12
+    e2e_tops = world * OPS / (r["e2e_ms"] * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["total_ms"] / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic", "config": dict(WORKLOAD, parallelism=f"replicas{world}"),
+        "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
+                     "unit": "TOPS", "frac": gemm_tops / int8_peak,
+                     "traffic": traffic_per_launch(),
+                     "kernel": "gemm_sm100_kernel<kind::i8, BN=256, bf16>",
+                     "peak_source": f"2 x bf16_tflops of MEASURED_PEAKS.json ({src})"},
+        "kernels": {
+            "quantize_rowwise": {"ms": avg_quant_ms, "GB/s": quant_gbs, "peak_GB/s": hbm,
+                                 "frac": quant_gbs / hbm, "bytes": quant_bytes},
+            "gemm_dequant_gelu": {"ms": avg_gemm_ms, "TOPS": gemm_tops},
+        },
+        "e2e": {"value": e2e_tops, "unit": "TOPS", "h2d_bytes_per_step": M * K * 2,
+                "d2h_bytes_per_step": M * N * 2, "ms_per_step": r["e2e_ms"],
+                "path": "imagine_b200.int8_linear on a pinned host X, result copied to pinned host"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": r["clocks"],
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = {k: v for k, v in cpu_baseline().items() if k != "seconds_per_sample"}
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

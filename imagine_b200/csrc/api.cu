@@ -138,7 +138,7 @@ int w8a8_gemm_dequant(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw
   if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
   if (int rc = check_epilogue(epi, N, true)) return rc;
   if (M == 0 || N == 0) return finish(0);
-  if (!q || !w || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if ((K > 0 && (!q || !w)) || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
   if (ldq < K || ldw < K || ldo < N) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
   GemmArgs g{};
   g.kind = 0;
@@ -162,7 +162,7 @@ int w8a8_gemm_s32(const int8_t* q, const int8_t* w, int32_t* acc, int64_t M, int
                   const w8a8_gemm_config_t* cfg, void* stream) {
   if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   if (M == 0 || N == 0) return finish(0);
-  if (!q || !w || !acc) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if ((K > 0 && (!q || !w)) || !acc) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
   GemmArgs g{};
   g.kind = 0;
   g.a = q;
@@ -233,7 +233,7 @@ int w8a8_fp8_gemm(const uint8_t* a, const uint8_t* b, const float* sa, const flo
   if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
   if (M == 0 || N == 0) return finish(0);
-  if (!a || !b || !sa || !sb || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if ((K > 0 && (!a || !b)) || !sa || !sb || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
   w8a8_epilogue_t epi{};
   epi.ws_numel = 1;
   epi.bias = bias;

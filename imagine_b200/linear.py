@@ -215,7 +215,7 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
                                         _code(out_dtype), m, n, k, stream))
     else:
         q = torch.empty((m, k), dtype=torch.int8, device=dev)
-        xs = torch.empty((m,), dtype=torch.float32, device=dev)
+        xs = (torch.empty if k > 0 else torch.zeros)((m,), dtype=torch.float32, device=dev)
         if m > 0 and k > 0:
             N.check(N.LIB.w8a8_quantize_rowwise(_vp(x2), _code(x2.dtype), m, k, k, _vp(q), k,
                                                 _vp(xs), SCALE_MODE[scale_mode], 0, 0, stream))
