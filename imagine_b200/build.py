@@ -24,7 +24,7 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libw8a8.so")
 
 SOURCES = ["api.cu", "quantize.cu", "gemm_sm100.cu", "gemv.cu"]
-HEADERS = ["sm100_ptx.cuh", "epilogue.cuh", "w8a8_internal.h"]
+HEADERS = ["sm100_ptx.cuh", "epilogue.cuh", "quant_common.cuh", "w8a8_internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3",

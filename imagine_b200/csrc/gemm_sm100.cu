@@ -35,8 +35,10 @@
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
+#include <type_traits>
 
 #include "epilogue.cuh"
+#include "quant_common.cuh"
 #include "sm100_ptx.cuh"
 #include "w8a8_internal.h"
 
@@ -66,7 +68,7 @@ namespace {
 constexpr int kBM = 128;          // rows per tile (TMEM lanes)
 constexpr int kBK = 128;          // K bytes per pipeline stage (one 128B swizzle row)
 constexpr int kUmmaK = 32;        // K per tcgen05.mma for 8-bit operand kinds
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;   // two per TMEM lane quadrant, splitting the columns
 constexpr int kProducerWarp = kEpiWarps;
 constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kThreads = (kEpiWarps + 2) * 32;
@@ -152,7 +154,39 @@ __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-template <int KIND, int BN, typename OutT>
+// Output rounding to OutT's precision (value kept as fp32).  bf16 uses the
+// exact integer round-to-nearest-even (ALU instead of the XU pipe).
+template <typename OutT>
+__device__ __forceinline__ float round_out(float v) {
+  if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+    return round_bf16_alu(v);
+  } else {
+    return OutTraits<OutT>::round(v);
+  }
+}
+
+// One output element of the fused epilogue, with the dequant order (ORDER)
+// and the output activation (ACT) fixed at compile time.  Returns the value
+// rounded to OutT before the optional residual.
+template <typename OutT, int ORDER, int ACT>
+__device__ __forceinline__ float epi_elem(float a, float xs_row, float ws_col, float bias_col,
+                                          bool has_bias) {
+  float y;
+  if constexpr (ORDER == kDqEager) {
+    y = round_out<OutT>(__fmul_rn(a, __fmul_rn(xs_row, ws_col)));
+    if (has_bias) y = round_out<OutT>(__fadd_rn(y, bias_col));
+  } else if constexpr (ORDER == kDqScaleProduct) {
+    const float sc = __fmul_rn(xs_row, ws_col);
+    y = round_out<OutT>(has_bias ? __fmaf_rn(a, sc, bias_col) : __fmul_rn(a, sc));
+  } else {
+    const float t = __fmul_rn(a, xs_row);
+    y = round_out<OutT>(has_bias ? __fmaf_rn(t, ws_col, bias_col) : __fmul_rn(t, ws_col));
+  }
+  if constexpr (ACT == kActGeluTanh) y = round_out<OutT>(gelu_tanh(y));
+  return y;
+}
+
+template <int KIND, int BN, typename OutT, int ORDER, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmD, int M, int N, int K, int num_m_tiles,
@@ -262,7 +296,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    // Warp e owns TMEM lane quadrant e % 4 (rows 32q..32q+31 of the tile) and
+    // the 32-column chunks c with c % 2 == e / 4.
+    const int quad = warp & 3;
+    const int half = warp >> 2;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     uint8_t* stage0 = sD + warp * 2 * C::kStageD;
     const bool has_bias = ep.bias != nullptr;
     const bool has_resid = ep.residual != nullptr;
@@ -280,17 +318,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int row0 = mb * kBM + warp * 32;
+      const int row0 = mb * kBM + quad * 32;
       const int grow = row0 + lane;
       float xs_row = 0.0f;
       if constexpr (KIND == 0 && !kRaw) xs_row = grow < M ? __ldg(ep.xs + grow) : 0.0f;
-      for (int c = 0; c < BN / 32; ++c) {
+      if constexpr (KIND == 1) xs_row = fp8_scale;
+      for (int c = half; c < BN / 32; c += 2) {
         const int col0 = col_base + c * 32;
         if (col0 >= N) break;
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + c * 32, r);
-        tmem_ld_wait();
-        float wsv[32], bv[32], rsv[32];
+        float wsv[32], bv[32];
         if constexpr (!kRaw) {
           if constexpr (KIND == 0) {
             if (ep.ws_scalar) {
@@ -300,9 +338,39 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               load_cols32<float>(ep.ws, col0, N, ep.vec_ws, wsv);
             }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) wsv[j] = 1.0f;
           }
-          if (has_bias) load_cols32<OutT>(ep.bias, col0, N, ep.vec_bias, bv);
-          if (has_resid) load_cols32<OutT>(ep.rscale, col0, N, ep.vec_rscale, rsv);
+          if (has_bias) {
+            load_cols32<OutT>(ep.bias, col0, N, ep.vec_bias, bv);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) bv[j] = 0.0f;
+          }
+        }
+        tmem_ld_wait();
+        float y[32];
+        if constexpr (!kRaw) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float a = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(r[j]))
+                                        : __uint_as_float(r[j]);
+            y[j] = epi_elem<OutT, (KIND == 0 ? ORDER : kDqChained), ACT>(a, xs_row, wsv[j], bv[j],
+                                                                          has_bias);
+          }
+          if (has_resid) {
+            float rsv[32];
+            load_cols32<OutT>(ep.rscale, col0, N, ep.vec_rscale, rsv);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float res = (grow < M && col0 + j < N)
+                                    ? OutTraits<OutT>::load(ep.residual,
+                                                            static_cast<int64_t>(grow) * ep.ldr + col0 + j)
+                                    : 0.0f;
+              y[j] = round_out<OutT>(__fmaf_rn(y[j], rsv[j], res));
+            }
+          }
         }
         uint8_t* st = stage0 + (chunk_ctr & 1u) * C::kStageD;
         if (lane == 0) tma_store_wait_read<1>();
@@ -311,35 +379,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           // 32 x 4-byte values = 8 chunks of 16 B; 128B swizzle: chunk ^= row & 7.
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc) {
-            uint32_t w4[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int j = cc * 4 + e;
-              if constexpr (kRaw) {
-                w4[e] = r[j];
-              } else {
-                const float a = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(r[j]))
-                                            : __uint_as_float(r[j]);
-                float y;
-                if constexpr (KIND == 0) {
-                  y = dequant_one<OutT>(a, xs_row, wsv[j], (has_bias ? bv[j] : 0.0f), has_bias,
-                                        ep.dq_order);
-                } else {
-                  y = dequant_one<OutT>(a, fp8_scale, 1.0f, (has_bias ? bv[j] : 0.0f), has_bias,
-                                        kDqChained);
-                }
-                float res = 0.0f;
-                if (has_resid && grow < M && col0 + j < N) {
-                  res = OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(grow) * ep.ldr +
-                                                               col0 + j);
-                }
-                y = finish_one<OutT>(y, res, (has_resid ? rsv[j] : 0.0f), has_resid, ep.act);
-                w4[e] = __float_as_uint(y);
-              }
+            uint4 v;
+            if constexpr (kRaw) {
+              v = make_uint4(r[cc * 4], r[cc * 4 + 1], r[cc * 4 + 2], r[cc * 4 + 3]);
+            } else {
+              v = make_uint4(__float_as_uint(y[cc * 4]), __float_as_uint(y[cc * 4 + 1]),
+                             __float_as_uint(y[cc * 4 + 2]), __float_as_uint(y[cc * 4 + 3]));
             }
             const int phys = cc ^ (lane & 7);
-            *reinterpret_cast<uint4*>(st + lane * 128 + phys * 16) =
-                make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            *reinterpret_cast<uint4*>(st + lane * 128 + phys * 16) = v;
           }
         } else {
           // 32 x 2-byte values = 4 chunks of 16 B; 64B swizzle: chunk ^= (row >> 1) & 3.
@@ -348,28 +396,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t w4[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              float y2[2];
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int j = cc * 8 + e * 2 + h;
-                const float a = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(r[j]))
-                                            : __uint_as_float(r[j]);
-                float y;
-                if constexpr (KIND == 0) {
-                  y = dequant_one<OutT>(a, xs_row, wsv[j], (has_bias ? bv[j] : 0.0f), has_bias,
-                                        ep.dq_order);
-                } else {
-                  y = dequant_one<OutT>(a, fp8_scale, 1.0f, (has_bias ? bv[j] : 0.0f), has_bias,
-                                        kDqChained);
-                }
-                float res = 0.0f;
-                if (has_resid && grow < M && col0 + j < N) {
-                  res = OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(grow) * ep.ldr +
-                                                               col0 + j);
-                }
-                y2[h] = finish_one<OutT>(y, res, (has_resid ? rsv[j] : 0.0f), has_resid, ep.act);
+              const float lo = y[cc * 8 + e * 2];
+              const float hi = y[cc * 8 + e * 2 + 1];
+              if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+                // values are already exact bf16: take the high halves
+                w4[e] = __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+              } else {
+                w4[e] = pack2<OutT>(lo, hi);
               }
-              w4[e] = pack2<OutT>(y2[0], y2[1]);
             }
             const int phys = cc ^ ((lane >> 1) & 3);
             *reinterpret_cast<uint4*>(st + lane * 64 + phys * 16) =
@@ -505,11 +539,11 @@ EpilogueParams to_params(const GemmArgs& g) {
   return ep;
 }
 
-template <int KIND, int BN, typename OutT>
+template <int KIND, int BN, typename OutT, int ORDER, int ACT>
 int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
               int group_m, int max_ctas, cudaStream_t stream) {
   using C = Cfg<BN, OutT>;
-  auto kern = gemm_sm100_kernel<KIND, BN, OutT>;
+  auto kern = gemm_sm100_kernel<KIND, BN, OutT, ORDER, ACT>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -575,8 +609,32 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
               static_cast<long long>(g.M), static_cast<long long>(g.N), static_cast<long long>(g.K));
     return W8A8_ERR_RUNTIME;
   }
-  if (bn == 128) return launch_tc<KIND, 128, OutT>(g, ma, mb, md, group_m, max_ctas, stream);
-  return launch_tc<KIND, 256, OutT>(g, ma, mb, md, group_m, max_ctas, stream);
+  auto by_bn = [&](auto order_c, auto act_c) {
+    constexpr int O = decltype(order_c)::value;
+    constexpr int A = decltype(act_c)::value;
+    if (bn == 128) return launch_tc<KIND, 128, OutT, O, A>(g, ma, mb, md, group_m, max_ctas, stream);
+    return launch_tc<KIND, 256, OutT, O, A>(g, ma, mb, md, group_m, max_ctas, stream);
+  };
+  using I0 = std::integral_constant<int, 0>;
+  using I1 = std::integral_constant<int, 1>;
+  using I2 = std::integral_constant<int, 2>;
+  if constexpr (std::is_same<OutT, int32_t>::value) {
+    return by_bn(I0{}, I0{});
+  } else {
+    const int order = (KIND == 0 && g.epi) ? g.epi->dequant_order : kDqChained;
+    const int act = g.epi ? g.epi->activation : kActNone;
+    if (KIND == 1) {
+      return act == kActGeluTanh ? by_bn(I2{}, I1{}) : by_bn(I2{}, I0{});
+    }
+    switch (order * 2 + (act == kActGeluTanh ? 1 : 0)) {
+      case 0: return by_bn(I0{}, I0{});
+      case 1: return by_bn(I0{}, I1{});
+      case 2: return by_bn(I1{}, I0{});
+      case 3: return by_bn(I1{}, I1{});
+      case 4: return by_bn(I2{}, I0{});
+      default: return by_bn(I2{}, I1{});
+    }
+  }
 }
 
 }  // namespace

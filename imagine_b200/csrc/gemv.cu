@@ -21,6 +21,7 @@
 #include <cstdint>
 
 #include "epilogue.cuh"
+#include "quant_common.cuh"
 #include "w8a8_internal.h"
 
 namespace w8a8 {
@@ -89,18 +90,13 @@ __device__ void quantize_rows_to_smem(const T* __restrict__ x, int rows, int K, 
     float amax = 0.0f;
     for (int c = threadIdx.x; c < K; c += kGemvThreads) amax = fmaxf(amax, fabsf(In<T>::f(xr[c])));
     amax = block_max(amax, red);
-    float scale;
-    if (scale_mode == W8A8_SCALE_KITCHEN) {
-      scale = fmaxf(__fmul_rn(fminf(amax, In<T>::kFinite), 1.0f / 127.0f), 1.0e-30f);
-    } else {
-      scale = fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-30f);
-    }
-    float div = In<T>::r(scale);
-    if (div == 0.0f) div = In<T>::kTiny;
+    const float scale = quant_row_scale<T>(amax, scale_mode);
+    const float div = quant_divisor<T>(scale);
+    const float recip = __frcp_rn(div);
     if (threadIdx.x == 0) s_scale[m] = scale;
     for (int c = threadIdx.x; c < K; c += kGemvThreads) {
-      const float v = rintf(In<T>::r(__fdiv_rn(In<T>::f(xr[c]), div)));
-      sq[m * K + c] = static_cast<int8_t>(static_cast<int>(fminf(127.0f, fmaxf(-128.0f, v))));
+      const int v = quant_code<T>(In<T>::f(xr[c]), div, recip);
+      sq[m * K + c] = static_cast<int8_t>(v);
     }
   }
 }

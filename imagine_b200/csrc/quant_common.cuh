@@ -1,0 +1,116 @@
+// Exact element step of the row-wise INT8 quantiser, shared by the stand-alone
+// quantiser and the fused small-M linear.
+//
+// The reference computes q = clamp(rne(T(x / T(scale))), -128, 127) with an
+// IEEE fp32 divide (inference/src/eager.rs:159-171, torch's bf16 `div`;
+// native/comfy-port/kitchen/int8_linear.cu:47-51).  A divide per element is
+// the dominant cost of a bandwidth-bound kernel, so the quotient is formed as
+// x * r with r = RN(1 / T(scale)):
+//   |x*r - x/s| <= 2^-23 |x/s| (r and the product each round once), i.e. the
+//   product is within 2 ulp of the correctly rounded quotient.
+// Rounding that fp32 value to T can only differ from rounding the correctly
+// rounded quotient if a T rounding midpoint lies within those ulps; the
+// midpoint of bf16 (f16) rounding is low 16 (13) bits == 0x8000 (0x1000), so
+// any product whose discarded bits sit within +-8 ulp of the midpoint takes the
+// exact divide.  For fp32 inputs (no intermediate rounding) the same guard is
+// applied around the half-integer boundaries of rne.  Results are therefore
+// bit-identical to the divide; the slow path is taken for ~0.03% of elements.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace w8a8 {
+
+// Round an fp32 value to the nearest bf16 (ties to even) with integer ops,
+// returned as the fp32 value of that bf16.  Bit-identical to
+// __float2bfloat16_rn for every finite input (NaN is not produced by the
+// callers); keeps the conversion off the XU pipe.
+__device__ __forceinline__ float round_bf16_alu(float v) {
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t r = u + 0x7FFFu + ((u >> 16) & 1u);
+  return __uint_as_float(r & 0xFFFF0000u);
+}
+
+// rne(t) for |t| < 2^22 as an int, on the FMA pipe: adding 1.5 * 2^23 makes
+// the FPU round t to an integer (ties to even) in the low mantissa bits.
+__device__ __forceinline__ int rne_small_int(float t) {
+  return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+}
+
+template <typename T>
+struct QuantTraits;
+
+template <>
+struct QuantTraits<__nv_bfloat16> {
+  static constexpr int kPerVec = 8;
+  static constexpr float kFiniteMax = 3.3895313892515355e38f;
+  static constexpr float kTiny = 1.1754943508222875e-38f;
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ float round_t(float v) { return round_bf16_alu(v); }
+  // true if rounding v to bf16 is insensitive to an error of a few fp32 ulp
+  static __device__ __forceinline__ bool safe(float v) {
+    const uint32_t low = __float_as_uint(v) & 0xFFFFu;
+    return (low - 0x7FF8u) > 16u;  // unsigned: outside [0x7FF8, 0x8008]
+  }
+};
+
+template <>
+struct QuantTraits<__half> {
+  static constexpr int kPerVec = 8;
+  static constexpr float kFiniteMax = 65504.0f;
+  static constexpr float kTiny = 6.103515625e-05f;
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ float round_t(float v) { return __half2float(__float2half_rn(v)); }
+  static __device__ __forceinline__ bool safe(float v) {
+    const uint32_t low = __float_as_uint(v) & 0x1FFFu;
+    // f16 is normal for |v| >= 2^-14; below 0.25 the code is 0 either way
+    return (low - 0x0FF8u) > 16u || fabsf(v) < 0.25f;
+  }
+};
+
+template <>
+struct QuantTraits<float> {
+  static constexpr int kPerVec = 4;
+  static constexpr float kFiniteMax = 3.4028234663852886e38f;
+  static constexpr float kTiny = 1.1754943508222875e-38f;
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float round_t(float v) { return v; }
+  // rne(v) is insensitive to a few ulp unless v is near k + 0.5
+  static __device__ __forceinline__ bool safe(float v) {
+    const float f = fabsf(v - truncf(v));
+    return fabsf(f - 0.5f) > 8.0f * 1.1920929e-07f * fmaxf(fabsf(v), 1.0f);
+  }
+};
+
+// Row scale (fp32) from the row's absmax.
+//   eager   (inference/src/eager.rs:163-166):      max(amax / 127, 1e-30)
+//   kitchen (native/.../int8_linear.cu:206-208):   max(min(amax, finite) * (1/127), 1e-30)
+template <typename T>
+__device__ __forceinline__ float quant_row_scale(float amax, int kitchen_mode) {
+  if (kitchen_mode) {
+    return fmaxf(__fmul_rn(fminf(amax, QuantTraits<T>::kFiniteMax), 1.0f / 127.0f), 1.0e-30f);
+  }
+  return fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-30f);
+}
+
+// Divisor actually applied to the elements: the scale rounded to T, with an
+// exact zero replaced by T's smallest normal (inference/src/eager.rs:94-109).
+template <typename T>
+__device__ __forceinline__ float quant_divisor(float scale) {
+  const float s = QuantTraits<T>::round_t(scale);
+  return s == 0.0f ? QuantTraits<T>::kTiny : s;
+}
+
+// One code: clamp(rne(T(x / div)), -128, 127), given recip = RN(1 / div).
+// |x / div| <= 127 * (1 + 2^-7) for every element of the row, so the value
+// handed to rne_small_int is far inside its exact range.
+template <typename T>
+__device__ __forceinline__ int quant_code(float x, float div, float recip) {
+  float y = __fmul_rn(x, recip);
+  if (!QuantTraits<T>::safe(y)) y = __fdiv_rn(x, div);
+  const int q = rne_small_int(QuantTraits<T>::round_t(y));
+  return min(127, max(-128, q));
+}
+
+}  // namespace w8a8

@@ -13,8 +13,9 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 
-#include "epilogue.cuh"
+#include "quant_common.cuh"
 #include "w8a8_internal.h"
 
 namespace w8a8 {
@@ -24,82 +25,36 @@ constexpr int kMaxVec = 16;          // 16-byte vectors per thread (64 registers
 constexpr int kQuantThreads = 256;   // threads per CTA
 
 template <typename T>
-struct InTraits;
-template <>
-struct InTraits<float> {
-  static constexpr int kPerVec = 4;
-  static __device__ __forceinline__ float to_f(float v) { return v; }
-  static __device__ __forceinline__ float round_t(float v) { return v; }
-  static constexpr float kFiniteMax = 3.4028234663852886e38f;
-  static constexpr float kTiny = 1.1754943508222875e-38f;
-};
-template <>
-struct InTraits<__nv_bfloat16> {
-  static constexpr int kPerVec = 8;
-  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
-  static __device__ __forceinline__ float round_t(float v) {
-    return __bfloat162float(__float2bfloat16_rn(v));
-  }
-  static constexpr float kFiniteMax = 3.3895313892515355e38f;
-  static constexpr float kTiny = 1.1754943508222875e-38f;
-};
-template <>
-struct InTraits<__half> {
-  static constexpr int kPerVec = 8;
-  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
-  static __device__ __forceinline__ float round_t(float v) { return __half2float(__float2half_rn(v)); }
-  static constexpr float kFiniteMax = 65504.0f;
-  static constexpr float kTiny = 6.103515625e-05f;
-};
-
-// Row scale from the row's absmax.
-//   eager   (inference/src/eager.rs:163-166):       max(amax / 127, 1e-30)
-//   kitchen (native/.../int8_linear.cu:206-208):    max(min(amax, finite) * (1/127), 1e-30)
-template <typename T>
-__device__ __forceinline__ float row_scale(float amax, int mode) {
-  if (mode == W8A8_SCALE_KITCHEN) {
-    return fmaxf(__fmul_rn(fminf(amax, InTraits<T>::kFiniteMax), 1.0f / 127.0f), 1.0e-30f);
-  }
-  return fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-30f);
-}
-
-// The divisor actually used for the elements: the scale rounded to T, with an
-// exact zero replaced by T's smallest normal (inference/src/eager.rs:94-109).
-template <typename T>
-__device__ __forceinline__ float scale_divisor(float scale) {
-  const float s = InTraits<T>::round_t(scale);
-  return s == 0.0f ? InTraits<T>::kTiny : s;
-}
+using InTraits = QuantTraits<T>;
 
 // PCG-hash stochastic rounding noise of the reference's CUDA quantiser
 // (native/comfy-port/kitchen/int8_linear.cu:82-95): uniform in [0,1) with 24
-// bits, rounded to T.
+// bits, rounded to T, added in T, then floor.
 __device__ __forceinline__ uint32_t pcg_hash(uint32_t x) {
   const uint32_t state = x * 747796405u + 2891336453u;
   const uint32_t word = ((state >> ((state >> 28u) + 4u)) ^ state) * 277803737u;
   return (word >> 22u) ^ word;
 }
 
-template <typename T>
-__device__ __forceinline__ float quant_elem(float xv, float div, bool stochastic, int64_t idx,
-                                            uint64_t seed) {
-  const float scaled = InTraits<T>::round_t(__fdiv_rn(xv, div));
-  float r;
-  if (stochastic) {
+template <typename T, bool kStochastic>
+__device__ __forceinline__ int quant_elem(float xv, float div, float recip, int64_t idx,
+                                          uint64_t seed) {
+  if constexpr (!kStochastic) {
+    return quant_code<T>(xv, div, recip);
+  } else {
+    const float scaled = InTraits<T>::round_t(__fdiv_rn(xv, div));
     const uint64_t key = static_cast<uint64_t>(idx) + seed;
     const uint32_t folded = static_cast<uint32_t>(key) ^ static_cast<uint32_t>(key >> 32);
     const float noise = InTraits<T>::round_t(static_cast<float>(pcg_hash(folded) >> 8) * 0x1.0p-24f);
-    r = floorf(InTraits<T>::round_t(__fadd_rn(scaled, noise)));
-  } else {
-    r = rintf(scaled);
+    const float r = floorf(InTraits<T>::round_t(__fadd_rn(scaled, noise)));
+    return static_cast<int>(fminf(127.0f, fmaxf(-128.0f, r)));
   }
-  return fminf(127.0f, fmaxf(-128.0f, r));
 }
 
-template <typename T, int WPR>
+template <typename T, int WPR, bool kStochastic>
 __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
     const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q, int64_t ldq,
-    float* __restrict__ scales, int rows, int cols, int scale_mode, int stochastic, uint64_t seed) {
+    float* __restrict__ scales, int rows, int cols, int scale_mode, uint64_t seed) {
   constexpr int kPer = InTraits<T>::kPerVec;
   constexpr int kGroupThreads = WPR * 32;
   constexpr int kRowsPerCta = kQuantThreads / kGroupThreads;
@@ -136,9 +91,10 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
     for (int w = 1; w < WPR; ++w) amax = fmaxf(amax, red[group * WPR + w]);
   }
   if (!live) return;
-  const float scale = row_scale<T>(amax, scale_mode);
+  const float scale = quant_row_scale<T>(amax, scale_mode);
   if (gt == 0) scales[row] = scale;
-  const float div = scale_divisor<T>(scale);
+  const float div = quant_divisor<T>(scale);
+  const float recip = __frcp_rn(div);
   int8_t* qrow = q + static_cast<int64_t>(row) * ldq;
   const int64_t base_idx = static_cast<int64_t>(row) * cols;
 #pragma unroll
@@ -153,9 +109,9 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int c = vi * kPer + w * 4 + j;
-          const float qv = quant_elem<T>(InTraits<T>::to_f(e[w * 4 + j]), div, stochastic != 0,
-                                         base_idx + c, seed);
-          word |= (static_cast<uint32_t>(static_cast<int>(qv)) & 0xFFu) << (8 * j);
+          const int qv = quant_elem<T, kStochastic>(InTraits<T>::to_f(e[w * 4 + j]), div, recip,
+                                                    base_idx + c, seed);
+          word |= (static_cast<uint32_t>(qv) & 0xFFu) << (8 * j);
         }
         packed[w] = word;
       }
@@ -169,10 +125,10 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
 }
 
 // Scalar two-pass fallback: one CTA per row.
-template <typename T>
+template <typename T, bool kStochastic>
 __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_scalar_kernel(
     const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q, int64_t ldq,
-    float* __restrict__ scales, int rows, int cols, int scale_mode, int stochastic, uint64_t seed) {
+    float* __restrict__ scales, int rows, int cols, int scale_mode, uint64_t seed) {
   __shared__ float red[kQuantThreads / 32];
   const int row = blockIdx.x;
   const T* xr = x + static_cast<int64_t>(row) * ldx;
@@ -184,14 +140,15 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_scalar_kernel(
   __syncthreads();
   amax = red[0];
   for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
-  const float scale = row_scale<T>(amax, scale_mode);
+  const float scale = quant_row_scale<T>(amax, scale_mode);
   if (threadIdx.x == 0) scales[row] = scale;
-  const float div = scale_divisor<T>(scale);
+  const float div = quant_divisor<T>(scale);
+  const float recip = __frcp_rn(div);
   int8_t* qr = q + static_cast<int64_t>(row) * ldq;
   const int64_t base_idx = static_cast<int64_t>(row) * cols;
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    qr[c] = static_cast<int8_t>(static_cast<int>(
-        quant_elem<T>(InTraits<T>::to_f(xr[c]), div, stochastic != 0, base_idx + c, seed)));
+    qr[c] = static_cast<int8_t>(
+        quant_elem<T, kStochastic>(InTraits<T>::to_f(xr[c]), div, recip, base_idx + c, seed));
   }
 }
 
@@ -215,14 +172,22 @@ int launch_quant(const void* x, int64_t ldx, int8_t* q, int64_t ldq, float* scal
   auto go = [&](auto kernel, int rows_per_cta) {
     const int grid = (rows + rows_per_cta - 1) / rows_per_cta;
     kernel<<<grid, kQuantThreads, 0, stream>>>(static_cast<const T*>(x), ldx, q, ldq, scales, rows,
-                                               cols, scale_mode, stochastic, seed);
+                                               cols, scale_mode, seed);
   };
-  switch (wpr) {
-    case 1: go(quantize_rowwise_vec_kernel<T, 1>, 8); break;
-    case 2: go(quantize_rowwise_vec_kernel<T, 2>, 4); break;
-    case 4: go(quantize_rowwise_vec_kernel<T, 4>, 2); break;
-    case 8: go(quantize_rowwise_vec_kernel<T, 8>, 1); break;
-    default: go(quantize_rowwise_scalar_kernel<T>, 1); break;
+  auto pick = [&](auto stoch) {
+    constexpr bool S = decltype(stoch)::value;
+    switch (wpr) {
+      case 1: go(quantize_rowwise_vec_kernel<T, 1, S>, 8); break;
+      case 2: go(quantize_rowwise_vec_kernel<T, 2, S>, 4); break;
+      case 4: go(quantize_rowwise_vec_kernel<T, 4, S>, 2); break;
+      case 8: go(quantize_rowwise_vec_kernel<T, 8, S>, 1); break;
+      default: go(quantize_rowwise_scalar_kernel<T, S>, 1); break;
+    }
+  };
+  if (stochastic) {
+    pick(std::true_type{});
+  } else {
+    pick(std::false_type{});
   }
   return 0;
 }
