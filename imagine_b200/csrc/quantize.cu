@@ -4,7 +4,7 @@
 // its Triton twin (KSRC backends/triton/quantization.py:771-816), with the
 // numerics of the eager path (inference/src/eager.rs:159-171) by default.
 //
-// Layout: a group of WPR warps owns one row.  Each thread loads up to kMaxVec
+// Layout: a group of WPR warps owns one row.  Each thread loads up to MAXV
 // 16-byte vectors of the row into registers (one HBM read of x), the group
 // reduces |x| with shuffles (+ shared memory across warps), and the same
 // registers are scaled, rounded and written as int8.  Rows whose byte length or
@@ -21,7 +21,6 @@
 namespace w8a8 {
 namespace {
 
-constexpr int kMaxVec = 16;          // 16-byte vectors per thread (64 registers)
 constexpr int kQuantThreads = 256;   // threads per CTA
 
 template <typename T>
@@ -51,7 +50,32 @@ __device__ __forceinline__ int quant_elem(float xv, float div, float recip, int6
   }
 }
 
-template <typename T, int WPR, bool kStochastic>
+// |x| max of one 16-byte vector, packed two-at-a-time for 16-bit types.
+template <typename T>
+__device__ __forceinline__ float vec_absmax(const uint4& v);
+template <>
+__device__ __forceinline__ float vec_absmax<__nv_bfloat16>(const uint4& v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+  __nv_bfloat162 m = __hmax2(__habs2(h[0]), __habs2(h[1]));
+  m = __hmax2(m, __hmax2(__habs2(h[2]), __habs2(h[3])));
+  return fmaxf(__low2float(m), __high2float(m));
+}
+template <>
+__device__ __forceinline__ float vec_absmax<__half>(const uint4& v) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+  __half2 m = __hmax2(__habs2(h[0]), __habs2(h[1]));
+  m = __hmax2(m, __hmax2(__habs2(h[2]), __habs2(h[3])));
+  return fmaxf(__low2float(m), __high2float(m));
+}
+template <>
+__device__ __forceinline__ float vec_absmax<float>(const uint4& v) {
+  return fmaxf(fmaxf(fabsf(__uint_as_float(v.x)), fabsf(__uint_as_float(v.y))),
+               fmaxf(fabsf(__uint_as_float(v.z)), fabsf(__uint_as_float(v.w))));
+}
+
+// A group of WPR warps owns one row; each thread holds up to MAXV 16-byte
+// vectors of it in registers.
+template <typename T, int WPR, int MAXV, bool kStochastic>
 __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
     const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q, int64_t ldq,
     float* __restrict__ scales, int rows, int cols, int scale_mode, uint64_t seed) {
@@ -69,17 +93,17 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
   const int nvec = cols / kPer;
 
   const uint4* xrow = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(live ? row : 0) * ldx);
-  uint4 v[kMaxVec];
+  uint4 v[MAXV];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = gt + i * kGroupThreads;
+    if (live && vi < nvec) v[i] = __ldg(xrow + vi);
+  }
   float amax = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < MAXV; ++i) {
     const int vi = gt + i * kGroupThreads;
-    if (live && vi < nvec) {
-      v[i] = __ldg(xrow + vi);
-      const T* e = reinterpret_cast<const T*>(&v[i]);
-#pragma unroll
-      for (int j = 0; j < kPer; ++j) amax = fmaxf(amax, fabsf(InTraits<T>::to_f(e[j])));
-    }
+    if (live && vi < nvec) amax = fmaxf(amax, vec_absmax<T>(v[i]));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -98,7 +122,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
   int8_t* qrow = q + static_cast<int64_t>(row) * ldq;
   const int64_t base_idx = static_cast<int64_t>(row) * cols;
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < MAXV; ++i) {
     const int vi = gt + i * kGroupThreads;
     if (vi < nvec) {
       const T* e = reinterpret_cast<const T*>(&v[i]);
@@ -160,13 +184,19 @@ int launch_quant(const void* x, int64_t ldx, int8_t* q, int64_t ldq, float* scal
                        (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (cols % kPer == 0) &&
                        ((ldx * static_cast<int64_t>(sizeof(T))) % 16 == 0) && (ldq % 8 == 0);
   const int nvec = cols / kPer;
-  int wpr = 0;
+  // Smallest warps-per-row giving each thread at most 4 vectors, then 8, then
+  // 16 (large K); 0 selects the scalar path.
+  int wpr = 0, maxv = 0;
   if (aligned) {
-    for (int w : {1, 2, 4, 8}) {
-      if (nvec <= w * 32 * kMaxVec) {
-        wpr = w;
-        break;
+    for (int mv : {4, 8, 16}) {
+      for (int w : {1, 2, 4, 8}) {
+        if (nvec <= w * 32 * mv) {
+          wpr = w;
+          maxv = mv;
+          break;
+        }
       }
+      if (wpr) break;
     }
   }
   auto go = [&](auto kernel, int rows_per_cta) {
@@ -176,12 +206,23 @@ int launch_quant(const void* x, int64_t ldx, int8_t* q, int64_t ldq, float* scal
   };
   auto pick = [&](auto stoch) {
     constexpr bool S = decltype(stoch)::value;
-    switch (wpr) {
-      case 1: go(quantize_rowwise_vec_kernel<T, 1, S>, 8); break;
-      case 2: go(quantize_rowwise_vec_kernel<T, 2, S>, 4); break;
-      case 4: go(quantize_rowwise_vec_kernel<T, 4, S>, 2); break;
-      case 8: go(quantize_rowwise_vec_kernel<T, 8, S>, 1); break;
-      default: go(quantize_rowwise_scalar_kernel<T, S>, 1); break;
+    auto by_w = [&](auto mv_c) {
+      constexpr int MV = decltype(mv_c)::value;
+      switch (wpr) {
+        case 1: go(quantize_rowwise_vec_kernel<T, 1, MV, S>, 8); break;
+        case 2: go(quantize_rowwise_vec_kernel<T, 2, MV, S>, 4); break;
+        case 4: go(quantize_rowwise_vec_kernel<T, 4, MV, S>, 2); break;
+        default: go(quantize_rowwise_vec_kernel<T, 8, MV, S>, 1); break;
+      }
+    };
+    if (wpr == 0) {
+      go(quantize_rowwise_scalar_kernel<T, S>, 1);
+    } else if (maxv == 4) {
+      by_w(std::integral_constant<int, 4>{});
+    } else if (maxv == 8) {
+      by_w(std::integral_constant<int, 8>{});
+    } else {
+      by_w(std::integral_constant<int, 16>{});
     }
   };
   if (stochastic) {

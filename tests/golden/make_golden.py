@@ -19,6 +19,9 @@ Two sources, both the reference's own:
    Triton INT8 route: codes, row scales and dequantised outputs; inputs are the
    closed forms of inference/tests/primitives.rs:2268-2290).  Only that JSON
    member is read from the archive.
+3. ``autotuning_policy.json`` -- the reference's recorded autotuner fixture
+   (member ``runtime/autotuning-policy.json``): the do_bench device trace and
+   quantiles, and the candidate-selection trace with ties and failures.
 """
 from __future__ import annotations
 
@@ -186,15 +189,20 @@ def kitchen_cases(q):
     return out, meta
 
 
-def probe_cases(reference: str):
+def fixture_member(reference: str, member: str) -> bytes:
+    """One JSON member of the split fixture archive (nothing else is extracted)."""
     parts = sorted(os.path.join(reference, "inference/fixtures/stage-1", p)
                    for p in os.listdir(os.path.join(reference, "inference/fixtures/stage-1"))
                    if p.startswith("oracles.tar.gz.part-"))
     cat = subprocess.Popen(["cat", *parts], stdout=subprocess.PIPE)
-    tar = subprocess.run(["tar", "-xzOf", "-", "int8-aot/probe.json"], stdin=cat.stdout,
+    tar = subprocess.run(["tar", "-xzOf", "-", member], stdin=cat.stdout,
                          capture_output=True, check=True)
     cat.wait()
-    d = json.load(io.BytesIO(tar.stdout))
+    return tar.stdout
+
+
+def probe_cases(reference: str):
+    d = json.load(io.BytesIO(fixture_member(reference, "int8-aot/probe.json")))
 
     def lst(v):
         return np.asarray(v if isinstance(v, list) else json.loads(v), dtype=np.uint8)
@@ -222,6 +230,9 @@ def main():
         q = load_kitchen(args.reference, tmp)
         arrays, names = kitchen_cases(q)
     np.savez_compressed(os.path.join(HERE, "kitchen_eager.npz"), **arrays)
+    policy = json.loads(fixture_member(args.reference, "runtime/autotuning-policy.json"))
+    with open(os.path.join(HERE, "autotuning_policy.json"), "w") as f:
+        json.dump(policy, f, indent=1)
     parrays, pmeta = probe_cases(args.reference)
     np.savez_compressed(os.path.join(HERE, "triton_probe.npz"), **parrays)
     with open(os.path.join(HERE, "manifest.json"), "w") as f:
