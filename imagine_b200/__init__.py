@@ -1,13 +1,30 @@
 """B200-native (sm_100a) W8A8 / FP8 linear family with the reference's
-operator interface.  Importing loads libw8a8.so and raises if it is missing."""
-from .linear import (  # noqa: F401
-    dequantize_int8_linear,
-    device_error,
-    fp8_linear,
-    int8_gemm_s32,
-    int8_gemv,
-    int8_linear,
-    quantize_int8_rowwise,
-    quantize_per_tensor_fp8,
-    quantize_weight,
+operator interface.
+
+The operators load libw8a8.so on first use and raise if it is missing (there
+is no fallback).  Importing the package itself does not load the library, so
+`imagine_b200.build` can run on a checkout that has not been built yet.
+"""
+_OPS = (
+    "dequantize_int8_linear",
+    "device_error",
+    "fp8_linear",
+    "int8_gemm_s32",
+    "int8_gemv",
+    "int8_linear",
+    "quantize_int8_rowwise",
+    "quantize_per_tensor_fp8",
+    "quantize_weight",
+    "row_absmax",
+    "quantize_int8_rowwise_given_absmax",
 )
+
+__all__ = list(_OPS)
+
+
+def __getattr__(name):
+    if name in _OPS:
+        from . import linear
+
+        return getattr(linear, name)
+    raise AttributeError(name)

@@ -128,7 +128,40 @@ int w8a8_quantize_rowwise(const void* x, int x_dtype, int64_t rows, int64_t cols
     return fail(W8A8_ERR_VALUE, "quantize_int8_rowwise only supports rows, K <= INT_MAX");
   }
   return finish(quantize_rowwise_launch(x, x_dtype, rows, cols, ldx, q, ldq, scale, scale_mode,
-                                        stochastic, seed, static_cast<cudaStream_t>(stream)));
+                                        stochastic, seed, 0, nullptr,
+                                        static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_row_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
+                    float* amax, void* stream) {
+  if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
+  if (rows == 0) return finish(0);
+  if (!amax || (cols > 0 && !x)) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldx < cols) return fail(W8A8_ERR_VALUE, "row stride smaller than cols");
+  if (cols > 0x7fffffffLL || rows > 0x7fffffffLL) return fail(W8A8_ERR_VALUE, "rows, K <= INT_MAX");
+  if (cols == 0) {
+    cudaError_t e = cudaMemsetAsync(amax, 0, rows * sizeof(float), static_cast<cudaStream_t>(stream));
+    return finish(e == cudaSuccess ? 0 : W8A8_ERR_ACCELERATOR);
+  }
+  return finish(quantize_rowwise_launch(x, x_dtype, rows, cols, ldx, nullptr, cols, amax, 0, 0, 0,
+                                        1, nullptr, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_quantize_rowwise_given_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                                       int64_t ldx, const float* amax, int8_t* q, int64_t ldq,
+                                       float* scale, int scale_mode, void* stream) {
+  if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
+  if (scale_mode != W8A8_SCALE_EAGER && scale_mode != W8A8_SCALE_KITCHEN) {
+    return fail(W8A8_ERR_VALUE, "unknown scale mode %d", scale_mode);
+  }
+  if (rows == 0 || cols == 0) return finish(0);
+  if (!x || !q || !scale || !amax) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldx < cols || ldq < cols) return fail(W8A8_ERR_VALUE, "row stride smaller than cols");
+  if (cols > 0x7fffffffLL || rows > 0x7fffffffLL) return fail(W8A8_ERR_VALUE, "rows, K <= INT_MAX");
+  return finish(quantize_rowwise_launch(x, x_dtype, rows, cols, ldx, q, ldq, scale, scale_mode, 0, 0,
+                                        2, amax, static_cast<cudaStream_t>(stream)));
 }
 
 int w8a8_gemm_dequant(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw, const float* xs,

@@ -186,6 +186,55 @@ __device__ __forceinline__ float epi_elem(float a, float xs_row, float ws_col, f
   return y;
 }
 
+// Two adjacent output elements; for bf16 every rounding step rounds the pair
+// with one cvt.rn.bf16x2.f32 (same RNE result as two scalar conversions).
+__device__ __forceinline__ void round2_bf16(float& a, float& b) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&p);
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xFFFF0000u);
+}
+
+template <typename OutT>
+__device__ __forceinline__ void round2_out(float& a, float& b) {
+  if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+    round2_bf16(a, b);
+  } else {
+    a = OutTraits<OutT>::round(a);
+    b = OutTraits<OutT>::round(b);
+  }
+}
+
+template <typename OutT, int ORDER, int ACT>
+__device__ __forceinline__ void epi_pair(float a0, float a1, float xs_row, float w0, float w1,
+                                         float b0, float b1, bool has_bias, float& y0, float& y1) {
+  if constexpr (ORDER == kDqEager) {
+    y0 = __fmul_rn(a0, __fmul_rn(xs_row, w0));
+    y1 = __fmul_rn(a1, __fmul_rn(xs_row, w1));
+    round2_out<OutT>(y0, y1);
+    if (has_bias) {
+      y0 = __fadd_rn(y0, b0);
+      y1 = __fadd_rn(y1, b1);
+      round2_out<OutT>(y0, y1);
+    }
+  } else if constexpr (ORDER == kDqScaleProduct) {
+    const float s0 = __fmul_rn(xs_row, w0), s1 = __fmul_rn(xs_row, w1);
+    y0 = has_bias ? __fmaf_rn(a0, s0, b0) : __fmul_rn(a0, s0);
+    y1 = has_bias ? __fmaf_rn(a1, s1, b1) : __fmul_rn(a1, s1);
+    round2_out<OutT>(y0, y1);
+  } else {
+    const float t0 = __fmul_rn(a0, xs_row), t1 = __fmul_rn(a1, xs_row);
+    y0 = has_bias ? __fmaf_rn(t0, w0, b0) : __fmul_rn(t0, w0);
+    y1 = has_bias ? __fmaf_rn(t1, w1, b1) : __fmul_rn(t1, w1);
+    round2_out<OutT>(y0, y1);
+  }
+  if constexpr (ACT == kActGeluTanh) {
+    y0 = gelu_tanh(y0);
+    y1 = gelu_tanh(y1);
+    round2_out<OutT>(y0, y1);
+  }
+}
+
 template <int KIND, int BN, typename OutT, int ORDER, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -323,11 +372,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       float xs_row = 0.0f;
       if constexpr (KIND == 0 && !kRaw) xs_row = grow < M ? __ldg(ep.xs + grow) : 0.0f;
       if constexpr (KIND == 1) xs_row = fp8_scale;
+      // TMEM loads are software-pipelined: chunk c+2's tcgen05.ld is issued
+      // as soon as chunk c's registers are free, so its latency overlaps the
+      // arithmetic of chunk c.
+      uint32_t r[32];
+      if (half * 32 < BN && col_base + half * 32 < N) {
+        tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + half * 32, r);
+      }
       for (int c = half; c < BN / 32; c += 2) {
         const int col0 = col_base + c * 32;
         if (col0 >= N) break;
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + c * 32, r);
         float wsv[32], bv[32];
         if constexpr (!kRaw) {
           if constexpr (KIND == 0) {
@@ -350,14 +404,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         tmem_ld_wait();
+        uint32_t cur[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) cur[j] = r[j];
+        if (c + 2 < BN / 32 && col0 + 64 < N) {
+          tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + (c + 2) * 32, r);
+        }
         float y[32];
         if constexpr (!kRaw) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float a = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(r[j]))
-                                        : __uint_as_float(r[j]);
-            y[j] = epi_elem<OutT, (KIND == 0 ? ORDER : kDqChained), ACT>(a, xs_row, wsv[j], bv[j],
-                                                                          has_bias);
+          for (int j = 0; j < 32; j += 2) {
+            const float a0 = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(cur[j]))
+                                         : __uint_as_float(cur[j]);
+            const float a1 = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(cur[j + 1]))
+                                         : __uint_as_float(cur[j + 1]);
+            epi_pair<OutT, (KIND == 0 ? ORDER : kDqChained), ACT>(
+                a0, a1, xs_row, wsv[j], wsv[j + 1], bv[j], bv[j + 1], has_bias, y[j], y[j + 1]);
           }
           if (has_resid) {
             float rsv[32];
@@ -381,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int cc = 0; cc < 8; ++cc) {
             uint4 v;
             if constexpr (kRaw) {
-              v = make_uint4(r[cc * 4], r[cc * 4 + 1], r[cc * 4 + 2], r[cc * 4 + 3]);
+              v = make_uint4(cur[cc * 4], cur[cc * 4 + 1], cur[cc * 4 + 2], cur[cc * 4 + 3]);
             } else {
               v = make_uint4(__float_as_uint(y[cc * 4]), __float_as_uint(y[cc * 4 + 1]),
                              __float_as_uint(y[cc * 4 + 2]), __float_as_uint(y[cc * 4 + 3]));

@@ -113,4 +113,43 @@ __device__ __forceinline__ int quant_code(float x, float div, float recip) {
   return min(127, max(-128, q));
 }
 
+// Eight codes from one 16-byte vector of bf16 (the hot path of the
+// quantiser): products for all eight, one branch to the exact divide if any
+// product sits near a bf16 rounding midpoint, paired hardware bf16 rounding,
+// rne via the 1.5*2^23 trick, and saturating packs (the clamp to [-128, 127]).
+__device__ __forceinline__ uint2 quant8_bf16(const uint4& v, float div, float recip) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float x[8], y[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = __uint_as_float(w[i] << 16);
+    x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+  bool unsafe = false;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    y[j] = __fmul_rn(x[j], recip);
+    unsafe |= !QuantTraits<__nv_bfloat16>::safe(y[j]);
+  }
+  if (unsafe) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = __fdiv_rn(x[j], div);
+  }
+  int q[8];
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(y[j], y[j + 1]);  // .x = y[j]
+    const uint32_t bits = *reinterpret_cast<const uint32_t*>(&b);
+    q[j] = rne_small_int(__uint_as_float(bits << 16));
+    q[j + 1] = rne_small_int(__uint_as_float(bits & 0xFFFF0000u));
+  }
+  // cvt.pack.sat.s8.s32.b32 d, a, b, c: d = c[15:0] << 16 | sat(a) << 8 | sat(b)
+  uint32_t t0, t1, lo, hi;
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(t0) : "r"(q[3]), "r"(q[2]));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(lo) : "r"(q[1]), "r"(q[0]), "r"(t0));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(t1) : "r"(q[7]), "r"(q[6]));
+  asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(q[5]), "r"(q[4]), "r"(t1));
+  return make_uint2(lo, hi);
+}
+
 }  // namespace w8a8

@@ -75,10 +75,14 @@ __device__ __forceinline__ float vec_absmax<float>(const uint4& v) {
 
 // A group of WPR warps owns one row; each thread holds up to MAXV 16-byte
 // vectors of it in registers.
-template <typename T, int WPR, int MAXV, bool kStochastic>
+// kMode: 0 quantise, 1 write the row absmax only (to `scales`), 2 quantise
+// with the row absmax read from `amax_in` (a K-sharded row whose absmax was
+// reduced across ranks) instead of the local one.
+template <typename T, int WPR, int MAXV, bool kStochastic, int kMode>
 __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
     const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q, int64_t ldq,
-    float* __restrict__ scales, int rows, int cols, int scale_mode, uint64_t seed) {
+    float* __restrict__ scales, int rows, int cols, int scale_mode, uint64_t seed,
+    const float* __restrict__ amax_in) {
   constexpr int kPer = InTraits<T>::kPerVec;
   constexpr int kGroupThreads = WPR * 32;
   constexpr int kRowsPerCta = kQuantThreads / kGroupThreads;
@@ -100,21 +104,29 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
     if (live && vi < nvec) v[i] = __ldg(xrow + vi);
   }
   float amax = 0.0f;
+  if constexpr (kMode == 2) {
+    if (live) amax = __ldg(amax_in + row);
+  } else {
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int vi = gt + i * kGroupThreads;
-    if (live && vi < nvec) amax = fmaxf(amax, vec_absmax<T>(v[i]));
-  }
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = gt + i * kGroupThreads;
+      if (live && vi < nvec) amax = fmaxf(amax, vec_absmax<T>(v[i]));
+    }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if constexpr (WPR > 1) {
-    if (lane == 0) red[warp] = amax;
-    __syncthreads();
-    amax = red[group * WPR];
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if constexpr (WPR > 1) {
+      if (lane == 0) red[warp] = amax;
+      __syncthreads();
+      amax = red[group * WPR];
 #pragma unroll
-    for (int w = 1; w < WPR; ++w) amax = fmaxf(amax, red[group * WPR + w]);
+      for (int w = 1; w < WPR; ++w) amax = fmaxf(amax, red[group * WPR + w]);
+    }
   }
   if (!live) return;
+  if constexpr (kMode == 1) {
+    if (gt == 0) scales[row] = amax;
+    return;
+  }
   const float scale = quant_row_scale<T>(amax, scale_mode);
   if (gt == 0) scales[row] = scale;
   const float div = quant_divisor<T>(scale);
@@ -124,6 +136,10 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int vi = gt + i * kGroupThreads;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value && !kStochastic) {
+      if (vi < nvec) reinterpret_cast<uint2*>(qrow)[vi] = quant8_bf16(v[i], div, recip);
+      continue;
+    }
     if (vi < nvec) {
       const T* e = reinterpret_cast<const T*>(&v[i]);
       uint32_t packed[kPer / 4];
@@ -149,21 +165,30 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
 }
 
 // Scalar two-pass fallback: one CTA per row.
-template <typename T, bool kStochastic>
+template <typename T, bool kStochastic, int kMode>
 __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_scalar_kernel(
     const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q, int64_t ldq,
-    float* __restrict__ scales, int rows, int cols, int scale_mode, uint64_t seed) {
+    float* __restrict__ scales, int rows, int cols, int scale_mode, uint64_t seed,
+    const float* __restrict__ amax_in) {
   __shared__ float red[kQuantThreads / 32];
   const int row = blockIdx.x;
   const T* xr = x + static_cast<int64_t>(row) * ldx;
   float amax = 0.0f;
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) amax = fmaxf(amax, fabsf(InTraits<T>::to_f(xr[c])));
+  if constexpr (kMode == 2) {
+    amax = __ldg(amax_in + row);
+  } else {
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) amax = fmaxf(amax, fabsf(InTraits<T>::to_f(xr[c])));
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-  __syncthreads();
-  amax = red[0];
-  for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+    for (int w = 1; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, red[w]);
+  }
+  if constexpr (kMode == 1) {
+    if (threadIdx.x == 0) scales[row] = amax;
+    return;
+  }
   const float scale = quant_row_scale<T>(amax, scale_mode);
   if (threadIdx.x == 0) scales[row] = scale;
   const float div = quant_divisor<T>(scale);
@@ -178,7 +203,8 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_scalar_kernel(
 
 template <typename T>
 int launch_quant(const void* x, int64_t ldx, int8_t* q, int64_t ldq, float* scales, int rows,
-                 int cols, int scale_mode, int stochastic, uint64_t seed, cudaStream_t stream) {
+                 int cols, int scale_mode, int stochastic, uint64_t seed, int mode,
+                 const float* amax_in, cudaStream_t stream) {
   constexpr int kPer = InTraits<T>::kPerVec;
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (cols % kPer == 0) &&
@@ -202,21 +228,22 @@ int launch_quant(const void* x, int64_t ldx, int8_t* q, int64_t ldq, float* scal
   auto go = [&](auto kernel, int rows_per_cta) {
     const int grid = (rows + rows_per_cta - 1) / rows_per_cta;
     kernel<<<grid, kQuantThreads, 0, stream>>>(static_cast<const T*>(x), ldx, q, ldq, scales, rows,
-                                               cols, scale_mode, seed);
+                                               cols, scale_mode, seed, amax_in);
   };
-  auto pick = [&](auto stoch) {
+  auto pick = [&](auto stoch, auto mode_c) {
     constexpr bool S = decltype(stoch)::value;
+    constexpr int MD = decltype(mode_c)::value;
     auto by_w = [&](auto mv_c) {
       constexpr int MV = decltype(mv_c)::value;
       switch (wpr) {
-        case 1: go(quantize_rowwise_vec_kernel<T, 1, MV, S>, 8); break;
-        case 2: go(quantize_rowwise_vec_kernel<T, 2, MV, S>, 4); break;
-        case 4: go(quantize_rowwise_vec_kernel<T, 4, MV, S>, 2); break;
-        default: go(quantize_rowwise_vec_kernel<T, 8, MV, S>, 1); break;
+        case 1: go(quantize_rowwise_vec_kernel<T, 1, MV, S, MD>, 8); break;
+        case 2: go(quantize_rowwise_vec_kernel<T, 2, MV, S, MD>, 4); break;
+        case 4: go(quantize_rowwise_vec_kernel<T, 4, MV, S, MD>, 2); break;
+        default: go(quantize_rowwise_vec_kernel<T, 8, MV, S, MD>, 1); break;
       }
     };
     if (wpr == 0) {
-      go(quantize_rowwise_scalar_kernel<T, S>, 1);
+      go(quantize_rowwise_scalar_kernel<T, S, MD>, 1);
     } else if (maxv == 4) {
       by_w(std::integral_constant<int, 4>{});
     } else if (maxv == 8) {
@@ -225,10 +252,17 @@ int launch_quant(const void* x, int64_t ldx, int8_t* q, int64_t ldq, float* scal
       by_w(std::integral_constant<int, 16>{});
     }
   };
-  if (stochastic) {
-    pick(std::true_type{});
+  using M0 = std::integral_constant<int, 0>;
+  using M1 = std::integral_constant<int, 1>;
+  using M2 = std::integral_constant<int, 2>;
+  if (mode == 1) {
+    pick(std::false_type{}, M1{});
+  } else if (mode == 2) {
+    pick(std::false_type{}, M2{});
+  } else if (stochastic) {
+    pick(std::true_type{}, M0{});
   } else {
-    pick(std::false_type{});
+    pick(std::false_type{}, M0{});
   }
   return 0;
 }
@@ -237,17 +271,17 @@ int launch_quant(const void* x, int64_t ldx, int8_t* q, int64_t ldq, float* scal
 
 int quantize_rowwise_launch(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
                             int8_t* q, int64_t ldq, float* scales, int scale_mode, int stochastic,
-                            uint64_t seed, cudaStream_t stream) {
+                            uint64_t seed, int mode, const float* amax_in, cudaStream_t stream) {
   switch (x_dtype) {
     case W8A8_BF16:
       return launch_quant<__nv_bfloat16>(x, ldx, q, ldq, scales, (int)rows, (int)cols, scale_mode,
-                                         stochastic, seed, stream);
+                                         stochastic, seed, mode, amax_in, stream);
     case W8A8_F16:
       return launch_quant<__half>(x, ldx, q, ldq, scales, (int)rows, (int)cols, scale_mode,
-                                  stochastic, seed, stream);
+                                  stochastic, seed, mode, amax_in, stream);
     case W8A8_F32:
       return launch_quant<float>(x, ldx, q, ldq, scales, (int)rows, (int)cols, scale_mode,
-                                 stochastic, seed, stream);
+                                 stochastic, seed, mode, amax_in, stream);
     default:
       return -1;
   }

@@ -10,9 +10,11 @@ namespace w8a8 {
 // Device-side error word (one per device, module-scope __device__ variable).
 int read_and_clear_device_error(cudaStream_t stream, int* value);
 
+// mode 0: quantise; 1: row absmax only (into `scales`); 2: quantise with the
+// row absmax given in `amax_in`.
 int quantize_rowwise_launch(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
                             int8_t* q, int64_t ldq, float* scales, int scale_mode, int stochastic,
-                            uint64_t seed, cudaStream_t stream);
+                            uint64_t seed, int mode, const float* amax_in, cudaStream_t stream);
 
 // kind 0: int8 x int8 (s32 accumulate); kind 1: e4m3 x e4m3 (f32 accumulate).
 // Returns 0 on success, a W8A8_ERR_* code otherwise (message via set_error).

@@ -87,6 +87,43 @@ def quantize_int8_rowwise(x: torch.Tensor, stochastic_rounding: int = 0, *,
     return q.reshape(x.shape), s.reshape(*x.shape[:-1], 1)
 
 
+def row_absmax(x: torch.Tensor) -> torch.Tensor:
+    """max |x| of every row (fp32 [..., 1]): the first half of the K-sharded
+    quantiser (all-reduce MAX the result across ranks, then
+    ``quantize_int8_rowwise_given_absmax``)."""
+    _cuda("x", x)
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    out = torch.empty((m,), dtype=torch.float32, device=x.device)
+    N.check(N.LIB.w8a8_row_absmax(_vp(x2), _code(x2.dtype), m, k, x2.stride(0) if m > 0 else k,
+                                  _vp(out), _stream(x.device)))
+    return out.reshape(*x.shape[:-1], 1)
+
+
+def quantize_int8_rowwise_given_absmax(x: torch.Tensor, absmax: torch.Tensor, *,
+                                       scale_mode: str = "eager"):
+    """Quantise x's rows with scales derived from the given per-row absmax (the
+    full row's, when x is one K-shard of it).  Returns ``(q, scale [..., 1])``."""
+    _cuda("x", x)
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    a = absmax.to(device=x.device, dtype=torch.float32).reshape(-1).contiguous()
+    if a.numel() != m:
+        raise ValueError(f"absmax has {a.numel()} entries for {m} rows")
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+    N.check(N.LIB.w8a8_quantize_rowwise_given_absmax(
+        _vp(x2), _code(x2.dtype), m, k, x2.stride(0) if m > 0 else k, _vp(a), _vp(q), k, _vp(s),
+        SCALE_MODE[scale_mode], _stream(x.device)))
+    return q.reshape(x.shape), s.reshape(*x.shape[:-1], 1)
+
+
 def quantize_weight(weight: torch.Tensor):
     """Offline per-output-channel weight quantisation
     (inference/src/layout_complete.rs:119-159 TensorWiseINT8Layout.from_float):

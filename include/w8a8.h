@@ -113,6 +113,19 @@ int w8a8_quantize_rowwise(const void* x, int x_dtype, int64_t rows, int64_t cols
                           int8_t* q, int64_t ldq, float* scale, int scale_mode, int stochastic,
                           uint64_t seed, void* stream);
 
+/* ---- row-parallel (K-sharded) quantisation --------------------------------
+ * No reference counterpart: the reference runs on one GPU.  A K-sharded
+ * activation needs the absmax of the whole row before any shard can be
+ * quantised.  w8a8_row_absmax writes each row's max |x| (fp32 [rows]); after
+ * an all-reduce(MAX) across ranks, w8a8_quantize_rowwise_given_absmax
+ * quantises the local shard with the scale the full row would get, so every
+ * rank's codes equal the single-GPU codes of its columns. */
+int w8a8_row_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
+                    float* amax, void* stream);
+int w8a8_quantize_rowwise_given_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                                       int64_t ldx, const float* amax, int8_t* q, int64_t ldq,
+                                       float* scale, int scale_mode, void* stream);
+
 /* ---- a3 / a4 / a6: INT8 GEMM with fused dequant epilogue -----------------
  * Replaces `cutlass_int8_dequant(q, w, xs, ws, bias, out, out_code, stream)`
  * and `cutlass_int8_dequant_residual(...)` (call sites
