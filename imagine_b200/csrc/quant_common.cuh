@@ -4,8 +4,10 @@
 // The reference computes q = clamp(rne(T(x / T(scale))), -128, 127) with an
 // IEEE fp32 divide (inference/src/eager.rs:159-171, torch's bf16 `div`;
 // native/comfy-port/kitchen/int8_linear.cu:47-51).  A divide per element is
-// the dominant cost of a bandwidth-bound kernel, so the quotient is formed as
-// x * r with r = RN(1 / T(scale)):
+// the dominant cost of a bandwidth-bound kernel.  For bf16/f16 inputs the
+// quotient is computed exactly with one FMA correction (div_exact_short,
+// proof at its definition).  For fp32 inputs it is formed as x * r with
+// r = RN(1 / T(scale)):
 //   |x*r - x/s| <= 2^-23 |x/s| (r and the product each round once), i.e. the
 //   product is within 2 ulp of the correctly rounded quotient.
 // Rounding that fp32 value to T can only differ from rounding the correctly
@@ -19,6 +21,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 
 namespace w8a8 {
 
@@ -105,43 +108,50 @@ __device__ __forceinline__ float quant_divisor(float scale) {
 // One code: clamp(rne(T(x / div)), -128, 127), given recip = RN(1 / div).
 // |x / div| <= 127 * (1 + 2^-7) for every element of the row, so the value
 // handed to rne_small_int is far inside its exact range.
+__device__ __forceinline__ float div_exact_short(float x, float d, float r);
+
 template <typename T>
 __device__ __forceinline__ int quant_code(float x, float div, float recip) {
-  float y = __fmul_rn(x, recip);
-  if (!QuantTraits<T>::safe(y)) y = __fdiv_rn(x, div);
+  float y;
+  if constexpr (std::is_same<T, float>::value) {
+    y = __fmul_rn(x, recip);
+    if (!QuantTraits<T>::safe(y)) y = __fdiv_rn(x, div);
+  } else {
+    y = div_exact_short(x, div, recip);  // 16-bit x and divisor: exact
+  }
   const int q = rne_small_int(QuantTraits<T>::round_t(y));
   return min(127, max(-128, q));
 }
 
+// Correctly rounded x / d for x, d with at most 11 significant bits (bf16 or
+// f16 values), from r = RN(1/d), using one FMA correction step:
+//   y0 = RN(x r), e = x - y0 d (exact by FMA), y1 = RN(y0 + e r).
+// y0 is within 2 ulp of q = x/d, so |e r - (q - y0)| <= |e| |r - 1/d| is
+// below 2^-22 ulp(q).  q = (mx/md) 2^k with md <= 2047 odd-part > 1 (else q is
+// exact), so q is at least ulp(q) / (4 md) >= 2^-13 ulp(q) away from every
+// fp32 rounding midpoint; the single rounding of y0 + e r therefore equals
+// RN(q).  Quotients below the fp32 normal range quantise to 0 either way.
+__device__ __forceinline__ float div_exact_short(float x, float d, float r) {
+  const float y0 = __fmul_rn(x, r);
+  const float e = __fmaf_rn(-y0, d, x);
+  return __fmaf_rn(e, r, y0);
+}
+
 // Eight codes from one 16-byte vector of bf16 (the hot path of the
-// quantiser): products for all eight, one branch to the exact divide if any
-// product sits near a bf16 rounding midpoint, paired hardware bf16 rounding,
-// rne via the 1.5*2^23 trick, and saturating packs (the clamp to [-128, 127]).
+// quantiser): exact quotients (div_exact_short), paired hardware bf16
+// rounding, rne via the 1.5*2^23 trick, and saturating packs (the clamp to
+// [-128, 127]).
 __device__ __forceinline__ uint2 quant8_bf16(const uint4& v, float div, float recip) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-  float x[8], y[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    x[2 * i] = __uint_as_float(w[i] << 16);
-    x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-  bool unsafe = false;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    y[j] = __fmul_rn(x[j], recip);
-    unsafe |= !QuantTraits<__nv_bfloat16>::safe(y[j]);
-  }
-  if (unsafe) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) y[j] = __fdiv_rn(x[j], div);
-  }
   int q[8];
 #pragma unroll
-  for (int j = 0; j < 8; j += 2) {
-    const __nv_bfloat162 b = __floats2bfloat162_rn(y[j], y[j + 1]);  // .x = y[j]
+  for (int i = 0; i < 4; ++i) {
+    const float y0 = div_exact_short(__uint_as_float(w[i] << 16), div, recip);
+    const float y1 = div_exact_short(__uint_as_float(w[i] & 0xFFFF0000u), div, recip);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(y0, y1);  // .x = y0
     const uint32_t bits = *reinterpret_cast<const uint32_t*>(&b);
-    q[j] = rne_small_int(__uint_as_float(bits << 16));
-    q[j + 1] = rne_small_int(__uint_as_float(bits & 0xFFFF0000u));
+    q[2 * i] = rne_small_int(__uint_as_float(bits << 16));
+    q[2 * i + 1] = rne_small_int(__uint_as_float(bits & 0xFFFF0000u));
   }
   // cvt.pack.sat.s8.s32.b32 d, a, b, c: d = c[15:0] << 16 | sat(a) << 8 | sat(b)
   uint32_t t0, t1, lo, hi;

@@ -1,0 +1,153 @@
+"""Multi-GPU placement of the W8A8 linear family (one process per GPU).
+
+The reference runs on a single GPU (design-document.md:92); this module adds
+the two tensor-parallel forms of its `int8_linear` operator and the CFG/seed
+placement plan.  Both linears are bit-identical to the single-GPU operator:
+
+* ``ColumnParallelInt8Linear`` shards W along N.  Every rank quantises the full
+  activation (identical codes on every rank), computes its N-slice, and
+  optionally all-gathers the slices.  Used for QKV, MLP-up and the AdaLN
+  modulation GEMV.
+* ``RowParallelInt8Linear`` shards W and the activation along K.  The per-token
+  scale needs the absmax of the whole row, so ranks all-reduce(MAX) their
+  shard's row absmax first; each rank then quantises its shard with the full
+  row's scale (its codes equal the single-GPU codes of those columns), runs an
+  int32 GEMM on its K-slice, and the int32 partial sums are all-reduced (SUM,
+  exact) before one dequant epilogue.  Used for the out-projection and
+  MLP-down.
+
+The numeric steps are delegated to a backend object; ``NativeBackend`` is the
+libw8a8 C ABI.  Collectives go through ``torch.distributed`` (NCCL on GPUs).
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+class NativeBackend:
+    """libw8a8 kernels (imagine_b200.linear)."""
+
+    def __init__(self):
+        from . import linear
+
+        self.L = linear
+
+    def linear(self, x, w, ws, bias, out_dtype, **kw):
+        return self.L.int8_linear(x, w, ws, bias, out_dtype=out_dtype, **kw)
+
+    def row_absmax(self, x):
+        return self.L.row_absmax(x)
+
+    def quantize_given_absmax(self, x, amax, scale_mode="eager"):
+        return self.L.quantize_int8_rowwise_given_absmax(x, amax, scale_mode=scale_mode)
+
+    def gemm_s32(self, q, w):
+        return self.L.int8_gemm_s32(q, w)
+
+    def dequant(self, acc, xs, ws, bias, out_dtype, dequant="eager"):
+        return self.L.dequantize_int8_linear(acc, xs, ws, bias, out_dtype, dequant=dequant)
+
+
+def split_sizes(total: int, world: int) -> List[int]:
+    """Contiguous near-equal split (the first `total % world` ranks get one more)."""
+    base, extra = divmod(total, world)
+    return [base + (1 if r < extra else 0) for r in range(world)]
+
+
+def shard_slice(total: int, rank: int, world: int) -> slice:
+    sizes = split_sizes(total, world)
+    start = sum(sizes[:rank])
+    return slice(start, start + sizes[rank])
+
+
+def _world(group) -> Tuple[int, int]:
+    if not dist.is_available() or not dist.is_initialized():
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+class ColumnParallelInt8Linear:
+    """W [N, K] int8 sharded along N; y = x W^T with each rank owning an N slice."""
+
+    def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor,
+                 bias: Optional[torch.Tensor] = None, *, group=None, gather_output: bool = True,
+                 backend=None, **linear_kwargs):
+        self.group = group
+        self.rank, self.world = _world(group)
+        n = weight.shape[0]
+        sl = shard_slice(n, self.rank, self.world)
+        self.sizes = split_sizes(n, self.world)
+        self.weight = weight[sl].contiguous()
+        ws = weight_scale.reshape(-1)
+        self.weight_scale = ws if ws.numel() == 1 else ws[sl].contiguous()
+        self.bias = bias[sl].contiguous() if bias is not None else None
+        self.gather_output = gather_output
+        self.backend = backend or NativeBackend()
+        self.kw = linear_kwargs
+
+    def __call__(self, x: torch.Tensor, out_dtype=None) -> torch.Tensor:
+        y = self.backend.linear(x, self.weight, self.weight_scale, self.bias,
+                                out_dtype or x.dtype, **self.kw)
+        if not self.gather_output or self.world == 1:
+            return y
+        lead = y.shape[:-1]
+        y2 = y.reshape(-1, y.shape[-1]).contiguous()
+        parts = [torch.empty((y2.shape[0], s), dtype=y2.dtype, device=y2.device) for s in self.sizes]
+        if len(set(self.sizes)) == 1:
+            dist.all_gather(parts, y2, group=self.group)
+        else:  # uneven shards: gather padded rows, then trim
+            pad = max(self.sizes)
+            buf = torch.zeros((y2.shape[0], pad), dtype=y2.dtype, device=y2.device)
+            buf[:, : y2.shape[1]] = y2
+            padded = [torch.empty_like(buf) for _ in self.sizes]
+            dist.all_gather(padded, buf, group=self.group)
+            parts = [p[:, :s] for p, s in zip(padded, self.sizes)]
+        return torch.cat(parts, dim=-1).reshape(*lead, -1)
+
+
+class RowParallelInt8Linear:
+    """W [N, K] int8 sharded along K; the input arrives sharded along K."""
+
+    def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor,
+                 bias: Optional[torch.Tensor] = None, *, group=None, backend=None,
+                 dequant: str = "eager", scale_mode: str = "eager"):
+        self.group = group
+        self.rank, self.world = _world(group)
+        k = weight.shape[1]
+        self.k_slice = shard_slice(k, self.rank, self.world)
+        self.weight = weight[:, self.k_slice].contiguous()
+        self.weight_scale = weight_scale.reshape(-1)
+        self.bias = bias
+        self.backend = backend or NativeBackend()
+        self.dequant = dequant
+        self.scale_mode = scale_mode
+
+    def shard_input(self, x_full: torch.Tensor) -> torch.Tensor:
+        return x_full[..., self.k_slice].contiguous()
+
+    def __call__(self, x_shard: torch.Tensor, out_dtype=None) -> torch.Tensor:
+        out_dtype = out_dtype or x_shard.dtype
+        lead = x_shard.shape[:-1]
+        x2 = x_shard.reshape(-1, x_shard.shape[-1])
+        amax = self.backend.row_absmax(x2).reshape(-1).contiguous()
+        if self.world > 1:
+            dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
+        q, xs = self.backend.quantize_given_absmax(x2, amax, scale_mode=self.scale_mode)
+        acc = self.backend.gemm_s32(q, self.weight)
+        if self.world > 1:
+            dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.group)
+        y = self.backend.dequant(acc, xs, self.weight_scale, self.bias, out_dtype, dequant=self.dequant)
+        return y.reshape(*lead, -1)
+
+
+def cfg_placement(world: int, samples: int, branches: int = 2) -> List[List[Tuple[int, int]]]:
+    """Which (sample, branch) units each rank runs: unit u = sample * branches +
+    branch goes to rank u % world (GPU g runs branch g mod 2 of sample g // 2
+    when world = 2 * samples).  Units are independent until the CFG combine."""
+    plan: List[List[Tuple[int, int]]] = [[] for _ in range(world)]
+    for u in range(samples * branches):
+        plan[u % world].append((u // branches, u % branches))
+    return plan

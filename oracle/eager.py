@@ -66,6 +66,15 @@ def quantize_int8_rowwise(x: torch.Tensor):
     return q, scale
 
 
+def quantize_int8_rowwise_given_absmax(x: torch.Tensor, amax: torch.Tensor):
+    """The eager row quantiser (inference/src/eager.rs:159-171) with the row
+    absmax supplied instead of computed: what a K-shard of a row must use so
+    that its codes equal those of the unsharded row."""
+    scale = (amax.reshape(*x.shape[:-1], 1).to(torch.float32) / 127.0).clamp(min=1e-30)
+    q = _round_int8(x / _scale_for_math(scale, x))
+    return q, scale
+
+
 def quantize_int8_rowwise_kitchen(x: torch.Tensor):
     """native/comfy-port/kitchen/int8_linear.cu:184-227 (deterministic branch).
 
@@ -148,8 +157,8 @@ def int8_accumulate(a: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """inference/src/int8_linear.rs:134-168: exact int32 sum_k a[m,k]*w[n,k].
 
     The reference pads K and N to multiples of 8 and calls ``_int_mm``; zero
-    padding does not change an integer sum, so the result is the exact product.
-    Computed in int64 and checked to fit int32 (it always does for K < 2^17).
+    padding does not change an integer sum, so the result is the exact product
+    (|sum| < 2^31 for K < 2^17).
     """
     m, k = a.shape
     n = w.shape[0]

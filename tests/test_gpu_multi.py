@@ -1,0 +1,69 @@
+"""Tensor-parallel linears on 2 GPUs over NCCL with the native kernels: both
+forms must equal the single-GPU int8_linear bit for bit.  Skips on boxes with
+fewer than two GPUs."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        import imagine_b200 as W
+        from imagine_b200 import tensor_parallel as TP
+
+        g = torch.Generator().manual_seed(3)
+        m, k, n = 600, 3072, 1536
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        wq, ws = W.quantize_weight(w)
+        ref = W.int8_linear(x, wq, ws, b)
+        col = TP.ColumnParallelInt8Linear(wq, ws, b)
+        row = TP.RowParallelInt8Linear(wq, ws, b)
+        y_col = col(x)
+        y_row = row(row.shard_input(x))
+        torch.cuda.synchronize()
+        q.put((rank, torch.equal(y_col.view(torch.int16), ref.view(torch.int16)),
+               torch.equal(y_row.view(torch.int16), ref.view(torch.int16))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tensor_parallel_nccl_bit_exact():
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, col_ok, row_ok in results:
+        assert col_ok and row_ok, (rank, col_ok, row_ok)

@@ -1,0 +1,89 @@
+"""Host logic of the tensor-parallel linears with world_size-2 gloo ranks on
+the CPU; the numeric steps come from the CPU oracle (injected backend), so the
+test checks the sharding and the collectives: both forms must reproduce the
+single-device int8_linear bit for bit."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from imagine_b200 import tensor_parallel as TP
+from oracle import eager as O
+
+
+class OracleBackend:
+    def linear(self, x, w, ws, bias, out_dtype, **kw):
+        return O.int8_linear(x, w, ws, bias, out_dtype=out_dtype, **kw)
+
+    def row_absmax(self, x):
+        return x.abs().amax(dim=-1, keepdim=True).to(torch.float32)
+
+    def quantize_given_absmax(self, x, amax, scale_mode="eager"):
+        return O.quantize_int8_rowwise_given_absmax(x, amax)
+
+    def gemm_s32(self, q, w):
+        return O.int8_accumulate(q, w)
+
+    def dequant(self, acc, xs, ws, bias, out_dtype, dequant="eager"):
+        return O.DEQUANT[dequant](acc, xs, ws, bias, out_dtype)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _case(m=37, k=520, n=262):
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    wq, ws = O.quantize_weight(w)
+    b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
+    return x, wq, ws, b
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        x, wq, ws, b = _case()
+        ref = O.int8_linear(x, wq, ws, b, out_dtype=torch.bfloat16)
+        col = TP.ColumnParallelInt8Linear(wq, ws, b, backend=OracleBackend())
+        y_col = col(x)
+        row = TP.RowParallelInt8Linear(wq, ws, b, backend=OracleBackend())
+        y_row = row(row.shard_input(x))
+        q.put((rank, torch.equal(y_col.view(torch.int16), ref.view(torch.int16)),
+               torch.equal(y_row.view(torch.int16), ref.view(torch.int16))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_tensor_parallel_matches_single_device(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, col_ok, row_ok in results:
+        assert col_ok, f"column-parallel mismatch on rank {rank}"
+        assert row_ok, f"row-parallel mismatch on rank {rank}"
+
+
+def test_split_and_placement():
+    assert TP.split_sizes(10, 3) == [4, 3, 3]
+    assert TP.shard_slice(10, 2, 3) == slice(7, 10)
+    plan = TP.cfg_placement(world=4, samples=2)
+    assert plan == [[(0, 0)], [(0, 1)], [(1, 0)], [(1, 1)]]
+    assert TP.cfg_placement(world=1, samples=1) == [[(0, 0), (0, 1)]]
