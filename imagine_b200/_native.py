@@ -45,7 +45,7 @@ class GemmConfig(ctypes.Structure):
         ("block_n", ctypes.c_int32),
         ("group_m", ctypes.c_int32),
         ("max_ctas", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("cta_group", ctypes.c_int32),
     ]
 
 

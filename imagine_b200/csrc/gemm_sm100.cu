@@ -74,10 +74,10 @@ constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kThreads = (kEpiWarps + 2) * 32;
 constexpr int kMaxSmem = 232448;  // 227 KB opt-in per CTA on sm_100
 
-template <int BN, typename OutT>
+template <int BN, typename OutT, int CG = 1>
 struct Cfg {
   static constexpr int kABytes = kBM * kBK;
-  static constexpr int kBBytes = BN * kBK;
+  static constexpr int kBBytes = (BN / CG) * kBK;  // each CTA of a pair holds half of B
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStageD = 32 * 32 * static_cast<int>(sizeof(OutT));  // one warp's tile
   static constexpr int kDBytes = kEpiWarps * 2 * kStageD;
@@ -235,12 +235,16 @@ __device__ __forceinline__ void epi_pair(float a0, float a1, float xs_row, float
   }
 }
 
-template <int KIND, int BN, typename OutT, int ORDER, int ACT>
+// CG = 1: one CTA computes a 128 x BN tile.  CG = 2: a cluster of two CTAs
+// computes a 256 x BN tile with 2-SM MMAs (the leader, cluster rank 0,
+// issues them); each CTA loads its own 128 rows of A and BN/2 rows of B and
+// drains its own 128 x BN accumulator.
+template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmD, int M, int N, int K, int num_m_tiles,
                       int num_n_tiles, int group_m, EpilogueParams ep) {
-  using C = Cfg<BN, OutT>;
+  using C = Cfg<BN, OutT, CG>;
   constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -260,6 +264,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x % 32;
   const int num_tiles = num_m_tiles * num_n_tiles;
   const int num_kb = (K + kBK - 1) / kBK;
+  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int first_tile = static_cast<int>(blockIdx.x) / CG;
+  const int tile_step = static_cast<int>(gridDim.x) / CG;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -268,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], kEpiWarps * 32);
+      mbar_init(&tempty[b], kEpiWarps * CG);  // one arrival per epilogue warp of each CTA
     }
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -279,11 +287,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (!kRaw) tma_prefetch_desc(&tmD);
   }
   if (warp == kMmaWarp) {
-    tmem_alloc<C::kTmemCols>(tmem_slot);
-    tmem_relinquish();
+    tmem_alloc<C::kTmemCols, CG>(tmem_slot);
+    tmem_relinquish<CG>();
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // the peer's barriers exist before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -291,9 +300,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int tile = first_tile; ok && tile < num_tiles; tile += tile_step) {
         int mb, nb;
         tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
+        const int a_row = mb * kBM * CG + static_cast<int>(rank) * kBM;
+        const int b_row = nb * BN + static_cast<int>(rank) * (BN / CG);
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = static_cast<int>(it % C::kStages);
           const uint32_t ph = (it / C::kStages) & 1u;
@@ -301,20 +312,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-          tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kBK, mb * kBM);
-          tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kBK, nb * BN);
+          if constexpr (CG == 1) {
+            mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+            tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kBK, a_row);
+            tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kBK, b_row);
+          } else {
+            // both CTAs' bytes are counted on the leader's barrier
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::kStageBytes);
+            const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+            tma_load_2d_pair(sA + s * C::kABytes, &tmA, bar, kb * kBK, a_row);
+            tma_load_2d_pair(sB + s * C::kBBytes, &tmB, bar, kb * kBK, b_row);
+          }
         }
       }
       if (!ok) spin_ns(1000000);  // let TMA loads already in flight land (bounded)
     }
   } else if (warp == kMmaWarp) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc<KIND>(kBM, BN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc<KIND>(kBM * CG, BN);
       uint32_t it = 0;
       uint32_t tl = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++tl) {
+      for (int tile = first_tile; ok && tile < num_tiles; tile += tile_step, ++tl) {
         const uint32_t acc = tl & 1u;
         const uint32_t use = tl >> 1;
         if (!mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abortv, &g_w8a8_device_error,
@@ -335,12 +354,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b0 = smem_u32(sB + s * C::kBBytes);
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
-            umma_ss<KIND>(d_tmem, smem_desc_k_sw128(a0 + k * kUmmaK),
-                          smem_desc_k_sw128(b0 + k * kUmmaK), idesc, (kb | k) != 0 ? 1u : 0u);
+            const uint64_t ad = smem_desc_k_sw128(a0 + k * kUmmaK);
+            const uint64_t bd = smem_desc_k_sw128(b0 + k * kUmmaK);
+            const uint32_t accumulate = (kb | k) != 0 ? 1u : 0u;
+            if constexpr (CG == 1) {
+              umma_ss<KIND>(d_tmem, ad, bd, idesc, accumulate);
+            } else {
+              umma_ss_pair<KIND>(d_tmem, ad, bd, idesc, accumulate);
+            }
           }
-          umma_commit(&empty[s]);
+          if constexpr (CG == 1) {
+            umma_commit(&empty[s]);
+          } else {
+            umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 0));
+            umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
+          }
         }
-        if (ok) umma_commit(&tfull[acc]);
+        if (ok) {
+          if constexpr (CG == 1) {
+            umma_commit(&tfull[acc]);
+          } else {
+            umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 0));
+            umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), 1));
+          }
+        }
       }
     }
   } else {
@@ -357,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (KIND == 1) fp8_scale = __fmul_rn(__ldg(ep.sa), __ldg(ep.sb));
     uint32_t tl = 0;
     uint32_t chunk_ctr = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tl) {
+    for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++tl) {
       int mb, nb;
       tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
       const uint32_t acc = tl & 1u;
@@ -367,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int row0 = mb * kBM + quad * 32;
+      const int row0 = mb * kBM * CG + static_cast<int>(rank) * kBM + quad * 32;
       const int grow = row0 + lane;
       float xs_row = 0.0f;
       if constexpr (KIND == 0 && !kRaw) xs_row = grow < M ? __ldg(ep.xs + grow) : 0.0f;
@@ -481,15 +518,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++chunk_ctr;
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (CG == 1) {
+          mbar_arrive(&tempty[acc]);
+        } else {
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+        }
+      }
     }
     if (lane == 0) tma_store_wait_all<0>();
   }
 
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // the peer is done with its TMEM and our barriers
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc<C::kTmemCols>(tmem_base);
+    tmem_dealloc<C::kTmemCols, CG>(tmem_base);
   }
 }
 
@@ -601,11 +646,11 @@ EpilogueParams to_params(const GemmArgs& g) {
   return ep;
 }
 
-template <int KIND, int BN, typename OutT, int ORDER, int ACT>
+template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG>
 int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
               int group_m, int max_ctas, cudaStream_t stream) {
-  using C = Cfg<BN, OutT>;
-  auto kern = gemm_sm100_kernel<KIND, BN, OutT, ORDER, ACT>;
+  using C = Cfg<BN, OutT, CG>;
+  auto kern = gemm_sm100_kernel<KIND, BN, OutT, ORDER, ACT, CG>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -618,16 +663,34 @@ int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, c
     }
     attr_set[dev] = true;
   }
-  const int num_m = static_cast<int>((g.M + kBM - 1) / kBM);
+  const int num_m = static_cast<int>((g.M + kBM * CG - 1) / (kBM * CG));
   const int num_n = static_cast<int>((g.N + BN - 1) / BN);
   const int tiles = num_m * num_n;
   const int sms = device_sm_count();
-  int grid = std::min(tiles, max_ctas > 0 ? max_ctas : sms);
-  if (grid < 1) grid = 1;
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ma, mb, md, static_cast<int>(g.M),
-                                                 static_cast<int>(g.N), static_cast<int>(g.K),
-                                                 num_m, num_n, group_m, to_params(g));
-  cudaError_t e = cudaGetLastError();
+  int units = std::min(tiles, (max_ctas > 0 ? max_ctas : sms) / CG);  // CTAs or CTA pairs
+  if (units < 1) units = 1;
+  const EpilogueParams ep = to_params(g);
+  const int Mi = static_cast<int>(g.M), Ni = static_cast<int>(g.N), Ki = static_cast<int>(g.K);
+  cudaError_t e;
+  if constexpr (CG == 1) {
+    kern<<<units, kThreads, C::kSmemBytes, stream>>>(ma, mb, md, Mi, Ni, Ki, num_m, num_n, group_m,
+                                                    ep);
+    e = cudaGetLastError();
+  } else {
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(static_cast<unsigned>(units * 2));
+    lc.blockDim = dim3(kThreads);
+    lc.dynamicSmemBytes = C::kSmemBytes;
+    lc.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    e = cudaLaunchKernelEx(&lc, kern, ma, mb, md, Mi, Ni, Ki, num_m, num_n, group_m, ep);
+  }
   if (e != cudaSuccess) {
     set_error("tcgen05 GEMM launch failed: %s", cudaGetErrorString(e));
     return W8A8_ERR_ACCELERATOR;
@@ -651,14 +714,14 @@ int launch_simt(const GemmArgs& g, cudaStream_t stream) {
 }
 
 template <int KIND, typename OutT>
-int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_ctas,
+int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_ctas, int cg,
                  cudaStream_t stream) {
   if (!tc_ok) return launch_simt<KIND, OutT>(g, stream);
   CUtensorMap ma, mb, md;
   bool ok = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.a, g.K, g.M, g.lda, kBK, kBM,
                         CU_TENSOR_MAP_SWIZZLE_128B);
   ok = ok && make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.b, g.K, g.N, g.ldb, kBK,
-                         static_cast<uint32_t>(bn), CU_TENSOR_MAP_SWIZZLE_128B);
+                         static_cast<uint32_t>(bn / cg), CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMapDataType dt;
   if constexpr (std::is_same<OutT, float>::value) dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   else if constexpr (std::is_same<OutT, int32_t>::value) dt = CU_TENSOR_MAP_DATA_TYPE_INT32;
@@ -674,8 +737,9 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
   auto by_bn = [&](auto order_c, auto act_c) {
     constexpr int O = decltype(order_c)::value;
     constexpr int A = decltype(act_c)::value;
-    if (bn == 128) return launch_tc<KIND, 128, OutT, O, A>(g, ma, mb, md, group_m, max_ctas, stream);
-    return launch_tc<KIND, 256, OutT, O, A>(g, ma, mb, md, group_m, max_ctas, stream);
+    if (bn == 128) return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, group_m, max_ctas, stream);
+    if (cg == 2) return launch_tc<KIND, 256, OutT, O, A, 2>(g, ma, mb, md, group_m, max_ctas, stream);
+    return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, md, group_m, max_ctas, stream);
   };
   using I0 = std::integral_constant<int, 0>;
   using I1 = std::integral_constant<int, 1>;
@@ -720,19 +784,26 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   }
   const int group_m = g.cfg && g.cfg->group_m > 0 ? g.cfg->group_m : 8;
   const int max_ctas = g.cfg ? g.cfg->max_ctas : 0;
+  int cg = g.cfg && g.cfg->cta_group ? g.cfg->cta_group : 0;
+  if (cg != 0 && cg != 1 && cg != 2) {
+    set_error("cta_group must be 1 or 2, got %d", cg);
+    return W8A8_ERR_VALUE;
+  }
+  if (cg == 0) cg = (bn == 256 && g.M > kBM) ? 2 : 1;
+  if (bn == 128) cg = 1;  // pairs are built for 256-column tiles
   if (g.kind == 0) {
     switch (g.out_dtype) {
-      case W8A8_BF16: return dispatch_out<0, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, stream);
-      case W8A8_F16: return dispatch_out<0, __half>(g, tc_ok, bn, group_m, max_ctas, stream);
-      case W8A8_F32: return dispatch_out<0, float>(g, tc_ok, bn, group_m, max_ctas, stream);
-      case W8A8_S32: return dispatch_out<0, int32_t>(g, tc_ok, bn, group_m, max_ctas, stream);
+      case W8A8_BF16: return dispatch_out<0, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
+      case W8A8_F16: return dispatch_out<0, __half>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
+      case W8A8_F32: return dispatch_out<0, float>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
+      case W8A8_S32: return dispatch_out<0, int32_t>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
       default: break;
     }
   } else {
     switch (g.out_dtype) {
-      case W8A8_BF16: return dispatch_out<1, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, stream);
-      case W8A8_F16: return dispatch_out<1, __half>(g, tc_ok, bn, group_m, max_ctas, stream);
-      case W8A8_F32: return dispatch_out<1, float>(g, tc_ok, bn, group_m, max_ctas, stream);
+      case W8A8_BF16: return dispatch_out<1, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
+      case W8A8_F16: return dispatch_out<1, __half>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
+      case W8A8_F32: return dispatch_out<1, float>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
       default: break;
     }
   }

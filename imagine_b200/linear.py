@@ -53,8 +53,8 @@ def _config(config) -> Optional[N.GemmConfig]:
         return None
     if isinstance(config, N.GemmConfig):
         return config
-    bn, gm, ctas = (tuple(config) + (0, 0, 0))[:3]
-    return N.GemmConfig(int(bn), int(gm), int(ctas), 0)
+    bn, gm, ctas, cg = (tuple(config) + (0, 0, 0, 0))[:4]
+    return N.GemmConfig(int(bn), int(gm), int(ctas), int(cg))
 
 
 def _cfg_ptr(cfg):
@@ -201,7 +201,7 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     ``dequant`` / ``scale_mode`` choose which of the reference routes' numerics
     to reproduce (default: the eager route, bit-exact); ``output_act`` applies
     GELU-tanh in the epilogue (the MLP-up fusion).  ``config`` is an optional
-    ``(block_n, group_m, max_ctas)`` tile configuration.
+    ``(block_n, group_m, max_ctas, cta_group)`` tile configuration.
     """
     _cuda("x", x)
     dev = x.device

@@ -81,10 +81,11 @@ typedef struct w8a8_epilogue {
 /* Optional GEMM launch configuration (what the autotuner selects).  A NULL
  * pointer, or zero fields, select the built-in heuristic. */
 typedef struct w8a8_gemm_config {
-  int32_t block_n;  /* 128 or 256 output columns per CTA tile */
-  int32_t group_m;  /* M tiles per rasterisation group (L2 reuse) */
-  int32_t max_ctas; /* persistent CTAs (0 = one per SM) */
-  int32_t reserved;
+  int32_t block_n;   /* 128 or 256 output columns per tile */
+  int32_t group_m;   /* M tiles per rasterisation group (L2 reuse) */
+  int32_t max_ctas;  /* persistent CTAs (0 = one per SM) */
+  int32_t cta_group; /* 1: one CTA per 128-row tile; 2: CTA pairs with 2-SM MMAs on
+                        256-row tiles (block_n 256 only); 0: heuristic */
 } w8a8_gemm_config_t;
 
 /* ---- library state ---------------------------------------------------- */

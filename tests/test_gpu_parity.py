@@ -114,13 +114,18 @@ def _rand_i8(g, *shape):
     return torch.randint(-128, 128, shape, generator=g, dtype=torch.int8)
 
 
+# (block_n, cta_group): heuristic, 128-column tiles, 256-column 1-CTA tiles,
+# 256x256 tiles on CTA pairs (2-SM MMA)
+TILE_CONFIGS = [(0, 0), (128, 1), (256, 1), (256, 2)]
+
+
 @pytest.mark.parametrize("m,k,n", GEMM_SHAPES)
-@pytest.mark.parametrize("bn", [0, 128, 256])
-def test_gemm_s32_exact(m, k, n, bn):
+@pytest.mark.parametrize("bn,cg", TILE_CONFIGS)
+def test_gemm_s32_exact(m, k, n, bn, cg):
     g = torch.Generator().manual_seed(m * 7 + k * 3 + n)
     q = _rand_i8(g, m, k)
     w = _rand_i8(g, n, k)
-    acc = W().int8_gemm_s32(q.to(cuda()), w.to(cuda()), config=(bn, 8, 0))
+    acc = W().int8_gemm_s32(q.to(cuda()), w.to(cuda()), config=(bn, 8, 0, cg))
     torch.cuda.synchronize()
     no_device_error()
     assert torch.equal(acc.cpu(), O.int8_accumulate(q, w))
@@ -128,13 +133,15 @@ def test_gemm_s32_exact(m, k, n, bn):
 
 @pytest.mark.parametrize("m,k,n", GEMM_SHAPES[:-1])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
-def test_int8_linear_eager_order_bit_exact(m, k, n, out_dtype):
+@pytest.mark.parametrize("cg", [1, 2])
+def test_int8_linear_eager_order_bit_exact(m, k, n, out_dtype, cg):
     g = torch.Generator().manual_seed(m + k + n)
     x = torch.randn(m, k, generator=g).to(out_dtype)
     w = (torch.randn(n, k, generator=g) * 0.02).to(out_dtype)
     wq, ws = O.quantize_weight(w)
     b = (torch.randn(n, generator=g) * 0.02).to(out_dtype)
-    y = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda()), out_dtype=out_dtype)
+    y = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda()), out_dtype=out_dtype,
+                        config=(256, 8, 0, cg))
     ref = O.int8_linear(x, wq, ws, b, out_dtype=out_dtype)
     no_device_error()
     assert np.array_equal(_b(y), _b(ref))
@@ -318,7 +325,8 @@ def test_fp8_quantize_golden(name):
 
 
 @pytest.mark.parametrize("m,k,n", [(300, 3072, 1024), (5600, 3072, 512), (130, 160, 264), (33, 100, 24)])
-def test_fp8_linear(m, k, n):
+@pytest.mark.parametrize("cg", [1, 2])
+def test_fp8_linear(m, k, n, cg):
     g = torch.Generator().manual_seed(m + n)
     x = torch.randn(m, k, generator=g)
     x = torch.where(torch.rand(m, k, generator=g) < 0.01, x * 20, x).to(torch.bfloat16)
@@ -329,7 +337,7 @@ def test_fp8_linear(m, k, n):
     aq = W().quantize_per_tensor_fp8(x.to(cuda()), sa.to(cuda()))
     wq = W().quantize_per_tensor_fp8(w.to(cuda()), sw.to(cuda()))
     assert np.array_equal(_b(aq), _b(O.quantize_fp8(x, sa)))
-    y = W().fp8_linear(aq, sa.to(cuda()), wq, sw.to(cuda()), b.to(cuda()))
+    y = W().fp8_linear(aq, sa.to(cuda()), wq, sw.to(cuda()), b.to(cuda()), config=(256, 8, 0, cg))
     no_device_error()
     # against the unrounded fp32 result (a bf16 rounding flip on a large element
     # is up to one ulp, which two independently rounded outputs can double)
