@@ -17,6 +17,8 @@ _OPS = (
     "quantize_weight",
     "row_absmax",
     "quantize_int8_rowwise_given_absmax",
+    "quantize_mxfp8",
+    "mxfp8_linear",
 )
 
 __all__ = list(_OPS)

@@ -76,6 +76,8 @@ SIGNATURES = {
     "w8a8_linear_small": (_i32, [_vp, _i32, _vp, _EP, _i32, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _vp]),
     "w8a8_quantize_fp8_tensor": (_i32, [_vp, _i32, _i64, _vp, _vp, _vp]),
     "w8a8_fp8_gemm": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _CFG, _vp]),
+    "w8a8_quantize_mxfp8": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "w8a8_mxfp8_gemm": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _CFG, _vp]),
 }
 
 

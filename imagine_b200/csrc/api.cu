@@ -290,4 +290,55 @@ int w8a8_fp8_gemm(const uint8_t* a, const uint8_t* b, const float* sa, const flo
   return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
 }
 
+int w8a8_quantize_mxfp8(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
+                        uint8_t* q, int64_t ldq, uint8_t* scales, void* stream) {
+  if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
+  if (cols % 32 != 0) return fail(W8A8_ERR_VALUE, "K dimension must be divisible by 32");
+  if (rows == 0 || cols == 0) return finish(0);
+  if (!x || !q || !scales) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldx < cols || ldq < cols) return fail(W8A8_ERR_VALUE, "row stride smaller than cols");
+  const int elem = x_dtype == W8A8_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(q)) % 16 != 0 ||
+      (ldx * elem) % 16 != 0 || ldq % 16 != 0) {
+    return fail(W8A8_ERR_VALUE, "mxfp8 quantiser needs 16-byte aligned rows");
+  }
+  if (cols > 0x7fffffffLL || rows > 0x7fffffffLL) return fail(W8A8_ERR_VALUE, "rows, K <= INT_MAX");
+  return finish(quantize_mxfp8_launch(x, x_dtype, rows, cols, ldx, q, ldq, scales,
+                                      static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_mxfp8_gemm(const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
+                    const uint8_t* b_scales, const void* bias, void* out, int out_dtype, int64_t M,
+                    int64_t N, int64_t K, const w8a8_gemm_config_t* cfg, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (K % 32 != 0) return fail(W8A8_ERR_VALUE, "K dimension must be divisible by 32");
+  if (M == 0 || N == 0) return finish(0);
+  if ((K > 0 && (!a || !b || !a_scales || !b_scales)) || !out) {
+    return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  }
+  w8a8_epilogue_t epi{};
+  epi.ws_numel = 1;
+  epi.bias = bias;
+  epi.dequant_order = W8A8_DQ_CHAINED;
+  GemmArgs g{};
+  g.kind = 2;
+  g.a = a;
+  g.lda = K;
+  g.b = b;
+  g.ldb = K;
+  g.epi = &epi;
+  g.out = out;
+  g.out_dtype = out_dtype;
+  g.ldo = N;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.cfg = cfg;
+  g.sfa = a_scales;
+  g.sfb = b_scales;
+  return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

@@ -74,19 +74,29 @@ constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kThreads = (kEpiWarps + 2) * 32;
 constexpr int kMaxSmem = 232448;  // 227 KB opt-in per CTA on sm_100
 
-template <int BN, typename OutT, int CG = 1>
+template <int BN, typename OutT, int CG = 1, int KIND = 0>
 struct Cfg {
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = (BN / CG) * kBK;  // each CTA of a pair holds half of B
   static constexpr int kStageBytes = kABytes + kBBytes;
+  // MXFP8: one 512-byte block of e8m0 scales for A and BN/128 for B per stage
+  static constexpr int kSFBytes = KIND == 2 ? 512 * (1 + BN / 128) : 0;
+  static constexpr int kSFCols = KIND == 2 ? 4 * (1 + BN / 128) : 0;  // TMEM columns per stage
   static constexpr int kStageD = 32 * 32 * static_cast<int>(sizeof(OutT));  // one warp's tile
-  static constexpr int kDBytes = kEpiWarps * 2 * kStageD;
+  // per epilogue warp: one store staging tile + the fp32 weight scale and bias
+  // of each of its column chunks for the current tile
+  static constexpr int kChunksPerWarp = (BN / 32 + 1) / 2;
+  static constexpr int kVecBytes = 2 * kChunksPerWarp * 32 * 4;
+  static constexpr int kDBytes = kEpiWarps * (kStageD + kVecBytes);
   static constexpr int kBarBytes = 256;
   static constexpr int kFixed = 1024 + kDBytes + kBarBytes;
-  static constexpr int kStagesRaw = (kMaxSmem - kFixed) / kStageBytes;
+  static constexpr int kStagesRaw = (kMaxSmem - kFixed) / (kStageBytes + kSFBytes);
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-  static constexpr int kSmemBytes = kFixed + kStages * kStageBytes;
-  static constexpr uint32_t kTmemCols = (2 * BN <= 256) ? 256u : 512u;
+  static constexpr int kSmemBytes = kFixed + kStages * (kStageBytes + kSFBytes);
+  static constexpr int kSFCol0 = 2 * BN;  // scale factors live after the two accumulators
+  static constexpr uint32_t kTmemCols =
+      (2 * BN + kStages * kSFCols <= 256) ? 256u : 512u;
+  static_assert(2 * BN + kStages * kSFCols <= 512, "TMEM budget exceeded");
   static_assert(kStages >= 2, "pipeline needs at least two stages");
   static_assert(kSmemBytes <= kMaxSmem, "shared memory budget exceeded");
 };
@@ -244,14 +254,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmD, int M, int N, int K, int num_m_tiles,
                       int num_n_tiles, int group_m, EpilogueParams ep) {
-  using C = Cfg<BN, OutT, CG>;
+  using C = Cfg<BN, OutT, CG, KIND>;
   constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::kStages * C::kABytes;
-  uint8_t* sD = smem + C::kStages * C::kStageBytes;
+  uint8_t* sSF = smem + C::kStages * C::kStageBytes;  // MXFP8 scale blocks (KIND 2)
+  uint8_t* sD = sSF + C::kStages * C::kSFBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sD + C::kDBytes);
   uint64_t* empty = full + C::kStages;
   uint64_t* tfull = empty + C::kStages;
@@ -313,9 +324,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           if constexpr (CG == 1) {
-            mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+            mbar_arrive_expect_tx(&full[s], C::kStageBytes + C::kSFBytes);
             tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kBK, a_row);
             tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kBK, b_row);
+            if constexpr (KIND == 2) {
+              // blocked scale layout: 512-byte block (row/128, kb) at
+              // ((row/128) * ncb + kb) * 512
+              uint8_t* sf = sSF + s * C::kSFBytes;
+              bulk_load(sf, ep.sfa + (static_cast<int64_t>(mb) * ep.sf_ncb + kb) * 512, 512,
+                        &full[s]);
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j) {
+                bulk_load(sf + 512 * (1 + j),
+                          ep.sfb + (static_cast<int64_t>(nb * (BN / 128) + j) * ep.sf_ncb + kb) * 512,
+                          512, &full[s]);
+              }
+            }
           } else {
             // both CTAs' bytes are counted on the leader's barrier
             if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::kStageBytes);
@@ -329,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = make_idesc<KIND>(kBM * CG, BN);
+      constexpr uint32_t idesc = make_idesc<KIND == 0 ? 0 : 1>(kBM * CG, BN);
       uint32_t it = 0;
       uint32_t tl = 0;
       bool ok = true;
@@ -352,15 +376,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + s * C::kABytes);
           const uint32_t b0 = smem_u32(sB + s * C::kBBytes);
+          if constexpr (KIND == 2) {
+            // scale blocks of this stage -> this stage's TMEM slot, then the
+            // four K=32 MMAs each pick their K sub-block with sf_id
+            const uint32_t sf_tmem = tmem_base + C::kSFCol0 + s * C::kSFCols;
+            const uint32_t sf_smem = smem_u32(sSF + s * C::kSFBytes);
+            tmem_cp_32x128b_x4(sf_tmem, smem_desc_sf(sf_smem));
 #pragma unroll
-          for (int k = 0; k < kBK / kUmmaK; ++k) {
-            const uint64_t ad = smem_desc_k_sw128(a0 + k * kUmmaK);
-            const uint64_t bd = smem_desc_k_sw128(b0 + k * kUmmaK);
-            const uint32_t accumulate = (kb | k) != 0 ? 1u : 0u;
-            if constexpr (CG == 1) {
-              umma_ss<KIND>(d_tmem, ad, bd, idesc, accumulate);
-            } else {
-              umma_ss_pair<KIND>(d_tmem, ad, bd, idesc, accumulate);
+            for (int j = 0; j < BN / 128; ++j) {
+              tmem_cp_32x128b_x4(sf_tmem + 4 * (1 + j), smem_desc_sf(sf_smem + 512 * (1 + j)));
+            }
+#pragma unroll
+            for (int k = 0; k < kBK / kUmmaK; ++k) {
+              umma_mx(d_tmem, smem_desc_k_sw128(a0 + k * kUmmaK), smem_desc_k_sw128(b0 + k * kUmmaK),
+                      make_idesc_mx(kBM, BN, static_cast<uint32_t>(k)), sf_tmem, sf_tmem + 4,
+                      (kb | k) != 0 ? 1u : 0u);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < kBK / kUmmaK; ++k) {
+              const uint64_t ad = smem_desc_k_sw128(a0 + k * kUmmaK);
+              const uint64_t bd = smem_desc_k_sw128(b0 + k * kUmmaK);
+              const uint32_t accumulate = (kb | k) != 0 ? 1u : 0u;
+              if constexpr (CG == 1) {
+                umma_ss<KIND>(d_tmem, ad, bd, idesc, accumulate);
+              } else {
+                umma_ss_pair<KIND>(d_tmem, ad, bd, idesc, accumulate);
+              }
             }
           }
           if constexpr (CG == 1) {
@@ -387,19 +429,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;
     const int half = warp >> 2;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-    uint8_t* stage0 = sD + warp * 2 * C::kStageD;
+    uint8_t* st = sD + warp * (C::kStageD + C::kVecBytes);
+    float* s_ws = reinterpret_cast<float*>(st + C::kStageD);    // [chunk][32]
+    float* s_bias = s_ws + C::kChunksPerWarp * 32;                // [chunk][32]
     const bool has_bias = ep.bias != nullptr;
     const bool has_resid = ep.residual != nullptr;
     float fp8_scale = 0.0f;
     if constexpr (KIND == 1) fp8_scale = __fmul_rn(__ldg(ep.sa), __ldg(ep.sb));
+    (void)fp8_scale;
     uint32_t tl = 0;
-    uint32_t chunk_ctr = 0;
     for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++tl) {
       int mb, nb;
       tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
       const uint32_t acc = tl & 1u;
       const uint32_t use = tl >> 1;
       const int col_base = nb * BN;
+      if constexpr (!kRaw) {
+        // Stage this warp's per-column weight scales and bias while the MMA
+        // is still running: lane j loads column j of each of the warp's chunks.
+        // (The previous tile's readers of these slots are this warp's own
+        // lanes, all past their last read.)
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < C::kChunksPerWarp; ++i) {
+          const int col = col_base + (half + 2 * i) * 32 + lane;
+          const bool in = (half + 2 * i) < BN / 32 && col < N;
+          float wv = 1.0f, bvv = 0.0f;
+          if constexpr (KIND == 0) wv = in ? __ldg(ep.ws + (ep.ws_scalar ? 0 : col)) : 0.0f;
+          if (has_bias && in) bvv = OutTraits<OutT>::load(ep.bias, col);
+          s_ws[i * 32 + lane] = wv;
+          s_bias[i * 32 + lane] = bvv;
+        }
+        __syncwarp();
+      }
       if (!mbar_wait(&tfull[acc], use & 1u, abortv, &g_w8a8_device_error, kDevTimeoutTmemFull)) {
         break;
       }
@@ -409,6 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float xs_row = 0.0f;
       if constexpr (KIND == 0 && !kRaw) xs_row = grow < M ? __ldg(ep.xs + grow) : 0.0f;
       if constexpr (KIND == 1) xs_row = fp8_scale;
+      if constexpr (KIND == 2) xs_row = 1.0f;  // block scales are applied by the MMA
       // TMEM loads are software-pipelined: chunk c+2's tcgen05.ld is issued
       // as soon as chunk c's registers are free, so its latency overlaps the
       // arithmetic of chunk c.
@@ -419,27 +482,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = half; c < BN / 32; c += 2) {
         const int col0 = col_base + c * 32;
         if (col0 >= N) break;
-        float wsv[32], bv[32];
-        if constexpr (!kRaw) {
-          if constexpr (KIND == 0) {
-            if (ep.ws_scalar) {
-              const float w0 = __ldg(ep.ws);
-#pragma unroll
-              for (int j = 0; j < 32; ++j) wsv[j] = w0;
-            } else {
-              load_cols32<float>(ep.ws, col0, N, ep.vec_ws, wsv);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) wsv[j] = 1.0f;
-          }
-          if (has_bias) {
-            load_cols32<OutT>(ep.bias, col0, N, ep.vec_bias, bv);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) bv[j] = 0.0f;
-          }
-        }
+        const int ci = (c - half) >> 1;  // this warp's chunk index
+        const float4* wsq = reinterpret_cast<const float4*>(s_ws + ci * 32);
+        const float4* bq = reinterpret_cast<const float4*>(s_bias + ci * 32);
         tmem_ld_wait();
         uint32_t cur[32];
 #pragma unroll
@@ -450,13 +495,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         float y[32];
         if constexpr (!kRaw) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const float a0 = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(cur[j]))
-                                         : __uint_as_float(cur[j]);
-            const float a1 = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(cur[j + 1]))
-                                         : __uint_as_float(cur[j + 1]);
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 w4 = wsq[j4];
+            const float4 b4 = bq[j4];
+            const int j = j4 * 4;
+            float a[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              a[t] = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(cur[j + t]))
+                                 : __uint_as_float(cur[j + t]);
+            }
             epi_pair<OutT, (KIND == 0 ? ORDER : kDqChained), ACT>(
-                a0, a1, xs_row, wsv[j], wsv[j + 1], bv[j], bv[j + 1], has_bias, y[j], y[j + 1]);
+                a[0], a[1], xs_row, w4.x, w4.y, b4.x, b4.y, has_bias, y[j], y[j + 1]);
+            epi_pair<OutT, (KIND == 0 ? ORDER : kDqChained), ACT>(
+                a[2], a[3], xs_row, w4.z, w4.w, b4.z, b4.w, has_bias, y[j + 2], y[j + 3]);
           }
           if (has_resid) {
             float rsv[32];
@@ -471,8 +523,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        uint8_t* st = stage0 + (chunk_ctr & 1u) * C::kStageD;
-        if (lane == 0) tma_store_wait_read<1>();
+        // single staging tile: the previous chunk's store was issued a whole
+        // chunk of arithmetic ago
+        if (lane == 0) tma_store_wait_read<0>();
         __syncwarp();
         if constexpr (sizeof(OutT) == 4) {
           // 32 x 4-byte values = 8 chunks of 16 B; 128B swizzle: chunk ^= row & 7.
@@ -515,7 +568,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_store_2d(&tmD, st, col0, row0);
           tma_store_commit();
         }
-        ++chunk_ctr;
       }
       tc_fence_before();
       __syncwarp();
@@ -554,15 +606,34 @@ __global__ void __launch_bounds__(128) gemm_simt_kernel(const uint8_t* __restric
   const uint8_t* br = b + static_cast<int64_t>(n) * ldb;
   float af = 0.0f;
   int32_t ai = 0;
-  for (int k = 0; k < K; ++k) {
-    if constexpr (KIND == 0) {
-      ai += static_cast<int32_t>(static_cast<int8_t>(ar[k])) *
-            static_cast<int32_t>(static_cast<int8_t>(br[k]));
-    } else {
-      __nv_fp8_e4m3 x, y;
-      x.__x = ar[k];
-      y.__x = br[k];
-      af = __fmaf_rn(static_cast<float>(x), static_cast<float>(y), af);
+  if constexpr (KIND == 2) {
+    // per 32-element block: exact partial dot product times both block scales
+    for (int kb = 0; kb < K / 32; ++kb) {
+      float part = 0.0f;
+      for (int k = kb * 32; k < kb * 32 + 32; ++k) {
+        __nv_fp8_e4m3 x, y;
+        x.__x = ar[k];
+        y.__x = br[k];
+        part = __fmaf_rn(static_cast<float>(x), static_cast<float>(y), part);
+      }
+      const auto sf = [&](const uint8_t* t, int row) {
+        const int64_t blk = static_cast<int64_t>(row >> 7) * ep.sf_ncb + (kb >> 2);
+        const uint32_t e = t[blk * 512 + (row & 31) * 16 + ((row >> 5) & 3) * 4 + (kb & 3)];
+        return e == 0 ? 0x1.0p-127f : __uint_as_float(e << 23);
+      };
+      af = __fmaf_rn(part, __fmul_rn(sf(ep.sfa, m), sf(ep.sfb, n)), af);
+    }
+  } else {
+    for (int k = 0; k < K; ++k) {
+      if constexpr (KIND == 0) {
+        ai += static_cast<int32_t>(static_cast<int8_t>(ar[k])) *
+              static_cast<int32_t>(static_cast<int8_t>(br[k]));
+      } else {
+        __nv_fp8_e4m3 x, y;
+        x.__x = ar[k];
+        y.__x = br[k];
+        af = __fmaf_rn(static_cast<float>(x), static_cast<float>(y), af);
+      }
     }
   }
   const int64_t o = static_cast<int64_t>(m) * ldo + n;
@@ -575,9 +646,11 @@ __global__ void __launch_bounds__(128) gemm_simt_kernel(const uint8_t* __restric
     if constexpr (KIND == 0) {
       y = dequant_one<OutT>(static_cast<float>(ai), __ldg(ep.xs + m),
                             __ldg(ep.ws + (ep.ws_scalar ? 0 : n)), bias, has_bias, ep.dq_order);
-    } else {
+    } else if constexpr (KIND == 1) {
       y = dequant_one<OutT>(af, __fmul_rn(__ldg(ep.sa), __ldg(ep.sb)), 1.0f, bias, has_bias,
                             kDqChained);
+    } else {
+      y = dequant_one<OutT>(af, 1.0f, 1.0f, bias, has_bias, kDqChained);
     }
     const bool has_resid = ep.residual != nullptr;
     const float res = has_resid ? OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(m) * ep.ldr + n) : 0.0f;
@@ -639,6 +712,9 @@ EpilogueParams to_params(const GemmArgs& g) {
     ep.dq_order = g.epi->dequant_order;
     ep.act = g.epi->activation;
   }
+  ep.sfa = static_cast<const uint8_t*>(g.sfa);
+  ep.sfb = static_cast<const uint8_t*>(g.sfb);
+  ep.sf_ncb = static_cast<int>((g.K + 127) / 128);
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   ep.vec_ws = ep.ws && a16(ep.ws);
   ep.vec_bias = ep.bias && a16(ep.bias);
@@ -737,9 +813,13 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
   auto by_bn = [&](auto order_c, auto act_c) {
     constexpr int O = decltype(order_c)::value;
     constexpr int A = decltype(act_c)::value;
-    if (bn == 128) return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, group_m, max_ctas, stream);
-    if (cg == 2) return launch_tc<KIND, 256, OutT, O, A, 2>(g, ma, mb, md, group_m, max_ctas, stream);
-    return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, md, group_m, max_ctas, stream);
+    if constexpr (KIND == 2) {
+      return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, group_m, max_ctas, stream);
+    } else {
+      if (bn == 128) return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, group_m, max_ctas, stream);
+      if (cg == 2) return launch_tc<KIND, 256, OutT, O, A, 2>(g, ma, mb, md, group_m, max_ctas, stream);
+      return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, md, group_m, max_ctas, stream);
+    }
   };
   using I0 = std::integral_constant<int, 0>;
   using I1 = std::integral_constant<int, 1>;
@@ -749,7 +829,7 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
   } else {
     const int order = (KIND == 0 && g.epi) ? g.epi->dequant_order : kDqChained;
     const int act = g.epi ? g.epi->activation : kActNone;
-    if (KIND == 1) {
+    if (KIND != 0) {
       return act == kActGeluTanh ? by_bn(I2{}, I1{}) : by_bn(I2{}, I0{});
     }
     switch (order * 2 + (act == kActGeluTanh ? 1 : 0)) {
@@ -797,6 +877,14 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
       case W8A8_F16: return dispatch_out<0, __half>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
       case W8A8_F32: return dispatch_out<0, float>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
       case W8A8_S32: return dispatch_out<0, int32_t>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
+      default: break;
+    }
+  } else if (g.kind == 2) {
+    const bool mx_ok = tc_ok && g.K % 32 == 0 && a16(g.sfa) && a16(g.sfb);
+    switch (g.out_dtype) {
+      case W8A8_BF16: return dispatch_out<2, __nv_bfloat16>(g, mx_ok, 128, group_m, max_ctas, 1, stream);
+      case W8A8_F16: return dispatch_out<2, __half>(g, mx_ok, 128, group_m, max_ctas, 1, stream);
+      case W8A8_F32: return dispatch_out<2, float>(g, mx_ok, 128, group_m, max_ctas, 1, stream);
       default: break;
     }
   } else {

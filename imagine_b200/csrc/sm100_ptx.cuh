@@ -140,6 +140,16 @@ __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tma
       : "memory");
 }
 
+// Untiled bulk copy global -> shared (both 16-byte aligned, bytes % 16 == 0).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_src, int32_t x,
                                              int32_t y) {
   asm volatile(
@@ -251,6 +261,47 @@ __device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, u
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
   }
+}
+
+// Block-scaled MMA, kind::mxf8f6f4 (e4m3 x e4m3, one e8m0 scale per 32 K
+// elements per row), scale factors read from TMEM.
+__device__ __forceinline__ void umma_mx(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Shared -> TMEM copy of a 32 x 16 B block, replicated into the four 32-lane
+// quadrants (the scale-factor layout of a 128-row block).
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+// Descriptor of a 32-row x 16-byte shared-memory block with no swizzle: 8-row
+// core matrices of 128 contiguous bytes, 128 B apart (stride byte offset).
+__device__ __forceinline__ uint64_t smem_desc_sf(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(128u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  return d;
+}
+
+// Instruction descriptor of the block-scaled MMA: E4M3 x E4M3, UE8M0 scales,
+// both operands K-major, sf_id selects the byte (K sub-block) of each scale
+// word for A and B.
+__host__ __device__ constexpr uint32_t make_idesc_mx(int m, int n, uint32_t sf_id) {
+  return (sf_id << 4)                                  // B scale factor id
+         | (static_cast<uint32_t>(n >> 3) << 17)        // N >> 3
+         | (1u << 23)                                   // scale format: UE8M0
+         | (static_cast<uint32_t>(m >> 4) << 24)        // M >> 4
+         | (sf_id << 29);                               // A scale factor id
 }
 
 // Arrive on the barrier at shared::cluster address `bar_cluster` (this CTA's

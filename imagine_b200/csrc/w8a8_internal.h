@@ -16,7 +16,8 @@ int quantize_rowwise_launch(const void* x, int x_dtype, int64_t rows, int64_t co
                             int8_t* q, int64_t ldq, float* scales, int scale_mode, int stochastic,
                             uint64_t seed, int mode, const float* amax_in, cudaStream_t stream);
 
-// kind 0: int8 x int8 (s32 accumulate); kind 1: e4m3 x e4m3 (f32 accumulate).
+// kind 0: int8 x int8 (s32 accumulate); kind 1: e4m3 x e4m3 (f32 accumulate);
+// kind 2: MXFP8 e4m3 x e4m3 with e8m0 block scales (f32 accumulate).
 // Returns 0 on success, a W8A8_ERR_* code otherwise (message via set_error).
 struct GemmArgs {
   int kind;
@@ -33,6 +34,8 @@ struct GemmArgs {
   int64_t ldo;
   int64_t M, N, K;
   const w8a8_gemm_config_t* cfg;
+  const void* sfa;  // kind 2 (MXFP8): blocked e8m0 scales of a and b
+  const void* sfb;
 };
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);
 
@@ -45,6 +48,9 @@ int gemv_launch(const int8_t* q, const int8_t* w, const float* xs, const w8a8_ep
 int linear_small_launch(const void* x, int x_dtype, const int8_t* w, const w8a8_epilogue_t* epi,
                         int scale_mode, int8_t* q_out, float* xs_out, void* out, int out_dtype,
                         int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+
+int quantize_mxfp8_launch(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
+                          uint8_t* q, int64_t ldq, uint8_t* sf, cudaStream_t stream);
 
 int quantize_fp8_tensor_launch(const void* x, int x_dtype, int64_t numel, const float* scale,
                                uint8_t* out, cudaStream_t stream);

@@ -351,6 +351,48 @@ def fp8_linear(a: torch.Tensor, scale_a: torch.Tensor, w: torch.Tensor, scale_w:
     return out.reshape(*lead, n)
 
 
+# --------------------------------------------------------------------------
+# a10: MXFP8
+# --------------------------------------------------------------------------
+def quantize_mxfp8(x: torch.Tensor):
+    """Kitchen ``quantize_mxfp8(x, pad_32x=False)`` (inference/src/eager.rs:176-225):
+    returns ``(payload float8_e4m3fn [M, K], scales uint8 [ceil(M/128)*128,
+    ceil(K/128)*4])``, the scales in the cuBLAS blocked layout."""
+    _cuda("x", x)
+    if x.dim() != 2:
+        raise ValueError("Input must be 2D")
+    m, k = x.shape
+    if k % 32:
+        raise ValueError("K dimension must be divisible by 32")
+    xc = x.contiguous()
+    q = torch.empty((m, k), dtype=torch.float8_e4m3fn, device=x.device)
+    sf = torch.empty(((m + 127) // 128 * 128, (k // 32 + 3) // 4 * 4), dtype=torch.uint8,
+                     device=x.device)
+    N.check(N.LIB.w8a8_quantize_mxfp8(_vp(xc), _code(xc.dtype), m, k, k, _vp(q), k, _vp(sf),
+                                      _stream(x.device)))
+    return q, sf
+
+
+def mxfp8_linear(a: torch.Tensor, a_scales: torch.Tensor, w: torch.Tensor, w_scales: torch.Tensor,
+                 bias: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.bfloat16,
+                 config=None) -> torch.Tensor:
+    """``scaled_mm_mxfp8`` (inference/src/backend_quant.rs:320-343) on tcgen05
+    kind::mxf8f6f4.block_scale: a [M, K] and w [N, K] e4m3 with blocked e8m0
+    scales from ``quantize_mxfp8``."""
+    _cuda("a", a)
+    dev = a.device
+    _cuda("w", w, dev)
+    m, k = a.shape
+    n = w.shape[0]
+    b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
+    out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    cfg = _config(config)
+    N.check(N.LIB.w8a8_mxfp8_gemm(_vp(a.contiguous()), _vp(a_scales.contiguous()),
+                                  _vp(w.contiguous()), _vp(w_scales.contiguous()), _vp(b), _vp(out),
+                                  _code(out_dtype), m, n, k, _cfg_ptr(cfg), _stream(dev)))
+    return out
+
+
 def device_error(device=None) -> int:
     """Read-and-clear the device-side error word (nonzero: a bounded wait in a
     tcgen05 kernel gave up)."""

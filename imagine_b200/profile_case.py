@@ -26,34 +26,73 @@ def main():
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--block-n", type=int, default=0)
+    ap.add_argument("--cta-group", type=int, default=0)
+    ap.add_argument("--time", action="store_true",
+                    help="time each launch with CUDA events (L2 flushed before each) and print "
+                         "the median")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     g = torch.Generator().manual_seed(0)
     x = torch.randn(a.m, a.k, generator=g).to(torch.bfloat16).to(dev)
-    cfg = (a.block_n, 8, 0)
-    if a.kernel == "quantize":
+    cfg = (a.block_n, 8, 0, a.cta_group)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev) if a.time else None
+    times = []
+
+    def run(fn):
         for _ in range(a.iters):
-            W.quantize_int8_rowwise(x)
+            if flush is not None:
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            else:
+                fn()
+
+    if a.kernel == "quantize":
+        run(lambda: W.quantize_int8_rowwise(x))
     else:
         w = (torch.randn(a.n, a.k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
         b = (torch.randn(a.n, generator=g) * 0.02).to(torch.bfloat16).to(dev)
         wq, ws = W.quantize_weight(w)
         if a.kernel in ("gemm", "gemm_gelu", "gemv"):
             act = "gelu_tanh" if a.kernel == "gemm_gelu" else None
-            for _ in range(a.iters):
-                W.int8_linear(x, wq, ws, b, output_act=act, config=cfg)
+            if a.time and a.kernel != "gemv":
+                # time the GEMM alone on pre-quantised activations
+                import ctypes
+                from imagine_b200 import _native as NAT
+                from imagine_b200.linear import _config, _epilogue, _stream, _vp
+                q, xs = W.quantize_int8_rowwise(x)
+                y = torch.empty((a.m, a.n), dtype=torch.bfloat16, device=dev)
+                ep = _epilogue(ws, b, None, None, "eager", act, a.n, a.n)
+                c = _config(cfg)
+                run(lambda: NAT.check(NAT.LIB.w8a8_gemm_dequant(
+                    _vp(q), a.k, _vp(wq), a.k, _vp(xs), ctypes.byref(ep), _vp(y), NAT.BF16, a.n,
+                    a.m, a.n, a.k, ctypes.byref(c), _stream(dev))))
+            else:
+                run(lambda: W.int8_linear(x, wq, ws, b, output_act=act, config=cfg))
         else:
             sa = (x.abs().max().float() / 448).reshape(1)
             sw = (w.abs().max().float() / 448).reshape(1)
             aq = W.quantize_per_tensor_fp8(x, sa)
             wq8 = W.quantize_per_tensor_fp8(w, sw)
-            for _ in range(a.iters):
-                W.fp8_linear(aq, sa, wq8, sw, b, config=cfg)
+            run(lambda: W.fp8_linear(aq, sa, wq8, sw, b, config=cfg))
     torch.cuda.synchronize()
     err = W.device_error()
     if err:
         raise SystemExit(f"device error {err}")
-    print("ok", a.kernel, a.m, a.k, a.n)
+    msg = f"ok {a.kernel} {a.m} {a.k} {a.n} block_n={a.block_n} cta_group={a.cta_group}"
+    if times:
+        t = sorted(times)[len(times) // 2]
+        ops = 2.0 * a.m * a.n * a.k
+        msg += f" median_ms={t:.4f}"
+        if a.kernel != "quantize":
+            msg += f" TOPS={ops / t / 1e9:.1f}"
+        else:
+            msg += f" GB/s={(a.m * a.k * 3 + 4 * a.m) / t / 1e6:.1f}"
+    print(msg)
 
 
 if __name__ == "__main__":

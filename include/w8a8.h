@@ -191,6 +191,27 @@ int w8a8_fp8_gemm(const uint8_t* a, const uint8_t* b, const float* sa, const flo
                   const void* bias, void* out, int out_dtype, int64_t M, int64_t N, int64_t K,
                   const w8a8_gemm_config_t* cfg, void* stream);
 
+/* ---- a10: MXFP8 (32-element K blocks, e8m0 scales) ------------------------
+ * Replaces `quantize_mxfp8(x, pad_32x=false)` (inference/src/eager.rs:176-225;
+ * KSRC backends/cuda/ops/quantize_mxfp8.cu:40-147) with the eager numerics.
+ * x [rows, cols] (cols % 32 == 0, 16-byte aligned rows) -> payload e4m3
+ * [rows, cols] (row stride ldq) and e8m0 scales in the cuBLAS blocked layout
+ * of inference/src/block_scales.rs:4-31: a buffer of
+ * ceil(rows/128)*128 x ceil(cols/128)*4 bytes, padding written as zeros.
+ * A block with 0 < amax <= 448 * 2^-127 gets scale byte 0 and a finite payload
+ * (the reference divides by its zero decoding of byte 0). */
+int w8a8_quantize_mxfp8(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
+                        uint8_t* q, int64_t ldq, uint8_t* scales, void* stream);
+
+/* MXFP8 GEMM on tcgen05 kind::mxf8f6f4.block_scale: out = sum over 32-element
+ * blocks of (a . b) * 2^(ea-127) * 2^(eb-127) + bias.  Replaces
+ * `scaled_mm_mxfp8` -> at::_scaled_mm_v2 BlockWise1x32 with SWIZZLE_32_4_4
+ * (inference/src/backend_quant.rs:320-343).  a e4m3 [M, K], b e4m3 [N, K],
+ * scales as written by w8a8_quantize_mxfp8, K % 32 == 0. */
+int w8a8_mxfp8_gemm(const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
+                    const uint8_t* b_scales, const void* bias, void* out, int out_dtype, int64_t M,
+                    int64_t N, int64_t K, const w8a8_gemm_config_t* cfg, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

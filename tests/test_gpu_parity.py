@@ -344,3 +344,41 @@ def test_fp8_linear(m, k, n, cg):
     assert_rms_close(y, O.fp8_linear_exact(aq.cpu(), sa, wq.cpu(), sw, b, out_dtype=torch.float32))
     # and against the reference's own fallback (bf16-dequantised operands)
     assert_rms_close(y, O.fp8_linear(aq.cpu(), sa, wq.cpu(), sw, b), tol=0.03)
+
+
+# ---------------------------------------------------------------- MXFP8
+@pytest.mark.parametrize("name", [n for n in MAN["kitchen_eager"] if n.startswith("mxfp8/")])
+def test_mxfp8_quantize_golden(name):
+    dt = G.DT[name.split("/")[-1]]
+    x = G.tensor(KE[name + "/x"], dt).to(cuda())
+    p, sf = W().quantize_mxfp8(x)
+    assert np.array_equal(_b(p), KE[name + "/q"].reshape(-1))
+    assert np.array_equal(_b(sf), KE[name + "/sf"].reshape(-1))
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("m,k", [(5600, 3072), (130, 160), (1, 32), (257, 4096)])
+def test_mxfp8_quantize_random(dt, m, k):
+    g = torch.Generator().manual_seed(m + k)
+    x = torch.randn(m, k, generator=g)
+    x = torch.where(torch.rand(m, k, generator=g) < 0.01, x * 20, x).to(dt)
+    x[0, :32] = 0
+    p, sf = W().quantize_mxfp8(x.to(cuda()))
+    po, sfo = O.quantize_mxfp8(x)
+    assert np.array_equal(_b(sf), _b(sfo))
+    assert np.array_equal(_b(p), _b(po))
+
+
+@pytest.mark.parametrize("m,k,n", [(300, 3072, 1024), (5600, 3072, 512), (130, 160, 264), (128, 256, 128)])
+def test_mxfp8_linear(m, k, n):
+    g = torch.Generator().manual_seed(m + k + n)
+    x = torch.randn(m, k, generator=g)
+    x = torch.where(torch.rand(m, k, generator=g) < 0.01, x * 20, x).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
+    aq, asf = W().quantize_mxfp8(x.to(cuda()))
+    wq, wsf = W().quantize_mxfp8(w.to(cuda()))
+    y = W().mxfp8_linear(aq, asf, wq, wsf, b.to(cuda()))
+    no_device_error()
+    ref = O.mxfp8_linear(aq.cpu(), asf.cpu(), wq.cpu(), wsf.cpu(), b, out_dtype=torch.float32)
+    assert_rms_close(y, ref)
