@@ -88,6 +88,7 @@ struct Cfg {
   static constexpr int kChunksPerWarp = (BN / 32 + 1) / 2;
   static constexpr int kVecBytes = 2 * kChunksPerWarp * 32 * 4;
   static constexpr int kDBytes = kEpiWarps * (kStageD + kVecBytes);
+  static_assert(kStageD % 1024 == 0, "staging tiles must keep 1024-byte alignment");
   static constexpr int kBarBytes = 256;
   static constexpr int kFixed = 1024 + kDBytes + kBarBytes;
   static constexpr int kStagesRaw = (kMaxSmem - kFixed) / (kStageBytes + kSFBytes);
@@ -429,9 +430,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;
     const int half = warp >> 2;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-    uint8_t* st = sD + warp * (C::kStageD + C::kVecBytes);
-    float* s_ws = reinterpret_cast<float*>(st + C::kStageD);    // [chunk][32]
-    float* s_bias = s_ws + C::kChunksPerWarp * 32;                // [chunk][32]
+    // staging tiles first (each a multiple of 1024 B, as the TMA swizzle
+    // needs), then the per-warp vectors
+    uint8_t* st = sD + warp * C::kStageD;
+    float* s_ws = reinterpret_cast<float*>(sD + kEpiWarps * C::kStageD + warp * C::kVecBytes);
+    float* s_bias = s_ws + C::kChunksPerWarp * 32;  // [chunk][32] each
     const bool has_bias = ep.bias != nullptr;
     const bool has_resid = ep.residual != nullptr;
     float fp8_scale = 0.0f;
