@@ -330,8 +330,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kBK, b_row);
             if constexpr (KIND == 2) {
               // blocked scale layout: 512-byte block (row/128, kb) at
-              // ((row/128) * ncb + kb) * 512
+              // ((row/128) * ncb + kb) * 512; blocks outside the buffers the
+              // caller sized from M, N, K are refused (error 5, abort).
               uint8_t* sf = sSF + s * C::kSFBytes;
+              const int a_blocks = (M + 127) / 128, b_blocks = (N + 127) / 128;
+              bool in = mb < a_blocks && kb < ep.sf_ncb;
+#pragma unroll
+              for (int j = 0; j < BN / 128; ++j) in = in && (nb * (BN / 128) + j) < b_blocks;
+              if (!in) {
+                atomicCAS(&g_w8a8_device_error, 0, kDevBadScaleBlock);
+                *abort_flag = 1;
+                ok = false;
+                break;
+              }
               bulk_load(sf, ep.sfa + (static_cast<int64_t>(mb) * ep.sf_ncb + kb) * 512, 512,
                         &full[s]);
 #pragma unroll

@@ -23,6 +23,7 @@ enum DeviceError : int {
   kDevTimeoutEmpty = 2,     // producer waited too long for a free stage
   kDevTimeoutTmemFull = 3,  // epilogue waited too long for an accumulator
   kDevTimeoutTmemEmpty = 4, // MMA issuer waited too long for a free accumulator
+  kDevBadScaleBlock = 5,    // an MXFP8 scale block outside the caller's buffers
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -1,0 +1,164 @@
+/*
+ * Scalar C restatement of the reference's eager W8A8 path -- TEST
+ * INFRASTRUCTURE ONLY (an independent cross-check of oracle/eager.py; the
+ * product library never links it).
+ *
+ * bf16 values travel as their uint16 bit patterns.  Each function names the
+ * reference lines it restates (paths relative to the reference repository).
+ * Build: make -C oracle   ->  oracle/_build/libref_w8a8.so
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+static float bf16_to_f(uint16_t b) {
+  uint32_t u = (uint32_t)b << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+/* round-to-nearest-even fp32 -> bf16 (finite inputs) */
+static uint16_t f_to_bf16(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) return (uint16_t)((u >> 16) | 0x40);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+static float round_bf16(float f) { return bf16_to_f(f_to_bf16(f)); }
+
+/* inference/src/eager.rs:159-171 (quantize_int8_rowwise, seed <= 0):
+ * scale = max(amax / 127, 1e-30) in fp32; q = clamp(rne(bf16(x / bf16(scale)))) */
+void ref_quantize_rowwise_bf16(const uint16_t* x, int64_t rows, int64_t cols, int8_t* q,
+                               float* scale) {
+  for (int64_t r = 0; r < rows; ++r) {
+    const uint16_t* xr = x + r * cols;
+    float amax = 0.0f;
+    for (int64_t c = 0; c < cols; ++c) {
+      float v = fabsf(bf16_to_f(xr[c]));
+      if (v > amax) amax = v;
+    }
+    float s = amax / 127.0f;
+    if (s < 1e-30f) s = 1e-30f;
+    scale[r] = s;
+    float d = round_bf16(s);
+    if (d == 0.0f) d = 1.17549435e-38f; /* finfo(bfloat16).tiny, eager.rs:94-109 */
+    for (int64_t c = 0; c < cols; ++c) {
+      float t = round_bf16(bf16_to_f(xr[c]) / d);
+      t = rintf(t);
+      if (t < -128.0f) t = -128.0f;
+      if (t > 127.0f) t = 127.0f;
+      q[r * cols + c] = (int8_t)t;
+    }
+  }
+}
+
+/* inference/src/int8_linear.rs:134-168: exact int32 accumulate of a . w^T */
+void ref_int8_gemm(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int64_t k,
+                   int32_t* acc) {
+  for (int64_t i = 0; i < m; ++i)
+    for (int64_t j = 0; j < n; ++j) {
+      int64_t s = 0;
+      for (int64_t t = 0; t < k; ++t) s += (int64_t)a[i * k + t] * (int64_t)w[j * k + t];
+      acc[i * n + j] = (int32_t)s;
+    }
+}
+
+/* inference/src/int8_linear.rs:244-268 (bf16 out): y = bf16(acc * (xs * ws));
+ * y = bf16(y + bias) */
+void ref_dequant_eager_bf16(const int32_t* acc, const float* xs, const float* ws, int64_t ws_numel,
+                            const uint16_t* bias, int64_t m, int64_t n, uint16_t* out) {
+  for (int64_t i = 0; i < m; ++i)
+    for (int64_t j = 0; j < n; ++j) {
+      const float sc = xs[i] * ws[ws_numel == 1 ? 0 : j];
+      float y = round_bf16((float)acc[i * n + j] * sc);
+      if (bias) y = round_bf16(y + bf16_to_f(bias[j]));
+      out[i * n + j] = f_to_bf16(y);
+    }
+}
+
+/* e4m3fn encoding of a finite |v| <= 448, round to nearest even (what
+ * torch's float -> float8_e4m3fn cast does for clamped inputs). */
+static uint8_t f_to_e4m3(float v) {
+  uint8_t sign = 0;
+  if (v < 0 || (v == 0 && signbit(v))) {
+    sign = 0x80;
+    v = -v;
+  }
+  if (v == 0.0f) return sign;
+  /* candidate codes are 0x00..0x7E; pick the nearest, ties to even code */
+  int e;
+  frexpf(v, &e); /* v = f * 2^e, f in [0.5, 1) */
+  int exp_unb = e - 1;           /* v in [2^exp_unb, 2^(exp_unb+1)) */
+  double step;
+  int base_code;
+  if (exp_unb < -6) { /* subnormal range: step 2^-9 */
+    step = ldexp(1.0, -9);
+    double units = v / step;
+    double r = nearbyint(units); /* ties to even under default rounding */
+    int code = (int)r;           /* 0..8 (8 = smallest normal 2^-6) */
+    return (uint8_t)(sign | code);
+  }
+  step = ldexp(1.0, exp_unb - 3);
+  double units = v / step; /* in [8, 16) */
+  double r = nearbyint(units);
+  int mant = (int)r - 8;
+  int ebias = exp_unb + 7;
+  if (mant == 8) {
+    mant = 0;
+    ebias += 1;
+  }
+  base_code = (ebias << 3) | mant;
+  if (base_code > 0x7E) base_code = 0x7E;
+  return (uint8_t)(sign | base_code);
+}
+
+/* inference/src/eager.rs:74-88: e4m3(clamp(bf16(x * bf16(1/scale)), +-448)) */
+void ref_quantize_fp8_bf16(const uint16_t* x, int64_t numel, float scale, uint8_t* out) {
+  const float recip = round_bf16(1.0f / scale);
+  for (int64_t i = 0; i < numel; ++i) {
+    float t = round_bf16(bf16_to_f(x[i]) * recip);
+    if (t > 448.0f) t = 448.0f;
+    if (t < -448.0f) t = -448.0f;
+    out[i] = f_to_e4m3(t);
+  }
+}
+
+/* inference/src/eager.rs:176-225 + block_scales.rs:4-31 (bf16 input,
+ * cols % 32 == 0): payload [rows, cols], scales in the blocked layout
+ * [ceil(rows/128)*128, ceil(cols/128)*4]. */
+void ref_quantize_mxfp8_bf16(const uint16_t* x, int64_t rows, int64_t cols, uint8_t* q,
+                             uint8_t* sf) {
+  const int64_t nkb = cols / 32, ncb = (nkb + 3) / 4;
+  const int64_t rows_pad = (rows + 127) / 128 * 128;
+  memset(sf, 0, (size_t)(rows_pad * ncb * 4));
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t kb = 0; kb < nkb; ++kb) {
+      const uint16_t* xb = x + r * cols + kb * 32;
+      float amax = 0.0f;
+      for (int j = 0; j < 32; ++j) {
+        float v = fabsf(bf16_to_f(xb[j]));
+        if (v > amax) amax = v;
+      }
+      int e = 0;
+      float scale_f = 1.0f;
+      if (amax != 0.0f) {
+        float need = amax / 448.0f;
+        if (need < ldexpf(1.0f, -127)) need = ldexpf(1.0f, -127);
+        e = (int)ceil(log2((double)need)) + 127;
+        if (e < 0) e = 0;
+        if (e > 254) e = 254;
+        scale_f = ldexpf(1.0f, e - 127);
+      }
+      for (int j = 0; j < 32; ++j) {
+        float t = amax != 0.0f ? bf16_to_f(xb[j]) / scale_f : 0.0f;
+        if (t > 448.0f) t = 448.0f;
+        if (t < -448.0f) t = -448.0f;
+        q[r * cols + kb * 32 + j] = f_to_e4m3(t);
+      }
+      const int64_t blk = (r / 128) * ncb + kb / 4;
+      sf[blk * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (kb % 4)] = (uint8_t)e;
+    }
+}

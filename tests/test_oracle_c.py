@@ -1,0 +1,82 @@
+"""The scalar C restatement (oracle/ref_w8a8.c) agrees with the torch oracle
+and with the reference's golden vectors: two independent CPU restatements."""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import eager as O
+from tests import _golden as G
+
+ORACLE_DIR = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle")
+
+
+@pytest.fixture(scope="module")
+def ref():
+    subprocess.run(["make", "-s", "-C", ORACLE_DIR], check=True)
+    lib = ctypes.CDLL(os.path.join(ORACLE_DIR, "_build", "libref_w8a8.so"))
+    vp, i64 = ctypes.c_void_p, ctypes.c_int64
+    lib.ref_quantize_rowwise_bf16.argtypes = [vp, i64, i64, vp, vp]
+    lib.ref_int8_gemm.argtypes = [vp, vp, i64, i64, i64, vp]
+    lib.ref_dequant_eager_bf16.argtypes = [vp, vp, vp, i64, vp, i64, i64, vp]
+    lib.ref_quantize_fp8_bf16.argtypes = [vp, i64, ctypes.c_float, vp]
+    lib.ref_quantize_mxfp8_bf16.argtypes = [vp, i64, i64, vp, vp]
+    return lib
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def test_c_quantiser_and_linear_match(ref):
+    g = torch.Generator().manual_seed(5)
+    m, k, n = 37, 160, 72
+    x = (torch.randn(m, k, generator=g) * 3).to(torch.bfloat16)
+    x[1] = 0
+    q = torch.empty(m, k, dtype=torch.int8)
+    s = torch.empty(m, dtype=torch.float32)
+    ref.ref_quantize_rowwise_bf16(_p(x), m, k, _p(q), _p(s))
+    qo, so = O.quantize_int8_rowwise(x)
+    assert torch.equal(q, qo) and torch.equal(s, so.reshape(-1))
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    wq, ws = O.quantize_weight(w)
+    acc = torch.empty(m, n, dtype=torch.int32)
+    ref.ref_int8_gemm(_p(q), _p(wq), m, n, k, _p(acc))
+    assert torch.equal(acc, O.int8_accumulate(qo, wq))
+    b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
+    y = torch.empty(m, n, dtype=torch.bfloat16)
+    ref.ref_dequant_eager_bf16(_p(acc), _p(s), _p(ws), n, _p(b), m, n, _p(y))
+    yo = O.int8_linear(x, wq, ws, b, out_dtype=torch.bfloat16)
+    assert torch.equal(y.view(torch.int16), yo.view(torch.int16))
+
+
+@pytest.mark.parametrize("name", [n for n in G.manifest()["kitchen_eager"]
+                                  if n.startswith("quant/") and n.endswith("/bf16")])
+def test_c_quantiser_golden(ref, name):
+    ke = G.load("kitchen_eager")
+    x = G.tensor(ke[name + "/x"], torch.bfloat16)
+    m, k = x.shape
+    q = torch.empty(m, k, dtype=torch.int8)
+    s = torch.empty(m, dtype=torch.float32)
+    ref.ref_quantize_rowwise_bf16(_p(x.contiguous()), m, k, _p(q), _p(s))
+    assert np.array_equal(O.as_bytes(q), ke[name + "/q"].view(np.uint8).reshape(-1))
+
+
+def test_c_fp8_and_mxfp8_golden(ref):
+    ke = G.load("kitchen_eager")
+    x = G.tensor(ke["fp8/bf16/x"], torch.bfloat16).contiguous()
+    sc = float(G.tensor(ke["fp8/bf16/scale"], torch.float32)[0])
+    out = torch.empty(x.numel(), dtype=torch.uint8)
+    ref.ref_quantize_fp8_bf16(_p(x), x.numel(), sc, _p(out))
+    assert np.array_equal(out.numpy(), ke["fp8/bf16/q"].reshape(-1))
+    for name in [n for n in G.manifest()["kitchen_eager"] if n.startswith("mxfp8/") and n.endswith("bf16")]:
+        x = G.tensor(ke[name + "/x"], torch.bfloat16).contiguous()
+        m, k = x.shape
+        q = torch.empty(m, k, dtype=torch.uint8)
+        sf = torch.empty(((m + 127) // 128 * 128) * ((k // 32 + 3) // 4 * 4), dtype=torch.uint8)
+        ref.ref_quantize_mxfp8_bf16(_p(x), m, k, _p(q), _p(sf))
+        assert np.array_equal(q.numpy().reshape(-1), ke[name + "/q"].reshape(-1)), name
+        assert np.array_equal(sf.numpy(), ke[name + "/sf"].reshape(-1)), name
