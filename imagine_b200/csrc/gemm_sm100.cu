@@ -894,7 +894,13 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
       default: break;
     }
   } else if (g.kind == 2) {
-    const bool mx_ok = tc_ok && g.K % 32 == 0 && a16(g.sfa) && a16(g.sfb);
+    // The tcgen05 block-scaled variant (KIND 2 with tcgen05.cp scale copies)
+    // raised an illegal-address fault on a 128x128x256 case and is not
+    // dispatched until the cause is understood; MXFP8 runs on the CUDA-core
+    // path.
+    constexpr bool kBlockScaledTcgen05Enabled = false;
+    const bool mx_ok = kBlockScaledTcgen05Enabled && tc_ok && g.K % 32 == 0 && a16(g.sfa) &&
+                       a16(g.sfb);
     switch (g.out_dtype) {
       case W8A8_BF16: return dispatch_out<2, __nv_bfloat16>(g, mx_ok, 128, group_m, max_ctas, 1, stream);
       case W8A8_F16: return dispatch_out<2, __half>(g, mx_ok, 128, group_m, max_ctas, 1, stream);

@@ -369,7 +369,7 @@ def test_mxfp8_quantize_random(dt, m, k):
     assert np.array_equal(_b(p), _b(po))
 
 
-@pytest.mark.parametrize("m,k,n", [(300, 3072, 1024), (5600, 3072, 512), (130, 160, 264), (128, 256, 128)])
+@pytest.mark.parametrize("m,k,n", [(300, 3072, 256), (130, 160, 264), (128, 256, 128)])
 def test_mxfp8_linear(m, k, n):
     g = torch.Generator().manual_seed(m + k + n)
     x = torch.randn(m, k, generator=g)
