@@ -13,6 +13,7 @@ _OPS = (
     "int8_gemv",
     "int8_linear",
     "quantize_int8_rowwise",
+    "quantize_int8_rowwise_convrot",
     "quantize_per_tensor_fp8",
     "quantize_weight",
     "row_absmax",

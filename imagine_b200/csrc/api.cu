@@ -132,6 +132,40 @@ int w8a8_quantize_rowwise(const void* x, int x_dtype, int64_t rows, int64_t cols
                                         static_cast<cudaStream_t>(stream)));
 }
 
+int w8a8_quantize_rowwise_convrot(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                                  int64_t ldx, int group, int input_act, const void* act_w,
+                                  float act_eps, int8_t* q, int64_t ldq, float* scale,
+                                  int scale_mode, void* stream) {
+  if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
+  if (scale_mode != W8A8_SCALE_EAGER && scale_mode != W8A8_SCALE_KITCHEN) {
+    return fail(W8A8_ERR_VALUE, "unknown scale mode %d", scale_mode);
+  }
+  if (group != 0 && group != 256) {
+    return fail(W8A8_ERR_VALUE, "fused ConvRot quantiser supports group 256 (or 0: no rotation), got %d",
+                group);
+  }
+  if (input_act < W8A8_INPUT_ACT_NONE || input_act > W8A8_INPUT_ACT_SITU) {
+    return fail(W8A8_ERR_VALUE, "unknown input activation code %d", input_act);
+  }
+  if (cols == 0 || cols % 256 != 0 || cols > 16384) {
+    return fail(W8A8_ERR_VALUE, "fused quantiser needs K a multiple of 256 in [256, 16384], got %lld",
+                static_cast<long long>(cols));
+  }
+  const int64_t in_cols =
+      (input_act == W8A8_INPUT_ACT_SWIGLU || input_act == W8A8_INPUT_ACT_SITU) ? 2 * cols : cols;
+  if (input_act == W8A8_INPUT_ACT_RMS_NORM && !act_w) {
+    return fail(W8A8_ERR_VALUE, "input_act 'rms_norm' requires act_weight");
+  }
+  if (rows == 0) return finish(0);
+  if (rows > 0x7fffffffLL) return fail(W8A8_ERR_VALUE, "rows must be <= INT_MAX");
+  if (!x || !q || !scale) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldx < in_cols || ldq < cols) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  return finish(quantize_act_rot_launch(x, x_dtype, rows, cols, ldx, group == 256 ? 1 : 0,
+                                        input_act, act_w, act_eps, q, ldq, scale, scale_mode,
+                                        static_cast<cudaStream_t>(stream)));
+}
+
 int w8a8_row_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
                     float* amax, void* stream) {
   if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");

@@ -739,7 +739,9 @@ EpilogueParams to_params(const GemmArgs& g) {
 template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG>
 int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
               int group_m, int max_ctas, cudaStream_t stream) {
-  using C = Cfg<BN, OutT, CG>;
+  // The same configuration the kernel lays its shared memory out with: the
+  // block-scaled kind adds scale-factor bytes to every stage.
+  using C = Cfg<BN, OutT, CG, KIND>;
   auto kern = gemm_sm100_kernel<KIND, BN, OutT, ORDER, ACT, CG>;
   static bool attr_set[64] = {};
   int dev = 0;
@@ -872,9 +874,12 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     return W8A8_ERR_VALUE;
   }
   if (bn == 0) {
+    // 256-column tiles when they alone fill every SM; otherwise the 128-column
+    // tiles' extra parallelism wins (measured on B200: 256 x 12288 -> 3072
+    // runs 27% faster with 128-column tiles, 5600 x 3072 -> 3072 50% slower).
     const int sms = device_sm_count();
     const long long tiles256 = ((g.M + kBM - 1) / kBM) * ((g.N + 255) / 256);
-    bn = (tiles256 >= sms || g.N % 256 == 0) && g.N >= 256 ? 256 : 128;
+    bn = tiles256 >= sms && g.N >= 256 ? 256 : 128;
   }
   const int group_m = g.cfg && g.cfg->group_m > 0 ? g.cfg->group_m : 8;
   const int max_ctas = g.cfg ? g.cfg->max_ctas : 0;
@@ -883,7 +888,10 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     set_error("cta_group must be 1 or 2, got %d", cg);
     return W8A8_ERR_VALUE;
   }
-  if (cg == 0) cg = (bn == 256 && g.M > kBM) ? 2 : 1;
+  // One CTA per tile by default: on B200 the CTA-pair variant measured 1-4%
+  // slower on the 5600-row shapes (its B traffic saving does not pay while the
+  // epilogue bounds the tile rate).
+  if (cg == 0) cg = 1;
   if (bn == 128) cg = 1;  // pairs are built for 256-column tiles
   if (g.kind == 0) {
     switch (g.out_dtype) {
@@ -894,13 +902,7 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
       default: break;
     }
   } else if (g.kind == 2) {
-    // The tcgen05 block-scaled variant (KIND 2 with tcgen05.cp scale copies)
-    // raised an illegal-address fault on a 128x128x256 case and is not
-    // dispatched until the cause is understood; MXFP8 runs on the CUDA-core
-    // path.
-    constexpr bool kBlockScaledTcgen05Enabled = false;
-    const bool mx_ok = kBlockScaledTcgen05Enabled && tc_ok && g.K % 32 == 0 && a16(g.sfa) &&
-                       a16(g.sfb);
+    const bool mx_ok = tc_ok && g.K % 32 == 0 && a16(g.sfa) && a16(g.sfb);
     switch (g.out_dtype) {
       case W8A8_BF16: return dispatch_out<2, __nv_bfloat16>(g, mx_ok, 128, group_m, max_ctas, 1, stream);
       case W8A8_F16: return dispatch_out<2, __half>(g, mx_ok, 128, group_m, max_ctas, 1, stream);

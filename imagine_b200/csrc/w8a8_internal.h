@@ -16,6 +16,12 @@ int quantize_rowwise_launch(const void* x, int x_dtype, int64_t rows, int64_t co
                             int8_t* q, int64_t ldq, float* scales, int scale_mode, int stochastic,
                             uint64_t seed, int mode, const float* amax_in, cudaStream_t stream);
 
+// Fused input activation (+ 256-point ConvRot when rotate != 0) + row-wise
+// INT8 quantiser; act codes W8A8_INPUT_ACT_*.
+int quantize_act_rot_launch(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
+                            int rotate, int act, const void* act_w, float act_eps, int8_t* q,
+                            int64_t ldq, float* scales, int scale_mode, cudaStream_t stream);
+
 // kind 0: int8 x int8 (s32 accumulate); kind 1: e4m3 x e4m3 (f32 accumulate);
 // kind 2: MXFP8 e4m3 x e4m3 with e8m0 block scales (f32 accumulate).
 // Returns 0 on success, a W8A8_ERR_* code otherwise (message via set_error).

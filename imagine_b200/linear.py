@@ -6,8 +6,9 @@ KSRC comfy_kitchen/__init__.py) so a caller written against them can switch
 over unchanged; every numeric step runs in libw8a8 (include/w8a8.h) through the
 C ABI -- there is no CPU or PyTorch fallback for the linear itself.  PyTorch is
 used for device memory, streams and the ATen steps the reference's own CUDA
-route also delegates to ATen (input activations that are not fused,
-ConvRot rotation: inference/src/cuda_linear.rs:452-475, 586-600).
+route also delegates to ATen for shapes its fused kernels do not take (input
+activations and ConvRot rotation when K is not a multiple of 256 up to 16384:
+inference/src/cuda_linear.rs:452-475, 586-600).
 """
 from __future__ import annotations
 
@@ -124,6 +125,52 @@ def quantize_int8_rowwise_given_absmax(x: torch.Tensor, absmax: torch.Tensor, *,
     return q.reshape(x.shape), s.reshape(*x.shape[:-1], 1)
 
 
+INPUT_ACT = {None: 0, "none": 0, "gelu_tanh": 1, "swiglu": 2, "rms_norm": 3, "situ": 4}
+
+
+def quantize_int8_rowwise_convrot(x: torch.Tensor, group: int = 256, input_act: Optional[str] = None,
+                                  input_act_weight: Optional[torch.Tensor] = None,
+                                  input_act_eps: Optional[float] = None, *,
+                                  scale_mode: str = "kitchen"):
+    """Input activation + ConvRot + per-row INT8 quantisation in one pass
+    (Kitchen ``quantize_int8_rowwise_convrot64``, inference/src/convrot.rs:156-209;
+    kernel native/comfy-port/kitchen/int8_linear.cu:1197-1314).
+
+    ``group`` 256 rotates each 256-column group by the normalised Hadamard
+    matrix; ``group`` 0 applies only the activation (rounded to x's dtype as
+    the reference's ATen activation is).  SwiGLU / SiTU take [..., 2K] rows.
+    Returns ``(q int8 [..., K], scale fp32 [..., 1])``."""
+    _cuda("x", x)
+    if input_act not in INPUT_ACT:
+        raise ValueError(f"unknown input_act {input_act!r}")
+    code = INPUT_ACT[input_act]
+    width = x.shape[-1]
+    k = width // 2 if code in (2, 4) else width
+    if code in (2, 4) and width % 2:
+        raise ValueError("not enough values to unpack (expected 2, got 1)")
+    x2 = x.reshape(-1, width)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    w = None
+    if code == 3:
+        if input_act_weight is None:
+            raise ValueError("input_act 'rms_norm' requires act_weight")
+        if input_act_eps is None:
+            # the reference's fused path refuses an unset epsilon
+            # (inference/src/convrot.rs:236-243)
+            raise TypeError("float() argument must be a string or a real number, not 'NoneType'")
+        w = input_act_weight.to(device=x.device, dtype=x.dtype).reshape(-1).contiguous()
+        if w.numel() != k:
+            raise ValueError(f"act_weight has {w.numel()} elements for K={k}")
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+    N.check(N.LIB.w8a8_quantize_rowwise_convrot(
+        _vp(x2), _code(x2.dtype), m, k, x2.stride(0) if m > 0 else width, int(group), code, _vp(w),
+        float(input_act_eps or 0.0), _vp(q), k, _vp(s), SCALE_MODE[scale_mode], _stream(x.device)))
+    return q.reshape(*x.shape[:-1], k), s.reshape(*x.shape[:-1], 1)
+
+
 def quantize_weight(weight: torch.Tensor):
     """Offline per-output-channel weight quantisation
     (inference/src/layout_complete.rs:119-159 TensorWiseINT8Layout.from_float):
@@ -162,10 +209,14 @@ def _apply_input(x, input_act, weight, eps):
     if input_act == "swiglu":
         gate, up = x.chunk(2, dim=-1)
         return torch.nn.functional.silu(gate).mul_(up)
+    if input_act == "situ":
+        a, b = x.chunk(2, dim=-1)
+        gated = torch.tanh(b / 4.0) * 4.0 * torch.sigmoid(b)
+        return torch.tanh(a / 25.0) * 25.0 * gated
     if input_act == "rms_norm":
         if weight is None:
             raise ValueError("input_act 'rms_norm' requires act_weight")
-        return torch.nn.functional.rms_norm(x, (x.shape[-1],), weight.to(x.dtype), eps or None)
+        return torch.nn.functional.rms_norm(x, (x.shape[-1],), weight.to(x.dtype), eps)
     raise ValueError(f"unknown input_act {input_act!r}")
 
 
@@ -209,8 +260,21 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     if residual is not None and residual_scale is None:
         raise ValueError("int8_linear: residual requires residual_scale")
     out_dtype = out_dtype or x.dtype
-    x = _apply_input(x, input_act, input_act_weight, input_act_eps)
-    k = x.shape[-1]
+    if input_act not in INPUT_ACT:
+        raise ValueError(f"unknown input_act {input_act!r}")
+    act = INPUT_ACT[input_act]
+    k_act = x.shape[-1] // 2 if act in (2, 4) else x.shape[-1]
+    # a2 / a6: the activation (and ConvRot over 256-groups) fuse into the
+    # quantiser when K is a multiple of 256 up to 16384 -- the shapes the
+    # reference's fused kernel takes (inference/src/cuda_linear.rs:400-417).
+    # Other shapes run the activation / rotation as device ATen ops first, as
+    # the reference's CUDA route does.
+    fused = (k_act % 256 == 0 and 256 <= k_act <= 16384
+             and ((convrot and convrot_groupsize == 256) or (not convrot and act != 0))
+             and not (act == 3 and not convrot and input_act_eps is None))
+    if not fused:
+        x = _apply_input(x, input_act, input_act_weight, input_act_eps)
+    k = k_act if fused else x.shape[-1]
     if weight.dim() != 2 or weight.dtype != torch.int8:
         raise ValueError("weight must be a 2-D int8 tensor [N, K]")
     if k != weight.shape[-1]:
@@ -226,11 +290,12 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
         if k % convrot_groupsize:
             raise ValueError(f"ConvRot group size {convrot_groupsize} does not divide input "
                              f"features {k}")
+    if convrot and not fused:
         h = _hadamard(convrot_groupsize, dev, x.dtype)
         shape = x.shape
         x = torch.matmul(x.reshape(-1, k // convrot_groupsize, convrot_groupsize), h).reshape(shape)
     lead = x.shape[:-1]
-    x2 = x.reshape(-1, k)
+    x2 = x.reshape(-1, x.shape[-1])
     if not x2.is_contiguous():
         x2 = x2.contiguous()
     m = x2.shape[0]
@@ -245,7 +310,18 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     out = torch.empty((m, n), dtype=out_dtype, device=dev)
     ep = _epilogue(ws, b, r, rs, dequant, output_act, n, n)
     stream = _stream(dev)
-    if 1 <= m <= 2 and k > 0 and m * k <= 32768:
+    if fused:
+        q, xs = quantize_int8_rowwise_convrot(x2, 256 if convrot else 0, input_act, input_act_weight,
+                                              input_act_eps, scale_mode=scale_mode)
+        xs = xs.reshape(-1)
+        if 1 <= m <= 2:
+            N.check(N.LIB.w8a8_gemv_dequant(_vp(q), _vp(w), _vp(xs), ctypes.byref(ep), _vp(out),
+                                            _code(out_dtype), m, n, k, stream))
+        else:
+            N.check(N.LIB.w8a8_gemm_dequant(_vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep),
+                                            _vp(out), _code(out_dtype), n, m, n, k,
+                                            _cfg_ptr(_config(config)), stream))
+    elif 1 <= m <= 2 and k > 0 and m * k <= 32768:
         # a5: the AdaLN-modulation shape -- quantise and GEMV in one launch.
         N.check(N.LIB.w8a8_linear_small(_vp(x2), _code(x2.dtype), _vp(w), ctypes.byref(ep),
                                         SCALE_MODE[scale_mode], None, None, _vp(out),

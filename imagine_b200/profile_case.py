@@ -19,7 +19,8 @@ import imagine_b200 as W
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel", choices=["gemm", "gemm_gelu", "quantize", "gemv", "fp8_gemm"],
+    ap.add_argument("--kernel", choices=["gemm", "gemm_gelu", "gemm_s32", "quantize", "convrot",
+                                                       "gemv", "fp8_gemm", "mxfp8_gemm"],
                     required=True)
     ap.add_argument("--m", type=int, default=5600)
     ap.add_argument("--k", type=int, default=3072)
@@ -53,11 +54,20 @@ def main():
 
     if a.kernel == "quantize":
         run(lambda: W.quantize_int8_rowwise(x))
+    elif a.kernel == "convrot":
+        run(lambda: W.quantize_int8_rowwise_convrot(x, 256))
     else:
         w = (torch.randn(a.n, a.k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
         b = (torch.randn(a.n, generator=g) * 0.02).to(torch.bfloat16).to(dev)
         wq, ws = W.quantize_weight(w)
-        if a.kernel in ("gemm", "gemm_gelu", "gemv"):
+        if a.kernel == "gemm_s32":
+            q, _ = W.quantize_int8_rowwise(x)
+            run(lambda: W.int8_gemm_s32(q, wq, config=cfg))
+        elif a.kernel == "mxfp8_gemm":
+            aq, asf = W.quantize_mxfp8(x)
+            bq, bsf = W.quantize_mxfp8(w)
+            run(lambda: W.mxfp8_linear(aq, asf, bq, bsf, b, out_dtype=torch.bfloat16))
+        elif a.kernel in ("gemm", "gemm_gelu", "gemv"):
             act = "gelu_tanh" if a.kernel == "gemm_gelu" else None
             if a.time and a.kernel != "gemv":
                 # time the GEMM alone on pre-quantised activations
@@ -88,7 +98,7 @@ def main():
         t = sorted(times)[len(times) // 2]
         ops = 2.0 * a.m * a.n * a.k
         msg += f" median_ms={t:.4f}"
-        if a.kernel != "quantize":
+        if a.kernel not in ("quantize", "convrot"):
             msg += f" TOPS={ops / t / 1e9:.1f}"
         else:
             msg += f" GB/s={(a.m * a.k * 3 + 4 * a.m) / t / 1e6:.1f}"

@@ -114,6 +114,28 @@ int w8a8_quantize_rowwise(const void* x, int x_dtype, int64_t rows, int64_t cols
                           int8_t* q, int64_t ldq, float* scale, int scale_mode, int stochastic,
                           uint64_t seed, void* stream);
 
+/* ---- a2 / a6: input activation + ConvRot fused into the quantiser ---------
+ * Replaces `quantize_int8_rowwise_convrot64(x, q, s, group, stochastic,
+ * act_code, seed, act_w, eps, stream)` (call site inference/src/convrot.rs:
+ * 156-209, chosen by inference/src/cuda_linear.rs:400-417, 586-589; kernel
+ * native/comfy-port/kitchen/int8_linear.cu:1197-1314).  group 256: the row is
+ * activated and rotated by the normalised 256-point Hadamard matrix in fp32,
+ * then quantised (the reference kernel's numerics).  group 0: activation
+ * only, rounded to the input dtype the way the reference's ATen activation
+ * (inference/src/int8_linear.rs:37-97) rounds it, then quantised.  cols is
+ * the quantised width K (a multiple of 256, at most 16384); SwiGLU and SiTU
+ * read [gate | up] rows 2*K wide.  act_w [K] (input dtype) is required for
+ * RMSNorm.  Stochastic rounding is not offered on this path. */
+#define W8A8_INPUT_ACT_NONE 0
+#define W8A8_INPUT_ACT_GELU_TANH 1
+#define W8A8_INPUT_ACT_SWIGLU 2
+#define W8A8_INPUT_ACT_RMS_NORM 3
+#define W8A8_INPUT_ACT_SITU 4
+int w8a8_quantize_rowwise_convrot(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                                  int64_t ldx, int group, int input_act, const void* act_w,
+                                  float act_eps, int8_t* q, int64_t ldq, float* scale,
+                                  int scale_mode, void* stream);
+
 /* ---- row-parallel (K-sharded) quantisation --------------------------------
  * No reference counterpart: the reference runs on one GPU.  A K-sharded
  * activation needs the absmax of the whole row before any shard can be

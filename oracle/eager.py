@@ -121,6 +121,11 @@ def apply_input(x: torch.Tensor, act: str | None, weight=None, eps=None) -> torc
     if act == "swiglu":
         gate, up = x.chunk(2, dim=-1)
         return torch.nn.functional.silu(gate).mul_(up)
+    if act == "situ":
+        # inference/src/int8_linear.rs:54-74: 25 tanh(a/25) * (4 tanh(b/4) * sigmoid(b))
+        a, b = x.chunk(2, dim=-1)
+        gated = torch.tanh(b / 4.0).mul_(4.0).mul_(torch.sigmoid(b))
+        return torch.tanh(a / 25.0).mul_(25.0).mul_(gated)
     if act == "rms_norm":
         if weight is None:
             raise ValueError("input_act 'rms_norm' requires act_weight")

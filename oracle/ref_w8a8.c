@@ -9,6 +9,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 static float bf16_to_f(uint16_t b) {
@@ -161,4 +162,98 @@ void ref_quantize_mxfp8_bf16(const uint16_t* x, int64_t rows, int64_t cols, uint
       const int64_t blk = (r / 128) * ncb + kb / 4;
       sf[blk * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (kb % 4)] = (uint8_t)e;
     }
+}
+
+/* ---- fused input activation + ConvRot quantiser --------------------------
+ * Follows native/comfy-port/kitchen/int8_linear.cu:1197-1314
+ * (quantize_int8_rowwise_convrot64_kernel), its FHT stages :881-934 and
+ * butterfly rows :253-261, its activations :1175-1200 and :1239-1267, and the
+ * element step quant_div_float_to_float :53-57.  x holds the fp32 values of
+ * the input elements; dtype is the input dtype code (0 f32, 1 f16, 2 bf16),
+ * which sets every rounding to "T".  rotate = 0 restates the unfused
+ * sequence instead: the ATen activation of inference/src/int8_linear.rs:37-97
+ * (each op rounded to T) followed by the row quantiser. */
+static float round_t(float v, int dtype) {
+  if (dtype == 2) return round_bf16(v);
+  if (dtype == 1) return (float)(_Float16)v;
+  return v;
+}
+
+/* in-place normalised 256-point Hadamard transform of one group: digit
+ * strides 1, 4, 16, 64, each output 0.5 * (sum left to right) */
+void ref_fht256(float* v) {
+  float t[256];
+  for (int s = 1; s <= 64; s *= 4) {
+    for (int i = 0; i < 256; ++i) {
+      const int d = (i / s) & 3, base = i - d * s;
+      const float x0 = v[base], x1 = v[base + s], x2 = v[base + 2 * s], x3 = v[base + 3 * s];
+      float y;
+      switch (d) {
+        case 0: y = x0 + x1 + x2 - x3; break;
+        case 1: y = x0 + x1 - x2 + x3; break;
+        case 2: y = x0 - x1 + x2 + x3; break;
+        default: y = -x0 + x1 + x2 + x3; break;
+      }
+      t[i] = 0.5f * y;
+    }
+    memcpy(v, t, sizeof(t));
+  }
+}
+
+static float act_one(int act, int rot, int dtype, float g, float u) {
+  /* rot: fp32 throughout (the fused kernel); else each ATen op rounds to T */
+#define RT(v) (rot ? (v) : round_t((v), dtype))
+  switch (act) {
+    case 1: return RT(0.5f * g * (1.0f + tanhf(0.7978845608028654f * (g + 0.044715f * g * g * g))));
+    case 2: return RT(RT(g / (1.0f + expf(-g))) * u);
+    case 4: {
+      const float a = RT(25.0f * RT(tanhf(RT(g / 25.0f))));
+      const float t4 = RT(4.0f * RT(tanhf(RT(u / 4.0f))));
+      const float gated = RT(t4 * RT(1.0f / (1.0f + expf(-u))));
+      return RT(a * gated);
+    }
+    default: return g;
+  }
+#undef RT
+}
+
+void ref_quantize_act_rot(const float* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
+                          int rotate, int act, const float* act_w, float eps, int kitchen,
+                          int8_t* q, float* scale) {
+  const float finite = dtype == 2 ? 3.3895313892515355e38f : dtype == 1 ? 65504.0f : 3.4028234663852886e38f;
+  const float tiny = dtype == 1 ? 6.103515625e-05f : 1.1754943508222875e-38f;
+  float* v = (float*)malloc(sizeof(float) * (size_t)k);
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * ldx;
+    if (act == 3) {
+      float ss = 0.0f;
+      for (int64_t c = 0; c < k; ++c) ss += xr[c] * xr[c];
+      const float rstd = 1.0f / sqrtf(ss / (float)k + eps);
+      for (int64_t c = 0; c < k; ++c) {
+        const float t = xr[c] * rstd * act_w[c];
+        v[c] = rotate ? t : round_t(t, dtype);
+      }
+    } else {
+      for (int64_t c = 0; c < k; ++c) v[c] = act_one(act, rotate, dtype, xr[c], (act == 2 || act == 4) ? xr[k + c] : 0.0f);
+    }
+    if (rotate) for (int64_t g = 0; g < k / 256; ++g) ref_fht256(v + g * 256);
+    float amax = 0.0f;
+    for (int64_t c = 0; c < k; ++c) amax = fmaxf(amax, fabsf(v[c]));
+    float s;
+    if (kitchen) {
+      s = fmaxf(fminf(amax, finite) * (1.0f / 127.0f), 1.0e-30f);
+    } else {
+      s = fmaxf(round_t(amax, dtype) / 127.0f, 1.0e-30f);
+    }
+    scale[r] = s;
+    float d = round_t(s, dtype);
+    if (d == 0.0f) d = tiny;
+    for (int64_t c = 0; c < k; ++c) {
+      float t = rintf(round_t(round_t(v[c], dtype) / d, dtype));
+      if (t < -128.0f) t = -128.0f;
+      if (t > 127.0f) t = 127.0f;
+      q[r * k + c] = (int8_t)t;
+    }
+  }
+  free(v);
 }

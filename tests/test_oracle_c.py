@@ -80,3 +80,60 @@ def test_c_fp8_and_mxfp8_golden(ref):
         ref.ref_quantize_mxfp8_bf16(_p(x), m, k, _p(q), _p(sf))
         assert np.array_equal(q.numpy().reshape(-1), ke[name + "/q"].reshape(-1)), name
         assert np.array_equal(sf.numpy(), ke[name + "/sf"].reshape(-1)), name
+
+
+def test_c_fht_is_the_normalised_hadamard():
+    """The C FHT (the reference kernel's radix-4 butterfly order) computes
+    x . H_256 of inference/src/int8_utils.rs:21-58."""
+    from tests import _cref
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(4, 512, generator=g)
+    got = _cref.fht256(x).double()
+    h = O.hadamard(256, torch.float64)
+    want = (x.double().reshape(4, 2, 256) @ h).reshape(4, 512)
+    assert (got - want).abs().max().item() < 1e-5
+
+
+def _golden_linear_kwargs(ke, name, dt):
+    kw = {}
+    k = ke[name + "/wq"].shape[1]
+    x = G.tensor(ke[name + "/x"], dt)
+    if "input_act" in name:
+        if name + "/act_w" in ke:
+            kw.update(act="rms_norm", act_w=G.tensor(ke[name + "/act_w"], dt), eps=1e-6)
+        elif x.shape[1] == 2 * k:
+            kw.update(act="swiglu")
+        else:
+            kw.update(act="gelu_tanh")
+    return x, kw
+
+
+@pytest.mark.parametrize("name", [n for n in G.manifest()["kitchen_eager"] if n.startswith("linear/")
+                                  and ("input_act" in n or "convrot" in n)])
+def test_c_fused_quantiser_against_golden_linear(name):
+    """The fused-quantiser restatement, completed with the exact int32 GEMM and
+    the eager dequant, lands within the tolerance bar (1% of output RMS) of
+    the reference's golden linear outputs for its input-activation and
+    ConvRot cases."""
+    from tests import _cref
+    ke = G.load("kitchen_eager")
+    dn = [p for p in name.split("_") if p in G.DT][0]
+    dt = G.DT[dn]
+    x, kw = _golden_linear_kwargs(ke, name, dt)
+    q, s = _cref.quantize_act_rot(x, "convrot" in name, kitchen=False, **kw)
+    wq = G.tensor(ke[name + "/wq"], torch.int8)
+    ws = G.tensor(ke[name + "/ws"], torch.float32)
+    b = G.tensor(ke[name + "/bias"], dt) if name + "/bias" in ke else None
+    y = O.dequant_eager(O.int8_accumulate(q, wq), s, ws, b, dt).float()
+    ref = G.tensor(ke[name + "/y"], dt).float()
+    rms = ref.pow(2).mean().sqrt().item()
+    assert (y - ref).abs().max().item() <= 0.01 * rms + 2 ** -7 * ref.abs().max().item()
+
+
+def test_c_act_only_none_equals_eager_quantiser():
+    from tests import _cref
+    g = torch.Generator().manual_seed(12)
+    x = (torch.randn(9, 512, generator=g) * 2).to(torch.bfloat16)
+    q, s = _cref.quantize_act_rot(x, False, kitchen=False)
+    qo, so = O.quantize_int8_rowwise(x)
+    assert torch.equal(q, qo) and torch.equal(s, so.reshape(-1))
