@@ -14,6 +14,10 @@ _OPS = (
     "int8_linear",
     "quantize_int8_rowwise",
     "quantize_int8_rowwise_convrot",
+    "quantize_int8_rowwise_modulated",
+    "int8_linear_modulated",
+    "int8_linear_rms_modulated",
+    "adaln_int8_linear",
     "quantize_per_tensor_fp8",
     "quantize_weight",
     "row_absmax",

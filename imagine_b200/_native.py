@@ -69,9 +69,15 @@ SIGNATURES = {
     "w8a8_quantize_rowwise": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _i32, _i32, _u64, _vp]),
     "w8a8_quantize_rowwise_convrot": (_i32, [_vp, _i32, _i64, _i64, _i64, _i32, _i32, _vp,
                                              ctypes.c_float, _vp, _i64, _vp, _i32, _vp]),
+    "w8a8_quantize_rowwise_modulated": (_i32, [_vp, _i32, _i64, _i64, _i64, _i32, _vp,
+                                               ctypes.c_float, _vp, _vp, _i64, _i32, _vp, _i64,
+                                               _vp, _i32, _vp]),
     "w8a8_row_absmax": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp]),
     "w8a8_quantize_rowwise_given_absmax": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp]),
     "w8a8_gemm_dequant": (_i32, [_vp, _i64, _vp, _i64, _vp, _EP, _vp, _i32, _i64, _i64, _i64, _i64, _CFG, _vp]),
+    "w8a8_gemm_splitk_workspace_bytes": (_i64, [_i64, _i64]),
+    "w8a8_gemm_dequant_splitk": (_i32, [_vp, _i64, _vp, _i64, _vp, _EP, _vp, _i32, _i64, _i64, _i64,
+                                        _i64, _i32, _vp, _i64, _CFG, _vp]),
     "w8a8_gemm_s32": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _CFG, _vp]),
     "w8a8_dequantize_linear": (_i32, [_vp, _vp, _EP, _vp, _i32, _i64, _i64, _vp]),
     "w8a8_gemv_dequant": (_i32, [_vp, _vp, _vp, _EP, _vp, _i32, _i64, _i64, _i64, _vp]),

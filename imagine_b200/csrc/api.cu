@@ -162,8 +162,44 @@ int w8a8_quantize_rowwise_convrot(const void* x, int x_dtype, int64_t rows, int6
   if (!x || !q || !scale) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
   if (ldx < in_cols || ldq < cols) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
   return finish(quantize_act_rot_launch(x, x_dtype, rows, cols, ldx, group == 256 ? 1 : 0,
-                                        input_act, act_w, act_eps, q, ldq, scale, scale_mode,
-                                        static_cast<cudaStream_t>(stream)));
+                                        input_act, act_w, act_eps, nullptr, nullptr, 1, q, ldq,
+                                        scale, scale_mode, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_quantize_rowwise_modulated(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                                    int64_t ldx, int mode, const void* norm_w, float eps,
+                                    const void* mod_scale, const void* mod_shift,
+                                    int64_t mod_group, int group, int8_t* q, int64_t ldq,
+                                    float* scale, int scale_mode, void* stream) {
+  if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
+  if (scale_mode != W8A8_SCALE_EAGER && scale_mode != W8A8_SCALE_KITCHEN) {
+    return fail(W8A8_ERR_VALUE, "unknown scale mode %d", scale_mode);
+  }
+  if (mode < W8A8_MOD_SCALE || mode > W8A8_MOD_RMS_ADALN) {
+    return fail(W8A8_ERR_VALUE, "unknown modulation mode %d", mode);
+  }
+  if (group != 0 && group != 256) {
+    return fail(W8A8_ERR_VALUE, "fused ConvRot quantiser supports group 256 (or 0: no rotation), got %d",
+                group);
+  }
+  if (cols == 0 || cols % 256 != 0 || cols > 16384) {
+    return fail(W8A8_ERR_VALUE, "fused quantiser needs K a multiple of 256 in [256, 16384], got %lld",
+                static_cast<long long>(cols));
+  }
+  if (mod_group < 1) return fail(W8A8_ERR_VALUE, "modulation group must be >= 1");
+  if (!mod_scale) return fail(W8A8_ERR_VALUE, "modulation scale pointer is NULL");
+  if ((mode == W8A8_MOD_ADALN || mode == W8A8_MOD_RMS_ADALN) && !mod_shift) {
+    return fail(W8A8_ERR_VALUE, "modulation shift pointer is NULL");
+  }
+  if (mode == W8A8_MOD_RMS_SCALE && !norm_w) return fail(W8A8_ERR_VALUE, "norm weight pointer is NULL");
+  if (rows == 0) return finish(0);
+  if (rows > 0x7fffffffLL) return fail(W8A8_ERR_VALUE, "rows must be <= INT_MAX");
+  if (!x || !q || !scale) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldx < cols || ldq < cols) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  return finish(quantize_act_rot_launch(x, x_dtype, rows, cols, ldx, group == 256 ? 1 : 0, mode + 5,
+                                        norm_w, eps, mod_scale, mod_shift, mod_group, q, ldq, scale,
+                                        scale_mode, static_cast<cudaStream_t>(stream)));
 }
 
 int w8a8_row_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
@@ -222,6 +258,45 @@ int w8a8_gemm_dequant(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw
   g.N = N;
   g.K = K;
   g.cfg = cfg;
+  return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
+int64_t w8a8_gemm_splitk_workspace_bytes(int64_t M, int64_t N) {
+  if (M < 0 || N < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  return splitk_workspace_bytes(M, N);
+}
+
+int w8a8_gemm_dequant_splitk(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,
+                             const float* xs, const w8a8_epilogue_t* epi, void* out, int out_dtype,
+                             int64_t ldo, int64_t M, int64_t N, int64_t K, int split_k,
+                             void* workspace, int64_t workspace_bytes,
+                             const w8a8_gemm_config_t* cfg, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (split_k < 0) return fail(W8A8_ERR_VALUE, "split_k must be >= 0, got %d", split_k);
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (M == 0 || N == 0) return finish(0);
+  if ((K > 0 && (!q || !w)) || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldq < K || ldw < K || ldo < N) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  if (split_k != 1 && !workspace) return fail(W8A8_ERR_VALUE, "split-K needs a scratch buffer");
+  GemmArgs g{};
+  g.kind = 0;
+  g.a = q;
+  g.lda = ldq;
+  g.b = w;
+  g.ldb = ldw;
+  g.xs = xs;
+  g.epi = epi;
+  g.out = out;
+  g.out_dtype = out_dtype;
+  g.ldo = ldo;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.cfg = cfg;
+  g.split_k = split_k;
+  g.workspace = workspace;
+  g.workspace_bytes = workspace_bytes;
   return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
 }
 

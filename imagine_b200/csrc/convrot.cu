@@ -8,7 +8,7 @@
 // then quantise" sequence for an input activation without ConvRot
 // (inference/src/int8_linear.rs:37-97 followed by the row quantiser).
 //
-// Numerics with ROT (the reference's fused kernel):
+// Numerics with ROT and kitchen scales (the reference's fused kernel):
 //   v   = act(x) in fp32 (GELU-tanh, SwiGLU = silu(gate) * up, RMSNorm =
 //         x * rsqrt(mean(x^2) + eps) * w, or SiTU), no rounding
 //   v   = H_256 v per 256-group: four radix-4 stages (digit strides 1, 4, 16,
@@ -17,16 +17,20 @@
 //   s   = max(min(amax_fp32, finite_max(T)) * (1/127), 1e-30)     (kitchen)
 //         max(T(amax_fp32) / 127, 1e-30)                          (eager)
 //   q   = clamp(rne(T(T(v) / T(s))), -128, 127)      (int8_linear.cu:53-57)
-// Without ROT the activation output is rounded to T after each op the ATen
-// sequence rounds after, then quantised like the plain row quantiser.
+// With eager scales, and always without ROT, the activation output is rounded
+// to T after each op the reference's ATen sequence rounds after (its eager
+// route: ATen activation, T-typed Hadamard matmul, row quantiser); the
+// rotation itself is the same fp32 butterfly.
 //
-// Layout: one CTA per row; a team of 16 threads owns one 256-group at a time,
-// each thread 16 elements.  Stages 1 and 4 run on 16 contiguous elements in
-// registers (e = 16 r + j); the team transposes through a bank-conflict-free
-// swizzled shared buffer to e = r + 16 j for stages 16 and 64; the int8 codes
-// go back through shared memory as bytes so every thread stores 16 contiguous
-// bytes.  A thread keeps GPT groups in registers (K <= 16 teams x GPT x 256),
-// so x is read from HBM exactly once.
+// Layout: one CTA per row; a team of 16 threads owns two 256-groups of the
+// row at a time, each thread element 16 r + j (j < 16) of both, held as
+// packed fp32 pairs so every f32x2 add / mul serves the two groups.  Stages 1
+// and 4 of the transform run in registers; the team transposes the pairs
+// through an XOR-swizzled (bank-conflict-free) shared buffer to element
+// r + 16 j for stages 16 and 64.  Codes go back through shared memory as
+// bytes so every thread stores 16 contiguous bytes per group.  A thread keeps
+// up to two group pairs in registers (K <= 16 teams x 4 x 256), so x is read
+// from HBM exactly once.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -42,9 +46,28 @@ namespace {
 constexpr int kGroup = 256;
 constexpr int kTeam = 16;          // threads per group
 constexpr int kMaxTeams = 16;      // 256 threads per CTA
-constexpr int kTeamFloats = kGroup + 16;  // padded: teams of one warp use disjoint banks
 
-enum InputAct : int { kInNone = 0, kInGeluTanh = 1, kInSwiGLU = 2, kInRmsNorm = 3, kInSiTU = 4 };
+// 0-4: the reference's input activations (input_act_codes.h, plus SiTU);
+// 5-8: modulations applied before the linear (W8A8_MOD_* + 5).
+enum InputAct : int {
+  kInNone = 0,
+  kInGeluTanh = 1,
+  kInSwiGLU = 2,
+  kInRmsNorm = 3,
+  kInSiTU = 4,
+  kInModScale = 5,     // x * (1 + s)
+  kInRmsModScale = 6,  // rms_norm(x, w) * (1 + s)
+  kInAdaLN = 7,        // layer_norm(x) * (1 + s) + shift
+  kInRmsAdaLN = 8,     // rms_norm(x) * (1 + s) + shift
+};
+
+// Modulation rows: scale / shift [rows / group, K] in the input dtype; x row
+// i takes modulation row i / group.
+struct ModArgs {
+  const void* scale;
+  const void* shift;
+  int64_t group;
+};
 
 template <typename T>
 struct Ld;
@@ -119,14 +142,10 @@ __device__ __forceinline__ void load16(const void* p, int64_t i, bool vec, float
   }
 }
 
-// Round to T when the ATen sequence would (ROUND), otherwise keep fp32.
-template <typename T, bool ROUND>
-__device__ __forceinline__ float rt(float v) {
-  if constexpr (ROUND) {
-    return QuantTraits<T>::round_t(v);
-  } else {
-    return v;
-  }
+// Round to T when the ATen sequence would (round), otherwise keep fp32.
+template <typename T>
+__device__ __forceinline__ float rt(float v, bool round) {
+  return round ? QuantTraits<T>::round_t(v) : v;
 }
 
 // GELU-tanh: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
@@ -141,39 +160,80 @@ __device__ __forceinline__ float in_silu(float g) { return g / (1.0f + expf(-g))
 
 __device__ __forceinline__ float in_sigmoid(float g) { return 1.0f / (1.0f + expf(-g)); }
 
-// One radix-4 butterfly of the normalised H4 (rows ++ +-, ++-+, +-++, -+++),
-// every sum left to right exactly as int8_linear.cu:253-261 orders it;
-// (-a) + b is computed as b - a, which rounds identically.
-__device__ __forceinline__ void h4(float& a, float& b, float& c, float& d) {
-  const float ab = __fadd_rn(a, b);
-  const float amb = __fsub_rn(a, b);
-  const float bma = __fsub_rn(b, a);
-  const float y0 = __fsub_rn(__fadd_rn(ab, c), d);
-  const float y1 = __fadd_rn(__fsub_rn(ab, c), d);
-  const float y2 = __fadd_rn(__fadd_rn(amb, c), d);
-  const float y3 = __fadd_rn(__fadd_rn(bma, c), d);
-  a = __fmul_rn(0.5f, y0);
-  b = __fmul_rn(0.5f, y1);
-  c = __fmul_rn(0.5f, y2);
-  d = __fmul_rn(0.5f, y3);
+// ---- packed pairs: element j of two 256-groups of the row in one 64-bit
+// register pair, so every f32x2 instruction serves both groups.
+__device__ __forceinline__ uint64_t pk(float a, float b) {
+  return static_cast<uint64_t>(__float_as_uint(a)) | (static_cast<uint64_t>(__float_as_uint(b)) << 32);
+}
+__device__ __forceinline__ float lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
 }
 
-// 16 codes (values already T-representable) -> 16 bytes.
+// One radix-4 butterfly of the normalised H4 (rows ++ +-, ++-+, +-++, -+++),
+// every sum left to right exactly as int8_linear.cu:253-261 orders it;
+// (-a) + b is computed as b - a, which rounds identically.  Packed: two
+// independent butterflies per call.
+__device__ __forceinline__ void h4x2(uint64_t& a, uint64_t& b, uint64_t& c, uint64_t& d) {
+  const uint64_t half = pk(0.5f, 0.5f);
+  const uint64_t ab = add2(a, b);
+  const uint64_t amb = sub2(a, b);
+  const uint64_t bma = sub2(b, a);
+  const uint64_t y0 = sub2(add2(ab, c), d);
+  const uint64_t y1 = add2(sub2(ab, c), d);
+  const uint64_t y2 = add2(add2(amb, c), d);
+  const uint64_t y3 = add2(add2(bma, c), d);
+  a = mul2(half, y0);
+  b = mul2(half, y1);
+  c = mul2(half, y2);
+  d = mul2(half, y3);
+}
+
+// Codes of a pair of values (their low bytes are the int8 codes, two's
+// complement): clamp(rne(T(T(v) / div)), -128, 127).
 template <typename T>
-__device__ __forceinline__ uint4 quant16(const float* v, float div, float recip) {
-  int q[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) q[j] = quant_code<T>(v[j], div, recip);
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t t;
-    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, 0;" : "=r"(t) : "r"(q[4 * i + 3]), "r"(q[4 * i + 2]));
-    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;"
-        : "=r"(w[i])
-        : "r"(q[4 * i + 1]), "r"(q[4 * i]), "r"(t));
+__device__ __forceinline__ void quant_pair(uint64_t p, float div, float recip, uint32_t& c0,
+                                           uint32_t& c1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    // paired RN conversions; exact quotients by one packed FMA correction
+    // (div_exact_short); rne by adding 1.5 * 2^23
+    uint32_t b;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(b) : "f"(hi(p)), "f"(lo(p)));
+    const uint64_t xv = pk(__uint_as_float(b << 16), __uint_as_float(b & 0xFFFF0000u));
+    const uint64_t r2 = pk(recip, recip);
+    const uint64_t y0 = mul2(xv, r2);
+    const uint64_t e = fma2(y0, pk(-div, -div), xv);
+    const uint64_t y = fma2(e, r2, y0);
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(b) : "f"(hi(y)), "f"(lo(y)));
+    // |quotient| <= 127.75, so only the upper end needs a clamp (-127.75
+    // rounds to -128)
+    const float q0 = fminf(__uint_as_float(b << 16), 127.0f);
+    const float q1 = fminf(__uint_as_float(b & 0xFFFF0000u), 127.0f);
+    const uint64_t t = add2(pk(q0, q1), pk(12582912.0f, 12582912.0f));
+    c0 = __float_as_uint(lo(t));
+    c1 = __float_as_uint(hi(t));
+  } else {
+    c0 = static_cast<uint32_t>(quant_code<T>(QuantTraits<T>::round_t(lo(p)), div, recip));
+    c1 = static_cast<uint32_t>(quant_code<T>(QuantTraits<T>::round_t(hi(p)), div, recip));
   }
-  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 template <int NW>
@@ -195,13 +255,22 @@ __device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) 
   return r;
 }
 
-// GPT: 256-groups per team kept in registers.
-template <typename T, int ACT, bool ROT, int GPT>
+// Shared memory of one team: the FHT transpose buffer (16 threads x 16
+// packed pairs, 128 B per thread, chunks XOR-swizzled) and the code bytes of
+// its two groups (272 B each: teams of one warp land on different banks).
+constexpr int kTransBytes = kTeam * 16 * 8;
+constexpr int kCodeStride = kGroup + 16;
+constexpr int kTeamBytes = kTransBytes + 2 * kCodeStride;
+static_assert(kTeamBytes % 16 == 0, "team buffers must keep 16-byte alignment");
+
+// PPT: group pairs per team kept in registers.  Team t owns group pairs
+// (2 (t + i teams), 2 (t + i teams) + 1), i < PPT.
+template <typename T, int ACT, bool ROT, int PPT>
 __global__ void __launch_bounds__(kMaxTeams * kTeam) quantize_act_rot_kernel(
     const void* __restrict__ x, int64_t ldx, const void* __restrict__ act_w, float act_eps,
-    int8_t* __restrict__ q, int64_t ldq, float* __restrict__ scales, int K, int kitchen_mode,
-    int vec_in, int vec_out) {
-  __shared__ __align__(16) float xbuf[kMaxTeams * kTeamFloats];
+    ModArgs mod, int8_t* __restrict__ q, int64_t ldq, float* __restrict__ scales, int K,
+    int kitchen_mode, int vec_in, int vec_out) {
+  extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ float red[8];
   const int row = blockIdx.x;
   const int team = threadIdx.x / kTeam;
@@ -209,48 +278,63 @@ __global__ void __launch_bounds__(kMaxTeams * kTeam) quantize_act_rot_kernel(
   const int teams = blockDim.x / kTeam;
   const int G = K / kGroup;
   const int64_t xrow = static_cast<int64_t>(row) * ldx;
-  float* tb = xbuf + team * kTeamFloats;
-  // Without ROT the values are T-rounded at each step the ATen sequence rounds.
-  constexpr bool kRound = !ROT;
+  uint8_t* tbuf = dsm + team * kTeamBytes;
+  uint8_t* cbuf = tbuf + kTransBytes;
+  // The activation is T-rounded at each step the ATen sequence rounds, except
+  // for the kitchen numerics of the fused ConvRot kernel (fp32 throughout).
+  const bool kRound = !ROT || !kitchen_mode;
 
-  float v[GPT][16];
+  // v[i][h][j]: element 16 r + j of group 2 (team + i teams) + h
+  float v[PPT][2][16];
+  float sumsq = 0.0f, sum = 0.0f;
   // ---- load (+ elementwise activation)
-  float sumsq = 0.0f;
 #pragma unroll
-  for (int i = 0; i < GPT; ++i) {
-    const int g = team + i * teams;
-    const int col = g * kGroup + kTeam * r;
-    if (g < G) {
-      if constexpr (ACT == kInSwiGLU || ACT == kInSiTU) {
-        float gate[16], up[16];
-        load16<T>(x, xrow + col, vec_in, gate);
-        load16<T>(x, xrow + K + col, vec_in, up);
+  for (int i = 0; i < PPT; ++i) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if constexpr (ACT == kInSwiGLU) {
-            v[i][j] = rt<T, kRound>(rt<T, kRound>(in_silu(gate[j])) * up[j]);
-          } else {
-            // 25 tanh(a / 25) * (4 tanh(b / 4) * sigmoid(b))
-            // (inference/src/int8_linear.rs:54-74)
-            const float a = rt<T, kRound>(25.0f * rt<T, kRound>(tanhf(rt<T, kRound>(gate[j] / 25.0f))));
-            const float t4 = rt<T, kRound>(4.0f * rt<T, kRound>(tanhf(rt<T, kRound>(up[j] / 4.0f))));
-            const float gated = rt<T, kRound>(t4 * rt<T, kRound>(in_sigmoid(up[j])));
-            v[i][j] = rt<T, kRound>(a * gated);
+    for (int h = 0; h < 2; ++h) {
+      const int g = 2 * (team + i * teams) + h;
+      const int col = g * kGroup + kTeam * r;
+      float* f = v[i][h];
+      if (g < G) {
+        if constexpr (ACT == kInSwiGLU || ACT == kInSiTU) {
+          float gate[16], up[16];
+          load16<T>(x, xrow + col, vec_in, gate);
+          load16<T>(x, xrow + K + col, vec_in, up);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if constexpr (ACT == kInSwiGLU) {
+              f[j] = rt<T>(rt<T>(in_silu(gate[j]), kRound) * up[j], kRound);
+            } else {
+              // 25 tanh(a / 25) * (4 tanh(b / 4) * sigmoid(b))
+              // (inference/src/int8_linear.rs:54-74)
+              const float a =
+                  rt<T>(25.0f * rt<T>(tanhf(rt<T>(gate[j] / 25.0f, kRound)), kRound), kRound);
+              const float t4 =
+                  rt<T>(4.0f * rt<T>(tanhf(rt<T>(up[j] / 4.0f, kRound)), kRound), kRound);
+              const float gated = rt<T>(t4 * rt<T>(in_sigmoid(up[j]), kRound), kRound);
+              f[j] = rt<T>(a * gated, kRound);
+            }
+          }
+        } else {
+          load16<T>(x, xrow + col, vec_in, f);
+          if constexpr (ACT == kInGeluTanh) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) f[j] = rt<T>(in_gelu_tanh(f[j]), kRound);
+          } else if constexpr (ACT == kInRmsNorm || ACT == kInRmsModScale || ACT == kInRmsAdaLN) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) sumsq = __fmaf_rn(f[j], f[j], sumsq);
+          } else if constexpr (ACT == kInAdaLN) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              sum = __fadd_rn(sum, f[j]);
+              sumsq = __fmaf_rn(f[j], f[j], sumsq);
+            }
           }
         }
       } else {
-        load16<T>(x, xrow + col, vec_in, v[i]);
-        if constexpr (ACT == kInGeluTanh) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[i][j] = rt<T, kRound>(in_gelu_tanh(v[i][j]));
-        } else if constexpr (ACT == kInRmsNorm) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) sumsq = __fmaf_rn(v[i][j], v[i][j], sumsq);
-        }
+        for (int j = 0; j < 16; ++j) f[j] = 0.0f;
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[i][j] = 0.0f;
     }
   }
   if constexpr (ACT == kInRmsNorm) {
@@ -259,55 +343,149 @@ __global__ void __launch_bounds__(kMaxTeams * kTeam) quantize_act_rot_kernel(
     const float ss = block_reduce<8>(sumsq, false, red);
     const float rstd = rsqrtf(ss / static_cast<float>(K) + act_eps);
 #pragma unroll
-    for (int i = 0; i < GPT; ++i) {
-      const int g = team + i * teams;
-      if (g < G) {
-        float w[16];
-        load16<T>(act_w, g * kGroup + kTeam * r, vec_in, w);
+    for (int i = 0; i < PPT; ++i) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[i][j] = rt<T, kRound>(__fmul_rn(__fmul_rn(v[i][j], rstd), w[j]));
+      for (int h = 0; h < 2; ++h) {
+        const int g = 2 * (team + i * teams) + h;
+        if (g < G) {
+          float w[16];
+          load16<T>(act_w, g * kGroup + kTeam * r, vec_in, w);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            v[i][h][j] = rt<T>(__fmul_rn(__fmul_rn(v[i][h][j], rstd), w[j]), kRound);
+          }
+        }
+      }
+    }
+  }
+  if constexpr (ACT >= kInModScale) {
+    // Modulation (the reference materialises its output in T, so the value
+    // is always rounded to T before quantising).
+    //   kitchen: the reference's CUDA adaln (KSRC backends/cuda/ops/adaln.cu:
+    //            103-190): one-pass mean / E[x^2] - mean^2 statistics,
+    //            (x - mean) * rstd * (1 + s) + shift in fp32, one rounding;
+    //   eager:   its ATen sequence (inference/src/backend_eager.rs:176-197,
+    //            inference/src/backend_bindings.rs:329-405): the normalised row
+    //            rounded to T, times T(1 + s) rounded, plus shift rounded.
+    float mean = 0.0f, rstd = 1.0f;
+    if constexpr (ACT == kInRmsModScale || ACT == kInRmsAdaLN) {
+      const float ss = block_reduce<8>(sumsq, false, red);
+      rstd = rsqrtf(ss / static_cast<float>(K) + act_eps);
+    } else if constexpr (ACT == kInAdaLN) {
+      const float inv_k = 1.0f / static_cast<float>(K);
+      const float s1 = block_reduce<8>(sum, false, red);
+      mean = s1 * inv_k;
+      if (kitchen_mode) {
+        const float s2 = block_reduce<8>(sumsq, false, red);
+        rstd = rsqrtf(fmaxf(s2 * inv_k - mean * mean, 0.0f) + act_eps);
+      } else {
+        // second pass over the registers: sum of squared deviations
+        float dev = 0.0f;
+#pragma unroll
+        for (int i = 0; i < PPT; ++i) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (2 * (team + i * teams) + h < G) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float d = __fsub_rn(v[i][h][j], mean);
+                dev = __fmaf_rn(d, d, dev);
+              }
+            }
+          }
+        }
+        const float s2 = block_reduce<8>(dev, false, red);
+        rstd = rsqrtf(s2 * inv_k + act_eps);
+      }
+    }
+    const int64_t mrow = (static_cast<int64_t>(row) / mod.group) * K;
+#pragma unroll
+    for (int i = 0; i < PPT; ++i) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int g = 2 * (team + i * teams) + h;
+        if (g < G) {
+          const int col = g * kGroup + kTeam * r;
+          float sc[16], sh[16], w[16];
+          load16<T>(mod.scale, mrow + col, vec_in, sc);
+          if constexpr (ACT == kInAdaLN || ACT == kInRmsAdaLN) load16<T>(mod.shift, mrow + col, vec_in, sh);
+          if constexpr (ACT == kInRmsModScale) load16<T>(act_w, col, vec_in, w);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float xv = v[i][h][j];
+            float y;
+            if constexpr (ACT == kInModScale) {
+              y = __fmul_rn(xv, QuantTraits<T>::round_t(__fadd_rn(1.0f, sc[j])));
+            } else if constexpr (ACT == kInRmsModScale) {
+              const float nrm = QuantTraits<T>::round_t(__fmul_rn(__fmul_rn(xv, rstd), w[j]));
+              y = __fmul_rn(nrm, QuantTraits<T>::round_t(__fadd_rn(1.0f, sc[j])));
+            } else {
+              const float nrm = __fmul_rn(__fsub_rn(xv, mean), rstd);
+              if (kitchen_mode) {
+                y = __fmaf_rn(nrm, __fadd_rn(1.0f, sc[j]), sh[j]);
+              } else {
+                const float t = QuantTraits<T>::round_t(__fmul_rn(
+                    QuantTraits<T>::round_t(nrm), QuantTraits<T>::round_t(__fadd_rn(1.0f, sc[j]))));
+                y = __fadd_rn(t, sh[j]);
+              }
+            }
+            v[i][h][j] = QuantTraits<T>::round_t(y);
+          }
+        }
       }
     }
   }
 
-  // ---- Hadamard transform per 256-group
+  // ---- Hadamard transform per 256-group (both groups of a pair at once)
   if constexpr (ROT) {
 #pragma unroll
-    for (int i = 0; i < GPT; ++i) {
-      // stride 1 and stride 4 on e = 16 r + j, j = d0 + 4 d1
+    for (int i = 0; i < PPT; ++i) {
+      uint64_t P[16];
 #pragma unroll
-      for (int d1 = 0; d1 < 4; ++d1) h4(v[i][4 * d1], v[i][4 * d1 + 1], v[i][4 * d1 + 2], v[i][4 * d1 + 3]);
+      for (int j = 0; j < 16; ++j) P[j] = pk(v[i][0][j], v[i][1][j]);
+      // strides 1 and 4 on e = 16 r + j, j = d0 + 4 d1
 #pragma unroll
-      for (int d0 = 0; d0 < 4; ++d0) h4(v[i][d0], v[i][d0 + 4], v[i][d0 + 8], v[i][d0 + 12]);
-      // transpose to e = r + 16 j: float4 chunk c of thread r is stored at
-      // chunk 4 r + (c ^ ((r >> 1) & 3)) of the team's buffer
+      for (int d1 = 0; d1 < 4; ++d1) h4x2(P[4 * d1], P[4 * d1 + 1], P[4 * d1 + 2], P[4 * d1 + 3]);
+#pragma unroll
+      for (int d0 = 0; d0 < 4; ++d0) h4x2(P[d0], P[d0 + 4], P[d0 + 8], P[d0 + 12]);
+      // transpose to e = r + 16 j: thread r's 16-byte chunk c (pairs 2c,
+      // 2c + 1) is stored at chunk c ^ (r & 7) of its 128-byte row
       __syncwarp();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int pc = 4 * r + (c ^ ((r >> 1) & 3));
-        *reinterpret_cast<float4*>(tb + 4 * pc) =
-            make_float4(v[i][4 * c], v[i][4 * c + 1], v[i][4 * c + 2], v[i][4 * c + 3]);
+      for (int c = 0; c < 8; ++c) {
+        *reinterpret_cast<uint4*>(tbuf + 128 * r + 16 * (c ^ (r & 7))) =
+            make_uint4(__float_as_uint(lo(P[2 * c])), __float_as_uint(hi(P[2 * c])),
+                       __float_as_uint(lo(P[2 * c + 1])), __float_as_uint(hi(P[2 * c + 1])));
       }
       __syncwarp();
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        // element r + 16 j was written by thread j as its chunk r >> 2, word r & 3
-        v[i][j] = tb[16 * j + 4 * ((r >> 2) ^ ((j >> 1) & 3)) + (r & 3)];
+        // element r + 16 j was written by thread j as pair r of its row
+        P[j] = *reinterpret_cast<const uint64_t*>(tbuf + 128 * j + 16 * ((r >> 1) ^ (j & 7)) +
+                                                  8 * (r & 1));
       }
-      // stride 16 and stride 64 on j = d2 + 4 d3
+      // strides 16 and 64 on j = d2 + 4 d3
 #pragma unroll
-      for (int d3 = 0; d3 < 4; ++d3) h4(v[i][4 * d3], v[i][4 * d3 + 1], v[i][4 * d3 + 2], v[i][4 * d3 + 3]);
+      for (int d3 = 0; d3 < 4; ++d3) h4x2(P[4 * d3], P[4 * d3 + 1], P[4 * d3 + 2], P[4 * d3 + 3]);
 #pragma unroll
-      for (int d2 = 0; d2 < 4; ++d2) h4(v[i][d2], v[i][d2 + 4], v[i][d2 + 8], v[i][d2 + 12]);
+      for (int d2 = 0; d2 < 4; ++d2) h4x2(P[d2], P[d2 + 4], P[d2 + 8], P[d2 + 12]);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        v[i][0][j] = lo(P[j]);
+        v[i][1][j] = hi(P[j]);
+      }
     }
   }
 
   // ---- row scale
   float amax = 0.0f;
 #pragma unroll
-  for (int i = 0; i < GPT; ++i) {
+  for (int i = 0; i < PPT; ++i) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[i][h][j]));
+    }
   }
   amax = block_reduce<8>(amax, true, red);
   // eager: the reference's rotated row is T-typed, so its absmax is T(amax)
@@ -316,61 +494,61 @@ __global__ void __launch_bounds__(kMaxTeams * kTeam) quantize_act_rot_kernel(
   const float div = quant_divisor<T>(s);
   const float recip = __frcp_rn(div);
 
-  // ---- codes
+  // ---- codes: bytes into the team's code buffer at the element's position,
+  // then 16 contiguous bytes per thread and group to global memory
   int8_t* qrow = q + static_cast<int64_t>(row) * ldq;
 #pragma unroll
-  for (int i = 0; i < GPT; ++i) {
-    const int g = team + i * teams;
-    float t[16];
+  for (int i = 0; i < PPT; ++i) {
+    __syncwarp();
 #pragma unroll
-    for (int j = 0; j < 16; ++j) t[j] = QuantTraits<T>::round_t(v[i][j]);
-    const uint4 c = quant16<T>(t, div, recip);
-    uint4 out = c;
-    if constexpr (ROT) {
-      // codes are for e = r + 16 j: bounce through shared memory as bytes
-      uint8_t* cb = reinterpret_cast<uint8_t*>(tb);
-      __syncwarp();
-      const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-      for (int j = 0; j < 16; ++j) cb[r + 16 * j] = static_cast<uint8_t>(w[j >> 2] >> (8 * (j & 3)));
-      __syncwarp();
-      out = *reinterpret_cast<const uint4*>(cb + 16 * r);
+    for (int j = 0; j < 16; ++j) {
+      uint32_t c0, c1;
+      quant_pair<T>(pk(v[i][0][j], v[i][1][j]), div, recip, c0, c1);
+      const int e = ROT ? r + 16 * j : 16 * r + j;
+      cbuf[e] = static_cast<uint8_t>(c0);
+      cbuf[kCodeStride + e] = static_cast<uint8_t>(c1);
     }
-    if (g < G) {
-      const int col = g * kGroup + kTeam * r;
-      if (vec_out) {
-        *reinterpret_cast<uint4*>(qrow + col) = out;
-      } else {
-        const uint32_t w[4] = {out.x, out.y, out.z, out.w};
+    __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) qrow[col + j] = static_cast<int8_t>(w[j >> 2] >> (8 * (j & 3)));
+    for (int h = 0; h < 2; ++h) {
+      const int g = 2 * (team + i * teams) + h;
+      if (g < G) {
+        const uint4 out = *reinterpret_cast<const uint4*>(cbuf + h * kCodeStride + 16 * r);
+        const int col = g * kGroup + kTeam * r;
+        if (vec_out) {
+          *reinterpret_cast<uint4*>(qrow + col) = out;
+        } else {
+          const uint32_t w[4] = {out.x, out.y, out.z, out.w};
+#pragma unroll
+          for (int j = 0; j < 16; ++j) qrow[col + j] = static_cast<int8_t>(w[j >> 2] >> (8 * (j & 3)));
+        }
       }
     }
   }
 }
 
 template <typename T, int ACT, bool ROT>
-int launch_act_rot(const void* x, int64_t ldx, const void* act_w, float eps, int8_t* q,
-                   int64_t ldq, float* scales, int64_t rows, int K, int kitchen_mode,
+int launch_act_rot(const void* x, int64_t ldx, const void* act_w, float eps, ModArgs mod,
+                   int8_t* q, int64_t ldq, float* scales, int64_t rows, int K, int kitchen_mode,
                    cudaStream_t stream) {
   const int G = K / kGroup;
-  const int gpt = (G + kMaxTeams - 1) / kMaxTeams;
-  const int teams = (G + gpt - 1) / gpt;
+  const int pairs = (G + 1) / 2;
+  const int ppt = (pairs + kMaxTeams - 1) / kMaxTeams;  // 1 or 2 for K <= 16384
+  const int teams = (pairs + ppt - 1) / ppt;
   const int threads = (teams * kTeam + 31) / 32 * 32;
+  const size_t smem = static_cast<size_t>(threads / kTeam) * kTeamBytes;
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  const int vec_in = a16(x) && (ldx % Ld<T>::kAlign) == 0 && (act_w == nullptr || a16(act_w));
+  const int vec_in = a16(x) && (ldx % Ld<T>::kAlign) == 0 && (act_w == nullptr || a16(act_w)) &&
+                     (mod.scale == nullptr || a16(mod.scale)) && (mod.shift == nullptr || a16(mod.shift));
   const int vec_out = a16(q) && (ldq % 16) == 0;
   const dim3 grid(static_cast<unsigned>(rows));
-#define W8A8_LAUNCH_GPT(N)                                                                        \
-  quantize_act_rot_kernel<T, ACT, ROT, N><<<grid, threads, 0, stream>>>(                           \
-      x, ldx, act_w, eps, q, ldq, scales, K, kitchen_mode, vec_in, vec_out)
-  switch (gpt) {
-    case 1: W8A8_LAUNCH_GPT(1); break;
-    case 2: W8A8_LAUNCH_GPT(2); break;
-    case 3: W8A8_LAUNCH_GPT(3); break;
-    default: W8A8_LAUNCH_GPT(4); break;
+  if (ppt == 1) {
+    quantize_act_rot_kernel<T, ACT, ROT, 1><<<grid, threads, smem, stream>>>(
+        x, ldx, act_w, eps, mod, q, ldq, scales, K, kitchen_mode, vec_in, vec_out);
+  } else {
+    quantize_act_rot_kernel<T, ACT, ROT, 2><<<grid, threads, smem, stream>>>(
+        x, ldx, act_w, eps, mod, q, ldq, scales, K, kitchen_mode, vec_in, vec_out);
   }
-#undef W8A8_LAUNCH_GPT
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error("ConvRot quantiser launch failed: %s", cudaGetErrorString(e));
@@ -380,16 +558,24 @@ int launch_act_rot(const void* x, int64_t ldx, const void* act_w, float eps, int
 }
 
 template <typename T, bool ROT>
-int by_act(int act, const void* x, int64_t ldx, const void* act_w, float eps, int8_t* q,
-           int64_t ldq, float* scales, int64_t rows, int K, int kitchen_mode, cudaStream_t stream) {
+int by_act(int act, const void* x, int64_t ldx, const void* act_w, float eps, ModArgs mod,
+           int8_t* q, int64_t ldq, float* scales, int64_t rows, int K, int kitchen_mode,
+           cudaStream_t stream) {
+#define W8A8_ACT_CASE(A) \
+  case A: return launch_act_rot<T, A, ROT>(x, ldx, act_w, eps, mod, q, ldq, scales, rows, K, kitchen_mode, stream)
   switch (act) {
-    case kInNone: return launch_act_rot<T, kInNone, ROT>(x, ldx, act_w, eps, q, ldq, scales, rows, K, kitchen_mode, stream);
-    case kInGeluTanh: return launch_act_rot<T, kInGeluTanh, ROT>(x, ldx, act_w, eps, q, ldq, scales, rows, K, kitchen_mode, stream);
-    case kInSwiGLU: return launch_act_rot<T, kInSwiGLU, ROT>(x, ldx, act_w, eps, q, ldq, scales, rows, K, kitchen_mode, stream);
-    case kInRmsNorm: return launch_act_rot<T, kInRmsNorm, ROT>(x, ldx, act_w, eps, q, ldq, scales, rows, K, kitchen_mode, stream);
-    case kInSiTU: return launch_act_rot<T, kInSiTU, ROT>(x, ldx, act_w, eps, q, ldq, scales, rows, K, kitchen_mode, stream);
+    W8A8_ACT_CASE(kInNone);
+    W8A8_ACT_CASE(kInGeluTanh);
+    W8A8_ACT_CASE(kInSwiGLU);
+    W8A8_ACT_CASE(kInRmsNorm);
+    W8A8_ACT_CASE(kInSiTU);
+    W8A8_ACT_CASE(kInModScale);
+    W8A8_ACT_CASE(kInRmsModScale);
+    W8A8_ACT_CASE(kInAdaLN);
+    W8A8_ACT_CASE(kInRmsAdaLN);
     default: break;
   }
+#undef W8A8_ACT_CASE
   set_error("unknown input activation code %d", act);
   return W8A8_ERR_VALUE;
 }
@@ -397,21 +583,24 @@ int by_act(int act, const void* x, int64_t ldx, const void* act_w, float eps, in
 }  // namespace
 
 int quantize_act_rot_launch(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
-                            int rotate, int act, const void* act_w, float act_eps, int8_t* q,
-                            int64_t ldq, float* scales, int scale_mode, cudaStream_t stream) {
+                            int rotate, int act, const void* act_w, float act_eps,
+                            const void* mod_scale, const void* mod_shift, int64_t mod_group,
+                            int8_t* q, int64_t ldq, float* scales, int scale_mode,
+                            cudaStream_t stream) {
   if (rows == 0) return 0;
   const int K = static_cast<int>(cols);
   const int km = scale_mode == W8A8_SCALE_KITCHEN ? 1 : 0;
+  const ModArgs mod{mod_scale, mod_shift, mod_group > 0 ? mod_group : 1};
   switch (x_dtype) {
     case W8A8_BF16:
-      return rotate ? by_act<__nv_bfloat16, true>(act, x, ldx, act_w, act_eps, q, ldq, scales, rows, K, km, stream)
-                    : by_act<__nv_bfloat16, false>(act, x, ldx, act_w, act_eps, q, ldq, scales, rows, K, km, stream);
+      return rotate ? by_act<__nv_bfloat16, true>(act, x, ldx, act_w, act_eps, mod, q, ldq, scales, rows, K, km, stream)
+                    : by_act<__nv_bfloat16, false>(act, x, ldx, act_w, act_eps, mod, q, ldq, scales, rows, K, km, stream);
     case W8A8_F16:
-      return rotate ? by_act<__half, true>(act, x, ldx, act_w, act_eps, q, ldq, scales, rows, K, km, stream)
-                    : by_act<__half, false>(act, x, ldx, act_w, act_eps, q, ldq, scales, rows, K, km, stream);
+      return rotate ? by_act<__half, true>(act, x, ldx, act_w, act_eps, mod, q, ldq, scales, rows, K, km, stream)
+                    : by_act<__half, false>(act, x, ldx, act_w, act_eps, mod, q, ldq, scales, rows, K, km, stream);
     case W8A8_F32:
-      return rotate ? by_act<float, true>(act, x, ldx, act_w, act_eps, q, ldq, scales, rows, K, km, stream)
-                    : by_act<float, false>(act, x, ldx, act_w, act_eps, q, ldq, scales, rows, K, km, stream);
+      return rotate ? by_act<float, true>(act, x, ldx, act_w, act_eps, mod, q, ldq, scales, rows, K, km, stream)
+                    : by_act<float, false>(act, x, ldx, act_w, act_eps, mod, q, ldq, scales, rows, K, km, stream);
     default: break;
   }
   set_error("unsupported input dtype code %d", x_dtype);

@@ -74,7 +74,7 @@ constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kThreads = (kEpiWarps + 2) * 32;
 constexpr int kMaxSmem = 232448;  // 227 KB opt-in per CTA on sm_100
 
-template <int BN, typename OutT, int CG = 1, int KIND = 0>
+template <int BN, typename OutT, int CG = 1, int KIND = 0, bool SPLIT = false>
 struct Cfg {
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = (BN / CG) * kBK;  // each CTA of a pair holds half of B
@@ -82,7 +82,8 @@ struct Cfg {
   // MXFP8: one 512-byte block of e8m0 scales for A and BN/128 for B per stage
   static constexpr int kSFBytes = KIND == 2 ? 512 * (1 + BN / 128) : 0;
   static constexpr int kSFCols = KIND == 2 ? 4 * (1 + BN / 128) : 0;  // TMEM columns per stage
-  static constexpr int kStageD = 32 * 32 * static_cast<int>(sizeof(OutT));  // one warp's tile
+  // one warp's staging tile; split-K also stages 32 x 32 int32 partials in it
+  static constexpr int kStageD = 32 * 32 * (SPLIT ? 4 : static_cast<int>(sizeof(OutT)));
   // per epilogue warp: one store staging tile + the fp32 weight scale and bias
   // of each of its column chunks for the current tile
   static constexpr int kChunksPerWarp = (BN / 32 + 1) / 2;
@@ -246,16 +247,131 @@ __device__ __forceinline__ void epi_pair(float a0, float a1, float xs_row, float
   }
 }
 
+// Split-K scratch: int32 [M, N] partial sums (row stride N) and one arrival
+// counter per (tile, epilogue warp); both all-zero between calls.
+struct SplitArgs {
+  int32_t* acc;
+  unsigned* cnt;
+  int splits;
+};
+
+// Dequant epilogue of one 32 x 32 chunk (lane = row) from its raw 32-bit
+// accumulators, staged in `st` and TMA-stored to (col0, row0) of the output.
+template <int KIND, typename OutT, int ORDER, int ACT>
+__device__ __forceinline__ void finish_chunk(const uint32_t (&cur)[32], const float* wsv,
+                                             const float* bv, float xs_row, bool has_bias,
+                                             bool has_resid, const EpilogueParams& ep, int grow,
+                                             int col0, int row0, int M, int N, uint8_t* st,
+                                             const CUtensorMap* tmD, int lane) {
+  constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
+  float y[32];
+  if constexpr (!kRaw) {
+    const float4* wsq = reinterpret_cast<const float4*>(wsv);
+    const float4* bq = reinterpret_cast<const float4*>(bv);
+#pragma unroll
+    for (int j4 = 0; j4 < 8; ++j4) {
+      const float4 w4 = wsq[j4];
+      const float4 b4 = bq[j4];
+      const int j = j4 * 4;
+      float a[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        a[t] = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(cur[j + t]))
+                           : __uint_as_float(cur[j + t]);
+      }
+      epi_pair<OutT, (KIND == 0 ? ORDER : kDqChained), ACT>(
+          a[0], a[1], xs_row, w4.x, w4.y, b4.x, b4.y, has_bias, y[j], y[j + 1]);
+      epi_pair<OutT, (KIND == 0 ? ORDER : kDqChained), ACT>(
+          a[2], a[3], xs_row, w4.z, w4.w, b4.z, b4.w, has_bias, y[j + 2], y[j + 3]);
+    }
+    if (has_resid) {
+      float rsv[32];
+      load_cols32<OutT>(ep.rscale, col0, N, ep.vec_rscale, rsv);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float res = (grow < M && col0 + j < N)
+                              ? OutTraits<OutT>::load(ep.residual,
+                                                      static_cast<int64_t>(grow) * ep.ldr + col0 + j)
+                              : 0.0f;
+        y[j] = round_out<OutT>(__fmaf_rn(y[j], rsv[j], res));
+      }
+    }
+  }
+  // single staging tile: the previous chunk's store was issued a whole chunk
+  // of arithmetic ago
+  if (lane == 0) tma_store_wait_read<0>();
+  __syncwarp();
+  if constexpr (sizeof(OutT) == 4) {
+    // 32 x 4-byte values = 8 chunks of 16 B; 128B swizzle: chunk ^= row & 7.
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {
+      uint4 v;
+      if constexpr (kRaw) {
+        v = make_uint4(cur[cc * 4], cur[cc * 4 + 1], cur[cc * 4 + 2], cur[cc * 4 + 3]);
+      } else {
+        v = make_uint4(__float_as_uint(y[cc * 4]), __float_as_uint(y[cc * 4 + 1]),
+                       __float_as_uint(y[cc * 4 + 2]), __float_as_uint(y[cc * 4 + 3]));
+      }
+      const int phys = cc ^ (lane & 7);
+      *reinterpret_cast<uint4*>(st + lane * 128 + phys * 16) = v;
+    }
+  } else {
+    // 32 x 2-byte values = 4 chunks of 16 B; 64B swizzle: chunk ^= (row >> 1) & 3.
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t w4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float lo = y[cc * 8 + e * 2];
+        const float hi = y[cc * 8 + e * 2 + 1];
+        if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+          // values are already exact bf16: take the high halves
+          w4[e] = __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+        } else {
+          w4[e] = pack2<OutT>(lo, hi);
+        }
+      }
+      const int phys = cc ^ ((lane >> 1) & 3);
+      *reinterpret_cast<uint4*>(st + lane * 64 + phys * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && row0 < M) {
+    tma_store_2d(tmD, st, col0, row0);
+    tma_store_commit();
+  }
+}
+
+// 32 x 32 raw 32-bit values (lane = row) into a 128B-swizzled staging tile.
+__device__ __forceinline__ void stage_raw32(uint8_t* st, const uint32_t (&cur)[32], int lane) {
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc) {
+    const uint4 v = make_uint4(cur[cc * 4], cur[cc * 4 + 1], cur[cc * 4 + 2], cur[cc * 4 + 3]);
+    *reinterpret_cast<uint4*>(st + lane * 128 + ((cc ^ (lane & 7)) * 16)) = v;
+  }
+}
+
 // CG = 1: one CTA computes a 128 x BN tile.  CG = 2: a cluster of two CTAs
 // computes a 256 x BN tile with 2-SM MMAs (the leader, cluster rank 0,
 // issues them); each CTA loads its own 128 rows of A and BN/2 rows of B and
 // drains its own 128 x BN accumulator.
-template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG>
+//
+// SPLIT: the K range of every tile is cut into sk.splits units run by
+// different CTAs.  Each unit TMA-reduce-adds its int32 partial tile into the
+// sk.acc scratch (exact and order-independent); epilogue warp e of each unit
+// then counts itself in at sk.cnt[tile * 8 + e], and the last of the splits to
+// arrive reads the summed chunks back, applies the epilogue, and returns the
+// chunks and its counter to zero.  Results equal the unsplit GEMM's bit for
+// bit.
+template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ CUtensorMap tmD, int M, int N, int K, int num_m_tiles,
-                      int num_n_tiles, int group_m, EpilogueParams ep) {
-  using C = Cfg<BN, OutT, CG, KIND>;
+                      const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmW,
+                      int M, int N, int K, int num_m_tiles, int num_n_tiles, int group_m,
+                      EpilogueParams ep, SplitArgs sk) {
+  using C = Cfg<BN, OutT, CG, KIND, SPLIT>;
+  static_assert(!SPLIT || (CG == 1 && KIND == 0), "split-K is built for the 1-CTA int8 GEMM");
   constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -276,6 +392,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x % 32;
   const int num_tiles = num_m_tiles * num_n_tiles;
   const int num_kb = (K + kBK - 1) / kBK;
+  const int S = SPLIT ? sk.splits : 1;  // K splits per tile
+  const int num_units = num_tiles * S;
   const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
   const bool leader = rank == 0;
   const int first_tile = static_cast<int>(blockIdx.x) / CG;
@@ -297,6 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if constexpr (!kRaw) tma_prefetch_desc(&tmD);
+    if constexpr (SPLIT) tma_prefetch_desc(&tmW);
   }
   if (warp == kMmaWarp) {
     tmem_alloc<C::kTmemCols, CG>(tmem_slot);
@@ -312,12 +431,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = first_tile; ok && tile < num_tiles; tile += tile_step) {
+      for (int unit = first_tile; ok && unit < num_units; unit += tile_step) {
+        const int tile = unit / S;
+        const int sp = unit - tile * S;
+        const int kb_lo = sp * num_kb / S, kb_hi = (sp + 1) * num_kb / S;
         int mb, nb;
         tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
         const int a_row = mb * kBM * CG + static_cast<int>(rank) * kBM;
         const int b_row = nb * BN + static_cast<int>(rank) * (BN / CG);
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const int s = static_cast<int>(it % C::kStages);
           const uint32_t ph = (it / C::kStages) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, abortv, &g_w8a8_device_error, kDevTimeoutEmpty)) {
@@ -369,7 +491,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       uint32_t tl = 0;
       bool ok = true;
-      for (int tile = first_tile; ok && tile < num_tiles; tile += tile_step, ++tl) {
+      for (int unit = first_tile; ok && unit < num_units; unit += tile_step, ++tl) {
+        const int sp = unit - (unit / S) * S;
+        const int kb_lo = sp * num_kb / S, kb_hi = (sp + 1) * num_kb / S;
         const uint32_t acc = tl & 1u;
         const uint32_t use = tl >> 1;
         if (!mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abortv, &g_w8a8_device_error,
@@ -378,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const int s = static_cast<int>(it % C::kStages);
           const uint32_t ph = (it / C::kStages) & 1u;
           if (!mbar_wait(&full[s], ph, abortv, &g_w8a8_device_error, kDevTimeoutFull)) {
@@ -402,14 +526,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k < kBK / kUmmaK; ++k) {
               umma_mx(d_tmem, smem_desc_k_sw128(a0 + k * kUmmaK), smem_desc_k_sw128(b0 + k * kUmmaK),
                       make_idesc_mx(kBM, BN, static_cast<uint32_t>(k)), sf_tmem, sf_tmem + 4,
-                      (kb | k) != 0 ? 1u : 0u);
+                      (kb != kb_lo || k != 0) ? 1u : 0u);
             }
           } else {
 #pragma unroll
             for (int k = 0; k < kBK / kUmmaK; ++k) {
               const uint64_t ad = smem_desc_k_sw128(a0 + k * kUmmaK);
               const uint64_t bd = smem_desc_k_sw128(b0 + k * kUmmaK);
-              const uint32_t accumulate = (kb | k) != 0 ? 1u : 0u;
+              const uint32_t accumulate = (kb != kb_lo || k != 0) ? 1u : 0u;
               if constexpr (CG == 1) {
                 umma_ss<KIND>(d_tmem, ad, bd, idesc, accumulate);
               } else {
@@ -452,7 +576,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (KIND == 1) fp8_scale = __fmul_rn(__ldg(ep.sa), __ldg(ep.sb));
     (void)fp8_scale;
     uint32_t tl = 0;
-    for (int tile = first_tile; tile < num_tiles; tile += tile_step, ++tl) {
+    for (int unit = first_tile; unit < num_units; unit += tile_step, ++tl) {
+      const int tile = unit / S;
       int mb, nb;
       tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
       const uint32_t acc = tl & 1u;
@@ -497,8 +622,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int col0 = col_base + c * 32;
         if (col0 >= N) break;
         const int ci = (c - half) >> 1;  // this warp's chunk index
-        const float4* wsq = reinterpret_cast<const float4*>(s_ws + ci * 32);
-        const float4* bq = reinterpret_cast<const float4*>(s_bias + ci * 32);
         tmem_ld_wait();
         uint32_t cur[32];
 #pragma unroll
@@ -506,81 +629,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c + 2 < BN / 32 && col0 + 64 < N) {
           tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + (c + 2) * 32, r);
         }
-        float y[32];
-        if constexpr (!kRaw) {
-#pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4) {
-            const float4 w4 = wsq[j4];
-            const float4 b4 = bq[j4];
-            const int j = j4 * 4;
-            float a[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              a[t] = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(cur[j + t]))
-                                 : __uint_as_float(cur[j + t]);
-            }
-            epi_pair<OutT, (KIND == 0 ? ORDER : kDqChained), ACT>(
-                a[0], a[1], xs_row, w4.x, w4.y, b4.x, b4.y, has_bias, y[j], y[j + 1]);
-            epi_pair<OutT, (KIND == 0 ? ORDER : kDqChained), ACT>(
-                a[2], a[3], xs_row, w4.z, w4.w, b4.z, b4.w, has_bias, y[j + 2], y[j + 3]);
-          }
-          if (has_resid) {
-            float rsv[32];
-            load_cols32<OutT>(ep.rscale, col0, N, ep.vec_rscale, rsv);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float res = (grow < M && col0 + j < N)
-                                    ? OutTraits<OutT>::load(ep.residual,
-                                                            static_cast<int64_t>(grow) * ep.ldr + col0 + j)
-                                    : 0.0f;
-              y[j] = round_out<OutT>(__fmaf_rn(y[j], rsv[j], res));
-            }
-          }
-        }
-        // single staging tile: the previous chunk's store was issued a whole
-        // chunk of arithmetic ago
-        if (lane == 0) tma_store_wait_read<0>();
-        __syncwarp();
-        if constexpr (sizeof(OutT) == 4) {
-          // 32 x 4-byte values = 8 chunks of 16 B; 128B swizzle: chunk ^= row & 7.
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            uint4 v;
-            if constexpr (kRaw) {
-              v = make_uint4(cur[cc * 4], cur[cc * 4 + 1], cur[cc * 4 + 2], cur[cc * 4 + 3]);
-            } else {
-              v = make_uint4(__float_as_uint(y[cc * 4]), __float_as_uint(y[cc * 4 + 1]),
-                             __float_as_uint(y[cc * 4 + 2]), __float_as_uint(y[cc * 4 + 3]));
-            }
-            const int phys = cc ^ (lane & 7);
-            *reinterpret_cast<uint4*>(st + lane * 128 + phys * 16) = v;
+        if constexpr (SPLIT) {
+          // this unit's int32 partial -> += scratch (TMA reduction)
+          if (lane == 0) tma_store_wait_read<0>();
+          __syncwarp();
+          stage_raw32(st, cur, lane);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && row0 < M) {
+            tma_reduce_add_2d(&tmW, st, col0, row0);
+            tma_store_commit();
           }
         } else {
-          // 32 x 2-byte values = 4 chunks of 16 B; 64B swizzle: chunk ^= (row >> 1) & 3.
-#pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            uint32_t w4[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float lo = y[cc * 8 + e * 2];
-              const float hi = y[cc * 8 + e * 2 + 1];
-              if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
-                // values are already exact bf16: take the high halves
-                w4[e] = __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
-              } else {
-                w4[e] = pack2<OutT>(lo, hi);
-              }
-            }
-            const int phys = cc ^ ((lane >> 1) & 3);
-            *reinterpret_cast<uint4*>(st + lane * 64 + phys * 16) =
-                make_uint4(w4[0], w4[1], w4[2], w4[3]);
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && row0 < M) {
-          tma_store_2d(&tmD, st, col0, row0);
-          tma_store_commit();
+          finish_chunk<KIND, OutT, ORDER, ACT>(cur, s_ws + ci * 32, s_bias + ci * 32, xs_row,
+                                               has_bias, has_resid, ep, grow, col0, row0, M, N, st,
+                                               &tmD, lane);
         }
       }
       tc_fence_before();
@@ -590,6 +653,53 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&tempty[acc]);
         } else {
           mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+        }
+      }
+      if constexpr (SPLIT) {
+        // Count this warp's chunks in; the last split to arrive finishes them.
+        unsigned last = 0;
+        unsigned* cnt = sk.cnt + static_cast<int64_t>(tile) * kEpiWarps + warp;
+        if (lane == 0) {
+          tma_store_wait_all<0>();      // this warp's reductions are complete
+          fence_proxy_async_global();
+          __threadfence();
+          last = atomicAdd(cnt, 1u) == static_cast<unsigned>(S - 1) ? 1u : 0u;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          for (int c = half; c < BN / 32; c += 2) {
+            const int col0 = col_base + c * 32;
+            if (col0 >= N) break;
+            const int ci = (c - half) >> 1;
+            uint32_t cur[32];
+            int32_t* src = sk.acc + static_cast<int64_t>(grow) * N + col0;
+            if (grow < M && col0 + 32 <= N) {
+              // rows of the scratch are 16-byte aligned (N % 4 == 0)
+              int4* s4 = reinterpret_cast<int4*>(src);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int4 v = __ldcg(s4 + i);
+                cur[4 * i] = static_cast<uint32_t>(v.x);
+                cur[4 * i + 1] = static_cast<uint32_t>(v.y);
+                cur[4 * i + 2] = static_cast<uint32_t>(v.z);
+                cur[4 * i + 3] = static_cast<uint32_t>(v.w);
+              }
+#pragma unroll
+              for (int i = 0; i < 8; ++i) __stcg(s4 + i, make_int4(0, 0, 0, 0));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const bool in = grow < M && col0 + j < N;
+                cur[j] = in ? static_cast<uint32_t>(__ldcg(src + j)) : 0u;
+                if (in) __stcg(src + j, 0);
+              }
+            }
+            finish_chunk<KIND, OutT, ORDER, ACT>(cur, s_ws + ci * 32, s_bias + ci * 32, xs_row,
+                                                 has_bias, has_resid, ep, grow, col0, row0, M, N,
+                                                 st, &tmD, lane);
+          }
+          if (lane == 0) *cnt = 0u;
         }
       }
     }
@@ -736,13 +846,16 @@ EpilogueParams to_params(const GemmArgs& g) {
   return ep;
 }
 
-template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG>
+// mw / sk: the split-K scratch map and pointers (SPLIT only; otherwise the
+// output map stands in for the unused map parameter).
+template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG, bool SPLIT = false>
 int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
-              int group_m, int max_ctas, cudaStream_t stream) {
+              const CUtensorMap& mw, SplitArgs sk, int group_m, int max_ctas, cudaStream_t stream) {
   // The same configuration the kernel lays its shared memory out with: the
-  // block-scaled kind adds scale-factor bytes to every stage.
-  using C = Cfg<BN, OutT, CG, KIND>;
-  auto kern = gemm_sm100_kernel<KIND, BN, OutT, ORDER, ACT, CG>;
+  // block-scaled kind adds scale-factor bytes to every stage, split-K wider
+  // staging tiles.
+  using C = Cfg<BN, OutT, CG, KIND, SPLIT>;
+  auto kern = gemm_sm100_kernel<KIND, BN, OutT, ORDER, ACT, CG, SPLIT>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -759,14 +872,17 @@ int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, c
   const int num_n = static_cast<int>((g.N + BN - 1) / BN);
   const int tiles = num_m * num_n;
   const int sms = device_sm_count();
-  int units = std::min(tiles, (max_ctas > 0 ? max_ctas : sms) / CG);  // CTAs or CTA pairs
+  if (!SPLIT) sk.splits = 1;
+  int units = static_cast<int>(
+      std::min<int64_t>(static_cast<int64_t>(tiles) * sk.splits,
+                        (max_ctas > 0 ? max_ctas : sms) / CG));  // CTAs or CTA pairs
   if (units < 1) units = 1;
   const EpilogueParams ep = to_params(g);
   const int Mi = static_cast<int>(g.M), Ni = static_cast<int>(g.N), Ki = static_cast<int>(g.K);
   cudaError_t e;
   if constexpr (CG == 1) {
-    kern<<<units, kThreads, C::kSmemBytes, stream>>>(ma, mb, md, Mi, Ni, Ki, num_m, num_n, group_m,
-                                                    ep);
+    kern<<<units, kThreads, C::kSmemBytes, stream>>>(ma, mb, md, mw, Mi, Ni, Ki, num_m, num_n,
+                                                    group_m, ep, sk);
     e = cudaGetLastError();
   } else {
     cudaLaunchConfig_t lc{};
@@ -781,7 +897,7 @@ int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, c
     attr[0].val.clusterDim.z = 1;
     lc.attrs = attr;
     lc.numAttrs = 1;
-    e = cudaLaunchKernelEx(&lc, kern, ma, mb, md, Mi, Ni, Ki, num_m, num_n, group_m, ep);
+    e = cudaLaunchKernelEx(&lc, kern, ma, mb, md, mw, Mi, Ni, Ki, num_m, num_n, group_m, ep, sk);
   }
   if (e != cudaSuccess) {
     set_error("tcgen05 GEMM launch failed: %s", cudaGetErrorString(e));
@@ -807,9 +923,9 @@ int launch_simt(const GemmArgs& g, cudaStream_t stream) {
 
 template <int KIND, typename OutT>
 int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_ctas, int cg,
-                 cudaStream_t stream) {
+                 int splits, cudaStream_t stream) {
   if (!tc_ok) return launch_simt<KIND, OutT>(g, stream);
-  CUtensorMap ma, mb, md;
+  CUtensorMap ma, mb, md, mw;
   bool ok = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.a, g.K, g.M, g.lda, kBK, kBM,
                         CU_TENSOR_MAP_SWIZZLE_128B);
   ok = ok && make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.b, g.K, g.N, g.ldb, kBK,
@@ -821,6 +937,18 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
   else dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   ok = ok && make_map_2d(&md, dt, static_cast<int>(sizeof(OutT)), g.out, g.N, g.M, g.ldo, 32, 32,
                          sizeof(OutT) == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  SplitArgs sk{nullptr, nullptr, 1};
+  if (splits > 1) {
+    // int32 [M, N] partial sums, then the arrival counters
+    sk.acc = static_cast<int32_t*>(g.workspace);
+    sk.cnt = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(g.workspace) +
+                                         splitk_acc_bytes(g.M, g.N));
+    sk.splits = splits;
+    ok = ok && make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, g.workspace, g.N, g.M, g.N, 32,
+                           32, CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    mw = md;
+  }
   if (!ok) {
     set_error("cuTensorMapEncodeTiled rejected the operands (M=%lld N=%lld K=%lld)",
               static_cast<long long>(g.M), static_cast<long long>(g.N), static_cast<long long>(g.K));
@@ -830,11 +958,21 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
     constexpr int O = decltype(order_c)::value;
     constexpr int A = decltype(act_c)::value;
     if constexpr (KIND == 2) {
-      return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, group_m, max_ctas, stream);
+      return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
     } else {
-      if (bn == 128) return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, group_m, max_ctas, stream);
-      if (cg == 2) return launch_tc<KIND, 256, OutT, O, A, 2>(g, ma, mb, md, group_m, max_ctas, stream);
-      return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, md, group_m, max_ctas, stream);
+      if constexpr (KIND == 0 && !std::is_same<OutT, int32_t>::value) {
+        if (splits > 1) {
+          return launch_tc<KIND, 128, OutT, O, A, 1, true>(g, ma, mb, md, mw, sk, group_m, max_ctas,
+                                                           stream);
+        }
+      }
+      if (bn == 128) {
+        return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
+      }
+      if (cg == 2) {
+        return launch_tc<KIND, 256, OutT, O, A, 2>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
+      }
+      return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
     }
   };
   using I0 = std::integral_constant<int, 0>;
@@ -860,6 +998,13 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
 }
 
 }  // namespace
+
+int64_t splitk_acc_bytes(int64_t M, int64_t N) { return (M * N * 4 + 255) / 256 * 256; }
+
+int64_t splitk_workspace_bytes(int64_t M, int64_t N) {
+  const int64_t tiles128 = ((M + kBM - 1) / kBM) * ((N + 127) / 128);
+  return splitk_acc_bytes(M, N) + tiles128 * kEpiWarps * 4;
+}
 
 int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if (g.M == 0 || g.N == 0) return 0;
@@ -893,27 +1038,59 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   // epilogue bounds the tile rate).
   if (cg == 0) cg = 1;
   if (bn == 128) cg = 1;  // pairs are built for 256-column tiles
+  // Split-K (int8 with a dequant epilogue, scratch given): when one split
+  // per 128-column tile leaves SMs idle, cut K so tiles x splits fills them,
+  // keeping at least 4 K-blocks (512 bytes of K) per split.
+  int splits = 1;
+  if (g.workspace && g.kind == 0 && g.out_dtype != W8A8_S32 && tc_ok && g.N % 4 == 0 &&
+      g.split_k != 1) {
+    const int num_kb = static_cast<int>((g.K + kBK - 1) / kBK);
+    const long long tiles128 = ((g.M + kBM - 1) / kBM) * ((g.N + 127) / 128);
+    if (g.split_k > 1) {
+      splits = std::min(g.split_k, num_kb);
+    } else {
+      const long long fill = device_sm_count() / std::max(1ll, tiles128);
+      splits = static_cast<int>(std::min<long long>(fill, std::min(8, num_kb / 4)));
+    }
+    if (splits > 1) {
+      if (g.workspace_bytes < splitk_workspace_bytes(g.M, g.N)) {
+        set_error("split-K scratch of %lld bytes is smaller than the %lld bytes M=%lld N=%lld need",
+                  static_cast<long long>(g.workspace_bytes),
+                  static_cast<long long>(splitk_workspace_bytes(g.M, g.N)),
+                  static_cast<long long>(g.M), static_cast<long long>(g.N));
+        return W8A8_ERR_VALUE;
+      }
+      if (reinterpret_cast<uintptr_t>(g.workspace) & 255u) {
+        set_error("split-K scratch must be 256-byte aligned");
+        return W8A8_ERR_VALUE;
+      }
+      bn = 128;
+      cg = 1;
+    } else {
+      splits = 1;
+    }
+  }
   if (g.kind == 0) {
     switch (g.out_dtype) {
-      case W8A8_BF16: return dispatch_out<0, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
-      case W8A8_F16: return dispatch_out<0, __half>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
-      case W8A8_F32: return dispatch_out<0, float>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
-      case W8A8_S32: return dispatch_out<0, int32_t>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
+      case W8A8_BF16: return dispatch_out<0, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, cg, splits, stream);
+      case W8A8_F16: return dispatch_out<0, __half>(g, tc_ok, bn, group_m, max_ctas, cg, splits, stream);
+      case W8A8_F32: return dispatch_out<0, float>(g, tc_ok, bn, group_m, max_ctas, cg, splits, stream);
+      case W8A8_S32: return dispatch_out<0, int32_t>(g, tc_ok, bn, group_m, max_ctas, cg, 1, stream);
       default: break;
     }
   } else if (g.kind == 2) {
     const bool mx_ok = tc_ok && g.K % 32 == 0 && a16(g.sfa) && a16(g.sfb);
     switch (g.out_dtype) {
-      case W8A8_BF16: return dispatch_out<2, __nv_bfloat16>(g, mx_ok, 128, group_m, max_ctas, 1, stream);
-      case W8A8_F16: return dispatch_out<2, __half>(g, mx_ok, 128, group_m, max_ctas, 1, stream);
-      case W8A8_F32: return dispatch_out<2, float>(g, mx_ok, 128, group_m, max_ctas, 1, stream);
+      case W8A8_BF16: return dispatch_out<2, __nv_bfloat16>(g, mx_ok, 128, group_m, max_ctas, 1, 1, stream);
+      case W8A8_F16: return dispatch_out<2, __half>(g, mx_ok, 128, group_m, max_ctas, 1, 1, stream);
+      case W8A8_F32: return dispatch_out<2, float>(g, mx_ok, 128, group_m, max_ctas, 1, 1, stream);
       default: break;
     }
   } else {
     switch (g.out_dtype) {
-      case W8A8_BF16: return dispatch_out<1, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
-      case W8A8_F16: return dispatch_out<1, __half>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
-      case W8A8_F32: return dispatch_out<1, float>(g, tc_ok, bn, group_m, max_ctas, cg, stream);
+      case W8A8_BF16: return dispatch_out<1, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, cg, 1, stream);
+      case W8A8_F16: return dispatch_out<1, __half>(g, tc_ok, bn, group_m, max_ctas, cg, 1, stream);
+      case W8A8_F32: return dispatch_out<1, float>(g, tc_ok, bn, group_m, max_ctas, cg, 1, stream);
       default: break;
     }
   }

@@ -18,9 +18,13 @@ int quantize_rowwise_launch(const void* x, int x_dtype, int64_t rows, int64_t co
 
 // Fused input activation (+ 256-point ConvRot when rotate != 0) + row-wise
 // INT8 quantiser; act codes W8A8_INPUT_ACT_*.
+// act 5-8 are the modulations (W8A8_MOD_* + 5) with scale / shift rows
+// [rows / mod_group, cols].
 int quantize_act_rot_launch(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
-                            int rotate, int act, const void* act_w, float act_eps, int8_t* q,
-                            int64_t ldq, float* scales, int scale_mode, cudaStream_t stream);
+                            int rotate, int act, const void* act_w, float act_eps,
+                            const void* mod_scale, const void* mod_shift, int64_t mod_group,
+                            int8_t* q, int64_t ldq, float* scales, int scale_mode,
+                            cudaStream_t stream);
 
 // kind 0: int8 x int8 (s32 accumulate); kind 1: e4m3 x e4m3 (f32 accumulate);
 // kind 2: MXFP8 e4m3 x e4m3 with e8m0 block scales (f32 accumulate).
@@ -42,8 +46,17 @@ struct GemmArgs {
   const w8a8_gemm_config_t* cfg;
   const void* sfa;  // kind 2 (MXFP8): blocked e8m0 scales of a and b
   const void* sfb;
+  // split-K (kind 0 with a dequant epilogue): 0 = choose, 1 = off, >1 = splits;
+  // used only with a zero-filled scratch of splitk_workspace_bytes(M, N)
+  int split_k;
+  void* workspace;
+  int64_t workspace_bytes;
 };
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);
+// Split-K scratch: int32 [M, N] partial sums (padded to 256 bytes), then one
+// arrival counter per (128 x 128 tile, epilogue warp).
+int64_t splitk_acc_bytes(int64_t M, int64_t N);
+int64_t splitk_workspace_bytes(int64_t M, int64_t N);
 
 int dequant_launch(const int32_t* acc, const float* xs, const w8a8_epilogue_t* epi, void* out,
                    int out_dtype, int64_t M, int64_t N, cudaStream_t stream);

@@ -171,6 +171,176 @@ def quantize_int8_rowwise_convrot(x: torch.Tensor, group: int = 256, input_act: 
     return q.reshape(*x.shape[:-1], k), s.reshape(*x.shape[:-1], 1)
 
 
+MODULATION = {"scale": 0, "rms_scale": 1, "adaln": 2, "rms_adaln": 3}
+
+
+def _mod_rows(t: torch.Tensor, rows: int, k: int, name: str, dev, dtype) -> tuple:
+    """Modulation tensor as contiguous [G, K] rows plus the number of x rows
+    each one covers (a [K] / [1, K] tensor covers all rows; [B, 1, K] or
+    [B, K] covers rows / B consecutive rows each)."""
+    t = t.to(device=dev, dtype=dtype)
+    if t.shape[-1] != k:
+        raise ValueError(f"{name} has {t.shape[-1]} features, expected {k}")
+    t = t.reshape(-1, k).contiguous()
+    g = t.shape[0]
+    if g == 0 or rows % g:
+        raise ValueError(f"{name} has {g} rows, which do not divide the {rows} activation rows")
+    return t, max(rows // g, 1)
+
+
+def quantize_int8_rowwise_modulated(x: torch.Tensor, mode: str, modulation_scale: torch.Tensor,
+                                    shift: Optional[torch.Tensor] = None,
+                                    norm_weight: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                                    convrot: bool = False, *, scale_mode: str = "eager"):
+    """Modulation (``scale``: x(1+s); ``rms_scale``: rms_norm(x, w)(1+s);
+    ``adaln``: layer_norm(x)(1+s)+shift; ``rms_adaln``: rms_norm(x)(1+s)+shift),
+    optional 256-group ConvRot, and per-row INT8 quantisation in one pass.
+    Returns ``(q int8 [..., K], scale fp32 [..., 1])``."""
+    _cuda("x", x)
+    if mode not in MODULATION:
+        raise ValueError(f"unknown modulation {mode!r}")
+    k = x.shape[-1]
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    sc, group = _mod_rows(modulation_scale, m, k, "modulation_scale", x.device, x.dtype)
+    sh = None
+    if mode in ("adaln", "rms_adaln"):
+        if shift is None:
+            raise ValueError(f"modulation {mode!r} needs a shift")
+        sh, g2 = _mod_rows(shift, m, k, "shift", x.device, x.dtype)
+        if g2 != group:
+            raise ValueError("scale and shift must have the same number of rows")
+    w = None
+    if mode == "rms_scale":
+        if norm_weight is None:
+            raise ValueError("modulation 'rms_scale' needs norm_weight")
+        w = norm_weight.to(device=x.device, dtype=x.dtype).reshape(-1).contiguous()
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m, 1), dtype=torch.float32, device=x.device)
+    N.check(N.LIB.w8a8_quantize_rowwise_modulated(
+        _vp(x2), _code(x2.dtype), m, k, x2.stride(0) if m > 0 else k, MODULATION[mode], _vp(w),
+        float(eps), _vp(sc), _vp(sh), group, 256 if convrot else 0, _vp(q), k, _vp(s),
+        SCALE_MODE[scale_mode], _stream(x.device)))
+    return q.reshape(x.shape), s.reshape(*x.shape[:-1], 1)
+
+
+def _modulated_linear(x, mode, modulation_scale, shift, norm_weight, eps, weight, weight_scale,
+                      bias, out_dtype, convrot, convrot_groupsize, scale_mode, dequant,
+                      output_act, aten_modulate):
+    """Shared body of the modulated linears: the fused quantiser when K fits
+    it, else the modulation as device ATen ops followed by int8_linear."""
+    k = x.shape[-1]
+    fused = k % 256 == 0 and 256 <= k <= 16384 and (not convrot or convrot_groupsize == 256)
+    if not fused:
+        return int8_linear(aten_modulate(x), weight, weight_scale, bias, out_dtype, convrot,
+                           convrot_groupsize, scale_mode=scale_mode, dequant=dequant,
+                           output_act=output_act)
+    _cuda("weight", weight, x.device)
+    if weight.dim() != 2 or weight.dtype != torch.int8:
+        raise ValueError("weight must be a 2-D int8 tensor [N, K]")
+    if k != weight.shape[-1]:
+        raise ValueError(f"Input and weight inner dimensions must match, got {k} and {weight.shape[-1]}")
+    n = weight.shape[0]
+    dev = x.device
+    out_dtype = out_dtype or x.dtype
+    ws = weight_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    if ws.numel() not in (1, n):
+        raise ValueError(f"INT8 weight scale must be scalar or per-output-channel, got "
+                         f"{tuple(weight_scale.shape)} for weight shape {tuple(weight.shape)}")
+    q, xs = quantize_int8_rowwise_modulated(x, mode, modulation_scale, shift, norm_weight, eps,
+                                            convrot, scale_mode=scale_mode)
+    lead = x.shape[:-1]
+    q = q.reshape(-1, k)
+    xs = xs.reshape(-1)
+    m = q.shape[0]
+    w = weight if weight.is_contiguous() else weight.contiguous()
+    b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
+    out = torch.empty((m, n), dtype=out_dtype, device=dev)
+    ep = _epilogue(ws, b, None, None, dequant, output_act, n, n)
+    stream = _stream(dev)
+    if 1 <= m <= 2:
+        N.check(N.LIB.w8a8_gemv_dequant(_vp(q), _vp(w), _vp(xs), ctypes.byref(ep), _vp(out),
+                                        _code(out_dtype), m, n, k, stream))
+    elif m > 0:
+        _gemm_dequant(q, w, xs, ep, out, out_dtype, m, n, k, None, None, stream)
+    return out.reshape(*lead, n)
+
+
+def int8_linear_modulated(x: torch.Tensor, modulation_scale: torch.Tensor, weight: torch.Tensor,
+                          weight_scale: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                          out_dtype: Optional[torch.dtype] = torch.bfloat16, convrot: bool = False,
+                          convrot_groupsize: int = 256, *, scale_mode: str = "eager",
+                          dequant: str = "eager", output_act: Optional[str] = None):
+    """Registry operator ``int8_linear_modulated`` (inference/src/backend_signatures.rs:
+    128-139; eager body inference/src/backend_bindings.rs:329-405):
+    ``int8_linear(x * (1 + modulation_scale), ...)`` for one batch-one
+    modulation row, with the modulation fused into the quantiser."""
+    _cuda("x", x)
+    k = x.shape[-1]
+    if modulation_scale.numel() != k:
+        raise ValueError(f"modulation_scale must contain one batch-one row of {k} values, got "
+                         f"{modulation_scale.numel()}")
+
+    def aten(t):
+        return t * (modulation_scale.to(device=t.device, dtype=t.dtype).reshape(-1) + 1)
+    return _modulated_linear(x, "scale", modulation_scale, None, None, 0.0, weight, weight_scale,
+                             bias, out_dtype, convrot, convrot_groupsize, scale_mode, dequant,
+                             output_act, aten)
+
+
+def int8_linear_rms_modulated(x: torch.Tensor, norm_weight: torch.Tensor, norm_eps: float,
+                              modulation_scale: torch.Tensor, weight: torch.Tensor,
+                              weight_scale: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                              out_dtype: Optional[torch.dtype] = torch.bfloat16,
+                              convrot: bool = False, convrot_groupsize: int = 256, *,
+                              scale_mode: str = "eager", dequant: str = "eager",
+                              output_act: Optional[str] = None):
+    """Registry operator ``int8_linear_rms_modulated`` (inference/src/backend_signatures.rs:
+    140-156): ``int8_linear_modulated(rms_norm(x, norm_weight, norm_eps), ...)``."""
+    _cuda("x", x)
+    k = x.shape[-1]
+    if modulation_scale.numel() != k:
+        raise ValueError(f"modulation_scale must contain one batch-one row of {k} values, got "
+                         f"{modulation_scale.numel()}")
+    eps = float(norm_eps or 0.0)
+
+    def aten(t):
+        nrm = torch.nn.functional.rms_norm(t, (k,), norm_weight.to(device=t.device, dtype=t.dtype), eps)
+        return nrm * (modulation_scale.to(device=t.device, dtype=t.dtype).reshape(-1) + 1)
+    return _modulated_linear(x, "rms_scale", modulation_scale, None, norm_weight, eps, weight,
+                             weight_scale, bias, out_dtype, convrot, convrot_groupsize, scale_mode,
+                             dequant, output_act, aten)
+
+
+def adaln_int8_linear(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
+                      weight: torch.Tensor, weight_scale: torch.Tensor,
+                      bias: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                      eps: float = 1e-6, rms: bool = False, convrot: bool = False,
+                      convrot_groupsize: int = 256, *, scale_mode: str = "eager",
+                      dequant: str = "eager", output_act: Optional[str] = None):
+    """AdaLN modulation (``adaln`` / ``rms_adaln``: norm(x)(1 + scale) + shift,
+    inference/src/backend_eager.rs:176-236) followed by the INT8 linear -- the
+    pre-QKV / pre-MLP-up step of an MMDiT block -- with the modulation fused
+    into the quantiser.  scale / shift: [K], or one row per sample ([B, 1, K]
+    for x [B, S, K])."""
+    _cuda("x", x)
+    k = x.shape[-1]
+
+    def aten(t):
+        sc = scale.to(device=t.device, dtype=t.dtype)
+        sh = shift.to(device=t.device, dtype=t.dtype)
+        if rms:
+            nrm = torch.nn.functional.rms_norm(t, (k,), None, eps)
+        else:
+            nrm = torch.nn.functional.layer_norm(t, (k,), None, None, eps)
+        return nrm * (sc + 1) + sh
+    return _modulated_linear(x, "rms_adaln" if rms else "adaln", scale, shift, None, eps, weight,
+                             weight_scale, bias, out_dtype, convrot, convrot_groupsize, scale_mode,
+                             dequant, output_act, aten)
+
+
 def quantize_weight(weight: torch.Tensor):
     """Offline per-output-channel weight quantisation
     (inference/src/layout_complete.rs:119-159 TensorWiseINT8Layout.from_float):
@@ -238,13 +408,47 @@ def _hadamard(size: int, device, dtype) -> torch.Tensor:
     return _HADAMARD[key]
 
 
+_SPLITK_SCRATCH: dict = {}
+
+
+def _splitk_scratch(dev: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-filled split-K scratch, one per (device, stream): the kernels leave
+    it zero-filled after every call, and calls on one stream never overlap."""
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    buf = _SPLITK_SCRATCH.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _SPLITK_SCRATCH[key] = buf
+    return buf
+
+
+def _gemm_dequant(q, w, xs, ep, out, out_dtype, m, n, k, cfg, split_k, stream):
+    """w8a8_gemm_dequant, or its split-K form when the 128 x 128 tiles of a
+    few-row shape would leave SMs idle (or splits were asked for)."""
+    dev = out.device
+    use_split = split_k is not None and split_k > 1
+    if split_k is None and m > 0 and n % 4 == 0 and k >= 1024:
+        tiles = -(-m // 128) * -(-n // 128)
+        use_split = 2 * tiles <= torch.cuda.get_device_properties(dev).multi_processor_count
+    if use_split:
+        nbytes = int(N.LIB.w8a8_gemm_splitk_workspace_bytes(m, n))
+        scratch = _splitk_scratch(dev, nbytes)
+        N.check(N.LIB.w8a8_gemm_dequant_splitk(
+            _vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep), _vp(out), _code(out_dtype), n, m, n, k,
+            int(split_k or 0), _vp(scratch), scratch.numel(), _cfg_ptr(cfg), stream))
+    else:
+        N.check(N.LIB.w8a8_gemm_dequant(_vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep), _vp(out),
+                                        _code(out_dtype), n, m, n, k, _cfg_ptr(cfg), stream))
+
+
 def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
                 bias: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                 convrot: bool = False, convrot_groupsize: int = 256,
                 input_act: Optional[str] = None, input_act_weight: Optional[torch.Tensor] = None,
                 input_act_eps: float = 0.0, residual: Optional[torch.Tensor] = None,
                 residual_scale: Optional[torch.Tensor] = None, *, dequant: str = "eager",
-                scale_mode: str = "eager", output_act: Optional[str] = None, config=None):
+                scale_mode: str = "eager", output_act: Optional[str] = None, config=None,
+                split_k: Optional[int] = None):
     """The registry operator ``int8_linear`` (inference/src/backend_signatures.rs:445-460;
     eager body inference/src/int8_linear.rs:198-277; CUDA route
     inference/src/cuda_linear.rs:419-824).
@@ -253,6 +457,9 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     to reproduce (default: the eager route, bit-exact); ``output_act`` applies
     GELU-tanh in the epilogue (the MLP-up fusion).  ``config`` is an optional
     ``(block_n, group_m, max_ctas, cta_group)`` tile configuration.
+    ``split_k``: None lets few-row shapes (whose tiles leave SMs idle) split K
+    across CTAs, 1 turns that off, n > 1 asks for n splits; results are the
+    same bit for bit either way.
     """
     _cuda("x", x)
     dev = x.device
@@ -318,9 +525,7 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
             N.check(N.LIB.w8a8_gemv_dequant(_vp(q), _vp(w), _vp(xs), ctypes.byref(ep), _vp(out),
                                             _code(out_dtype), m, n, k, stream))
         else:
-            N.check(N.LIB.w8a8_gemm_dequant(_vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep),
-                                            _vp(out), _code(out_dtype), n, m, n, k,
-                                            _cfg_ptr(_config(config)), stream))
+            _gemm_dequant(q, w, xs, ep, out, out_dtype, m, n, k, _config(config), split_k, stream)
     elif 1 <= m <= 2 and k > 0 and m * k <= 32768:
         # a5: the AdaLN-modulation shape -- quantise and GEMV in one launch.
         N.check(N.LIB.w8a8_linear_small(_vp(x2), _code(x2.dtype), _vp(w), ctypes.byref(ep),
@@ -333,8 +538,7 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
             N.check(N.LIB.w8a8_quantize_rowwise(_vp(x2), _code(x2.dtype), m, k, k, _vp(q), k,
                                                 _vp(xs), SCALE_MODE[scale_mode], 0, 0, stream))
         cfg = _config(config)
-        N.check(N.LIB.w8a8_gemm_dequant(_vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep), _vp(out),
-                                        _code(out_dtype), n, m, n, k, _cfg_ptr(cfg), stream))
+        _gemm_dequant(q, w, xs, ep, out, out_dtype, m, n, k, cfg, split_k, stream)
     return out.reshape(*lead, n)
 
 
@@ -473,4 +677,10 @@ def device_error(device=None) -> int:
     """Read-and-clear the device-side error word (nonzero: a bounded wait in a
     tcgen05 kernel gave up)."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    return N.LIB.w8a8_device_error(_stream(dev))
+    err = N.LIB.w8a8_device_error(_stream(dev))
+    if err:
+        # a kernel that gave up may have left split-K partial sums behind
+        for (index, _), buf in _SPLITK_SCRATCH.items():
+            if index == dev.index:
+                buf.zero_()
+    return err

@@ -28,6 +28,8 @@ def main():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--block-n", type=int, default=0)
     ap.add_argument("--cta-group", type=int, default=0)
+    ap.add_argument("--split-k", type=int, default=1,
+                    help="GEMM K splits (0: chosen from the SM count, 1: off)")
     ap.add_argument("--time", action="store_true",
                     help="time each launch with CUDA events (L2 flushed before each) and print "
                          "the median")
@@ -73,14 +75,19 @@ def main():
                 # time the GEMM alone on pre-quantised activations
                 import ctypes
                 from imagine_b200 import _native as NAT
-                from imagine_b200.linear import _config, _epilogue, _stream, _vp
+                from imagine_b200.linear import _config, _epilogue, _gemm_dequant, _stream, _vp
                 q, xs = W.quantize_int8_rowwise(x)
                 y = torch.empty((a.m, a.n), dtype=torch.bfloat16, device=dev)
                 ep = _epilogue(ws, b, None, None, "eager", act, a.n, a.n)
                 c = _config(cfg)
-                run(lambda: NAT.check(NAT.LIB.w8a8_gemm_dequant(
-                    _vp(q), a.k, _vp(wq), a.k, _vp(xs), ctypes.byref(ep), _vp(y), NAT.BF16, a.n,
-                    a.m, a.n, a.k, ctypes.byref(c), _stream(dev))))
+                if a.split_k != 1:
+                    sk = None if a.split_k == 0 else a.split_k
+                    run(lambda: _gemm_dequant(q, wq, xs.reshape(-1), ep, y, torch.bfloat16, a.m,
+                                              a.n, a.k, c, sk, _stream(dev)))
+                else:
+                    run(lambda: NAT.check(NAT.LIB.w8a8_gemm_dequant(
+                        _vp(q), a.k, _vp(wq), a.k, _vp(xs), ctypes.byref(ep), _vp(y), NAT.BF16, a.n,
+                        a.m, a.n, a.k, ctypes.byref(c), _stream(dev))))
             else:
                 run(lambda: W.int8_linear(x, wq, ws, b, output_act=act, config=cfg))
         else:
@@ -93,7 +100,8 @@ def main():
     err = W.device_error()
     if err:
         raise SystemExit(f"device error {err}")
-    msg = f"ok {a.kernel} {a.m} {a.k} {a.n} block_n={a.block_n} cta_group={a.cta_group}"
+    msg = (f"ok {a.kernel} {a.m} {a.k} {a.n} block_n={a.block_n} cta_group={a.cta_group} "
+           f"split_k={a.split_k}")
     if times:
         t = sorted(times)[len(times) // 2]
         ops = 2.0 * a.m * a.n * a.k

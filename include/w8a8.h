@@ -136,6 +136,35 @@ int w8a8_quantize_rowwise_convrot(const void* x, int x_dtype, int64_t rows, int6
                                   float act_eps, int8_t* q, int64_t ldq, float* scale,
                                   int scale_mode, void* stream);
 
+/* ---- a7: modulation fused into the quantiser ------------------------------
+ * The step before the QKV and MLP-up projections, applied on the way into the
+ * quantiser so the modulated activation never goes to HBM:
+ *   MOD_SCALE      x * (1 + s)                    `int8_linear_modulated`
+ *   MOD_RMS_SCALE  rms_norm(x, norm_w, eps) * (1 + s)
+ *                                                 `int8_linear_rms_modulated`
+ *                  (registry ops inference/src/backend_signatures.rs:128-156,
+ *                  eager body inference/src/backend_bindings.rs:329-405)
+ *   MOD_ADALN      layer_norm(x, eps) * (1 + s) + shift        `adaln`
+ *   MOD_RMS_ADALN  rms_norm(x, eps) * (1 + s) + shift          `rms_adaln`
+ *                  (inference/src/backend_eager.rs:176-236; KSRC
+ *                  backends/cuda/ops/adaln.cu:103-190)
+ * then the optional 256-group ConvRot (group 256) and the row quantiser.
+ * s and shift are [rows / mod_group, cols] in the input dtype (row i uses
+ * modulation row i / mod_group: the per-sample rows of a batch).  The
+ * modulated value is rounded to the input dtype, as the reference stores it;
+ * scale_mode KITCHEN follows the reference's CUDA adaln arithmetic (one-pass
+ * statistics, one rounding), EAGER its ATen sequence.  cols: a multiple of
+ * 256 up to 16384. */
+#define W8A8_MOD_SCALE 0
+#define W8A8_MOD_RMS_SCALE 1
+#define W8A8_MOD_ADALN 2
+#define W8A8_MOD_RMS_ADALN 3
+int w8a8_quantize_rowwise_modulated(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                                    int64_t ldx, int mode, const void* norm_w, float eps,
+                                    const void* mod_scale, const void* mod_shift,
+                                    int64_t mod_group, int group, int8_t* q, int64_t ldq,
+                                    float* scale, int scale_mode, void* stream);
+
 /* ---- row-parallel (K-sharded) quantisation --------------------------------
  * No reference counterpart: the reference runs on one GPU.  A K-sharded
  * activation needs the absmax of the whole row before any shard can be
@@ -166,6 +195,25 @@ int w8a8_gemm_dequant(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw
  * `cublas_gemm_int8(q, w, acc_i32, workspace, stream)` (call site
  * inference/src/cuda_linear.rs:769-780; KSRC backends/cuda/ops/cublas_gemm_int8.cu:89-230);
  * needs no workspace. */
+/* ---- a3: split-K form of w8a8_gemm_dequant for few-row shapes -----------
+ * Same arguments and results as w8a8_gemm_dequant (which it replaces at the
+ * same call sites, inference/src/cuda_linear.rs:724-764, when M is small: the
+ * 256-token text stream).  When the 128 x 128 output tiles alone would leave
+ * SMs idle, the K range is cut into split_k parts (0: chosen from the SM
+ * count, 1: off) run by different CTAs; their int32 partial tiles are added
+ * into `workspace`, so results are identical bit for bit to the unsplit
+ * GEMM.  The caller owns the workspace, as it owns cublas_gemm_int8's
+ * (cuda_linear.rs:769-780): at least w8a8_gemm_splitk_workspace_bytes(M, N)
+ * bytes, 256-byte aligned, zero-filled before the first call; every call
+ * leaves it zero-filled again.  Calls sharing a workspace must not overlap on
+ * the GPU.  After a nonzero w8a8_device_error the workspace must be cleared. */
+int64_t w8a8_gemm_splitk_workspace_bytes(int64_t M, int64_t N);
+int w8a8_gemm_dequant_splitk(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,
+                             const float* xs, const w8a8_epilogue_t* epi, void* out, int out_dtype,
+                             int64_t ldo, int64_t M, int64_t N, int64_t K, int split_k,
+                             void* workspace, int64_t workspace_bytes,
+                             const w8a8_gemm_config_t* cfg, void* stream);
+
 int w8a8_gemm_s32(const int8_t* q, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
                   const w8a8_gemm_config_t* cfg, void* stream);
 

@@ -269,6 +269,42 @@ def int8_linear(x, weight, weight_scale, bias=None, out_dtype=torch.bfloat16,
     return apply_residual(y, residual, residual_scale)
 
 
+# --------------------------------------------------------------------------
+# a7: modulation before the linear
+# --------------------------------------------------------------------------
+def adaln(x, scale, shift, eps=1e-6, rms=False):
+    """inference/src/backend_eager.rs:176-197 (KSRC backends/eager/adaln.py:11-20):
+    norm(x) * (1 + scale) + shift, every op in x's dtype."""
+    k = x.shape[-1]
+    if rms:
+        nrm = torch.nn.functional.rms_norm(x, (k,), None, eps)
+    else:
+        nrm = torch.nn.functional.layer_norm(x, (k,), None, None, eps)
+    return nrm * (scale.to(x.dtype) + 1) + shift.to(x.dtype)
+
+
+def int8_linear_modulated(x, modulation_scale, weight, weight_scale, bias=None,
+                          out_dtype=torch.bfloat16, convrot=False, convrot_groupsize=256):
+    """inference/src/backend_bindings.rs:329-405: int8_linear(x * (1 + s))."""
+    k = x.shape[-1]
+    if modulation_scale.numel() != k:
+        raise ValueError(f"modulation_scale must contain one batch-one row of {k} values, got "
+                         f"{modulation_scale.numel()}")
+    xm = x * (modulation_scale.to(x.dtype).reshape(-1) + 1)
+    return int8_linear(xm, weight, weight_scale, bias, out_dtype, convrot, convrot_groupsize)
+
+
+def int8_linear_rms_modulated(x, norm_weight, norm_eps, modulation_scale, weight, weight_scale,
+                              bias=None, out_dtype=torch.bfloat16, convrot=False,
+                              convrot_groupsize=256):
+    """inference/src/backend_bindings.rs:352-361: the modulated linear of
+    rms_norm(x, norm_weight, norm_eps)."""
+    k = x.shape[-1]
+    nrm = torch.nn.functional.rms_norm(x, (k,), norm_weight.to(x.dtype), float(norm_eps or 0.0))
+    return int8_linear_modulated(nrm, modulation_scale, weight, weight_scale, bias, out_dtype,
+                                 convrot, convrot_groupsize)
+
+
 def quantize_weight(w: torch.Tensor):
     """a12, inference/src/layout_complete.rs:119-159: offline per-output-channel
     weight quantisation = the row-wise quantiser applied to W [N, K]."""

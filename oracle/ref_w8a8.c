@@ -170,9 +170,9 @@ void ref_quantize_mxfp8_bf16(const uint16_t* x, int64_t rows, int64_t cols, uint
  * butterfly rows :253-261, its activations :1175-1200 and :1239-1267, and the
  * element step quant_div_float_to_float :53-57.  x holds the fp32 values of
  * the input elements; dtype is the input dtype code (0 f32, 1 f16, 2 bf16),
- * which sets every rounding to "T".  rotate = 0 restates the unfused
- * sequence instead: the ATen activation of inference/src/int8_linear.rs:37-97
- * (each op rounded to T) followed by the row quantiser. */
+ * which sets every rounding to "T".  With eager scales (kitchen = 0), or
+ * rotate = 0, the activation restates the unfused sequence instead: the ATen
+ * activation of inference/src/int8_linear.rs:37-97, each op rounded to T. */
 static float round_t(float v, int dtype) {
   if (dtype == 2) return round_bf16(v);
   if (dtype == 1) return (float)(_Float16)v;
@@ -200,9 +200,10 @@ void ref_fht256(float* v) {
   }
 }
 
-static float act_one(int act, int rot, int dtype, float g, float u) {
-  /* rot: fp32 throughout (the fused kernel); else each ATen op rounds to T */
-#define RT(v) (rot ? (v) : round_t((v), dtype))
+static float act_one(int act, int fp32, int dtype, float g, float u) {
+  /* fp32: no rounding (the fused kernel with kitchen scales); else each ATen
+   * op rounds to T (the eager route) */
+#define RT(v) (fp32 ? (v) : round_t((v), dtype))
   switch (act) {
     case 1: return RT(0.5f * g * (1.0f + tanhf(0.7978845608028654f * (g + 0.044715f * g * g * g))));
     case 2: return RT(RT(g / (1.0f + expf(-g))) * u);
@@ -217,11 +218,35 @@ static float act_one(int act, int rot, int dtype, float g, float u) {
 #undef RT
 }
 
+/* Row quantiser of the fused kernel on already pre-transformed fp32 values v
+ * (rotated first when rotate != 0). */
+static void quant_row(float* v, int64_t k, int dtype, int rotate, int kitchen, int8_t* q,
+                      float* scale) {
+  const float finite = dtype == 2 ? 3.3895313892515355e38f : dtype == 1 ? 65504.0f : 3.4028234663852886e38f;
+  const float tiny = dtype == 1 ? 6.103515625e-05f : 1.1754943508222875e-38f;
+  if (rotate) for (int64_t g = 0; g < k / 256; ++g) ref_fht256(v + g * 256);
+  float amax = 0.0f;
+  for (int64_t c = 0; c < k; ++c) amax = fmaxf(amax, fabsf(v[c]));
+  float s;
+  if (kitchen) {
+    s = fmaxf(fminf(amax, finite) * (1.0f / 127.0f), 1.0e-30f);
+  } else {
+    s = fmaxf(round_t(amax, dtype) / 127.0f, 1.0e-30f);
+  }
+  *scale = s;
+  float d = round_t(s, dtype);
+  if (d == 0.0f) d = tiny;
+  for (int64_t c = 0; c < k; ++c) {
+    float t = rintf(round_t(round_t(v[c], dtype) / d, dtype));
+    if (t < -128.0f) t = -128.0f;
+    if (t > 127.0f) t = 127.0f;
+    q[c] = (int8_t)t;
+  }
+}
+
 void ref_quantize_act_rot(const float* x, int dtype, int64_t rows, int64_t k, int64_t ldx,
                           int rotate, int act, const float* act_w, float eps, int kitchen,
                           int8_t* q, float* scale) {
-  const float finite = dtype == 2 ? 3.3895313892515355e38f : dtype == 1 ? 65504.0f : 3.4028234663852886e38f;
-  const float tiny = dtype == 1 ? 6.103515625e-05f : 1.1754943508222875e-38f;
   float* v = (float*)malloc(sizeof(float) * (size_t)k);
   for (int64_t r = 0; r < rows; ++r) {
     const float* xr = x + r * ldx;
@@ -231,29 +256,70 @@ void ref_quantize_act_rot(const float* x, int dtype, int64_t rows, int64_t k, in
       const float rstd = 1.0f / sqrtf(ss / (float)k + eps);
       for (int64_t c = 0; c < k; ++c) {
         const float t = xr[c] * rstd * act_w[c];
-        v[c] = rotate ? t : round_t(t, dtype);
+        v[c] = (rotate && kitchen) ? t : round_t(t, dtype);
       }
     } else {
-      for (int64_t c = 0; c < k; ++c) v[c] = act_one(act, rotate, dtype, xr[c], (act == 2 || act == 4) ? xr[k + c] : 0.0f);
+      for (int64_t c = 0; c < k; ++c) {
+        v[c] = act_one(act, rotate && kitchen, dtype, xr[c], (act == 2 || act == 4) ? xr[k + c] : 0.0f);
+      }
     }
-    if (rotate) for (int64_t g = 0; g < k / 256; ++g) ref_fht256(v + g * 256);
-    float amax = 0.0f;
-    for (int64_t c = 0; c < k; ++c) amax = fmaxf(amax, fabsf(v[c]));
-    float s;
-    if (kitchen) {
-      s = fmaxf(fminf(amax, finite) * (1.0f / 127.0f), 1.0e-30f);
-    } else {
-      s = fmaxf(round_t(amax, dtype) / 127.0f, 1.0e-30f);
+    quant_row(v, k, dtype, rotate, kitchen, q + r * k, scale + r);
+  }
+  free(v);
+}
+
+/* Modulations before the linear (mode 0 x*(1+s), 1 rms_norm(x,w)*(1+s),
+ * 2 layer_norm(x)*(1+s)+shift, 3 rms_norm(x)*(1+s)+shift).  kitchen: the
+ * reference CUDA adaln (KSRC backends/cuda/ops/adaln.cu:103-190): one-pass
+ * E[x], E[x^2] statistics, fp32 expression, one rounding.  eager: the ATen
+ * sequence (inference/src/backend_eager.rs:176-197, backend_bindings.rs:
+ * 329-405): two-pass variance, normalised row rounded, times T(1+s) rounded,
+ * plus shift rounded.  Row r uses modulation row r / mod_group. */
+void ref_quantize_modulated(const float* x, int dtype, int64_t rows, int64_t k, int mode,
+                            const float* norm_w, float eps, const float* mscale,
+                            const float* mshift, int64_t mod_group, int rotate, int kitchen,
+                            int8_t* q, float* scale) {
+  float* v = (float*)malloc(sizeof(float) * (size_t)k);
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* xr = x + r * k;
+    const float* sc = mscale + (r / mod_group) * k;
+    const float* sh = mshift ? mshift + (r / mod_group) * k : NULL;
+    float mean = 0.0f, rstd = 1.0f;
+    if (mode == 1 || mode == 3) {
+      float ss = 0.0f;
+      for (int64_t c = 0; c < k; ++c) ss += xr[c] * xr[c];
+      rstd = 1.0f / sqrtf(ss / (float)k + eps);
+    } else if (mode == 2) {
+      float s1 = 0.0f;
+      for (int64_t c = 0; c < k; ++c) s1 += xr[c];
+      mean = s1 / (float)k;
+      if (kitchen) {
+        float s2 = 0.0f;
+        for (int64_t c = 0; c < k; ++c) s2 += xr[c] * xr[c];
+        rstd = 1.0f / sqrtf(fmaxf(s2 / (float)k - mean * mean, 0.0f) + eps);
+      } else {
+        float s2 = 0.0f;
+        for (int64_t c = 0; c < k; ++c) s2 += (xr[c] - mean) * (xr[c] - mean);
+        rstd = 1.0f / sqrtf(s2 / (float)k + eps);
+      }
     }
-    scale[r] = s;
-    float d = round_t(s, dtype);
-    if (d == 0.0f) d = tiny;
     for (int64_t c = 0; c < k; ++c) {
-      float t = rintf(round_t(round_t(v[c], dtype) / d, dtype));
-      if (t < -128.0f) t = -128.0f;
-      if (t > 127.0f) t = 127.0f;
-      q[r * k + c] = (int8_t)t;
+      float y;
+      if (mode == 0) {
+        y = xr[c] * round_t(1.0f + sc[c], dtype);
+      } else if (mode == 1) {
+        y = round_t(xr[c] * rstd * norm_w[c], dtype) * round_t(1.0f + sc[c], dtype);
+      } else {
+        const float nrm = (xr[c] - mean) * rstd;
+        if (kitchen) {
+          y = fmaf(nrm, 1.0f + sc[c], sh[c]);
+        } else {
+          y = round_t(round_t(nrm, dtype) * round_t(1.0f + sc[c], dtype), dtype) + sh[c];
+        }
+      }
+      v[c] = round_t(y, dtype);
     }
+    quant_row(v, k, dtype, rotate, kitchen, q + r * k, scale + r);
   }
   free(v);
 }

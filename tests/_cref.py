@@ -26,6 +26,8 @@ def lib():
     so.ref_quantize_mxfp8_bf16.argtypes = [vp, i64, i64, vp, vp]
     so.ref_fht256.argtypes = [vp]
     so.ref_quantize_act_rot.argtypes = [vp, i32, i64, i64, i64, i32, i32, vp, f32, i32, vp, vp]
+    so.ref_quantize_modulated.argtypes = [vp, i32, i64, i64, i32, vp, f32, vp, vp, i64, i32, i32,
+                                          vp, vp]
     return so
 
 
@@ -55,4 +57,25 @@ def quantize_act_rot(x: torch.Tensor, rotate: bool, act=None, act_w=None, eps=0.
     s = torch.empty(m, dtype=torch.float32)
     lib().ref_quantize_act_rot(_p(xf), DTYPE[x.dtype], m, k, width, int(rotate), ACT[act], _p(w),
                                float(eps), int(kitchen), _p(q), _p(s))
+    return q, s
+
+
+MOD = {"scale": 0, "rms_scale": 1, "adaln": 2, "rms_adaln": 3}
+
+
+def quantize_modulated(x: torch.Tensor, mode: str, scale: torch.Tensor, shift=None, norm_w=None,
+                       eps=1e-6, rotate=False, kitchen=False):
+    """The fused modulation + (ConvRot) + row quantiser restated in C:
+    (q int8 [M, K], scale fp32 [M]); scale / shift are [G, K] rows covering
+    M / G x rows each."""
+    m, k = x.shape
+    sc = scale.to(torch.float32).reshape(-1, k).contiguous()
+    sh = shift.to(torch.float32).reshape(-1, k).contiguous() if shift is not None else None
+    w = norm_w.to(torch.float32).contiguous() if norm_w is not None else None
+    xf = x.to(torch.float32).contiguous()  # kept alive across the call
+    q = torch.empty(m, k, dtype=torch.int8)
+    s = torch.empty(m, dtype=torch.float32)
+    lib().ref_quantize_modulated(_p(xf), DTYPE[x.dtype], m, k,
+                                 MOD[mode], _p(w), float(eps), _p(sc), _p(sh), m // sc.shape[0],
+                                 int(rotate), int(kitchen), _p(q), _p(s))
     return q, s
