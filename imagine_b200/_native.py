@@ -78,6 +78,8 @@ SIGNATURES = {
     "w8a8_gemm_splitk_workspace_bytes": (_i64, [_i64, _i64]),
     "w8a8_gemm_dequant_splitk": (_i32, [_vp, _i64, _vp, _i64, _vp, _EP, _vp, _i32, _i64, _i64, _i64,
                                         _i64, _i32, _vp, _i64, _CFG, _vp]),
+    "w8a8_gemm_dequant_splitk_static": (_i32, [_vp, _i64, _vp, _i64, _vp, _EP, _vp, _i32, _i64,
+                                               _i64, _i64, _i64, _i32, _CFG, _vp]),
     "w8a8_gemm_s32": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _CFG, _vp]),
     "w8a8_dequantize_linear": (_i32, [_vp, _vp, _EP, _vp, _i32, _i64, _i64, _vp]),
     "w8a8_gemv_dequant": (_i32, [_vp, _vp, _vp, _EP, _vp, _i32, _i64, _i64, _i64, _vp]),

@@ -300,6 +300,36 @@ int w8a8_gemm_dequant_splitk(const int8_t* q, int64_t ldq, const int8_t* w, int6
   return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
 }
 
+int w8a8_gemm_dequant_splitk_static(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,
+                                    const float* xs, const w8a8_epilogue_t* epi, void* out,
+                                    int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                                    int split_k, const w8a8_gemm_config_t* cfg, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (split_k < 0) return fail(W8A8_ERR_VALUE, "split_k must be >= 0, got %d", split_k);
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (M == 0 || N == 0) return finish(0);
+  if ((K > 0 && (!q || !w)) || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldq < K || ldw < K || ldo < N) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  GemmArgs g{};
+  g.kind = 0;
+  g.a = q;
+  g.lda = ldq;
+  g.b = w;
+  g.ldb = ldw;
+  g.xs = xs;
+  g.epi = epi;
+  g.out = out;
+  g.out_dtype = out_dtype;
+  g.ldo = ldo;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.cfg = cfg;
+  g.split_k = split_k;
+  return finish(gemm_splitk_static_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
 int w8a8_gemm_s32(const int8_t* q, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
                   const w8a8_gemm_config_t* cfg, void* stream) {
   if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");

@@ -57,6 +57,8 @@ int gemm_launch(const GemmArgs& args, cudaStream_t stream);
 // arrival counter per (128 x 128 tile, epilogue warp).
 int64_t splitk_acc_bytes(int64_t M, int64_t N);
 int64_t splitk_workspace_bytes(int64_t M, int64_t N);
+// gemm_launch on the library's fixed split-K scratch (gemm_splitk_static.cu).
+int gemm_splitk_static_launch(GemmArgs g, cudaStream_t stream);
 
 int dequant_launch(const int32_t* acc, const float* xs, const w8a8_epilogue_t* epi, void* out,
                    int out_dtype, int64_t M, int64_t N, cudaStream_t stream);

@@ -214,6 +214,29 @@ int w8a8_gemm_dequant_splitk(const int8_t* q, int64_t ldq, const int8_t* w, int6
                              void* workspace, int64_t workspace_bytes,
                              const w8a8_gemm_config_t* cfg, void* stream);
 
+/* ---- the same split-K GEMM for callers that cannot allocate --------------
+ * No counterpart in the reference.  Some callers cannot hand the library a
+ * workspace: a plugin host whose enqueue call passes no workspace pointer, a
+ * serving loop that has frozen its memory pool after warm-up and may not call
+ * cudaMalloc again, or a binding from another language with no device
+ * allocator of its own.  This entry point takes the arguments of
+ * w8a8_gemm_dequant_splitk minus the workspace, returns the same results, and
+ * allocates nothing: its scratch is an array of
+ * W8A8_SPLITK_STATIC_SCRATCH_BYTES (8 MiB) built into the library, one per
+ * device.  Shapes whose scratch (w8a8_gemm_splitk_workspace_bytes(M, N):
+ * M * N * 4 bytes plus counters, e.g. up to 512 x 3072 or 256 x 6144) does not
+ * fit are rejected with W8A8_ERR_VALUE and a message.  The first call on a
+ * device, with that device current, looks the array up
+ * (cudaGetSymbolAddress); make it before any stream capture.  Each call clears
+ * the part of the array it uses on `stream` before the GEMM.  All calls share
+ * the array: calls that overlap on the GPU (other streams, other threads)
+ * race with each other. */
+#define W8A8_SPLITK_STATIC_SCRATCH_BYTES (8ll << 20)
+int w8a8_gemm_dequant_splitk_static(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,
+                                    const float* xs, const w8a8_epilogue_t* epi, void* out,
+                                    int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                                    int split_k, const w8a8_gemm_config_t* cfg, void* stream);
+
 int w8a8_gemm_s32(const int8_t* q, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
                   const w8a8_gemm_config_t* cfg, void* stream);
 
