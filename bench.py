@@ -37,7 +37,8 @@ WORKLOAD = {"workload": "mmdit_mlp_up_w8a8_linear", "M": M, "K": K, "N": N,
             "x": "bf16 N(0,1)", "w": "int8 per-channel from bf16 N(0,0.02)",
             "epilogue": "per-token x per-channel dequant + bias + gelu_tanh -> bf16",
             "quantiser": "per-token dynamic absmax (eager numerics)",
-            "l2": "flushed (256 MiB write) before every timed step"}
+            "l2": "flushed before every timed step: 256 MiB write, then a 256 MiB read so no "
+                  "dirty lines of the flush remain"}
 METRIC = "W8A8 linear TOPS (% int8 peak)"
 
 
@@ -144,7 +145,15 @@ def run_ours(args, rank, world, local_rank):
     xs = torch.empty((M,), dtype=torch.float32, device=dev)
     y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    clean = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     ep = _epilogue(ws, bias, None, None, "eager", "gelu_tanh", N, N)
+
+    def flush_l2():
+        # write 256 MiB (evicts everything), then read another 256 MiB so the
+        # written lines are back in HBM: the timed kernels start on a cold L2
+        # that holds no dirty lines of the flush itself
+        flush.zero_()
+        clean.sum()
     stream = torch.cuda.current_stream(dev)
     sp = _stream(dev)
 
@@ -157,7 +166,7 @@ def run_ours(args, rank, world, local_rank):
                                             _vp(y), NAT.BF16, N, M, N, K, None, sp))
 
     for _ in range(args.warmup):
-        flush.zero_()
+        flush_l2()
         quant()
         gemm()
     torch.cuda.synchronize()
@@ -173,7 +182,7 @@ def run_ours(args, rank, world, local_rank):
         sampler.start()
         time.sleep(0.3)
     for i in range(args.steps):
-        flush.zero_()
+        flush_l2()
         ev[i][0].record(stream)
         quant()
         ev[i][1].record(stream)

@@ -11,8 +11,8 @@ Mirrors the reference's INT8 autotuner (inference/src/autotuning.rs:86-268):
 * the winner is the lexicographic minimum of the quantile triples, first
   candidate on ties (Python ``min`` semantics, autotuning.rs:118-126).
 
-The candidates are this library's configurations (block_n, group_m, max_ctas)
-instead of Triton block shapes.  Timing goes through the ``BenchmarkDevice``
+The candidates are this library's configurations (block_n, group_m, max_ctas,
+cta_group) instead of Triton block shapes.  Timing goes through the ``BenchmarkDevice``
 protocol so the policy is testable with a fake clock on the CPU.
 """
 from __future__ import annotations
@@ -21,14 +21,16 @@ import math
 from dataclasses import dataclass, field
 from typing import Callable, Dict, List, Optional, Protocol, Sequence, Tuple
 
-# (block_n, group_m, max_ctas); max_ctas 0 = one persistent CTA per SM
-GEMM_CONFIGS: Tuple[Tuple[int, int, int], ...] = (
-    (256, 8, 0),
-    (256, 4, 0),
-    (256, 16, 0),
-    (128, 8, 0),
-    (128, 16, 0),
-    (256, 8, 132),
+# (block_n, group_m, max_ctas, cta_group); max_ctas 0 = one persistent CTA
+# (pair) per SM; cta_group 2 = CTA pairs with 2-SM MMAs on 256-row tiles
+GEMM_CONFIGS: Tuple[Tuple[int, ...], ...] = (
+    (256, 8, 0, 1),
+    (256, 4, 0, 1),
+    (256, 16, 0, 1),
+    (128, 8, 0, 1),
+    (128, 16, 0, 1),
+    (256, 8, 132, 1),
+    (256, 8, 0, 2),
 )
 
 
@@ -125,12 +127,12 @@ class ConfigRejected(Exception):
 
 @dataclass
 class GemmAutotuner:
-    configs: Tuple[Tuple[int, int, int], ...] = GEMM_CONFIGS
+    configs: Tuple[Tuple[int, ...], ...] = GEMM_CONFIGS
     cache: Dict[tuple, int] = field(default_factory=dict)
     best_config: Optional[int] = None
     last_timings: Optional[List[List[float]]] = None
 
-    def select(self, key: tuple, bench: Callable[[int, Tuple[int, int, int]], List[float]]) -> int:
+    def select(self, key: tuple, bench: Callable[[int, Tuple[int, ...]], List[float]]) -> int:
         if key in self.cache:
             index = self.cache[key]
         else:
@@ -163,8 +165,8 @@ def tuner(kernel: str) -> GemmAutotuner:
     return _TUNERS.setdefault(kernel, GemmAutotuner())
 
 
-def tune_gemm(kernel: str, key: tuple, run: Callable[[Tuple[int, int, int]], None],
-              device: Optional[BenchmarkDevice] = None) -> Tuple[int, int, int]:
+def tune_gemm(kernel: str, key: tuple, run: Callable[[Tuple[int, ...]], None],
+              device: Optional[BenchmarkDevice] = None) -> Tuple[int, ...]:
     """Pick (and cache) the configuration for `key`; `run(cfg)` launches the
     GEMM once with that configuration (raising ValueError if it is rejected)."""
     dev = device or CudaBenchmark()

@@ -50,8 +50,8 @@ def _code(dtype: torch.dtype) -> int:
 
 
 def _config(config) -> Optional[N.GemmConfig]:
-    if config is None:
-        return None
+    if config is None or config == "auto":
+        return config
     if isinstance(config, N.GemmConfig):
         return config
     bn, gm, ctas, cg = (tuple(config) + (0, 0, 0, 0))[:4]
@@ -59,7 +59,8 @@ def _config(config) -> Optional[N.GemmConfig]:
 
 
 def _cfg_ptr(cfg):
-    return ctypes.byref(cfg) if cfg is not None else None
+    # "auto" outside int8_linear's GEMM: the built-in heuristic
+    return ctypes.byref(cfg) if isinstance(cfg, N.GemmConfig) else None
 
 
 # --------------------------------------------------------------------------
@@ -422,10 +423,33 @@ def _splitk_scratch(dev: torch.device, nbytes: int) -> torch.Tensor:
     return buf
 
 
+def _autotuned_config(q, w, xs, ep, out, out_dtype, m, n, k, stream):
+    """config="auto": the tile configuration the autotuner picks for this
+    shape and epilogue (timed once per key, then cached), mirroring the
+    reference's Int8Autotuner use (inference/src/backend_triton_int8.rs:365-449)."""
+    from . import autotune
+
+    key = (m, n, k, "int8", "int8", str(out_dtype), int(ep.ws_numel == 1), int(ep.dequant_order),
+           int(ep.activation), ep.residual is not None, ep.bias is not None)
+
+    def run(cfg):
+        c = _config(cfg)
+        rc = N.LIB.w8a8_gemm_dequant(_vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep), _vp(out),
+                                     _code(out_dtype), n, m, n, k, ctypes.byref(c), stream)
+        if rc == N.ERR_VALUE:
+            raise ValueError(N.LIB.w8a8_last_error().decode(errors="replace"))
+        N.check(rc)
+
+    return _config(autotune.tune_gemm("int8_dequant", key, run, autotune.CudaBenchmark(out.device)))
+
+
 def _gemm_dequant(q, w, xs, ep, out, out_dtype, m, n, k, cfg, split_k, stream):
     """w8a8_gemm_dequant, or its split-K form when the 128 x 128 tiles of a
     few-row shape would leave SMs idle (or splits were asked for)."""
     dev = out.device
+    if cfg == "auto":
+        cfg = _autotuned_config(q, w, xs, ep, out, out_dtype, m, n, k, stream)
+        split_k = 1 if split_k is None else split_k
     use_split = split_k is not None and split_k > 1
     if split_k is None and m > 0 and n % 4 == 0 and k >= 1024:
         tiles = -(-m // 128) * -(-n // 128)
@@ -456,7 +480,8 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     ``dequant`` / ``scale_mode`` choose which of the reference routes' numerics
     to reproduce (default: the eager route, bit-exact); ``output_act`` applies
     GELU-tanh in the epilogue (the MLP-up fusion).  ``config`` is an optional
-    ``(block_n, group_m, max_ctas, cta_group)`` tile configuration.
+    ``(block_n, group_m, max_ctas, cta_group)`` tile configuration, or
+    ``"auto"`` to let the autotuner time the candidates once per shape.
     ``split_k``: None lets few-row shapes (whose tiles leave SMs idle) split K
     across CTAs, 1 turns that off, n > 1 asks for n splits; results are the
     same bit for bit either way.

@@ -39,12 +39,19 @@ def main():
     x = torch.randn(a.m, a.k, generator=g).to(torch.bfloat16).to(dev)
     cfg = (a.block_n, 8, 0, a.cta_group)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev) if a.time else None
+    clean = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev) if a.time else None
     times = []
 
     def run(fn):
         for _ in range(a.iters):
             if flush is not None:
+                # a ~100 us GPU sleep first gives the host time to enqueue the
+                # flush, the events and the launch, so no host work lands inside
+                # the timed window; the flush writes 256 MiB and reads another
+                # 256 MiB (cold L2 with no dirty lines left by the flush)
+                torch.cuda._sleep(200000)
                 flush.zero_()
+                clean.sum()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
                 fn()
@@ -106,7 +113,10 @@ def main():
         t = sorted(times)[len(times) // 2]
         ops = 2.0 * a.m * a.n * a.k
         msg += f" median_ms={t:.4f}"
-        if a.kernel not in ("quantize", "convrot"):
+        if a.kernel == "gemv":
+            nbytes = a.n * a.k + 2 * (a.m * a.k + a.m * a.n) + 4 * a.n
+            msg += f" GB/s={nbytes / t / 1e6:.1f}"
+        elif a.kernel not in ("quantize", "convrot"):
             msg += f" TOPS={ops / t / 1e9:.1f}"
         else:
             msg += f" GB/s={(a.m * a.k * 3 + 4 * a.m) / t / 1e6:.1f}"

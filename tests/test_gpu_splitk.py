@@ -118,3 +118,20 @@ def test_splitk_scratch_errors():
     with pytest.raises(ValueError, match="scratch"):
         _splitk(q, xs.reshape(-1), wq.to(cuda()), ws.to(cuda()), b.to(cuda()), torch.bfloat16, 4,
                 small)
+
+
+def test_autotuned_config_is_bit_identical():
+    """config="auto" times the candidate configurations once per shape (the
+    reference's autotuner policy) and the tuned launch gives the same bytes."""
+    m, k, n = 384, 3072, 1536
+    x, wq, ws, b = _case(m, k, n, 13)
+    args = (x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda()))
+    want = W().int8_linear(*args)
+    got = W().int8_linear(*args, config="auto")
+    again = W().int8_linear(*args, config="auto")  # cached choice
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    assert torch.equal(again.view(torch.int16), want.view(torch.int16))
+    from imagine_b200 import autotune
+
+    t = autotune.tuner("int8_dequant")
+    assert t.best_config is not None and len(t.last_timings) == len(autotune.GEMM_CONFIGS)
