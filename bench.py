@@ -203,8 +203,7 @@ def run_ours(args, rank, world, local_rank):
     y_pin = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
     e2e_steps = max(3, min(args.steps, 10))
     for _ in range(2):
-        yd = W.int8_linear(x_pin.to(dev, non_blocking=True), wq, ws, bias, output_act="gelu_tanh")
-        y_pin.copy_(yd, non_blocking=True)
+        W.int8_linear_host(x_pin, wq, ws, bias, out=y_pin, output_act="gelu_tanh")
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -212,8 +211,7 @@ def run_ours(args, rank, world, local_rank):
         torch.distributed.barrier()
     e0.record(stream)
     for _ in range(e2e_steps):
-        yd = W.int8_linear(x_pin.to(dev, non_blocking=True), wq, ws, bias, output_act="gelu_tanh")
-        y_pin.copy_(yd, non_blocking=True)
+        W.int8_linear_host(x_pin, wq, ws, bias, out=y_pin, output_act="gelu_tanh")
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
@@ -326,7 +324,7 @@ def main():
         },
         "e2e": {"value": e2e_tops, "unit": "TOPS", "h2d_bytes_per_step": M * K * 2,
                 "d2h_bytes_per_step": M * N * 2, "ms_per_step": r["e2e_ms"],
-                "path": "imagine_b200.int8_linear on a pinned host X, result copied to pinned host"},
+                "path": "imagine_b200.int8_linear_host: pinned host X in, pinned host Y out, 4 row blocks with uploads, kernels and downloads overlapped on three streams"},
         "gpu_launches": 2 * args.steps,
         "clocks": r["clocks"],
     }

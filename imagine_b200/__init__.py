@@ -12,12 +12,16 @@ _OPS = (
     "int8_gemm_s32",
     "int8_gemv",
     "int8_linear",
+    "int8_linear_host",
     "quantize_int8_rowwise",
     "quantize_int8_rowwise_convrot",
     "quantize_int8_rowwise_modulated",
     "int8_linear_modulated",
     "int8_linear_rms_modulated",
     "adaln_int8_linear",
+    "rms_rope",
+    "pack_weight_tiles",
+    "TiledInt8Weight",
     "quantize_per_tensor_fp8",
     "quantize_weight",
     "row_absmax",

@@ -24,7 +24,7 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libw8a8.so")
 
 SOURCES = ["api.cu", "quantize.cu", "convrot.cu", "gemm_sm100.cu", "gemm_splitk_static.cu", "gemv.cu",
-           "mxfp8.cu"]
+           "mxfp8.cu", "rope.cu"]
 HEADERS = ["sm100_ptx.cuh", "epilogue.cuh", "quant_common.cuh", "w8a8_internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -80,9 +80,41 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+SHIM = os.path.join(PKG, "libimagine_kitchen_w8a8.so")
+
+
+def build_shim(force: bool = False) -> str:
+    """The imagine_kitchen_call front end (csrc/kitchen_shim.cpp): compiled with
+    g++ against the LibTorch headers of the installed torch (the at::Tensor
+    handles the reference's crate passes), linked to libw8a8.so by rpath."""
+    import torch
+
+    src = os.path.join(CSRC, "kitchen_shim.cpp")
+    deps = [src, os.path.join(ROOT, "include", "w8a8.h"), LIB]
+    if not force and os.path.exists(SHIM) and os.path.getmtime(SHIM) >= _newest(deps):
+        return SHIM
+    tdir = os.path.dirname(torch.__file__)
+    tinc = os.path.join(tdir, "include")
+    tlib = os.path.join(tdir, "lib")
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(nvcc())), "include")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = SHIM + ".tmp"
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-fvisibility=hidden",
+           "-I", tinc, "-I", os.path.join(tinc, "torch", "csrc", "api", "include"), "-I", cuda_inc,
+           src, "-o", tmp, "-L", PKG, "-l:libw8a8.so", "-L", tlib, "-lc10", "-lc10_cuda", "-ltorch_cpu",
+           f"-Wl,-rpath,$ORIGIN:{tlib}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"kitchen shim build failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, SHIM)
+    return SHIM
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true", help="print ptxas resource usage")
     a = ap.parse_args()
     print(build(force=a.force, verbose=a.verbose))
+    print(build_shim(force=a.force))

@@ -202,6 +202,31 @@ int w8a8_quantize_rowwise_modulated(const void* x, int x_dtype, int64_t rows, in
                                         scale_mode, static_cast<cudaStream_t>(stream)));
 }
 
+int w8a8_rms_rope(const void* q, const void* k, void* q_out, void* k_out, int dtype, int64_t rows,
+                  int64_t heads, int64_t head_dim, int64_t ldq, int64_t ldk, int64_t ldqo,
+                  int64_t ldko, const float* freqs, int64_t freq_rows, const void* q_scale,
+                  const void* k_scale, float eps, void* stream) {
+  if (rows < 0 || heads < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(dtype)) return fail(W8A8_ERR_VALUE, "dtype code %d is not floating", dtype);
+  if (head_dim != 64 && head_dim != 128 && head_dim != 192 && head_dim != 256) {
+    return fail(W8A8_ERR_VALUE, "rms_rope supports head_dim 64, 128, 192 or 256, got %lld",
+                static_cast<long long>(head_dim));
+  }
+  if (rows == 0 || heads == 0) return finish(0);
+  if (rows * heads > (1ll << 40) || heads > 0x7fffffffLL) return fail(W8A8_ERR_VALUE, "shape too large");
+  if (!q || !q_out || !freqs || !q_scale) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (k && (!k_out || !k_scale)) return fail(W8A8_ERR_VALUE, "k needs k_out and k_scale");
+  if (freq_rows < 1) return fail(W8A8_ERR_VALUE, "freqs must have at least one row");
+  if (ldq < heads * head_dim || ldqo < heads * head_dim ||
+      (k && (ldk < heads * head_dim || ldko < heads * head_dim))) {
+    return fail(W8A8_ERR_VALUE, "row stride smaller than heads * head_dim");
+  }
+  if (reinterpret_cast<uintptr_t>(freqs) & 15u) return fail(W8A8_ERR_VALUE, "freqs must be 16-byte aligned");
+  return finish(rms_rope_launch(q, k, q_out, k_out, dtype, rows, static_cast<int>(heads),
+                                static_cast<int>(head_dim), ldq, ldk, ldqo, ldko, freqs, freq_rows,
+                                q_scale, k_scale, eps, static_cast<cudaStream_t>(stream)));
+}
+
 int w8a8_row_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
                     float* amax, void* stream) {
   if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
@@ -328,6 +353,55 @@ int w8a8_gemm_dequant_splitk_static(const int8_t* q, int64_t ldq, const int8_t* 
   g.cfg = cfg;
   g.split_k = split_k;
   return finish(gemm_splitk_static_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
+int64_t w8a8_weight_tiles_bytes(int64_t N, int64_t K) {
+  if (N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  return weight_tiles_bytes(N, K);
+}
+
+int w8a8_pack_weight_tiles(const int8_t* w, int64_t ldw, int64_t N, int64_t K, int8_t* tiles,
+                           void* stream) {
+  if (N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (N == 0 || K == 0) return finish(0);
+  if (!w || !tiles) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldw < K) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  if (reinterpret_cast<uintptr_t>(tiles) & 15u) return fail(W8A8_ERR_VALUE, "tiles must be 16-byte aligned");
+  return finish(pack_weight_tiles_launch(w, ldw, N, K, tiles, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_gemm_dequant_tiled(const int8_t* q, int64_t ldq, const int8_t* tiles, const float* xs,
+                            const w8a8_epilogue_t* epi, void* out, int out_dtype, int64_t ldo,
+                            int64_t M, int64_t N, int64_t K, int split_k, void* workspace,
+                            int64_t workspace_bytes, const w8a8_gemm_config_t* cfg,
+                            void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (split_k < 0) return fail(W8A8_ERR_VALUE, "split_k must be >= 0, got %d", split_k);
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (M == 0 || N == 0) return finish(0);
+  if (!q || !tiles || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldq < K || ldo < N) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  GemmArgs g{};
+  g.kind = 0;
+  g.a = q;
+  g.lda = ldq;
+  g.b = tiles;
+  g.ldb = 128;
+  g.xs = xs;
+  g.epi = epi;
+  g.out = out;
+  g.out_dtype = out_dtype;
+  g.ldo = ldo;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.cfg = cfg;
+  g.split_k = workspace ? split_k : 1;
+  g.workspace = workspace;
+  g.workspace_bytes = workspace_bytes;
+  g.b_tiled = 1;
+  return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
 }
 
 int w8a8_gemm_s32(const int8_t* q, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,

@@ -79,6 +79,8 @@ struct EpilogueParams {
   const uint8_t* sfa;      // MXFP8: e8m0 scales of A, blocked layout
   const uint8_t* sfb;      // MXFP8: e8m0 scales of B, blocked layout
   int sf_ncb;              // MXFP8: 4-wide column blocks per scale row = ceil(K / 128)
+  int b_tiles_kb;          // B pre-tiled (0: row-major): 128 x 128-byte tiles, this many
+                           // K-blocks per 128-row block
 };
 
 // Value of one output element before the optional residual, already rounded

@@ -449,7 +449,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (CG == 1) {
             mbar_arrive_expect_tx(&full[s], C::kStageBytes + C::kSFBytes);
             tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kBK, a_row);
-            tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kBK, b_row);
+            if (ep.b_tiles_kb) {
+              // pre-tiled B (128-column tiles): tile (nb, kb) is 16 KB contiguous
+              tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], 0, (nb * ep.b_tiles_kb + kb) * 128);
+            } else {
+              tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kBK, b_row);
+            }
             if constexpr (KIND == 2) {
               // blocked scale layout: 512-byte block (row/128, kb) at
               // ((row/128) * ncb + kb) * 512; blocks outside the buffers the
@@ -839,6 +844,7 @@ EpilogueParams to_params(const GemmArgs& g) {
   ep.sfa = static_cast<const uint8_t*>(g.sfa);
   ep.sfb = static_cast<const uint8_t*>(g.sfb);
   ep.sf_ncb = static_cast<int>((g.K + 127) / 128);
+  ep.b_tiles_kb = g.b_tiled ? static_cast<int>((g.K + kBK - 1) / kBK) : 0;
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   ep.vec_ws = ep.ws && a16(ep.ws);
   ep.vec_bias = ep.bias && a16(ep.bias);
@@ -928,8 +934,15 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
   CUtensorMap ma, mb, md, mw;
   bool ok = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.a, g.K, g.M, g.lda, kBK, kBM,
                         CU_TENSOR_MAP_SWIZZLE_128B);
-  ok = ok && make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.b, g.K, g.N, g.ldb, kBK,
-                         static_cast<uint32_t>(bn / cg), CU_TENSOR_MAP_SWIZZLE_128B);
+  if (g.b_tiled) {
+    // [ceil(N/128) * ceil(K/128) * 128 rows, 128 bytes]
+    const int64_t rows = (g.N + 127) / 128 * ((g.K + kBK - 1) / kBK) * 128;
+    ok = ok && make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.b, kBK, rows, kBK, kBK, 128,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    ok = ok && make_map_2d(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.b, g.K, g.N, g.ldb, kBK,
+                           static_cast<uint32_t>(bn / cg), CU_TENSOR_MAP_SWIZZLE_128B);
+  }
   CUtensorMapDataType dt;
   if constexpr (std::is_same<OutT, float>::value) dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   else if constexpr (std::is_same<OutT, int32_t>::value) dt = CU_TENSOR_MAP_DATA_TYPE_INT32;
@@ -1037,6 +1050,16 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   // slower on the 5600-row shapes (its B traffic saving does not pay while the
   // epilogue bounds the tile rate).
   if (cg == 0) cg = 1;
+  if (g.b_tiled) {
+    // pre-tiled weights: 128-column tiles, one CTA per tile, tcgen05 path only
+    if (!(g.kind == 0 && g.K > 0 && g.K % 16 == 0 && g.lda % 16 == 0 && a16(g.a) && a16(g.b) &&
+          a16(g.out) && (g.ldo * out_bytes) % 16 == 0)) {
+      set_error("pre-tiled weights need K %% 16 == 0 and 16-byte aligned operands");
+      return W8A8_ERR_VALUE;
+    }
+    bn = 128;
+    cg = 1;
+  }
   if (bn == 128) cg = 1;  // pairs are built for 256-column tiles
   // Split-K (int8 with a dequant epilogue, scratch given): when one split
   // per 128-column tile leaves SMs idle, cut K so tiles x splits fills them,

@@ -431,4 +431,59 @@ int quantize_fp8_tensor_launch(const void* x, int x_dtype, int64_t numel, const 
   return 0;
 }
 
+// ---- pre-tiled weights for few-row GEMMs -----------------------------------
+// tiles[((nb * KB + kb) * 128 + r) * 128 + c] = W[nb * 128 + r][kb * 128 + c]
+// (zero outside N x K): every 128 x 128-byte TMA tile of B is one contiguous
+// 16 KB block, so a GEMM streaming W from HBM reads it sequentially.
+namespace {
+__global__ void __launch_bounds__(256) pack_weight_tiles_kernel(const int8_t* __restrict__ w,
+                                                                int64_t ldw, int64_t N, int64_t K,
+                                                                int64_t kb_count, int vec,
+                                                                int8_t* __restrict__ tiles,
+                                                                int64_t chunks) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= chunks) return;
+  const int64_t row = i >> 3;  // tiled row (128 bytes = 8 chunks of 16)
+  const int c16 = static_cast<int>(i & 7);
+  const int64_t blk = row >> 7;  // (nb * KB + kb)
+  const int r = static_cast<int>(row & 127);
+  const int64_t nb = blk / kb_count, kb = blk - nb * kb_count;
+  const int64_t n = nb * 128 + r;
+  const int64_t k0 = kb * 128 + c16 * 16;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (n < N && k0 < K) {
+    const int8_t* src = w + n * ldw + k0;
+    if (vec && k0 + 16 <= K) {
+      v = __ldg(reinterpret_cast<const uint4*>(src));
+    } else {
+      uint8_t b[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) b[j] = k0 + j < K ? static_cast<uint8_t>(src[j]) : 0;
+      v = *reinterpret_cast<const uint4*>(b);
+    }
+  }
+  reinterpret_cast<uint4*>(tiles)[i] = v;
+}
+}  // namespace
+
+int64_t weight_tiles_bytes(int64_t N, int64_t K) {
+  return (N + 127) / 128 * ((K + 127) / 128) * 128 * 128;
+}
+
+int pack_weight_tiles_launch(const int8_t* w, int64_t ldw, int64_t N, int64_t K, int8_t* tiles,
+                             cudaStream_t stream) {
+  const int64_t chunks = weight_tiles_bytes(N, K) / 16;
+  if (chunks == 0) return 0;
+  const int vec = (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && ldw % 16 == 0;
+  const int64_t grid = (chunks + 255) / 256;
+  pack_weight_tiles_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(
+      w, ldw, N, K, (K + 127) / 128, vec, tiles, chunks);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("weight tile packing launch failed: %s", cudaGetErrorString(e));
+    return W8A8_ERR_ACCELERATOR;
+  }
+  return 0;
+}
+
 }  // namespace w8a8

@@ -51,12 +51,19 @@ struct GemmArgs {
   int split_k;
   void* workspace;
   int64_t workspace_bytes;
+  // B in the pre-tiled layout of w8a8_pack_weight_tiles (kind 0 only)
+  int b_tiled;
 };
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);
 // Split-K scratch: int32 [M, N] partial sums (padded to 256 bytes), then one
 // arrival counter per (128 x 128 tile, epilogue warp).
 int64_t splitk_acc_bytes(int64_t M, int64_t N);
 int64_t splitk_workspace_bytes(int64_t M, int64_t N);
+// Pre-tiled weights: [ceil(N/128)][ceil(K/128)][128 rows][128 bytes], zero
+// padded (gemv.cu).
+int64_t weight_tiles_bytes(int64_t N, int64_t K);
+int pack_weight_tiles_launch(const int8_t* w, int64_t ldw, int64_t N, int64_t K, int8_t* tiles,
+                             cudaStream_t stream);
 // gemm_launch on the library's fixed split-K scratch (gemm_splitk_static.cu).
 int gemm_splitk_static_launch(GemmArgs g, cudaStream_t stream);
 
@@ -75,6 +82,12 @@ int quantize_mxfp8_launch(const void* x, int x_dtype, int64_t rows, int64_t cols
 
 int quantize_fp8_tensor_launch(const void* x, int x_dtype, int64_t numel, const float* scale,
                                uint8_t* out, cudaStream_t stream);
+
+// Q/K RMSNorm + interleaved RoPE (rope.cu); k may be NULL.
+int rms_rope_launch(const void* q, const void* k, void* q_out, void* k_out, int dtype,
+                    int64_t rows, int heads, int head_dim, int64_t ldq, int64_t ldk, int64_t ldqo,
+                    int64_t ldko, const float* freqs, int64_t freq_rows, const void* q_scale,
+                    const void* k_scale, float eps, cudaStream_t stream);
 
 // Error reporting (thread-local), implemented in api.cu.
 void set_error(const char* fmt, ...);

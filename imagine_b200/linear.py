@@ -13,6 +13,7 @@ inference/src/cuda_linear.rs:452-475, 586-600).
 from __future__ import annotations
 
 import ctypes
+import math
 from typing import Optional
 
 import torch
@@ -342,11 +343,66 @@ def adaln_int8_linear(x: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor,
                              dequant, output_act, aten)
 
 
-def quantize_weight(weight: torch.Tensor):
+def rms_rope(q: torch.Tensor, k: Optional[torch.Tensor], freqs_cis: torch.Tensor,
+             q_scale: torch.Tensor, k_scale: Optional[torch.Tensor] = None,
+             epsilon: float = 1e-6):
+    """Kitchen op ``rms_rope(q, k, freqs_cis, q_scale, k_scale, epsilon)``
+    (inference/src/models/qwen_image21/dit.rs:486-505; eager body
+    inference/src/backend_rope.rs:146-223): per-head RMSNorm with weight, then
+    the interleaved-pair rotation.  q / k: [..., S, H, D]; freqs_cis: fp32
+    [S, D/2, 2, 2] or with leading broadcast dimensions ([B, S, 1, D/2, 2, 2]).
+    Returns ``(q_out, k_out)`` (``k_out`` is None without k)."""
+    _cuda("q", q)
+    d = q.shape[-1]
+    heads = q.shape[-2]
+    q2 = q.reshape(-1, heads * d)
+    if q2.stride(-1) != 1:
+        q2 = q2.contiguous()
+    rows = q2.shape[0]
+    k2 = None
+    if k is not None:
+        _cuda("k", k, q.device)
+        if k.shape != q.shape or k.dtype != q.dtype:
+            raise ValueError("q and k must have the same shape and dtype")
+        k2 = k.reshape(-1, heads * d)
+        if k2.stride(-1) != 1:
+            k2 = k2.contiguous()
+        if k_scale is None:
+            raise ValueError("k needs k_scale")
+    f = freqs_cis.to(device=q.device, dtype=torch.float32).reshape(-1, d // 2, 2, 2).contiguous()
+    if f.shape[0] == 0 or rows % f.shape[0]:
+        raise ValueError(f"freqs_cis has {f.shape[0]} positions for {rows} token rows")
+    qs = q_scale.to(device=q.device, dtype=q.dtype).reshape(-1).contiguous()
+    ks = (k_scale.to(device=q.device, dtype=q.dtype).reshape(-1).contiguous()
+          if k is not None else None)
+    if qs.numel() != d or (ks is not None and ks.numel() != d):
+        raise ValueError(f"q_scale / k_scale must have head_dim = {d} elements")
+    qo = torch.empty_like(q2)
+    ko = torch.empty_like(k2) if k2 is not None else None
+    N.check(N.LIB.w8a8_rms_rope(
+        _vp(q2), _vp(k2), _vp(qo), _vp(ko), _code(q.dtype), rows, heads, d, q2.stride(0),
+        k2.stride(0) if k2 is not None else 0, qo.stride(0), ko.stride(0) if ko is not None else 0,
+        _vp(f), f.shape[0], _vp(qs), _vp(ks), float(epsilon), _stream(q.device)))
+    return qo.reshape(q.shape), (ko.reshape(k.shape) if ko is not None else None)
+
+
+def quantize_weight(weight: torch.Tensor, convrot: bool = False, convrot_groupsize: int = 256, *,
+                    scale_mode: str = "eager"):
     """Offline per-output-channel weight quantisation
     (inference/src/layout_complete.rs:119-159 TensorWiseINT8Layout.from_float):
-    returns ``(w_q int8 [N, K], ws fp32 [N])``."""
-    q, s = quantize_int8_rowwise(weight)
+    returns ``(w_q int8 [N, K], ws fp32 [N])``.  ``convrot=True`` is the ConvRot
+    weight form (``quantize_int8_convrot_weight``, inference/src/convrot.rs:
+    378-435): each row rotated by the normalised Hadamard matrix per 256-group
+    of K, then quantised -- the fused kernel the reference's CUDA route picks
+    for these widths (its ``rowwise64`` path, convrot.rs:345-376)."""
+    if not convrot:
+        q, s = quantize_int8_rowwise(weight, scale_mode=scale_mode)
+        return q, s.reshape(-1)
+    if weight.dim() != 2:
+        raise ValueError("ConvRot INT8 weight quantization expects a 2D weight tensor")
+    if convrot_groupsize != 256:
+        raise ValueError("ConvRot weights are supported for group size 256")
+    q, s = quantize_int8_rowwise_convrot(weight.contiguous(), 256, scale_mode=scale_mode)
     return q, s.reshape(-1)
 
 
@@ -409,6 +465,48 @@ def _hadamard(size: int, device, dtype) -> torch.Tensor:
     return _HADAMARD[key]
 
 
+class TiledInt8Weight:
+    """An int8 weight [N, K] in the pre-tiled layout of w8a8_pack_weight_tiles
+    (128-row x 128-byte tiles, each 16 KB contiguous): what few-row GEMMs
+    stream from HBM.  int8_linear takes it in place of the [N, K] tensor."""
+
+    def __init__(self, tiles: torch.Tensor, n: int, k: int):
+        self.tiles, self.n, self.k = tiles, n, k
+
+    @property
+    def shape(self):
+        return torch.Size((self.n, self.k))
+
+    @property
+    def device(self):
+        return self.tiles.device
+
+    @property
+    def dtype(self):
+        return torch.int8
+
+    def dim(self):
+        return 2
+
+    def is_contiguous(self):
+        return True
+
+
+def pack_weight_tiles(weight: torch.Tensor) -> TiledInt8Weight:
+    """Pack an int8 [N, K] weight once (offline) into the pre-tiled layout."""
+    _cuda("weight", weight)
+    if weight.dim() != 2 or weight.dtype != torch.int8:
+        raise ValueError("weight must be a 2-D int8 tensor [N, K]")
+    n, k = weight.shape
+    if weight.stride(-1) != 1:
+        weight = weight.contiguous()
+    tiles = torch.empty(int(N.LIB.w8a8_weight_tiles_bytes(n, k)), dtype=torch.int8,
+                        device=weight.device)
+    N.check(N.LIB.w8a8_pack_weight_tiles(_vp(weight), weight.stride(0) if n else k, n, k,
+                                         _vp(tiles), _stream(weight.device)))
+    return TiledInt8Weight(tiles, n, k)
+
+
 _SPLITK_SCRATCH: dict = {}
 
 
@@ -447,6 +545,16 @@ def _gemm_dequant(q, w, xs, ep, out, out_dtype, m, n, k, cfg, split_k, stream):
     """w8a8_gemm_dequant, or its split-K form when the 128 x 128 tiles of a
     few-row shape would leave SMs idle (or splits were asked for)."""
     dev = out.device
+    if isinstance(w, TiledInt8Weight):
+        cfg = None if cfg == "auto" else cfg
+        scratch = None
+        if split_k != 1 and m > 0 and n % 4 == 0:
+            scratch = _splitk_scratch(dev, int(N.LIB.w8a8_gemm_splitk_workspace_bytes(m, n)))
+        N.check(N.LIB.w8a8_gemm_dequant_tiled(
+            _vp(q), k, _vp(w.tiles), _vp(xs), ctypes.byref(ep), _vp(out), _code(out_dtype), n, m,
+            n, k, int(split_k or 0), _vp(scratch), scratch.numel() if scratch is not None else 0,
+            _cfg_ptr(cfg), stream))
+        return
     if cfg == "auto":
         cfg = _autotuned_config(q, w, xs, ep, out, out_dtype, m, n, k, stream)
         split_k = 1 if split_k is None else split_k
@@ -488,7 +596,8 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     """
     _cuda("x", x)
     dev = x.device
-    _cuda("weight", weight, dev)
+    tiled = isinstance(weight, TiledInt8Weight)
+    _cuda("weight", weight.tiles if tiled else weight, dev)
     if residual is not None and residual_scale is None:
         raise ValueError("int8_linear: residual requires residual_scale")
     out_dtype = out_dtype or x.dtype
@@ -532,6 +641,8 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
         x2 = x2.contiguous()
     m = x2.shape[0]
     w = weight if weight.is_contiguous() else weight.contiguous()
+    if tiled and k == 0:
+        raise ValueError("pre-tiled weights need K > 0")
     b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
     r = rs = None
     if residual is not None:
@@ -546,12 +657,12 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
         q, xs = quantize_int8_rowwise_convrot(x2, 256 if convrot else 0, input_act, input_act_weight,
                                               input_act_eps, scale_mode=scale_mode)
         xs = xs.reshape(-1)
-        if 1 <= m <= 2:
+        if 1 <= m <= 2 and not tiled:
             N.check(N.LIB.w8a8_gemv_dequant(_vp(q), _vp(w), _vp(xs), ctypes.byref(ep), _vp(out),
                                             _code(out_dtype), m, n, k, stream))
         else:
             _gemm_dequant(q, w, xs, ep, out, out_dtype, m, n, k, _config(config), split_k, stream)
-    elif 1 <= m <= 2 and k > 0 and m * k <= 32768:
+    elif 1 <= m <= 2 and k > 0 and m * k <= 32768 and not tiled:
         # a5: the AdaLN-modulation shape -- quantise and GEMV in one launch.
         N.check(N.LIB.w8a8_linear_small(_vp(x2), _code(x2.dtype), _vp(w), ctypes.byref(ep),
                                         SCALE_MODE[scale_mode], None, None, _vp(out),
@@ -565,6 +676,104 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
         cfg = _config(config)
         _gemm_dequant(q, w, xs, ep, out, out_dtype, m, n, k, cfg, split_k, stream)
     return out.reshape(*lead, n)
+
+
+class _HostPipeline:
+    """Per-device streams and reusable device buffers of int8_linear_host."""
+
+    def __init__(self, dev):
+        self.dev = dev
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        self.bufs: dict = {}
+
+    def buffer(self, name, shape, dtype):
+        t = self.bufs.get(name)
+        if t is None or t.dtype != dtype or t.numel() < math.prod(shape):
+            t = torch.empty(math.prod(shape), dtype=dtype, device=self.dev)
+            self.bufs[name] = t
+        return t[: math.prod(shape)].view(shape)
+
+
+_PIPELINES: dict = {}
+
+
+def int8_linear_host(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
+                     bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None, *,
+                     out_dtype: Optional[torch.dtype] = None, chunks: int = 4,
+                     dequant: str = "eager", scale_mode: str = "eager",
+                     output_act: Optional[str] = None) -> torch.Tensor:
+    """int8_linear on a host-resident activation with a host-resident result:
+    x [M, K] and ``out`` [M, N] in pinned host memory, weight / scales / bias on
+    the device.  Rows are processed in ``chunks`` blocks on three streams so the
+    upload of block i+1, the quantise + GEMM of block i and the download of
+    block i-1 overlap (the transfers, not the kernels, bound this call).
+    Results equal int8_linear's (plain linear: bias, dequant order, output
+    activation) row for row; returns ``out``.  The call returns after the last
+    download has completed."""
+    if x.is_cuda:
+        raise ValueError("int8_linear_host takes a host x; use int8_linear for device tensors")
+    dev = weight.device
+    _cuda("weight", weight)
+    if x.dim() != 2:
+        raise ValueError("x must be [M, K]")
+    m, k = x.shape
+    n = weight.shape[0]
+    out_dtype = out_dtype or x.dtype
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, pin_memory=True)
+    if out.shape != (m, n) or out.dtype != out_dtype or out.is_cuda:
+        raise ValueError("out must be a host [M, N] tensor of the output dtype")
+    if weight.dim() != 2 or weight.dtype != torch.int8 or weight.shape[1] != k:
+        raise ValueError(f"weight must be an int8 [N, {k}] tensor")
+    pipe = _PIPELINES.get(dev.index)
+    if pipe is None:
+        pipe = _PIPELINES[dev.index] = _HostPipeline(dev)
+    compute = torch.cuda.current_stream(dev)
+    stream = _stream(dev)
+    rows = max(1, -(-m // max(1, chunks)))
+    xd = pipe.buffer("x", (2, rows, k), x.dtype)
+    yd = pipe.buffer("y", (2, rows, n), out_dtype)
+    qd = pipe.buffer("q", (2, rows, k), torch.int8)
+    sd = pipe.buffer("s", (2, rows), torch.float32)
+    w = weight if weight.is_contiguous() else weight.contiguous()
+    ws = weight_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    if ws.numel() not in (1, n):
+        raise ValueError("INT8 weight scale must be scalar or per-output-channel")
+    b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
+    ep = _epilogue(ws, b, None, None, dequant, output_act, n, n)
+    up_done = [torch.cuda.Event() for _ in range(2)]
+    comp_done = [torch.cuda.Event() for _ in range(2)]
+    down_done = [torch.cuda.Event() for _ in range(2)]
+    for i, r0 in enumerate(range(0, m, rows)):
+        r1 = min(m, r0 + rows)
+        slot = i % 2
+        xs, ys = xd[slot, : r1 - r0], yd[slot, : r1 - r0]
+        with torch.cuda.stream(pipe.h2d):
+            if i >= 2:
+                pipe.h2d.wait_event(comp_done[slot])  # slot's previous x consumed
+            xs.copy_(x[r0:r1], non_blocking=True)
+            up_done[slot].record(pipe.h2d)
+        compute.wait_event(up_done[slot])
+        if i >= 2:
+            compute.wait_event(down_done[slot])  # slot's previous y downloaded
+        r = r1 - r0
+        qs, ss = qd[slot, :r], sd[slot, :r]
+        N.check(N.LIB.w8a8_quantize_rowwise(_vp(xs), _code(x.dtype), r, k, k, _vp(qs), k, _vp(ss),
+                                            SCALE_MODE[scale_mode], 0, 0, stream))
+        N.check(N.LIB.w8a8_gemm_dequant(_vp(qs), k, _vp(w), k, _vp(ss), ctypes.byref(ep), _vp(ys),
+                                        _code(out_dtype), n, r, n, k, None, stream))
+        comp_done[slot].record(compute)
+        with torch.cuda.stream(pipe.d2h):
+            pipe.d2h.wait_event(comp_done[slot])
+            out[r0:r1].copy_(ys, non_blocking=True)
+            down_done[slot].record(pipe.d2h)
+    # work queued on the caller's stream afterwards (and events recorded on
+    # it) comes after the last download
+    for ev in down_done:
+        compute.wait_event(ev)
+    pipe.d2h.synchronize()
+    return out
 
 
 def int8_gemm_s32(q: torch.Tensor, w: torch.Tensor, config=None) -> torch.Tensor:

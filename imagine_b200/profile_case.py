@@ -20,7 +20,7 @@ import imagine_b200 as W
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", choices=["gemm", "gemm_gelu", "gemm_s32", "quantize", "convrot",
-                                                       "gemv", "fp8_gemm", "mxfp8_gemm"],
+                                                       "gemv", "fp8_gemm", "mxfp8_gemm", "rms_rope"],
                     required=True)
     ap.add_argument("--m", type=int, default=5600)
     ap.add_argument("--k", type=int, default=3072)
@@ -65,6 +65,16 @@ def main():
         run(lambda: W.quantize_int8_rowwise(x))
     elif a.kernel == "convrot":
         run(lambda: W.quantize_int8_rowwise_convrot(x, 256))
+    elif a.kernel == "rms_rope":
+        # q and k of m tokens with k / 128 heads of 128
+        heads = a.k // 128
+        kk = torch.randn(a.m, a.k, generator=g).to(torch.bfloat16).to(dev)
+        ang = torch.rand(a.m, 64, generator=g) * 6.283
+        c, sn = torch.cos(ang), torch.sin(ang)
+        f = torch.stack([torch.stack([c, -sn], -1), torch.stack([sn, c], -1)], -2).to(dev)
+        sc = torch.ones(128, dtype=torch.bfloat16, device=dev)
+        qv, kv = x.view(a.m, heads, 128), kk.view(a.m, heads, 128)
+        run(lambda: W.rms_rope(qv, kv, f, sc, sc, 1e-6))
     else:
         w = (torch.randn(a.n, a.k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
         b = (torch.randn(a.n, generator=g) * 0.02).to(torch.bfloat16).to(dev)
@@ -113,10 +123,13 @@ def main():
         t = sorted(times)[len(times) // 2]
         ops = 2.0 * a.m * a.n * a.k
         msg += f" median_ms={t:.4f}"
-        if a.kernel == "gemv":
+        if a.kernel == "rms_rope":
+            nbytes = 2 * 2 * a.m * a.k * 2 + a.m * 64 * 16
+            msg += f" GB/s={nbytes / t / 1e6:.1f}"
+        elif a.kernel == "gemv":
             nbytes = a.n * a.k + 2 * (a.m * a.k + a.m * a.n) + 4 * a.n
             msg += f" GB/s={nbytes / t / 1e6:.1f}"
-        elif a.kernel not in ("quantize", "convrot"):
+        elif a.kernel not in ("quantize", "convrot", "rms_rope"):
             msg += f" TOPS={ops / t / 1e9:.1f}"
         else:
             msg += f" GB/s={(a.m * a.k * 3 + 4 * a.m) / t / 1e6:.1f}"

@@ -165,6 +165,23 @@ int w8a8_quantize_rowwise_modulated(const void* x, int x_dtype, int64_t rows, in
                                     int64_t mod_group, int group, int8_t* q, int64_t ldq,
                                     float* scale, int scale_mode, void* stream);
 
+/* ---- a8: Q/K RMSNorm + RoPE after the QKV projection ---------------------
+ * Replaces `rms_rope(q, k, freqs_cis, q_scale, k_scale, epsilon)` (call site
+ * inference/src/models/qwen_image21/dit.rs:486-505; eager body
+ * inference/src/backend_rope.rs:146-223; kernel KSRC
+ * backends/cuda/ops/rms_rope.cu:38-240) for the interleaved rotation over the
+ * whole head: per (token, head) row of D values, n = T(x * rsqrt(mean(x^2) +
+ * eps) * scale), then each pair (n[2i], n[2i+1]) -> (f00 n0 + f01 n1,
+ * f10 n0 + f11 n1) in fp32, rounded to T.  q / k: [rows, ld] with heads * D
+ * values per row (dtype F32/F16/BF16); freqs: fp32 [freq_rows, D/2, 2, 2]
+ * (16-byte aligned), row r uses freqs row r % freq_rows; q_scale / k_scale:
+ * [D] in the same dtype.  k may be NULL (q only); q_out may equal q.
+ * D: 64, 128, 192 or 256. */
+int w8a8_rms_rope(const void* q, const void* k, void* q_out, void* k_out, int dtype, int64_t rows,
+                  int64_t heads, int64_t head_dim, int64_t ldq, int64_t ldk, int64_t ldqo,
+                  int64_t ldko, const float* freqs, int64_t freq_rows, const void* q_scale,
+                  const void* k_scale, float eps, void* stream);
+
 /* ---- row-parallel (K-sharded) quantisation --------------------------------
  * No reference counterpart: the reference runs on one GPU.  A K-sharded
  * activation needs the absmax of the whole row before any shard can be
@@ -213,6 +230,24 @@ int w8a8_gemm_dequant_splitk(const int8_t* q, int64_t ldq, const int8_t* w, int6
                              int64_t ldo, int64_t M, int64_t N, int64_t K, int split_k,
                              void* workspace, int64_t workspace_bytes,
                              const w8a8_gemm_config_t* cfg, void* stream);
+
+/* ---- a3: pre-tiled weights for few-row shapes ----------------------------
+ * No reference counterpart (the reference streams W row-major).  A GEMM with
+ * few rows (the 256-token text stream) reads all of W from HBM once; row-major
+ * W arrives as 128-byte pieces of 128 rows 12 KB apart.  w8a8_pack_weight_tiles
+ * rewrites an int8 W [N, K] (row stride ldw) once, offline, as 128-row x
+ * 128-byte tiles, each 16 KB contiguous, ordered (row block, K block), zero
+ * padded to multiples of 128: w8a8_weight_tiles_bytes(N, K) bytes, 16-byte
+ * aligned.  w8a8_gemm_dequant_tiled then equals w8a8_gemm_dequant_splitk on
+ * the original W bit for bit (workspace NULL: no split). */
+int64_t w8a8_weight_tiles_bytes(int64_t N, int64_t K);
+int w8a8_pack_weight_tiles(const int8_t* w, int64_t ldw, int64_t N, int64_t K, int8_t* tiles,
+                           void* stream);
+int w8a8_gemm_dequant_tiled(const int8_t* q, int64_t ldq, const int8_t* tiles, const float* xs,
+                            const w8a8_epilogue_t* epi, void* out, int out_dtype, int64_t ldo,
+                            int64_t M, int64_t N, int64_t K, int split_k, void* workspace,
+                            int64_t workspace_bytes, const w8a8_gemm_config_t* cfg,
+                            void* stream);
 
 /* ---- the same split-K GEMM for callers that cannot allocate --------------
  * No counterpart in the reference.  Some callers cannot hand the library a

@@ -305,6 +305,33 @@ def int8_linear_rms_modulated(x, norm_weight, norm_eps, modulation_scale, weight
                                  convrot, convrot_groupsize)
 
 
+# --------------------------------------------------------------------------
+# a8: Q/K RMSNorm + interleaved RoPE
+# --------------------------------------------------------------------------
+def rope_interleaved(x: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
+    """inference/src/backend_rope.rs:156-166 (eager_apply, non-split): pairs
+    (x[2i], x[2i+1]) rotated by freqs [.., D/2, 2, 2] in the freqs' dtype,
+    out_r = f[r][0] x0 + f[r][1] x1, cast back to x's dtype."""
+    shape = x.shape
+    inp = x.to(freqs.dtype).reshape(*shape[:-1], -1, 1, 2)
+    out = freqs[..., 0] * inp[..., 0]
+    out.addcmul_(freqs[..., 1], inp[..., 1])
+    return out.reshape(shape).to(x.dtype)
+
+
+def rms_rope(q, k, freqs, q_scale, k_scale, eps):
+    """inference/src/backend_rope.rs:203-223 (eager_rms with rot = D):
+    rms_norm(x, scale, eps) then the interleaved rotation, for q and k.
+    freqs: [S, D/2, 2, 2] broadcast over the leading dimensions of x [.., S, H, D]."""
+    d = q.shape[-1]
+    f = freqs.reshape(-1, 1, d // 2, 2, 2)  # [S, 1 (heads), D/2, 2, 2]
+
+    def one(x, s):
+        nrm = torch.nn.functional.rms_norm(x, (d,), s.to(x.dtype), eps)
+        return rope_interleaved(nrm, f)
+    return one(q, q_scale), (one(k, k_scale) if k is not None else None)
+
+
 def quantize_weight(w: torch.Tensor):
     """a12, inference/src/layout_complete.rs:119-159: offline per-output-channel
     weight quantisation = the row-wise quantiser applied to W [N, K]."""

@@ -225,3 +225,20 @@ def test_modulated_errors():
         W().quantize_int8_rowwise_modulated(x, "adaln", torch.zeros(512, device=cuda()))
     with pytest.raises(ValueError):
         W().quantize_int8_rowwise_modulated(x, "scale", torch.zeros(3, 512, device=cuda()))
+
+
+def test_convrot_weight_and_linear_identity():
+    """ConvRot weights: W rotated per 256-group and quantised per row (bit-exact
+    against the C restatement); a ConvRot linear with rotated weights equals
+    the plain product up to quantisation (H is orthogonal)."""
+    g = torch.Generator().manual_seed(50)
+    n, k, m = 384, 3072, 200
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    wq, ws = W().quantize_weight(w.to(cuda()), convrot=True)
+    rq, rs = _cref.quantize_act_rot(w, True, kitchen=False)
+    assert torch.equal(wq.cpu(), rq) and torch.equal(ws.cpu(), rs)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    y = W().int8_linear(x.to(cuda()), wq, ws, convrot=True).float().cpu()
+    ref = (x.float() @ w.float().t())
+    rel = (y - ref).pow(2).mean().sqrt() / ref.pow(2).mean().sqrt()
+    assert rel.item() < 0.02  # int8 quantisation noise of both operands

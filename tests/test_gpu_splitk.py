@@ -135,3 +135,16 @@ def test_autotuned_config_is_bit_identical():
 
     t = autotune.tuner("int8_dequant")
     assert t.best_config is not None and len(t.last_timings) == len(autotune.GEMM_CONFIGS)
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 4])
+def test_int8_linear_host_matches_device_path(chunks):
+    """The pipelined host-buffer linear returns int8_linear's bytes row for row."""
+    m, k, n = 1000, 3072, 768
+    x, wq, ws, b = _case(m, k, n, 14)
+    wd, wsd, bd = wq.to(cuda()), ws.to(cuda()), b.to(cuda())
+    want = W().int8_linear(x.to(cuda()), wd, wsd, bd, output_act="gelu_tanh").cpu()
+    xp = x.pin_memory()
+    for _ in range(2):
+        got = W().int8_linear_host(xp, wd, wsd, bd, chunks=chunks, output_act="gelu_tanh")
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16))
