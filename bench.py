@@ -53,60 +53,70 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms while active."""
+    """SM clock, power and clock-event (throttle) reasons sampled through NVML
+    every millisecond while active, so that the samples fall inside the timed
+    kernels (nvidia-smi's 200 ms period misses a few-millisecond region).
+    Reports the median SM clock over samples where the GPU was not idle."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+    IDLE = 0x1
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []
         self.thread = None
+        self.stop_flag = threading.Event()
+        self.handle = None
+        self.nvml = None
+
+    def _open(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        self.nvml = pynvml
+        try:
+            p = torch.cuda.get_device_properties(self.cuda_index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.gpu)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._open()
         except Exception:
-            self.proc = None
+            self.handle = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.max_mhz = self.nvml.nvmlDeviceGetMaxClockInfo(self.handle, self.nvml.NVML_CLOCK_SM)
+        self.thread = threading.Thread(target=self._run, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        n = self.nvml
+        while not self.stop_flag.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(0.001)
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
+        if self.handle is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        self.stop_flag.set()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        busy = [(m, r) for m, r in self.samples if not (r & self.IDLE)]
+        use = busy or self.samples
+        reasons = sorted({name for _, r in use for bit, name in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(m for m, _ in use) if use else None,
+                "sm_max_mhz": float(self.max_mhz), "reasons": reasons,
+                "samples": len(self.samples), "samples_under_load": len(busy),
+                "sampler": "NVML every 1 ms during the timed region"}
 
 
 def make_inputs(device, seed=0):
@@ -180,7 +190,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     if sampler:
         sampler.start()
-        time.sleep(0.3)
+        time.sleep(0.05)
     for i in range(args.steps):
         flush_l2()
         ev[i][0].record(stream)

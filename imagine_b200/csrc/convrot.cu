@@ -160,33 +160,9 @@ __device__ __forceinline__ float in_silu(float g) { return g / (1.0f + expf(-g))
 
 __device__ __forceinline__ float in_sigmoid(float g) { return 1.0f / (1.0f + expf(-g)); }
 
-// ---- packed pairs: element j of two 256-groups of the row in one 64-bit
-// register pair, so every f32x2 instruction serves both groups.
-__device__ __forceinline__ uint64_t pk(float a, float b) {
-  return static_cast<uint64_t>(__float_as_uint(a)) | (static_cast<uint64_t>(__float_as_uint(b)) << 32);
-}
-__device__ __forceinline__ float lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
-__device__ __forceinline__ float hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
+// Packed pairs (pk / lo / hi / add2 / sub2 / mul2 / fma2, quant_common.cuh):
+// element j of two 256-groups of the row in one 64-bit register pair, so
+// every f32x2 instruction serves both groups.
 
 // One radix-4 butterfly of the normalised H4 (rows ++ +-, ++-+, +-++, -+++),
 // every sum left to right exactly as int8_linear.cu:253-261 orders it;

@@ -247,6 +247,49 @@ __device__ __forceinline__ void epi_pair(float a0, float a1, float xs_row, float
   }
 }
 
+// ---- bf16 output on packed fp32 pairs: the dequant order's arithmetic and
+// the GELU on two adjacent elements per f32x2 instruction (each lane rounds
+// as the scalar form does), the final cvt.rn.bf16x2 word being what the
+// staging tile stores.
+__device__ __forceinline__ uint32_t cvt_bf16x2(uint64_t v) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi(v)), "f"(lo(v)));
+  return d;
+}
+
+__device__ __forceinline__ uint64_t unpack_bf16x2(uint32_t b) {
+  return pk(__uint_as_float(b << 16), __uint_as_float(b & 0xFFFF0000u));
+}
+
+template <int ORDER, int ACT>
+__device__ __forceinline__ uint32_t epi_pair_bf16x2(float a0, float a1, uint64_t xs2, float w0,
+                                                    float w1, float b0, float b1, bool has_bias) {
+  const uint64_t a = pk(a0, a1);
+  const uint64_t w = pk(w0, w1);
+  uint32_t bits;
+  if constexpr (ORDER == kDqEager) {
+    bits = cvt_bf16x2(mul2(a, mul2(xs2, w)));  // T(acc * (xs * ws))
+    if (has_bias) bits = cvt_bf16x2(add2(unpack_bf16x2(bits), pk(b0, b1)));
+  } else if constexpr (ORDER == kDqScaleProduct) {
+    const uint64_t sc = mul2(xs2, w);
+    bits = cvt_bf16x2(has_bias ? fma2(a, sc, pk(b0, b1)) : mul2(a, sc));
+  } else {
+    const uint64_t t = mul2(a, xs2);
+    bits = cvt_bf16x2(has_bias ? fma2(t, w, pk(b0, b1)) : mul2(t, w));
+  }
+  if constexpr (ACT == kActGeluTanh) {
+    // 0.5 x (1 + tanh(k0 (x + k1 x^3))) in gelu_tanh's operation order
+    const uint64_t x = unpack_bf16x2(bits);
+    const uint64_t p = mul2(mul2(pk(0.044715f, 0.044715f), x), x);
+    const uint64_t u = fma2(p, x, x);
+    const uint64_t in = mul2(pk(0.7978845608028654f, 0.7978845608028654f), u);
+    const uint64_t t = pk(tanh_fast(lo(in)), tanh_fast(hi(in)));
+    const uint64_t h = mul2(pk(0.5f, 0.5f), x);
+    bits = cvt_bf16x2(mul2(h, add2(pk(1.0f, 1.0f), t)));
+  }
+  return bits;
+}
+
 // Split-K scratch: int32 [M, N] partial sums (row stride N) and one arrival
 // counter per (tile, epilogue warp); both all-zero between calls.
 struct SplitArgs {
@@ -264,8 +307,49 @@ __device__ __forceinline__ void finish_chunk(const uint32_t (&cur)[32], const fl
                                              int col0, int row0, int M, int N, uint8_t* st,
                                              const CUtensorMap* tmD, int lane) {
   constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
+  constexpr bool kBf16 = std::is_same<OutT, __nv_bfloat16>::value;
   float y[32];
-  if constexpr (!kRaw) {
+  uint32_t packed[16];  // bf16 output: the staged words
+  if constexpr (kBf16) {
+    const float4* wsq = reinterpret_cast<const float4*>(wsv);
+    const float4* bq = reinterpret_cast<const float4*>(bv);
+    const uint64_t xs2 = pk(xs_row, xs_row);
+#pragma unroll
+    for (int j4 = 0; j4 < 8; ++j4) {
+      const float4 w4 = wsq[j4];
+      const float4 b4 = bq[j4];
+      const int j = j4 * 4;
+      float a[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        a[t] = (KIND == 0) ? static_cast<float>(static_cast<int32_t>(cur[j + t]))
+                           : __uint_as_float(cur[j + t]);
+      }
+      constexpr int kOrder = KIND == 0 ? ORDER : kDqChained;
+      packed[2 * j4] = epi_pair_bf16x2<kOrder, ACT>(a[0], a[1], xs2, w4.x, w4.y, b4.x, b4.y, has_bias);
+      packed[2 * j4 + 1] =
+          epi_pair_bf16x2<kOrder, ACT>(a[2], a[3], xs2, w4.z, w4.w, b4.z, b4.w, has_bias);
+    }
+    if (has_resid) {
+      float rsv[32];
+      load_cols32<OutT>(ep.rscale, col0, N, ep.vec_rscale, rsv);
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        const uint32_t bits = packed[j / 2];
+        float v0 = __uint_as_float(bits << 16), v1 = __uint_as_float(bits & 0xFFFF0000u);
+        const bool in_row = grow < M;
+        const float r0 = (in_row && col0 + j < N)
+                             ? OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(grow) * ep.ldr + col0 + j)
+                             : 0.0f;
+        const float r1 = (in_row && col0 + j + 1 < N)
+                             ? OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(grow) * ep.ldr + col0 + j + 1)
+                             : 0.0f;
+        v0 = __fmaf_rn(v0, rsv[j], r0);
+        v1 = __fmaf_rn(v1, rsv[j + 1], r1);
+        packed[j / 2] = cvt_bf16x2(pk(v0, v1));
+      }
+    }
+  } else if constexpr (!kRaw) {
     const float4* wsq = reinterpret_cast<const float4*>(wsv);
     const float4* bq = reinterpret_cast<const float4*>(bv);
 #pragma unroll
@@ -322,13 +406,10 @@ __device__ __forceinline__ void finish_chunk(const uint32_t (&cur)[32], const fl
       uint32_t w4[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float lo = y[cc * 8 + e * 2];
-        const float hi = y[cc * 8 + e * 2 + 1];
-        if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
-          // values are already exact bf16: take the high halves
-          w4[e] = __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+        if constexpr (kBf16) {
+          w4[e] = packed[cc * 4 + e];
         } else {
-          w4[e] = pack2<OutT>(lo, hi);
+          w4[e] = pack2<OutT>(y[cc * 8 + e * 2], y[cc * 8 + e * 2 + 1]);
         }
       }
       const int phys = cc ^ ((lane >> 1) & 3);

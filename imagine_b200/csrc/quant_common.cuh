@@ -137,21 +137,57 @@ __device__ __forceinline__ float div_exact_short(float x, float d, float r) {
   return __fmaf_rn(e, r, y0);
 }
 
+// ---- packed fp32 pairs (sm_100 add/sub/mul/fma.rn.f32x2): two elements in
+// one 64-bit register pair, one instruction for both; each lane rounds as
+// the scalar instruction would.
+__device__ __forceinline__ uint64_t pk(float a, float b) {
+  return static_cast<uint64_t>(__float_as_uint(a)) | (static_cast<uint64_t>(__float_as_uint(b)) << 32);
+}
+__device__ __forceinline__ float lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
 // Eight codes from one 16-byte vector of bf16 (the hot path of the
-// quantiser): exact quotients (div_exact_short), paired hardware bf16
-// rounding, rne via the 1.5*2^23 trick, and saturating packs (the clamp to
-// [-128, 127]).
+// quantiser): exact quotients (div_exact_short on packed pairs), paired
+// hardware bf16 rounding, rne via the 1.5*2^23 trick (packed), and saturating
+// packs (the clamp to [-128, 127]).
 __device__ __forceinline__ uint2 quant8_bf16(const uint4& v, float div, float recip) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const uint64_t r2 = pk(recip, recip);
+  const uint64_t nd2 = pk(-div, -div);
+  const uint64_t magic = pk(12582912.0f, 12582912.0f);
   int q[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float y0 = div_exact_short(__uint_as_float(w[i] << 16), div, recip);
-    const float y1 = div_exact_short(__uint_as_float(w[i] & 0xFFFF0000u), div, recip);
-    const __nv_bfloat162 b = __floats2bfloat162_rn(y0, y1);  // .x = y0
+    const uint64_t x = pk(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
+    // y0 = RN(x r), e = x - y0 d (exact), y = RN(y0 + e r)
+    const uint64_t y0 = mul2(x, r2);
+    const uint64_t e = fma2(y0, nd2, x);
+    const uint64_t y = fma2(e, r2, y0);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(lo(y), hi(y));  // .x = lo
     const uint32_t bits = *reinterpret_cast<const uint32_t*>(&b);
-    q[2 * i] = rne_small_int(__uint_as_float(bits << 16));
-    q[2 * i + 1] = rne_small_int(__uint_as_float(bits & 0xFFFF0000u));
+    const uint64_t t = add2(pk(__uint_as_float(bits << 16), __uint_as_float(bits & 0xFFFF0000u)), magic);
+    q[2 * i] = __float_as_int(lo(t)) - 0x4B400000;
+    q[2 * i + 1] = __float_as_int(hi(t)) - 0x4B400000;
   }
   // cvt.pack.sat.s8.s32.b32 d, a, b, c: d = c[15:0] << 16 | sat(a) << 8 | sat(b)
   uint32_t t0, t1, lo, hi;

@@ -28,6 +28,7 @@ def main():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--block-n", type=int, default=0)
     ap.add_argument("--cta-group", type=int, default=0)
+    ap.add_argument("--tiled", action="store_true", help="GEMM on the pre-tiled weight layout")
     ap.add_argument("--split-k", type=int, default=1,
                     help="GEMM K splits (0: chosen from the SM count, 1: off)")
     ap.add_argument("--time", action="store_true",
@@ -97,7 +98,12 @@ def main():
                 y = torch.empty((a.m, a.n), dtype=torch.bfloat16, device=dev)
                 ep = _epilogue(ws, b, None, None, "eager", act, a.n, a.n)
                 c = _config(cfg)
-                if a.split_k != 1:
+                if a.tiled:
+                    tw = W.pack_weight_tiles(wq)
+                    sk = None if a.split_k == 0 else a.split_k
+                    run(lambda: _gemm_dequant(q, tw, xs.reshape(-1), ep, y, torch.bfloat16, a.m,
+                                              a.n, a.k, c, sk, _stream(dev)))
+                elif a.split_k != 1:
                     sk = None if a.split_k == 0 else a.split_k
                     run(lambda: _gemm_dequant(q, wq, xs.reshape(-1), ep, y, torch.bfloat16, a.m,
                                               a.n, a.k, c, sk, _stream(dev)))
@@ -118,7 +124,7 @@ def main():
     if err:
         raise SystemExit(f"device error {err}")
     msg = (f"ok {a.kernel} {a.m} {a.k} {a.n} block_n={a.block_n} cta_group={a.cta_group} "
-           f"split_k={a.split_k}")
+           f"split_k={a.split_k}" + (" tiled" if a.tiled else ""))
     if times:
         t = sorted(times)[len(times) // 2]
         ops = 2.0 * a.m * a.n * a.k

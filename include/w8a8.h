@@ -238,8 +238,9 @@ int w8a8_gemm_dequant_splitk(const int8_t* q, int64_t ldq, const int8_t* w, int6
  * rewrites an int8 W [N, K] (row stride ldw) once, offline, as 128-row x
  * 128-byte tiles, each 16 KB contiguous, ordered (row block, K block), zero
  * padded to multiples of 128: w8a8_weight_tiles_bytes(N, K) bytes, 16-byte
- * aligned.  w8a8_gemm_dequant_tiled then equals w8a8_gemm_dequant_splitk on
- * the original W bit for bit (workspace NULL: no split). */
+ * aligned.  w8a8_gemm_dequant_tiled (K a multiple of 16, q rows and out
+ * 16-byte aligned) then equals w8a8_gemm_dequant_splitk on the original W bit
+ * for bit (workspace NULL: no split). */
 int64_t w8a8_weight_tiles_bytes(int64_t N, int64_t K);
 int w8a8_pack_weight_tiles(const int8_t* w, int64_t ldw, int64_t N, int64_t K, int8_t* tiles,
                            void* stream);

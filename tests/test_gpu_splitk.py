@@ -148,3 +148,19 @@ def test_int8_linear_host_matches_device_path(chunks):
     for _ in range(2):
         got = W().int8_linear_host(xp, wd, wsd, bd, chunks=chunks, output_act="gelu_tanh")
         assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+@pytest.mark.parametrize("m,k,n", [(256, 12288, 3072), (200, 3008, 1000), (64, 3072, 9216),
+                                   (2, 3072, 640)])
+@pytest.mark.parametrize("split_k", [None, 1])
+def test_pre_tiled_weights_bit_identical(m, k, n, split_k):
+    """int8_linear on a pre-tiled weight equals the row-major weight's result
+    (K and N tails included: the tiles are zero padded)."""
+    x, wq, ws, b = _case(m, k, n, 15 + m)
+    xd, wqd, wsd, bd = x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda())
+    tw = W().pack_weight_tiles(wqd)
+    assert tw.shape == (n, k)
+    want = W().int8_linear(xd, wqd, wsd, bd, split_k=1)
+    got = W().int8_linear(xd, tw, wsd, bd, split_k=split_k)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    assert W().device_error() == 0
