@@ -20,6 +20,8 @@ _OPS = (
     "int8_linear_rms_modulated",
     "adaln_int8_linear",
     "rms_rope",
+    "int8_linear_rms_rope",
+    "rope_freqs_rows",
     "pack_weight_tiles",
     "TiledInt8Weight",
     "quantize_per_tensor_fp8",

@@ -77,7 +77,13 @@ SIGNATURES = {
     "w8a8_gemm_dequant": (_i32, [_vp, _i64, _vp, _i64, _vp, _EP, _vp, _i32, _i64, _i64, _i64, _i64, _CFG, _vp]),
     "w8a8_rms_rope": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                              _vp, _i64, _vp, _vp, ctypes.c_float, _vp]),
+    "w8a8_gemm_dequant_rms_rope": (_i32, [_vp, _i64, _vp, _i64, _vp, _EP, _vp, _i64, _i64, _i64,
+                                          _i64, _i64, _vp, _i32, _vp, ctypes.c_float, _i32, _vp,
+                                          _i64, _CFG, _vp]),
+    "w8a8_rope_freqs_rows_bytes": (_i64, [_i64]),
+    "w8a8_rope_freqs_rows": (_i32, [_vp, _i64, _i64, _vp, _vp]),
     "w8a8_gemm_splitk_workspace_bytes": (_i64, [_i64, _i64]),
+    "w8a8_gemm_auto_workspace_bytes": (_i64, [_i64, _i64, _i64, _CFG]),
     "w8a8_weight_tiles_bytes": (_i64, [_i64, _i64]),
     "w8a8_pack_weight_tiles": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),
     "w8a8_gemm_dequant_tiled": (_i32, [_vp, _i64, _vp, _vp, _EP, _vp, _i32, _i64, _i64, _i64, _i64,

@@ -227,6 +227,74 @@ int w8a8_rms_rope(const void* q, const void* k, void* q_out, void* k_out, int dt
                                 q_scale, k_scale, eps, static_cast<cudaStream_t>(stream)));
 }
 
+int w8a8_gemm_dequant_rms_rope(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,
+                               const float* xs, const w8a8_epilogue_t* epi, void* out, int64_t ldo,
+                               int64_t M, int64_t N, int64_t K, int64_t rope_cols,
+                               const void* norm_w, int norm_w_per_column, const float* freqs_rows,
+                               float eps, int split_k, void* workspace, int64_t workspace_bytes,
+                               const w8a8_gemm_config_t* cfg, void* stream) {
+  if (M < 0 || N < 0 || K < 0 || rope_cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (split_k < 0) return fail(W8A8_ERR_VALUE, "split_k must be >= 0, got %d", split_k);
+  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (epi->activation != W8A8_ACT_NONE || epi->residual) {
+    return fail(W8A8_ERR_VALUE, "the RMSNorm + RoPE epilogue takes no output activation or residual");
+  }
+  if (N % 128 != 0 || rope_cols % 128 != 0 || rope_cols > N) {
+    return fail(W8A8_ERR_VALUE,
+                "N (%lld) and rope_cols (%lld) must be multiples of 128 with rope_cols <= N",
+                static_cast<long long>(N), static_cast<long long>(rope_cols));
+  }
+  if (M == 0 || N == 0) return finish(0);
+  if (!q || !w || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (rope_cols > 0 && (!norm_w || !freqs_rows)) {
+    return fail(W8A8_ERR_VALUE, "NULL norm weight or rotations");
+  }
+  if (ldq < K || ldw < K || ldo < N) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  if (split_k > 1 && !workspace) return fail(W8A8_ERR_VALUE, "split-K needs a scratch buffer");
+  GemmArgs g{};
+  g.kind = 0;
+  g.a = q;
+  g.lda = ldq;
+  g.b = w;
+  g.ldb = ldw;
+  g.xs = xs;
+  g.epi = epi;
+  g.out = out;
+  g.out_dtype = W8A8_BF16;
+  g.ldo = ldo;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.cfg = cfg;
+  g.split_k = workspace ? split_k : 1;
+  g.workspace = workspace;
+  g.workspace_bytes = workspace_bytes;
+  g.rms_rope = 1;
+  g.rope_w = norm_w;
+  g.rope_w_percol = norm_w_per_column ? 1 : 0;
+  g.rope_f = freqs_rows;
+  g.rope_cols = rope_cols;
+  g.rope_eps = eps;
+  return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
+int64_t w8a8_rope_freqs_rows_bytes(int64_t rows) {
+  if (rows < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  return (rows + 127) / 128 * 128 * 64 * 16;
+}
+
+int w8a8_rope_freqs_rows(const float* freqs, int64_t freq_rows, int64_t rows, float* out,
+                         void* stream) {
+  if (rows < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (rows == 0) return finish(0);
+  if (!freqs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (freq_rows < 1) return fail(W8A8_ERR_VALUE, "freqs must have at least one row");
+  if ((reinterpret_cast<uintptr_t>(freqs) & 15u) || (reinterpret_cast<uintptr_t>(out) & 15u)) {
+    return fail(W8A8_ERR_VALUE, "freqs and out must be 16-byte aligned");
+  }
+  return finish(rope_freqs_rows_launch(freqs, freq_rows, rows, out, static_cast<cudaStream_t>(stream)));
+}
+
 int w8a8_row_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
                     float* amax, void* stream) {
   if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
@@ -289,6 +357,24 @@ int w8a8_gemm_dequant(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw
 int64_t w8a8_gemm_splitk_workspace_bytes(int64_t M, int64_t N) {
   if (M < 0 || N < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   return splitk_workspace_bytes(M, N);
+}
+
+int64_t w8a8_gemm_auto_workspace_bytes(int64_t M, int64_t N, int64_t K,
+                                       const w8a8_gemm_config_t* cfg) {
+  if (M < 0 || N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (M == 0 || N == 0) return 0;
+  GemmArgs g{};
+  g.kind = 0;
+  g.out_dtype = W8A8_BF16;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.cfg = cfg;
+  g.split_k = 0;
+  GemmPlan plan{};
+  const bool tc_ok = K > 0 && K % 16 == 0 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31);
+  if (int rc = plan_gemm(g, tc_ok, plan)) return fail(rc, "%s", w8a8_last_error());
+  return plan.workspace_need;
 }
 
 int w8a8_gemm_dequant_splitk(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,

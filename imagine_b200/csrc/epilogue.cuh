@@ -17,7 +17,9 @@ namespace w8a8 {
 //   kDqChained      native/comfy-port/kitchen/int8_linear.cu:517-545, 585-708
 //                   y = T(fma(acc*xs, ws, bias))                  (one rounding)
 enum DequantOrder : int { kDqEager = 0, kDqScaleProduct = 1, kDqChained = 2 };
-enum OutputAct : int { kActNone = 0, kActGeluTanh = 1 };
+// kActRmsRope: per-head RMSNorm + interleaved RoPE of 128-column heads (the
+// QKV projection's epilogue; GEMM with 256-column tiles and bf16 output only)
+enum OutputAct : int { kActNone = 0, kActGeluTanh = 1, kActRmsRope = 2 };
 
 template <typename T>
 struct OutTraits;
@@ -81,6 +83,16 @@ struct EpilogueParams {
   int sf_ncb;              // MXFP8: 4-wide column blocks per scale row = ceil(K / 128)
   int b_tiles_kb;          // B pre-tiled (0: row-major): 128 x 128-byte tiles, this many
                            // K-blocks per 128-row block
+  // kActRmsRope: columns [0, rope_cols) are 128-column heads that get
+  // RMSNorm (weight rope_w: [128] shared, or [rope_cols] per column when
+  // rope_w_percol) and the interleaved rotation of their row (rope_f: the
+  // row-blocked float4 rotations, [row / 32][pair][row % 32]); later columns
+  // get the plain epilogue.
+  const void* rope_w;
+  int rope_w_percol;
+  const float* rope_f;
+  int rope_cols;
+  float rope_eps;
 };
 
 // Value of one output element before the optional residual, already rounded

@@ -82,11 +82,13 @@ struct Cfg {
   // MXFP8: one 512-byte block of e8m0 scales for A and BN/128 for B per stage
   static constexpr int kSFBytes = KIND == 2 ? 512 * (1 + BN / 128) : 0;
   static constexpr int kSFCols = KIND == 2 ? 4 * (1 + BN / 128) : 0;  // TMEM columns per stage
-  // one warp's staging tile; split-K also stages 32 x 32 int32 partials in it
-  static constexpr int kStageD = 32 * 32 * (SPLIT ? 4 : static_cast<int>(sizeof(OutT)));
+  // one warp's staging tile (split-K stages its int32 partials in 32 x 16
+  // halves, which fit the 2-byte outputs' tile)
+  static constexpr int kStageD = 32 * 32 * static_cast<int>(sizeof(OutT));
   // per epilogue warp: one store staging tile + the fp32 weight scale and bias
-  // of each of its column chunks for the current tile
-  static constexpr int kChunksPerWarp = (BN / 32 + 1) / 2;
+  // of each of its column chunks for the current tile (four: its half of a
+  // 256-column tile, or one 128-column head with kActRmsRope)
+  static constexpr int kChunksPerWarp = 4;
   static constexpr int kVecBytes = 2 * kChunksPerWarp * 32 * 4;
   static constexpr int kDBytes = kEpiWarps * (kStageD + kVecBytes);
   static_assert(kStageD % 1024 == 0, "staging tiles must keep 1024-byte alignment");
@@ -290,13 +292,24 @@ __device__ __forceinline__ uint32_t epi_pair_bf16x2(float a0, float a1, uint64_t
   return bits;
 }
 
-// Split-K scratch: int32 [M, N] partial sums (row stride N) and one arrival
-// counter per (tile, epilogue warp); both all-zero between calls.
+// Split-K: every tile is cut into `splits` units of consecutive K-blocks,
+// run by different CTAs.  Scratch: the int32 partial sums of tile t at rows
+// t * 128 .. +127 of a [tiles * 128, BN] array, then one arrival counter per
+// (tile, epilogue warp); both all-zero between calls.
 struct SplitArgs {
   int32_t* acc;
   unsigned* cnt;
   int splits;
 };
+
+// Unit -> tile and K-block range [kb_lo, kb_hi) (S units per tile).
+__device__ __forceinline__ void unit_range(int unit, int S, int num_kb, int& tile, int& kb_lo,
+                                           int& kb_hi) {
+  tile = unit / S;
+  const int sp = unit - tile * S;
+  kb_lo = sp * num_kb / S;
+  kb_hi = (sp + 1) * num_kb / S;
+}
 
 // Dequant epilogue of one 32 x 32 chunk (lane = row) from its raw 32-bit
 // accumulators, staged in `st` and TMA-stored to (col0, row0) of the output.
@@ -424,12 +437,182 @@ __device__ __forceinline__ void finish_chunk(const uint32_t (&cur)[32], const fl
   }
 }
 
-// 32 x 32 raw 32-bit values (lane = row) into a 128B-swizzled staging tile.
-__device__ __forceinline__ void stage_raw32(uint8_t* st, const uint32_t (&cur)[32], int lane) {
+// 16 packed bf16 words (a lane's 32 columns) into the 64B-swizzled staging
+// tile, then the chunk's TMA store to (col0, row0).
+__device__ __forceinline__ void store_chunk_bf16(const uint32_t (&w)[16], uint8_t* st,
+                                                 const CUtensorMap* tmD, int col0, int row0, int M,
+                                                 int lane) {
+  if (lane == 0) tma_store_wait_read<0>();
+  __syncwarp();
 #pragma unroll
-  for (int cc = 0; cc < 8; ++cc) {
-    const uint4 v = make_uint4(cur[cc * 4], cur[cc * 4 + 1], cur[cc * 4 + 2], cur[cc * 4 + 3]);
-    *reinterpret_cast<uint4*>(st + lane * 128 + ((cc ^ (lane & 7)) * 16)) = v;
+  for (int cc = 0; cc < 4; ++cc) {
+    const int phys = cc ^ ((lane >> 1) & 3);
+    *reinterpret_cast<uint4*>(st + lane * 64 + phys * 16) =
+        make_uint4(w[cc * 4], w[cc * 4 + 1], w[cc * 4 + 2], w[cc * 4 + 3]);
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && row0 < M) {
+    tma_store_2d(tmD, st, col0, row0);
+    tma_store_commit();
+  }
+}
+
+// ---- kActRmsRope: Q/K RMSNorm + interleaved RoPE fused into the projection
+// (the stand-alone form is rope.cu; reference call site
+// inference/src/models/qwen_image21/dit.rs:486-505, eager body
+// inference/src/backend_rope.rs:146-223).  An epilogue warp owns one whole
+// 128-column head of its 32 rows, one row per lane, so the row's statistics
+// need no cross-lane reduction.  Both passes fetch the head's four raw
+// accumulator chunks (from TMEM, or from the split-K scratch) and turn them
+// into exactly the bf16 words the plain GEMM would store: pass 1 sums their
+// squares, pass 2 normalises, rotates and stores them.  Fetching twice keeps
+// the head out of the registers, which the rotation's loads need.
+//
+// The 32 bf16 words of one chunk from its raw accumulators.
+template <int ORDER>
+__device__ __forceinline__ void rope_dequant_chunk(const uint32_t (&cur)[32], const float* wsv,
+                                                   const float* bv, uint64_t xs2, bool has_bias,
+                                                   uint32_t (&w)[16]) {
+  const float4* wsq = reinterpret_cast<const float4*>(wsv);
+  const float4* bq = reinterpret_cast<const float4*>(bv);
+#pragma unroll
+  for (int j4 = 0; j4 < 8; ++j4) {
+    const float4 w4 = wsq[j4];
+    const float4 b4 = bq[j4];
+    const int j = j4 * 4;
+    const float a0 = static_cast<float>(static_cast<int32_t>(cur[j]));
+    const float a1 = static_cast<float>(static_cast<int32_t>(cur[j + 1]));
+    const float a2 = static_cast<float>(static_cast<int32_t>(cur[j + 2]));
+    const float a3 = static_cast<float>(static_cast<int32_t>(cur[j + 3]));
+    w[2 * j4] = epi_pair_bf16x2<ORDER, kActNone>(a0, a1, xs2, w4.x, w4.y, b4.x, b4.y, has_bias);
+    w[2 * j4 + 1] = epi_pair_bf16x2<ORDER, kActNone>(a2, a3, xs2, w4.z, w4.w, b4.z, b4.w, has_bias);
+  }
+}
+
+// fetch(i, cur, second): chunk i's raw accumulators of this lane's row (the
+// second fetch of a chunk may release its storage).  wsv / bv: the head's
+// per-column weight scales and bias, [4][32] fp32.
+//   rrms = 1 / sqrt(sum(x^2) / 128 + eps); n = bf16(x * rrms * w);
+//   (y0, y1) = (f00 n0 + f01 n1, f10 n0 + f11 n1); out = bf16(y)
+// with f the token's 2 x 2 rotation of each pair.
+template <int ORDER, typename Fetch>
+__device__ __forceinline__ void rope_head(Fetch&& fetch, const float* wsv, const float* bv,
+                                          float xs_row, bool has_bias, const EpilogueParams& ep,
+                                          int grow, int hcol0, int row0, int M, uint8_t* st,
+                                          const CUtensorMap* tmD, int lane) {
+  const uint64_t xs2 = pk(xs_row, xs_row);
+  uint64_t ss2 = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t cur[32], w[16];
+    fetch(i, cur, false);
+    rope_dequant_chunk<ORDER>(cur, wsv + i * 32, bv + i * 32, xs2, has_bias, w);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint64_t v = unpack_bf16x2(w[j]);
+      ss2 = fma2(v, v, ss2);
+    }
+  }
+  const float ss = __fadd_rn(lo(ss2), hi(ss2));
+  // 1 / sqrt in two IEEE roundings, the form torch's rsqrt takes
+  const float rrms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / 128.0f), ep.rope_eps)));
+  const uint64_t rr2 = pk(rrms, rrms);
+  // this row's rotations: pair p at fr[p * 32] (row-blocked, 128-row padded,
+  // so every row of a tile has them); a warp's 32 rows read 512 contiguous bytes
+  const float4* fr = reinterpret_cast<const float4*>(ep.rope_f) +
+                     (static_cast<int64_t>(grow >> 5) * 64) * 32 + (grow & 31);
+  const uint4* nw4 = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(ep.rope_w) +
+                                                    (ep.rope_w_percol ? hcol0 : 0));
+  // Groups of 4 pairs (one 16-byte word of 8 norm weights, four rotations);
+  // the next group's loads are issued before this group's arithmetic, so
+  // their L2 latency overlaps the work instead of adding up over the 64 pairs.
+  float4 fc[4], fn[4];
+  uint4 wc = __ldg(nw4), wn = wc;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) fc[e] = __ldg(fr + e * 32);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t cur[32], w[16], out[16];
+    fetch(i, cur, true);
+    rope_dequant_chunk<ORDER>(cur, wsv + i * 32, bv + i * 32, xs2, has_bias, w);
+#pragma unroll
+    for (int g4 = 0; g4 < 4; ++g4) {
+      const int gi = i * 4 + g4;  // group of the head
+      if (gi + 1 < 16) {
+        wn = __ldg(nw4 + gi + 1);  // same address for every lane
+#pragma unroll
+        for (int e = 0; e < 4; ++e) fn[e] = __ldg(fr + (4 * (gi + 1) + e) * 32);
+      }
+      const uint32_t ww[4] = {wc.x, wc.y, wc.z, wc.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t nb =
+            cvt_bf16x2(mul2(mul2(unpack_bf16x2(w[g4 * 4 + e]), rr2), unpack_bf16x2(ww[e])));
+        const float n0 = __uint_as_float(nb << 16);
+        const float n1 = __uint_as_float(nb & 0xFFFF0000u);
+        const float4 f = fc[e];  // (f00, f01, f10, f11)
+        out[g4 * 4 + e] =
+            cvt_bf16x2(fma2(pk(f.y, f.w), pk(n1, n1), mul2(pk(f.x, f.z), pk(n0, n0))));
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) fc[e] = fn[e];
+      wc = wn;
+    }
+    store_chunk_bf16(out, st, tmD, hcol0 + i * 32, row0, M, lane);
+  }
+}
+
+// This unit's int32 partial chunk (32 rows x 32 columns, lane = row) +=
+// the scratch at (scol, srow): two 32 x 16 TMA reductions through the warp's
+// 64B-swizzled staging tile.
+__device__ __forceinline__ void splitk_reduce_chunk(const CUtensorMap* tmW, uint8_t* st,
+                                                    const uint32_t (&cur)[32], int scol, int srow,
+                                                    int lane) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (lane == 0) tma_store_wait_read<0>();
+    __syncwarp();
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      const int j = h * 16 + cc * 4;
+      *reinterpret_cast<uint4*>(st + lane * 64 + ((cc ^ ((lane >> 1) & 3)) * 16)) =
+          make_uint4(cur[j], cur[j + 1], cur[j + 2], cur[j + 3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_reduce_add_2d(tmW, st, scol + h * 16, srow);
+      tma_store_commit();
+    }
+  }
+}
+
+// Split-K read-back: the summed int32 chunk at scratch row srow, columns
+// scol..+31 (row length BN) into cur, leaving zeros behind for the next call
+// (unless !zero: the chunk is read again).  Rows of a tile past M hold zeros
+// and are skipped.
+template <int BN>
+__device__ __forceinline__ void splitk_take_chunk(const SplitArgs& sk, int srow, int scol,
+                                                  bool row_in, uint32_t (&cur)[32],
+                                                  bool zero = true) {
+  if (!row_in) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) cur[j] = 0u;
+    return;
+  }
+  int4* s4 = reinterpret_cast<int4*>(sk.acc + static_cast<int64_t>(srow) * BN + scol);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int4 v = __ldcg(s4 + i);
+    cur[4 * i] = static_cast<uint32_t>(v.x);
+    cur[4 * i + 1] = static_cast<uint32_t>(v.y);
+    cur[4 * i + 2] = static_cast<uint32_t>(v.z);
+    cur[4 * i + 3] = static_cast<uint32_t>(v.w);
+  }
+  if (zero) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) __stcg(s4 + i, make_int4(0, 0, 0, 0));
   }
 }
 
@@ -513,9 +696,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int unit = first_tile; ok && unit < num_units; unit += tile_step) {
-        const int tile = unit / S;
-        const int sp = unit - tile * S;
-        const int kb_lo = sp * num_kb / S, kb_hi = (sp + 1) * num_kb / S;
+        int tile, kb_lo, kb_hi;
+        unit_range(unit, S, num_kb, tile, kb_lo, kb_hi);
         int mb, nb;
         tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
         const int a_row = mb * kBM * CG + static_cast<int>(rank) * kBM;
@@ -578,8 +760,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t tl = 0;
       bool ok = true;
       for (int unit = first_tile; ok && unit < num_units; unit += tile_step, ++tl) {
-        const int sp = unit - (unit / S) * S;
-        const int kb_lo = sp * num_kb / S, kb_hi = (sp + 1) * num_kb / S;
+        int tile, kb_lo, kb_hi;
+        unit_range(unit, S, num_kb, tile, kb_lo, kb_hi);
         const uint32_t acc = tl & 1u;
         const uint32_t use = tl >> 1;
         if (!mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abortv, &g_w8a8_device_error,
@@ -658,12 +840,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* s_bias = s_ws + C::kChunksPerWarp * 32;  // [chunk][32] each
     const bool has_bias = ep.bias != nullptr;
     const bool has_resid = ep.residual != nullptr;
+    constexpr bool kRope = ACT == kActRmsRope;
+    static_assert(!kRope || (KIND == 0 && CG == 1 && std::is_same<OutT, __nv_bfloat16>::value),
+                  "the RMSNorm + RoPE epilogue is built for the 1-CTA int8 GEMM with bf16 output");
     float fp8_scale = 0.0f;
     if constexpr (KIND == 1) fp8_scale = __fmul_rn(__ldg(ep.sa), __ldg(ep.sb));
     (void)fp8_scale;
     uint32_t tl = 0;
     for (int unit = first_tile; unit < num_units; unit += tile_step, ++tl) {
-      const int tile = unit / S;
+      int tile, kb_lo, kb_hi;
+      unit_range(unit, S, num_kb, tile, kb_lo, kb_hi);
       int mb, nb;
       tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
       const uint32_t acc = tl & 1u;
@@ -677,8 +863,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
 #pragma unroll
         for (int i = 0; i < C::kChunksPerWarp; ++i) {
-          const int col = col_base + (half + 2 * i) * 32 + lane;
-          const bool in = (half + 2 * i) < BN / 32 && col < N;
+          const int ch = kRope ? 4 * half + i : half + 2 * i;  // chunk of the tile
+          const int col = col_base + ch * 32 + lane;
+          const bool in = ch < BN / 32 && col < N;
           float wv = 1.0f, bvv = 0.0f;
           if constexpr (KIND == 0) wv = in ? __ldg(ep.ws + (ep.ws_scalar ? 0 : col)) : 0.0f;
           if (has_bias && in) bvv = OutTraits<OutT>::load(ep.bias, col);
@@ -693,10 +880,85 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row0 = mb * kBM * CG + static_cast<int>(rank) * kBM + quad * 32;
       const int grow = row0 + lane;
+      // split-K: this warp's first scratch row; partials are added to the
+      // scratch instead of finishing the chunks
+      const int srow0 = tile * kBM + quad * 32;
+      constexpr bool do_reduce = SPLIT;
       float xs_row = 0.0f;
       if constexpr (KIND == 0 && !kRaw) xs_row = grow < M ? __ldg(ep.xs + grow) : 0.0f;
       if constexpr (KIND == 1) xs_row = fp8_scale;
       if constexpr (KIND == 2) xs_row = 1.0f;  // block scales are applied by the MMA
+      if constexpr (kRope) {
+        // this warp's head: chunks 4 half .. 4 half + 3 of the tile
+        const int hcol0 = col_base + half * 128;
+        const bool active = half * 128 < BN && hcol0 < N;
+        const bool roped = active && hcol0 < ep.rope_cols;
+        const uint32_t head_tmem = tmem_base + lane_base + acc * BN + half * 128;
+        if (active) {
+          if (do_reduce) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t cur[32];
+              tmem_ld_32x32b_x32(head_tmem + i * 32, cur);
+              tmem_ld_wait();
+              if (row0 < M) splitk_reduce_chunk(&tmW, st, cur, half * 128 + i * 32, srow0, lane);
+            }
+          } else if (roped) {
+            auto from_tmem = [&](int i, uint32_t (&cur)[32], bool) {
+              tmem_ld_32x32b_x32(head_tmem + i * 32, cur);
+              tmem_ld_wait();
+            };
+            rope_head<ORDER>(from_tmem, s_ws, s_bias, xs_row, has_bias, ep, grow, hcol0, row0, M,
+                             st, &tmD, lane);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t cur[32];
+              tmem_ld_32x32b_x32(head_tmem + i * 32, cur);
+              tmem_ld_wait();
+              finish_chunk<KIND, OutT, ORDER, kActNone>(cur, s_ws + i * 32, s_bias + i * 32, xs_row,
+                                                        has_bias, has_resid, ep, grow,
+                                                        hcol0 + i * 32, row0, M, N, st, &tmD, lane);
+            }
+          }
+        }
+        // the accumulator is free: the MMA warp may start the next tile on it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        if (do_reduce) {
+          unsigned last = 0;
+          unsigned* cnt = sk.cnt + static_cast<int64_t>(tile) * kEpiWarps + warp;
+          if (lane == 0) {
+            tma_store_wait_all<0>();
+            fence_proxy_async_global();
+            __threadfence();
+            last = atomicAdd(cnt, 1u) == static_cast<unsigned>(S - 1) ? 1u : 0u;
+          }
+          last = __shfl_sync(0xffffffffu, last, 0);
+          if (last && active) {
+            __threadfence();
+            auto from_scratch = [&](int i, uint32_t (&cur)[32], bool second) {
+              splitk_take_chunk<BN>(sk, srow0 + lane, half * 128 + i * 32, grow < M, cur, second);
+            };
+            if (roped) {
+              rope_head<ORDER>(from_scratch, s_ws, s_bias, xs_row, has_bias, ep, grow, hcol0, row0,
+                               M, st, &tmD, lane);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                uint32_t cur[32];
+                from_scratch(i, cur, true);
+                finish_chunk<KIND, OutT, ORDER, kActNone>(cur, s_ws + i * 32, s_bias + i * 32,
+                                                          xs_row, has_bias, has_resid, ep, grow,
+                                                          hcol0 + i * 32, row0, M, N, st, &tmD, lane);
+              }
+            }
+          }
+          if (last && lane == 0) *cnt = 0u;
+        }
+        continue;
+      }
       // TMEM loads are software-pipelined: chunk c+2's tcgen05.ld is issued
       // as soon as chunk c's registers are free, so its latency overlaps the
       // arithmetic of chunk c.
@@ -715,17 +977,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c + 2 < BN / 32 && col0 + 64 < N) {
           tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + (c + 2) * 32, r);
         }
-        if constexpr (SPLIT) {
+        if (do_reduce) {
           // this unit's int32 partial -> += scratch (TMA reduction)
-          if (lane == 0) tma_store_wait_read<0>();
-          __syncwarp();
-          stage_raw32(st, cur, lane);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && row0 < M) {
-            tma_reduce_add_2d(&tmW, st, col0, row0);
-            tma_store_commit();
-          }
+          if (row0 < M) splitk_reduce_chunk(&tmW, st, cur, c * 32, srow0, lane);
         } else {
           finish_chunk<KIND, OutT, ORDER, ACT>(cur, s_ws + ci * 32, s_bias + ci * 32, xs_row,
                                                has_bias, has_resid, ep, grow, col0, row0, M, N, st,
@@ -741,7 +995,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
         }
       }
-      if constexpr (SPLIT) {
+      if (do_reduce) {
         // Count this warp's chunks in; the last split to arrive finishes them.
         unsigned last = 0;
         unsigned* cnt = sk.cnt + static_cast<int64_t>(tile) * kEpiWarps + warp;
@@ -759,28 +1013,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (col0 >= N) break;
             const int ci = (c - half) >> 1;
             uint32_t cur[32];
-            int32_t* src = sk.acc + static_cast<int64_t>(grow) * N + col0;
-            if (grow < M && col0 + 32 <= N) {
-              // rows of the scratch are 16-byte aligned (N % 4 == 0)
-              int4* s4 = reinterpret_cast<int4*>(src);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const int4 v = __ldcg(s4 + i);
-                cur[4 * i] = static_cast<uint32_t>(v.x);
-                cur[4 * i + 1] = static_cast<uint32_t>(v.y);
-                cur[4 * i + 2] = static_cast<uint32_t>(v.z);
-                cur[4 * i + 3] = static_cast<uint32_t>(v.w);
-              }
-#pragma unroll
-              for (int i = 0; i < 8; ++i) __stcg(s4 + i, make_int4(0, 0, 0, 0));
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const bool in = grow < M && col0 + j < N;
-                cur[j] = in ? static_cast<uint32_t>(__ldcg(src + j)) : 0u;
-                if (in) __stcg(src + j, 0);
-              }
-            }
+            splitk_take_chunk<BN>(sk, srow0 + lane, c * 32, grow < M, cur);
             finish_chunk<KIND, OutT, ORDER, ACT>(cur, s_ws + ci * 32, s_bias + ci * 32, xs_row,
                                                  has_bias, has_resid, ep, grow, col0, row0, M, N,
                                                  st, &tmD, lane);
@@ -926,6 +1159,14 @@ EpilogueParams to_params(const GemmArgs& g) {
   ep.sfb = static_cast<const uint8_t*>(g.sfb);
   ep.sf_ncb = static_cast<int>((g.K + 127) / 128);
   ep.b_tiles_kb = g.b_tiled ? static_cast<int>((g.K + kBK - 1) / kBK) : 0;
+  if (g.rms_rope) {
+    ep.act = kActRmsRope;
+    ep.rope_w = g.rope_w;
+    ep.rope_w_percol = g.rope_w_percol;
+    ep.rope_f = g.rope_f;
+    ep.rope_cols = static_cast<int>(g.rope_cols);
+    ep.rope_eps = g.rope_eps;
+  }
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   ep.vec_ws = ep.ws && a16(ep.ws);
   ep.vec_bias = ep.bias && a16(ep.bias);
@@ -939,8 +1180,7 @@ template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG, bool SPLI
 int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
               const CUtensorMap& mw, SplitArgs sk, int group_m, int max_ctas, cudaStream_t stream) {
   // The same configuration the kernel lays its shared memory out with: the
-  // block-scaled kind adds scale-factor bytes to every stage, split-K wider
-  // staging tiles.
+  // block-scaled kind adds scale-factor bytes to every stage.
   using C = Cfg<BN, OutT, CG, KIND, SPLIT>;
   auto kern = gemm_sm100_kernel<KIND, BN, OutT, ORDER, ACT, CG, SPLIT>;
   static bool attr_set[64] = {};
@@ -1009,9 +1249,10 @@ int launch_simt(const GemmArgs& g, cudaStream_t stream) {
 }
 
 template <int KIND, typename OutT>
-int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_ctas, int cg,
-                 int splits, cudaStream_t stream) {
+int dispatch_out(const GemmArgs& g, bool tc_ok, const GemmPlan& plan, cudaStream_t stream) {
   if (!tc_ok) return launch_simt<KIND, OutT>(g, stream);
+  const int bn = plan.bn, cg = plan.cg, group_m = plan.group_m, max_ctas = plan.max_ctas;
+  const int splits = plan.splits;
   CUtensorMap ma, mb, md, mw;
   bool ok = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.a, g.K, g.M, g.lda, kBK, kBM,
                         CU_TENSOR_MAP_SWIZZLE_128B);
@@ -1033,13 +1274,14 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
                          sizeof(OutT) == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   SplitArgs sk{nullptr, nullptr, 1};
   if (splits > 1) {
-    // int32 [M, N] partial sums, then the arrival counters
+    // int32 [tiles * 128, bn] partial sums, then the arrival counters;
+    // reductions in 32-row x 16-column boxes
     sk.acc = static_cast<int32_t*>(g.workspace);
     sk.cnt = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(g.workspace) +
-                                         splitk_acc_bytes(g.M, g.N));
+                                         splitk_acc_bytes(plan.split_tiles, bn));
     sk.splits = splits;
-    ok = ok && make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, g.workspace, g.N, g.M, g.N, 32,
-                           32, CU_TENSOR_MAP_SWIZZLE_128B);
+    ok = ok && make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, g.workspace, bn,
+                           plan.split_tiles * kBM, bn, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   } else {
     mw = md;
   }
@@ -1051,12 +1293,35 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
   auto by_bn = [&](auto order_c, auto act_c) {
     constexpr int O = decltype(order_c)::value;
     constexpr int A = decltype(act_c)::value;
-    if constexpr (KIND == 2) {
+    if constexpr (A == kActRmsRope) {
+      // int8 with bf16 output only (checked by gemm_launch); one CTA per tile
+      if constexpr (KIND == 0 && std::is_same<OutT, __nv_bfloat16>::value) {
+        if (splits > 1) {
+          if (bn == 128) {
+            return launch_tc<KIND, 128, OutT, O, A, 1, true>(g, ma, mb, md, mw, sk, group_m,
+                                                             max_ctas, stream);
+          }
+          return launch_tc<KIND, 256, OutT, O, A, 1, true>(g, ma, mb, md, mw, sk, group_m, max_ctas,
+                                                           stream);
+        }
+        if (bn == 128) {
+          return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
+        }
+        return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
+      } else {
+        set_error("the RMSNorm + RoPE epilogue needs int8 operands and bf16 output");
+        return W8A8_ERR_VALUE;
+      }
+    } else if constexpr (KIND == 2) {
       return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
     } else {
       if constexpr (KIND == 0 && !std::is_same<OutT, int32_t>::value) {
         if (splits > 1) {
-          return launch_tc<KIND, 128, OutT, O, A, 1, true>(g, ma, mb, md, mw, sk, group_m, max_ctas,
+          if (bn == 128) {
+            return launch_tc<KIND, 128, OutT, O, A, 1, true>(g, ma, mb, md, mw, sk, group_m,
+                                                             max_ctas, stream);
+          }
+          return launch_tc<KIND, 256, OutT, O, A, 1, true>(g, ma, mb, md, mw, sk, group_m, max_ctas,
                                                            stream);
         }
       }
@@ -1080,6 +1345,15 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
     if (KIND != 0) {
       return act == kActGeluTanh ? by_bn(I2{}, I1{}) : by_bn(I2{}, I0{});
     }
+    if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+      if (g.rms_rope) {
+        switch (order) {
+          case 0: return by_bn(I0{}, I2{});
+          case 1: return by_bn(I1{}, I2{});
+          default: return by_bn(I2{}, I2{});
+        }
+      }
+    }
     switch (order * 2 + (act == kActGeluTanh ? 1 : 0)) {
       case 0: return by_bn(I0{}, I0{});
       case 1: return by_bn(I0{}, I1{});
@@ -1093,44 +1367,45 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, int bn, int group_m, int max_cta
 
 }  // namespace
 
-int64_t splitk_acc_bytes(int64_t M, int64_t N) { return (M * N * 4 + 255) / 256 * 256; }
+int64_t splitk_acc_bytes(int64_t split_tiles, int bn) {
+  return split_tiles * kBM * bn * 4;  // a multiple of 256 bytes
+}
 
 int64_t splitk_workspace_bytes(int64_t M, int64_t N) {
   const int64_t tiles128 = ((M + kBM - 1) / kBM) * ((N + 127) / 128);
-  return splitk_acc_bytes(M, N) + tiles128 * kEpiWarps * 4;
+  return splitk_acc_bytes(tiles128, 128) + tiles128 * kEpiWarps * 4;
 }
 
-int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
-  if (g.M == 0 || g.N == 0) return 0;
+int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& p) {
   const int out_bytes = g.out_dtype == W8A8_F32 || g.out_dtype == W8A8_S32 ? 4 : 2;
-  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  const bool tc_ok = g.K > 0 && g.K % 16 == 0 && g.lda % 16 == 0 && g.ldb % 16 == 0 &&
-                     a16(g.a) && a16(g.b) && a16(g.out) && (g.ldo * out_bytes) % 16 == 0 &&
-                     g.M < (1ll << 31) && g.N < (1ll << 31) && g.K < (1ll << 31);
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
   int bn = g.cfg && g.cfg->block_n ? g.cfg->block_n : 0;
   if (bn != 0 && bn != 128 && bn != 256) {
     set_error("block_n must be 128 or 256, got %d", bn);
     return W8A8_ERR_VALUE;
   }
+  const int sms = device_sm_count();
   if (bn == 0) {
     // 256-column tiles when they alone fill every SM; otherwise the 128-column
     // tiles' extra parallelism wins (measured on B200: 256 x 12288 -> 3072
     // runs 27% faster with 128-column tiles, 5600 x 3072 -> 3072 50% slower).
-    const int sms = device_sm_count();
     const long long tiles256 = ((g.M + kBM - 1) / kBM) * ((g.N + 255) / 256);
     bn = tiles256 >= sms && g.N >= 256 ? 256 : 128;
   }
-  const int group_m = g.cfg && g.cfg->group_m > 0 ? g.cfg->group_m : 8;
-  const int max_ctas = g.cfg ? g.cfg->max_ctas : 0;
+  p.group_m = g.cfg && g.cfg->group_m > 0 ? g.cfg->group_m : 8;
+  p.max_ctas = g.cfg ? g.cfg->max_ctas : 0;
   int cg = g.cfg && g.cfg->cta_group ? g.cfg->cta_group : 0;
   if (cg != 0 && cg != 1 && cg != 2) {
     set_error("cta_group must be 1 or 2, got %d", cg);
     return W8A8_ERR_VALUE;
   }
-  // One CTA per tile by default: on B200 the CTA-pair variant measured 1-4%
-  // slower on the 5600-row shapes (its B traffic saving does not pay while the
-  // epilogue bounds the tile rate).
-  if (cg == 0) cg = 1;
+  // Default: CTA pairs (each SM loading half of B, six pipeline stages instead
+  // of four) for int8 GEMMs with K >= 8192, one CTA per tile otherwise.  On
+  // B200 the pair runs 5600 x 12288 -> 3072 in 139 us against 148 us, while at
+  // K = 3072 it is 3-4% slower (5600 x 3072 -> 12288 + GELU: 153 us against
+  // 148 us): the longer a tile's K loop, the less the per-tile epilogue costs
+  // against the pair's cheaper operand stream.
+  if (cg == 0) cg = (g.kind == 0 && bn == 256 && g.K >= 8192) ? 2 : 1;
   if (g.b_tiled) {
     // pre-tiled weights: 128-column tiles, one CTA per tile, tcgen05 path only
     if (!(g.kind == 0 && g.K > 0 && g.K % 16 == 0 && g.lda % 16 == 0 && a16(g.a) && a16(g.b) &&
@@ -1141,60 +1416,113 @@ int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     bn = 128;
     cg = 1;
   }
-  if (bn == 128) cg = 1;  // pairs are built for 256-column tiles
-  // Split-K (int8 with a dequant epilogue, scratch given): when one split
-  // per 128-column tile leaves SMs idle, cut K so tiles x splits fills them,
-  // keeping at least 4 K-blocks (512 bytes of K) per split.
-  int splits = 1;
-  if (g.workspace && g.kind == 0 && g.out_dtype != W8A8_S32 && tc_ok && g.N % 4 == 0 &&
-      g.split_k != 1) {
+  if (g.rms_rope) cg = 1;  // heads of 128 columns per epilogue warp half, 1-CTA tiles
+  if (bn == 128) cg = 1;   // pairs are built for 256-column tiles
+  p.splits = 1;
+  p.split_tiles = 0;
+  p.workspace_need = 0;
+  // Split-K (int8 with a dequant epilogue, scratch given or asked about):
+  // explicit split_k > 1, or 128 x 128 tiles that leave SMs idle (few rows):
+  // every 128-column tile is cut into `splits` K ranges, keeping at least 4
+  // K-blocks (512 bytes of K) per split.  Large GEMMs run every tile whole:
+  // cutting only the trailing, partial wave of tiles in K measured slower on
+  // B200 (5600 x 3072 -> 3072: 48 us whole, 114 us with its last 84 tiles cut
+  // in five), because the TMA add-reductions of the int32 partials into L2
+  // sustain under 1 TB/s.
+  if (g.kind == 0 && g.out_dtype != W8A8_S32 && tc_ok && g.N % 4 == 0 && g.split_k != 1) {
     const int num_kb = static_cast<int>((g.K + kBK - 1) / kBK);
-    const long long tiles128 = ((g.M + kBM - 1) / kBM) * ((g.N + 127) / 128);
+    const int64_t tiles128 = ((g.M + kBM - 1) / kBM) * ((g.N + 127) / 128);
+    int full = 1;
     if (g.split_k > 1) {
-      splits = std::min(g.split_k, num_kb);
+      full = std::min(g.split_k, num_kb);
     } else {
-      const long long fill = device_sm_count() / std::max(1ll, tiles128);
-      splits = static_cast<int>(std::min<long long>(fill, std::min(8, num_kb / 4)));
+      const int64_t fill = sms / std::max<int64_t>(1, tiles128);
+      full = static_cast<int>(std::min<int64_t>(fill, std::min(8, num_kb / 4)));
     }
-    if (splits > 1) {
-      if (g.workspace_bytes < splitk_workspace_bytes(g.M, g.N)) {
-        set_error("split-K scratch of %lld bytes is smaller than the %lld bytes M=%lld N=%lld need",
-                  static_cast<long long>(g.workspace_bytes),
-                  static_cast<long long>(splitk_workspace_bytes(g.M, g.N)),
-                  static_cast<long long>(g.M), static_cast<long long>(g.N));
-        return W8A8_ERR_VALUE;
-      }
-      if (reinterpret_cast<uintptr_t>(g.workspace) & 255u) {
-        set_error("split-K scratch must be 256-byte aligned");
-        return W8A8_ERR_VALUE;
-      }
+    if (full > 1) {
+      p.splits = full;
+      p.split_tiles = tiles128;
+      p.workspace_need = splitk_acc_bytes(tiles128, 128) + tiles128 * kEpiWarps * 4;
       bn = 128;
       cg = 1;
-    } else {
-      splits = 1;
+    }
+  }
+  p.bn = bn;
+  p.cg = cg;
+  return 0;
+}
+
+int gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
+  GemmArgs g = g_in;  // split_k is cleared below when no scratch is given
+  if (g.M == 0 || g.N == 0) return 0;
+  const int out_bytes = g.out_dtype == W8A8_F32 || g.out_dtype == W8A8_S32 ? 4 : 2;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const bool tc_ok = g.K > 0 && g.K % 16 == 0 && g.lda % 16 == 0 && g.ldb % 16 == 0 &&
+                     a16(g.a) && a16(g.b) && a16(g.out) && (g.ldo * out_bytes) % 16 == 0 &&
+                     g.M < (1ll << 31) && g.N < (1ll << 31) && g.K < (1ll << 31);
+  if (g.rms_rope) {
+    // heads of 128 columns, one per epilogue warp half: the 1-CTA tcgen05 GEMM
+    if (!(g.kind == 0 && g.out_dtype == W8A8_BF16 && tc_ok && !g.b_tiled)) {
+      set_error("the RMSNorm + RoPE epilogue needs int8 operands, bf16 output, row-major weights, "
+                "K %% 16 == 0 and 16-byte aligned operands");
+      return W8A8_ERR_VALUE;
+    }
+    if (g.epi && (g.epi->activation != kActNone || g.epi->residual)) {
+      set_error("the RMSNorm + RoPE epilogue takes no output activation or residual");
+      return W8A8_ERR_VALUE;
+    }
+    if (g.rope_cols < 0 || g.rope_cols > g.N || g.rope_cols % 128 != 0 || g.N % 128 != 0) {
+      set_error("RoPE columns (%lld) and N (%lld) must be multiples of the 128-column head, "
+                "rope columns <= N", static_cast<long long>(g.rope_cols),
+                static_cast<long long>(g.N));
+      return W8A8_ERR_VALUE;
+    }
+    if (g.rope_cols > 0 && (!g.rope_w || !g.rope_f ||
+                            (reinterpret_cast<uintptr_t>(g.rope_w) & 15u) ||
+                            (reinterpret_cast<uintptr_t>(g.rope_f) & 15u))) {
+      set_error("RoPE needs a 16-byte aligned norm weight and rotations");
+      return W8A8_ERR_VALUE;
+    }
+  }
+  if (!g.workspace) g.split_k = 1;
+  GemmPlan plan{};
+  if (int rc = plan_gemm(g, tc_ok, plan)) return rc;
+  if (plan.splits > 1) {
+    if (g.workspace_bytes < plan.workspace_need) {
+      set_error("split-K scratch of %lld bytes is smaller than the %lld bytes M=%lld N=%lld need",
+                static_cast<long long>(g.workspace_bytes),
+                static_cast<long long>(plan.workspace_need), static_cast<long long>(g.M),
+                static_cast<long long>(g.N));
+      return W8A8_ERR_VALUE;
+    } else if (reinterpret_cast<uintptr_t>(g.workspace) & 255u) {
+      set_error("split-K scratch must be 256-byte aligned");
+      return W8A8_ERR_VALUE;
     }
   }
   if (g.kind == 0) {
     switch (g.out_dtype) {
-      case W8A8_BF16: return dispatch_out<0, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, cg, splits, stream);
-      case W8A8_F16: return dispatch_out<0, __half>(g, tc_ok, bn, group_m, max_ctas, cg, splits, stream);
-      case W8A8_F32: return dispatch_out<0, float>(g, tc_ok, bn, group_m, max_ctas, cg, splits, stream);
-      case W8A8_S32: return dispatch_out<0, int32_t>(g, tc_ok, bn, group_m, max_ctas, cg, 1, stream);
+      case W8A8_BF16: return dispatch_out<0, __nv_bfloat16>(g, tc_ok, plan, stream);
+      case W8A8_F16: return dispatch_out<0, __half>(g, tc_ok, plan, stream);
+      case W8A8_F32: return dispatch_out<0, float>(g, tc_ok, plan, stream);
+      case W8A8_S32: return dispatch_out<0, int32_t>(g, tc_ok, plan, stream);
       default: break;
     }
   } else if (g.kind == 2) {
     const bool mx_ok = tc_ok && g.K % 32 == 0 && a16(g.sfa) && a16(g.sfb);
+    GemmPlan mx_plan = plan;  // 128-column tiles, one CTA per tile
+    mx_plan.bn = 128;
+    mx_plan.cg = 1;
     switch (g.out_dtype) {
-      case W8A8_BF16: return dispatch_out<2, __nv_bfloat16>(g, mx_ok, 128, group_m, max_ctas, 1, 1, stream);
-      case W8A8_F16: return dispatch_out<2, __half>(g, mx_ok, 128, group_m, max_ctas, 1, 1, stream);
-      case W8A8_F32: return dispatch_out<2, float>(g, mx_ok, 128, group_m, max_ctas, 1, 1, stream);
+      case W8A8_BF16: return dispatch_out<2, __nv_bfloat16>(g, mx_ok, mx_plan, stream);
+      case W8A8_F16: return dispatch_out<2, __half>(g, mx_ok, mx_plan, stream);
+      case W8A8_F32: return dispatch_out<2, float>(g, mx_ok, mx_plan, stream);
       default: break;
     }
   } else {
     switch (g.out_dtype) {
-      case W8A8_BF16: return dispatch_out<1, __nv_bfloat16>(g, tc_ok, bn, group_m, max_ctas, cg, 1, stream);
-      case W8A8_F16: return dispatch_out<1, __half>(g, tc_ok, bn, group_m, max_ctas, cg, 1, stream);
-      case W8A8_F32: return dispatch_out<1, float>(g, tc_ok, bn, group_m, max_ctas, cg, 1, stream);
+      case W8A8_BF16: return dispatch_out<1, __nv_bfloat16>(g, tc_ok, plan, stream);
+      case W8A8_F16: return dispatch_out<1, __half>(g, tc_ok, plan, stream);
+      case W8A8_F32: return dispatch_out<1, float>(g, tc_ok, plan, stream);
       default: break;
     }
   }

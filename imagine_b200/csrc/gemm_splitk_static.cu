@@ -73,7 +73,8 @@ int gemm_splitk_static_launch(GemmArgs g, cudaStream_t stream) {
   const int64_t need = splitk_workspace_bytes(g.M, g.N);
   if (need > kStaticScratchBytes) {
     set_error("M=%lld x N=%lld needs %lld bytes of split-K scratch; the static scratch holds %lld "
-              "bytes (M * N * 4 plus one counter per 128 x 128 tile and epilogue warp)",
+              "bytes (64 KiB per 128 x 128 output tile plus one counter per tile and epilogue "
+              "warp)",
               static_cast<long long>(g.M), static_cast<long long>(g.N),
               static_cast<long long>(need), static_cast<long long>(kStaticScratchBytes));
     return W8A8_ERR_VALUE;

@@ -5,7 +5,7 @@
 // body inference/src/backend_rope.rs:146-223; Kitchen kernel KSRC
 // backends/cuda/ops/rms_rope.cu:38-240, rope_device.cuh:65-97) for the
 // interleaved (non-split) rotation over the full head:
-//   rrms  = rsqrt(sum(x^2) / D + eps)                       (fp32)
+//   rrms  = 1 / sqrt(sum(x^2) / D + eps)                    (fp32)
 //   n     = T(x * rrms * w)                                 (one rounding)
 //   (y0, y1) = (f00 n0 + f01 n1, f10 n0 + f11 n1)           (fp32)
 //   out   = T(y)
@@ -97,7 +97,8 @@ __device__ __forceinline__ void rms_rope_vals(float (&v)[EPL], const float (&wv)
   for (int j = 0; j < EPL; ++j) ss = __fmaf_rn(v[j], v[j], ss);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-  const float rrms = rsqrtf(ss / static_cast<float>(D) + eps);
+  // 1 / sqrt in two IEEE roundings, the form torch's rsqrt takes
+  const float rrms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), eps)));
 #pragma unroll
   for (int j = 0; j < EPL; j += 2) {
     const float n0 = RT<T>::f(RT<T>::t(__fmul_rn(__fmul_rn(v[j], rrms), wv[j])));
@@ -197,7 +198,39 @@ int launch_rope(const void* q, const void* k, void* q_out, void* k_out, int64_t 
   return 0;
 }
 
+// Row-blocked copy of the rotations for the fused projection epilogue (one
+// lane per row there): out[((r / 32) * 64 + p) * 32 + r % 32] = the float4
+// (f00, f01, f10, f11) of pair p at token r % freq_rows, for every row r of
+// rows_pad (a multiple of 128).  One thread per (row, pair); consecutive
+// threads write consecutive rows of one pair, so stores are coalesced.
+__global__ void __launch_bounds__(256) rope_freqs_rows_kernel(const float4* __restrict__ freqs,
+                                                             int64_t freq_rows, int64_t rows_pad,
+                                                             float4* __restrict__ out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;  // output float4
+  if (i >= rows_pad * 64) return;
+  const int64_t lane = i & 31;
+  const int64_t p = (i >> 5) & 63;
+  const int64_t blk = i >> 11;
+  const int64_t r = blk * 32 + lane;
+  out[i] = __ldg(freqs + (r % freq_rows) * 64 + p);
+}
+
 }  // namespace
+
+int rope_freqs_rows_launch(const float* freqs, int64_t freq_rows, int64_t rows, float* out,
+                           cudaStream_t stream) {
+  const int64_t rows_pad = (rows + 127) / 128 * 128;
+  const int64_t n = rows_pad * 64;
+  if (n == 0) return 0;
+  rope_freqs_rows_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(freqs), freq_rows, rows_pad, reinterpret_cast<float4*>(out));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("rope_freqs_rows launch failed: %s", cudaGetErrorString(e));
+    return W8A8_ERR_ACCELERATOR;
+  }
+  return 0;
+}
 
 int rms_rope_launch(const void* q, const void* k, void* q_out, void* k_out, int dtype,
                     int64_t rows, int heads, int head_dim, int64_t ldq, int64_t ldk, int64_t ldqo,

@@ -53,11 +53,27 @@ struct GemmArgs {
   int64_t workspace_bytes;
   // B in the pre-tiled layout of w8a8_pack_weight_tiles (kind 0 only)
   int b_tiled;
+  // per-head RMSNorm + RoPE epilogue (kind 0, bf16 output)
+  int rms_rope;
+  const void* rope_w;
+  int rope_w_percol;
+  const float* rope_f;  // row-blocked rotations (w8a8_rope_freqs_rows)
+  int64_t rope_cols;
+  float rope_eps;
 };
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);
-// Split-K scratch: int32 [M, N] partial sums (padded to 256 bytes), then one
-// arrival counter per (128 x 128 tile, epilogue warp).
-int64_t splitk_acc_bytes(int64_t M, int64_t N);
+// Tile shape and split-K layout gemm_launch uses for a GEMM.
+struct GemmPlan {
+  int bn, cg, group_m, max_ctas;
+  int splits;              // > 1: every tile is cut into this many K ranges
+  int64_t split_tiles;     // tiles cut in K
+  int64_t workspace_need;  // scratch bytes the split tiles use (0 without splits)
+};
+// tc_ok: the operands suit the tcgen05 path.  Returns 0 or an error code.
+int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& plan);
+// Split-K scratch: int32 partial sums [tiles * 128, bn], then one arrival
+// counter per (tile, epilogue warp).
+int64_t splitk_acc_bytes(int64_t split_tiles, int bn);
 int64_t splitk_workspace_bytes(int64_t M, int64_t N);
 // Pre-tiled weights: [ceil(N/128)][ceil(K/128)][128 rows][128 bytes], zero
 // padded (gemv.cu).
@@ -84,6 +100,9 @@ int quantize_fp8_tensor_launch(const void* x, int x_dtype, int64_t numel, const 
                                uint8_t* out, cudaStream_t stream);
 
 // Q/K RMSNorm + interleaved RoPE (rope.cu); k may be NULL.
+// Row-blocked rotations for the fused RMSNorm + RoPE epilogue (rope.cu).
+int rope_freqs_rows_launch(const float* freqs, int64_t freq_rows, int64_t rows, float* out,
+                           cudaStream_t stream);
 int rms_rope_launch(const void* q, const void* k, void* q_out, void* k_out, int dtype,
                     int64_t rows, int heads, int head_dim, int64_t ldq, int64_t ldk, int64_t ldqo,
                     int64_t ldko, const float* freqs, int64_t freq_rows, const void* q_scale,

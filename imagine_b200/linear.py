@@ -386,6 +386,102 @@ def rms_rope(q: torch.Tensor, k: Optional[torch.Tensor], freqs_cis: torch.Tensor
     return qo.reshape(q.shape), (ko.reshape(k.shape) if ko is not None else None)
 
 
+_FREQS_ROWS: dict = {}
+
+
+def rope_freqs_rows(freqs_cis: torch.Tensor, rows: int) -> torch.Tensor:
+    """The row-blocked rotations the fused RMSNorm + RoPE epilogue reads
+    (w8a8_rope_freqs_rows): freqs_cis [S, 64, 2, 2] (or with leading broadcast
+    dimensions) for ``rows`` token rows, row r at position r % S.  Built once
+    per (freqs_cis, rows) and cached: every block of a forward pass shares
+    them."""
+    _cuda("freqs_cis", freqs_cis)
+    f = freqs_cis.to(dtype=torch.float32).reshape(-1, 64, 2, 2).contiguous()
+    if f.shape[0] == 0 or rows % f.shape[0]:
+        raise ValueError(f"freqs_cis has {f.shape[0]} positions for {rows} token rows")
+    key = (f.device.index, f.data_ptr(), f._version, f.shape[0], rows)
+    hit = _FREQS_ROWS.get(key)
+    if hit is None:
+        if len(_FREQS_ROWS) >= 8:
+            _FREQS_ROWS.pop(next(iter(_FREQS_ROWS)))
+        n = int(N.LIB.w8a8_rope_freqs_rows_bytes(rows)) // 4
+        blocked = torch.empty(n, dtype=torch.float32, device=f.device)
+        N.check(N.LIB.w8a8_rope_freqs_rows(_vp(f), f.shape[0], rows, _vp(blocked),
+                                           _stream(f.device)))
+        # the entry keeps the source alive too: once freed, its address could
+        # come back holding other rotations under the same key
+        hit = _FREQS_ROWS[key] = (blocked, f)
+    return hit[0]
+
+
+def int8_linear_rms_rope(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tensor,
+                         bias: Optional[torch.Tensor], norm_weight: torch.Tensor,
+                         freqs_cis: torch.Tensor, epsilon: float = 1e-6,
+                         rope_cols: Optional[int] = None, *, dequant: str = "eager",
+                         scale_mode: str = "eager", split_k: Optional[int] = None, config=None):
+    """The Q (or K) projection with its RMSNorm + RoPE fused into the GEMM
+    epilogue: ``rms_rope(int8_linear(x, weight, ...))`` of the reference's
+    attention (inference/src/models/qwen_image21/dit.rs:427-429, 486-505) for
+    head_dim 128, with bf16 output.  Columns ``[0, rope_cols)`` (default: all)
+    are 128-column heads normalised with ``norm_weight`` -- [128] shared by
+    every head, or [rope_cols] per column (q_norm then k_norm for a fused QKV
+    weight) -- and rotated by ``freqs_cis`` [S, 64, 2, 2] (row r of x uses
+    position r % S); later columns (v) get the plain epilogue.  Returns
+    [..., N] bf16."""
+    _cuda("x", x)
+    dev = x.device
+    _cuda("weight", weight, dev)
+    if weight.dim() != 2 or weight.dtype != torch.int8:
+        raise ValueError("weight must be a 2-D int8 tensor [N, K]")
+    n, k = weight.shape
+    if x.shape[-1] != k:
+        raise ValueError(f"Input and weight inner dimensions must match, got {x.shape[-1]} and {k}")
+    rope_cols = n if rope_cols is None else int(rope_cols)
+    if n % 128 or rope_cols % 128 or not 0 <= rope_cols <= n:
+        raise ValueError(f"N ({n}) and rope_cols ({rope_cols}) must be multiples of the 128-column "
+                         "head with rope_cols <= N")
+    ws = weight_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    if ws.numel() not in (1, n):
+        raise ValueError(f"INT8 weight scale must be scalar or per-output-channel, got "
+                         f"{tuple(weight_scale.shape)} for weight shape {tuple(weight.shape)}")
+    nw = norm_weight.to(device=dev, dtype=torch.bfloat16).reshape(-1).contiguous()
+    if nw.numel() not in (128, rope_cols):
+        raise ValueError(f"norm_weight must have 128 or rope_cols = {rope_cols} elements, got "
+                         f"{nw.numel()}")
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, k)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    fr = rope_freqs_rows(freqs_cis, m) if rope_cols and m > 0 else None
+    w = weight if weight.is_contiguous() else weight.contiguous()
+    b = bias.to(device=dev, dtype=torch.bfloat16).reshape(-1).contiguous() if bias is not None else None
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    if m == 0:
+        return out.reshape(*lead, n)
+    ep = _epilogue(ws, b, None, None, dequant, None, n, n)
+    stream = _stream(dev)
+    q = torch.empty((m, k), dtype=torch.int8, device=dev)
+    xs = torch.empty((m,), dtype=torch.float32, device=dev)
+    N.check(N.LIB.w8a8_quantize_rowwise(_vp(x2), _code(x2.dtype), m, k, k, _vp(q), k, _vp(xs),
+                                        SCALE_MODE[scale_mode], 0, 0, stream))
+    cfg = _config(config)
+    cfg = cfg if isinstance(cfg, N.GemmConfig) else None
+    if split_k is None:
+        nbytes = _auto_workspace_bytes(dev, m, n, k, cfg)
+    elif split_k > 1:
+        nbytes = int(N.LIB.w8a8_gemm_splitk_workspace_bytes(m, n))
+    else:
+        nbytes = 0
+    scratch = _splitk_scratch(dev, nbytes) if nbytes > 0 else None
+    N.check(N.LIB.w8a8_gemm_dequant_rms_rope(
+        _vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep), _vp(out), n, m, n, k, rope_cols,
+        _vp(nw), 1 if nw.numel() != 128 else 0, _vp(fr), float(epsilon),
+        int(split_k or 0) if scratch is not None else 1, _vp(scratch),
+        scratch.numel() if scratch is not None else 0, _cfg_ptr(cfg), stream))
+    return out.reshape(*lead, n)
+
+
 def quantize_weight(weight: torch.Tensor, convrot: bool = False, convrot_groupsize: int = 256, *,
                     scale_mode: str = "eager"):
     """Offline per-output-channel weight quantisation
@@ -510,6 +606,23 @@ def pack_weight_tiles(weight: torch.Tensor) -> TiledInt8Weight:
 _SPLITK_SCRATCH: dict = {}
 
 
+_AUTO_WS: dict = {}
+
+
+def _auto_workspace_bytes(dev, m, n, k, cfg) -> int:
+    """Scratch bytes the library's automatic split policy uses for this shape
+    (few-row split-K, or the tail-wave spread of a large GEMM); 0 for none."""
+    c = cfg if isinstance(cfg, N.GemmConfig) else None
+    key = (dev.index, m, n, k, None if c is None else (c.block_n, c.group_m, c.max_ctas, c.cta_group))
+    v = _AUTO_WS.get(key)
+    if v is None:
+        with torch.cuda.device(dev):
+            v = int(N.LIB.w8a8_gemm_auto_workspace_bytes(m, n, k, _cfg_ptr(c)))
+        N.check(0 if v >= 0 else v)
+        _AUTO_WS[key] = v
+    return v
+
+
 def _splitk_scratch(dev: torch.device, nbytes: int) -> torch.Tensor:
     """Zero-filled split-K scratch, one per (device, stream): the kernels leave
     it zero-filled after every call, and calls on one stream never overlap."""
@@ -558,12 +671,12 @@ def _gemm_dequant(q, w, xs, ep, out, out_dtype, m, n, k, cfg, split_k, stream):
     if cfg == "auto":
         cfg = _autotuned_config(q, w, xs, ep, out, out_dtype, m, n, k, stream)
         split_k = 1 if split_k is None else split_k
-    use_split = split_k is not None and split_k > 1
-    if split_k is None and m > 0 and n % 4 == 0 and k >= 1024:
-        tiles = -(-m // 128) * -(-n // 128)
-        use_split = 2 * tiles <= torch.cuda.get_device_properties(dev).multi_processor_count
-    if use_split:
+    nbytes = 0
+    if split_k is None and m > 0:
+        nbytes = _auto_workspace_bytes(dev, m, n, k, cfg)
+    elif split_k is not None and split_k > 1:
         nbytes = int(N.LIB.w8a8_gemm_splitk_workspace_bytes(m, n))
+    if nbytes > 0:
         scratch = _splitk_scratch(dev, nbytes)
         N.check(N.LIB.w8a8_gemm_dequant_splitk(
             _vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep), _vp(out), _code(out_dtype), n, m, n, k,

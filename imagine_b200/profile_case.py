@@ -4,6 +4,7 @@ ncu summaries under profiles/ were captured with.
     python -m imagine_b200.profile_case --kernel gemm --m 5600 --k 3072 --n 3072
     python -m imagine_b200.profile_case --kernel quantize --m 5600 --k 3072
     python -m imagine_b200.profile_case --kernel gemv --m 2 --k 3072 --n 18432
+    python -m imagine_b200.profile_case --kernel gemm_rope --m 5600 --k 3072 --n 9216 --rope-cols 6144
 
 Inputs are seeded synthetic tensors of the BASELINE distributions; every
 launch is checked for device errors afterwards.
@@ -20,7 +21,8 @@ import imagine_b200 as W
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", choices=["gemm", "gemm_gelu", "gemm_s32", "quantize", "convrot",
-                                                       "gemv", "fp8_gemm", "mxfp8_gemm", "rms_rope"],
+                                                       "gemv", "fp8_gemm", "mxfp8_gemm", "rms_rope",
+                                                       "gemm_rope"],
                     required=True)
     ap.add_argument("--m", type=int, default=5600)
     ap.add_argument("--k", type=int, default=3072)
@@ -28,6 +30,8 @@ def main():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--block-n", type=int, default=0)
     ap.add_argument("--cta-group", type=int, default=0)
+    ap.add_argument("--rope-cols", type=int, default=-1,
+                    help="gemm_rope: columns that get RMSNorm + RoPE (default: all)")
     ap.add_argument("--tiled", action="store_true", help="GEMM on the pre-tiled weight layout")
     ap.add_argument("--split-k", type=int, default=1,
                     help="GEMM K splits (0: chosen from the SM count, 1: off)")
@@ -80,7 +84,34 @@ def main():
         w = (torch.randn(a.n, a.k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
         b = (torch.randn(a.n, generator=g) * 0.02).to(torch.bfloat16).to(dev)
         wq, ws = W.quantize_weight(w)
-        if a.kernel == "gemm_s32":
+        if a.kernel == "gemm_rope":
+            # the projection with its RMSNorm + RoPE epilogue, on pre-quantised
+            # activations (rows are the tokens of one sequence)
+            import ctypes
+            from imagine_b200 import _native as NAT
+            from imagine_b200.linear import _config, _epilogue, _stream, _vp
+            rc = a.n if a.rope_cols < 0 else a.rope_cols
+            q, xs = W.quantize_int8_rowwise(x)
+            y = torch.empty((a.m, a.n), dtype=torch.bfloat16, device=dev)
+            ep = _epilogue(ws, b, None, None, "eager", None, a.n, a.n)
+            c = _config(cfg)
+            ang = torch.rand(a.m, 64, generator=g) * 6.283
+            cs, sn = torch.cos(ang), torch.sin(ang)
+            f = torch.stack([torch.stack([cs, -sn], -1), torch.stack([sn, cs], -1)], -2).to(dev)
+            nw = torch.ones(max(rc, 128), dtype=torch.bfloat16, device=dev)
+            nbytes = 0
+            if a.split_k == 0:
+                with torch.cuda.device(dev):
+                    nbytes = NAT.LIB.w8a8_gemm_auto_workspace_bytes(a.m, a.n, a.k, ctypes.byref(c))
+            elif a.split_k > 1:
+                nbytes = NAT.LIB.w8a8_gemm_splitk_workspace_bytes(a.m, a.n)
+            ws_buf = torch.zeros(max(nbytes, 1), dtype=torch.uint8, device=dev)
+            fr = W.rope_freqs_rows(f, a.m)
+            run(lambda: NAT.check(NAT.LIB.w8a8_gemm_dequant_rms_rope(
+                _vp(q), a.k, _vp(wq), a.k, _vp(xs), ctypes.byref(ep), _vp(y), a.n, a.m, a.n, a.k,
+                rc, _vp(nw), 1 if rc != 128 else 0, _vp(fr), 1e-6, a.split_k,
+                _vp(ws_buf) if nbytes else None, nbytes, ctypes.byref(c), _stream(dev))))
+        elif a.kernel == "gemm_s32":
             q, _ = W.quantize_int8_rowwise(x)
             run(lambda: W.int8_gemm_s32(q, wq, config=cfg))
         elif a.kernel == "mxfp8_gemm":

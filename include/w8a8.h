@@ -182,6 +182,46 @@ int w8a8_rms_rope(const void* q, const void* k, void* q_out, void* k_out, int dt
                   int64_t ldko, const float* freqs, int64_t freq_rows, const void* q_scale,
                   const void* k_scale, float eps, void* stream);
 
+/* ---- a8 fused: the Q or K projection with its RMSNorm + RoPE epilogue ------
+ * Replaces the pair `project(q)` (w8a8_gemm_dequant, bf16 output) followed by
+ * `rms_rope(q, k, freqs_cis, q_scale, k_scale, epsilon)` (call sites
+ * inference/src/models/qwen_image21/dit.rs:427-429 and 486-505; eager body
+ * inference/src/backend_rope.rs:146-223) for head_dim 128: the projection's
+ * output never makes the round trip through HBM that the stand-alone
+ * w8a8_rms_rope pays.  out (bf16, stride ldo) = epilogue(q . w^T) as
+ * w8a8_gemm_dequant computes it (activation NONE, no residual); then each
+ * 128-column head in columns [0, rope_cols) of every row r is normalised and
+ * rotated as w8a8_rms_rope does, with norm_w (bf16) [128] shared by every
+ * head or, with norm_w_per_column, [rope_cols] (e.g. q_norm for the q heads
+ * then k_norm for the k heads of a fused QKV weight).  Columns from rope_cols
+ * on (the v heads of a fused QKV weight) are stored as the plain GEMM stores
+ * them.  The rotations come row-blocked (freqs_rows, built for these M rows
+ * by w8a8_rope_freqs_rows), so that the epilogue, which holds one row per
+ * lane, reads them with coalesced loads.  N and rope_cols: multiples of 128;
+ * K % 16 == 0, 16-byte aligned operands (the tcgen05 path); norm_w and
+ * freqs_rows 16-byte aligned.  split_k, workspace and workspace_bytes as in
+ * w8a8_gemm_dequant_splitk (workspace NULL: no split).  Before the norm the
+ * values equal the plain GEMM's bit for bit; the row's sum of squares is
+ * added in a different order than w8a8_rms_rope's, so an output may differ
+ * from GEMM-then-w8a8_rms_rope by one bf16 ulp per rotated pair. */
+int w8a8_gemm_dequant_rms_rope(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,
+                               const float* xs, const w8a8_epilogue_t* epi, void* out, int64_t ldo,
+                               int64_t M, int64_t N, int64_t K, int64_t rope_cols,
+                               const void* norm_w, int norm_w_per_column, const float* freqs_rows,
+                               float eps, int split_k, void* workspace, int64_t workspace_bytes,
+                               const w8a8_gemm_config_t* cfg, void* stream);
+
+/* Row-blocked rotations for w8a8_gemm_dequant_rms_rope.  freqs: fp32
+ * [freq_rows, 64, 2, 2] (16-byte aligned), row r of the GEMM using freqs row
+ * r % freq_rows, as in w8a8_rms_rope.  out: w8a8_rope_freqs_rows_bytes(rows)
+ * bytes, 16-byte aligned; out[((r / 32) * 64 + p) * 32 + r % 32] is the
+ * 16-byte rotation (f00, f01, f10, f11) of pair p for row r, over rows padded
+ * to a multiple of 128.  The rotations are the same for every block of a
+ * forward pass: build them once per (freqs, rows). */
+int64_t w8a8_rope_freqs_rows_bytes(int64_t rows);
+int w8a8_rope_freqs_rows(const float* freqs, int64_t freq_rows, int64_t rows, float* out,
+                         void* stream);
+
 /* ---- row-parallel (K-sharded) quantisation --------------------------------
  * No reference counterpart: the reference runs on one GPU.  A K-sharded
  * activation needs the absmax of the whole row before any shard can be
@@ -221,10 +261,18 @@ int w8a8_gemm_dequant(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw
  * into `workspace`, so results are identical bit for bit to the unsplit
  * GEMM.  The caller owns the workspace, as it owns cublas_gemm_int8's
  * (cuda_linear.rs:769-780): at least w8a8_gemm_splitk_workspace_bytes(M, N)
- * bytes, 256-byte aligned, zero-filled before the first call; every call
- * leaves it zero-filled again.  Calls sharing a workspace must not overlap on
+ * bytes (64 KiB per 128 x 128 output tile plus counters), or for split_k = 0
+ * w8a8_gemm_auto_workspace_bytes(M, N, K, cfg), 256-byte aligned,
+ * zero-filled before the first call; every call leaves it zero-filled again.  Calls sharing a workspace must not overlap on
  * the GPU.  After a nonzero w8a8_device_error the workspace must be cleared. */
 int64_t w8a8_gemm_splitk_workspace_bytes(int64_t M, int64_t N);
+/* Scratch the automatic policy (split_k = 0) uses for an M x N x K int8 GEMM
+ * with a floating output and tile configuration cfg (NULL: defaults) on the
+ * current device: w8a8_gemm_splitk_workspace_bytes(M, N) when it splits the
+ * few-row shape, 0 when it runs every tile whole (then the workspace may be
+ * NULL). */
+int64_t w8a8_gemm_auto_workspace_bytes(int64_t M, int64_t N, int64_t K,
+                                       const w8a8_gemm_config_t* cfg);
 int w8a8_gemm_dequant_splitk(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,
                              const float* xs, const w8a8_epilogue_t* epi, void* out, int out_dtype,
                              int64_t ldo, int64_t M, int64_t N, int64_t K, int split_k,
@@ -260,8 +308,8 @@ int w8a8_gemm_dequant_tiled(const int8_t* q, int64_t ldq, const int8_t* tiles, c
  * allocates nothing: its scratch is an array of
  * W8A8_SPLITK_STATIC_SCRATCH_BYTES (8 MiB) built into the library, one per
  * device.  Shapes whose scratch (w8a8_gemm_splitk_workspace_bytes(M, N):
- * M * N * 4 bytes plus counters, e.g. up to 512 x 3072 or 256 x 6144) does not
- * fit are rejected with W8A8_ERR_VALUE and a message.  The first call on a
+ * 64 KiB per 128 x 128 output tile plus counters, e.g. up to 512 x 3072 or
+ * 256 x 6144) does not fit are rejected with W8A8_ERR_VALUE and a message.  The first call on a
  * device, with that device current, looks the array up
  * (cudaGetSymbolAddress); make it before any stream capture.  Each call clears
  * the part of the array it uses on `stream` before the GEMM.  All calls share

@@ -1,10 +1,15 @@
 """GPU parity of rms_rope (w8a8_rms_rope) against the eager oracle
 (inference/src/backend_rope.rs:146-223 restated in oracle/eager.py).
 
-Bar: rsqrt and the rotation's fused multiply-add differ from the CPU's
-arithmetic in the last fp32 bits, so outputs are held to max-abs-error <= 1%
-of output RMS, and 16-bit outputs (which only move where the fp32 value sits
-on a rounding boundary) to >= 99% identical."""
+Bar: the head's fp32 sum of squares is added in a different order than
+torch's CPU cascade sum, so 1/rms can differ in its last bit.  fp32 outputs
+are held to max-abs-error <= 1% of output RMS; 16-bit outputs only move where
+the fp32 value sits on a rounding boundary: a flipped normalised value moves
+both outputs of its pair through the rotation (|f| <= 1).  They are held to
+sqrt(2) ulps of the pair's magnitude plus one ulp of the element, >= 99%
+identical, and an error RMS <= 1% of the output RMS (a max-abs bound of 1% of
+RMS cannot hold for a normalised 16-bit output: one bf16 ulp at |y| >= 2 RMS
+is 1.56% of RMS)."""
 import pytest
 import torch
 
@@ -51,11 +56,20 @@ def test_rms_rope_matches_eager(dtype, d, with_k):
         got = got.float().cpu()
         ref = ref.float()
         rms = ref.pow(2).mean().sqrt().item()
-        assert (got - ref).abs().max().item() <= 0.01 * rms
-        if dtype != torch.float32:
-            # a 16-bit output only moves where the fp32 value sits on a
-            # rounding boundary
-            assert (got == ref).float().mean().item() >= 0.99
+        d = (got - ref).abs()
+        if dtype == torch.float32:
+            assert d.max().item() <= 0.01 * rms
+        else:
+            bits = 8 if dtype == torch.bfloat16 else 11
+
+            def ulp(v):
+                _, e = torch.frexp(v)
+                return torch.ldexp(torch.ones_like(v), e - bits)
+            p = ref.reshape(*ref.shape[:-1], -1, 2)
+            r = p.pow(2).sum(-1, keepdim=True).sqrt().expand_as(p).reshape(ref.shape)
+            assert bool((d <= 1.4143 * ulp(r) + ulp(ref)).all()), d.max().item()
+            assert (d == 0).float().mean().item() >= 0.99
+            assert d.pow(2).mean().sqrt().item() <= 0.01 * rms
     assert W().device_error() == 0
 
 

@@ -164,3 +164,16 @@ def test_pre_tiled_weights_bit_identical(m, k, n, split_k):
     got = W().int8_linear(xd, tw, wsd, bd, split_k=split_k)
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
     assert W().device_error() == 0
+
+
+def test_auto_workspace_bytes():
+    """The automatic policy's scratch: the full split's for few-row shapes,
+    none for shapes whose tiles fill the SMs (they run every tile whole)."""
+    from imagine_b200 import _native as N
+
+    with torch.cuda.device(cuda()):
+        assert N.LIB.w8a8_gemm_auto_workspace_bytes(5600, 12288, 3072, None) == 0
+        assert N.LIB.w8a8_gemm_auto_workspace_bytes(1400, 3072, 3072, None) == 0
+        assert (N.LIB.w8a8_gemm_auto_workspace_bytes(256, 3072, 12288, None)
+                == N.LIB.w8a8_gemm_splitk_workspace_bytes(256, 3072))
+        assert N.LIB.w8a8_gemm_auto_workspace_bytes(256, 3072, 256, None) == 0  # K too short
