@@ -37,6 +37,7 @@ class Epilogue(ctypes.Structure):
         ("residual_scale", ctypes.c_void_p),
         ("dequant_order", ctypes.c_int32),
         ("activation", ctypes.c_int32),
+        ("residual_scale_rows", ctypes.c_int64),
     ]
 
 

@@ -76,6 +76,10 @@ int check_epilogue(const w8a8_epilogue_t* epi, int64_t N, bool need_ws) {
   if (epi->residual && !epi->residual_scale) {
     return fail(W8A8_ERR_VALUE, "int8_linear: residual requires residual_scale");
   }
+  if (epi->residual && epi->residual_scale_rows < 0) {
+    return fail(W8A8_ERR_VALUE, "residual_scale_rows must be >= 0, got %lld",
+                static_cast<long long>(epi->residual_scale_rows));
+  }
   if (epi->residual && epi->ldr < N) {
     return fail(W8A8_ERR_VALUE, "residual row stride %lld < N=%lld",
                 static_cast<long long>(epi->ldr), static_cast<long long>(N));
@@ -100,7 +104,7 @@ const char* w8a8_last_error(void) { return g_last_error; }
 
 int w8a8_last_accelerator_code(void) { return g_last_accel; }
 
-int w8a8_abi_version(void) { return 100; }
+int w8a8_abi_version(void) { return 101; }
 
 int w8a8_device_error(void* stream) {
   int v = 0;

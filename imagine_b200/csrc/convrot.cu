@@ -38,6 +38,7 @@
 #include <type_traits>
 
 #include "quant_common.cuh"
+#include "sm100_ptx.cuh"
 #include "w8a8_internal.h"
 
 namespace w8a8 {
@@ -248,6 +249,7 @@ __global__ void __launch_bounds__(kMaxTeams * kTeam) quantize_act_rot_kernel(
     int kitchen_mode, int vec_in, int vec_out) {
   extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ float red[8];
+  griddep_launch_dependents();  // the GEMM that reads q may start its prologue
   const int row = blockIdx.x;
   const int team = threadIdx.x / kTeam;
   const int r = threadIdx.x % kTeam;

@@ -72,7 +72,10 @@ struct EpilogueParams {
   const void* bias;        // [N] in the output dtype, or nullptr
   const void* residual;    // [M, ldr] in the output dtype, or nullptr
   int64_t ldr;             // residual row stride (elements)
-  const void* rscale;      // [N] in the output dtype (required with residual)
+  const void* rscale;      // [N] in the output dtype (required with residual), or
+                           // [ceil(M / rscale_rows), N] when rscale_rows > 0
+  int64_t rscale_rows;     // output rows per rscale row (0: one row for all)
+  int64_t ld_rscale;       // rscale row stride (elements): N
   int dq_order;            // DequantOrder
   int act;                 // OutputAct
   int vec_ws;              // 1 if ws is 16-byte aligned (vector loads allowed)
@@ -113,6 +116,11 @@ __device__ __forceinline__ float dequant_one(float a, float xs_row, float ws_col
     y = OutTraits<OutT>::round(has_bias ? __fmaf_rn(t, ws_col, bias_col) : __fmul_rn(t, ws_col));
   }
   return y;
+}
+
+// Element offset of output row m's residual-scale row (the per-sample gate).
+__device__ __forceinline__ int64_t rscale_row(const EpilogueParams& ep, int64_t m) {
+  return ep.rscale_rows > 0 ? (m / ep.rscale_rows) * ep.ld_rscale : 0;
 }
 
 template <typename OutT>

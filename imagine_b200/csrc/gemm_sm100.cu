@@ -149,6 +149,17 @@ __device__ __forceinline__ void load_cols32(const void* p, int col0, int N, bool
   }
 }
 
+// The residual scales of this lane's row for columns col0..+31: the shared
+// [N] row (the same addresses for every lane) or, with a per-sample gate, the
+// row of the lane's sample (lanes of one sample read the same addresses).
+template <typename T>
+__device__ __forceinline__ void load_rscale32(const EpilogueParams& ep, int grow, int M, int col0,
+                                              int N, float (&v)[32]) {
+  const int64_t off = rscale_row(ep, min(grow, M - 1));
+  const bool vec = ep.vec_rscale && (off * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+  load_cols32<T>(static_cast<const T*>(ep.rscale) + off, col0, N, vec, v);
+}
+
 __device__ __forceinline__ void spin_ns(uint64_t ns) {
   const uint64_t t0 = globaltimer_ns();
   while (globaltimer_ns() - t0 < ns) {
@@ -292,23 +303,48 @@ __device__ __forceinline__ uint32_t epi_pair_bf16x2(float a0, float a1, uint64_t
   return bits;
 }
 
-// Split-K: every tile is cut into `splits` units of consecutive K-blocks,
-// run by different CTAs.  Scratch: the int32 partial sums of tile t at rows
-// t * 128 .. +127 of a [tiles * 128, BN] array, then one arrival counter per
-// (tile, epilogue warp); both all-zero between calls.
+// How the tiles are divided into units of work.
+// Split-K (splits > 1): every tile is cut into `splits` units of consecutive
+// K-blocks, run by different CTAs.  Scratch: the int32 partial sums of tile t
+// at rows t * 128 .. +127 of a [tiles * 128, BN] array, then one arrival
+// counter per (tile, epilogue warp); both all-zero between calls.
+// Otherwise tiles from `half_from` on run as two units of 128 columns each:
+// the last, partial wave of 256-column tiles spread over twice as many SMs.
 struct SplitArgs {
   int32_t* acc;
   unsigned* cnt;
   int splits;
+  int half_from;
 };
 
-// Unit -> tile and K-block range [kb_lo, kb_hi) (S units per tile).
-__device__ __forceinline__ void unit_range(int unit, int S, int num_kb, int& tile, int& kb_lo,
-                                           int& kb_hi) {
-  tile = unit / S;
-  const int sp = unit - tile * S;
-  kb_lo = sp * num_kb / S;
-  kb_hi = (sp + 1) * num_kb / S;
+struct Unit {
+  int tile;
+  int kb_lo, kb_hi;  // K-block range
+  int col_off;       // first column within the tile
+  int width;         // columns: BN, or 128 for a half-width unit
+};
+
+template <int BN>
+__device__ __forceinline__ Unit unit_of(int unit, int S, int half_from, int num_kb) {
+  Unit u;
+  u.col_off = 0;
+  u.width = BN;
+  u.kb_lo = 0;
+  u.kb_hi = num_kb;
+  if (S > 1) {
+    u.tile = unit / S;
+    const int sp = unit - u.tile * S;
+    u.kb_lo = sp * num_kb / S;
+    u.kb_hi = (sp + 1) * num_kb / S;
+  } else if (unit < half_from) {
+    u.tile = unit;
+  } else {
+    const int v = unit - half_from;
+    u.tile = half_from + (v >> 1);
+    u.col_off = (v & 1) * 128;
+    u.width = 128;
+  }
+  return u;
 }
 
 // Dequant epilogue of one 32 x 32 chunk (lane = row) from its raw 32-bit
@@ -345,7 +381,7 @@ __device__ __forceinline__ void finish_chunk(const uint32_t (&cur)[32], const fl
     }
     if (has_resid) {
       float rsv[32];
-      load_cols32<OutT>(ep.rscale, col0, N, ep.vec_rscale, rsv);
+      load_rscale32<OutT>(ep, grow, M, col0, N, rsv);
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
         const uint32_t bits = packed[j / 2];
@@ -383,7 +419,7 @@ __device__ __forceinline__ void finish_chunk(const uint32_t (&cur)[32], const fl
     }
     if (has_resid) {
       float rsv[32];
-      load_cols32<OutT>(ep.rscale, col0, N, ep.vec_rscale, rsv);
+      load_rscale32<OutT>(ep, grow, M, col0, N, rsv);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const float res = (grow < M && col0 + j < N)
@@ -628,12 +664,16 @@ __device__ __forceinline__ void splitk_take_chunk(const SplitArgs& sk, int srow,
 // arrive reads the summed chunks back, applies the epilogue, and returns the
 // chunks and its counter to zero.  Results equal the unsplit GEMM's bit for
 // bit.
+//
+// Half-width units (tiles from sk.half_from on, CG = 1, BN = 256, no split-K)
+// load 128 rows of B through tmBh and issue N = 128 MMAs into the first 128
+// columns of the accumulator.
 template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmW,
-                      int M, int N, int K, int num_m_tiles, int num_n_tiles, int group_m,
-                      EpilogueParams ep, SplitArgs sk) {
+                      const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmD,
+                      const __grid_constant__ CUtensorMap tmW, int M, int N, int K, int num_m_tiles,
+                      int num_n_tiles, int group_m, EpilogueParams ep, SplitArgs sk) {
   using C = Cfg<BN, OutT, CG, KIND, SPLIT>;
   static_assert(!SPLIT || (CG == 1 && KIND == 0), "split-K is built for the 1-CTA int8 GEMM");
   constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
@@ -657,7 +697,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_tiles = num_m_tiles * num_n_tiles;
   const int num_kb = (K + kBK - 1) / kBK;
   const int S = SPLIT ? sk.splits : 1;  // K splits per tile
-  const int num_units = num_tiles * S;
+  // tiles run as two half-width units (only 1-CTA 256-column tiles)
+  const int half_from = (!SPLIT && CG == 1 && BN == 256) ? sk.half_from : num_tiles;
+  const int num_units = S > 1 ? num_tiles * S : half_from + 2 * (num_tiles - half_from);
   const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
   const bool leader = rank == 0;
   const int first_tile = static_cast<int>(blockIdx.x) / CG;
@@ -678,6 +720,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (half_from < num_tiles) tma_prefetch_desc(&tmBh);
     if constexpr (!kRaw) tma_prefetch_desc(&tmD);
     if constexpr (SPLIT) tma_prefetch_desc(&tmW);
   }
@@ -690,19 +733,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (CG == 2) cluster_sync();  // the peer's barriers exist before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above overlapped the tail of the kernel that wrote A and the
+  // row scales (launched with programmatic stream serialization); nothing
+  // below runs before that kernel has completed.
+  griddep_wait();
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
       for (int unit = first_tile; ok && unit < num_units; unit += tile_step) {
-        int tile, kb_lo, kb_hi;
-        unit_range(unit, S, num_kb, tile, kb_lo, kb_hi);
+        const Unit u = unit_of<BN>(unit, S, half_from, num_kb);
         int mb, nb;
-        tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
+        tile_coords(u.tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
         const int a_row = mb * kBM * CG + static_cast<int>(rank) * kBM;
-        const int b_row = nb * BN + static_cast<int>(rank) * (BN / CG);
-        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
+        const int b_row = nb * BN + u.col_off + static_cast<int>(rank) * (BN / CG);
+        const bool half_unit = u.width < BN;
+        for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
           const int s = static_cast<int>(it % C::kStages);
           const uint32_t ph = (it / C::kStages) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, abortv, &g_w8a8_device_error, kDevTimeoutEmpty)) {
@@ -710,9 +757,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           if constexpr (CG == 1) {
-            mbar_arrive_expect_tx(&full[s], C::kStageBytes + C::kSFBytes);
+            mbar_arrive_expect_tx(&full[s], C::kABytes + (half_unit ? C::kBBytes / 2 : C::kBBytes) +
+                                                C::kSFBytes);
             tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kBK, a_row);
-            if (ep.b_tiles_kb) {
+            if (half_unit) {
+              tma_load_2d(sB + s * C::kBBytes, &tmBh, &full[s], kb * kBK, b_row);
+            } else if (ep.b_tiles_kb) {
               // pre-tiled B (128-column tiles): tile (nb, kb) is 16 KB contiguous
               tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], 0, (nb * ep.b_tiles_kb + kb) * 128);
             } else {
@@ -756,12 +806,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     if (lane == 0 && leader) {
       constexpr uint32_t idesc = make_idesc<KIND == 0 ? 0 : 1>(kBM * CG, BN);
+      constexpr uint32_t idesc_half = make_idesc<KIND == 0 ? 0 : 1>(kBM, 128);
       uint32_t it = 0;
       uint32_t tl = 0;
       bool ok = true;
       for (int unit = first_tile; ok && unit < num_units; unit += tile_step, ++tl) {
-        int tile, kb_lo, kb_hi;
-        unit_range(unit, S, num_kb, tile, kb_lo, kb_hi);
+        const Unit u = unit_of<BN>(unit, S, half_from, num_kb);
+        const int kb_lo = u.kb_lo, kb_hi = u.kb_hi;
+        const uint32_t id = u.width < BN ? idesc_half : idesc;
+        (void)id;
         const uint32_t acc = tl & 1u;
         const uint32_t use = tl >> 1;
         if (!mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abortv, &g_w8a8_device_error,
@@ -803,7 +856,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint64_t bd = smem_desc_k_sw128(b0 + k * kUmmaK);
               const uint32_t accumulate = (kb != kb_lo || k != 0) ? 1u : 0u;
               if constexpr (CG == 1) {
-                umma_ss<KIND>(d_tmem, ad, bd, idesc, accumulate);
+                umma_ss<KIND>(d_tmem, ad, bd, id, accumulate);
               } else {
                 umma_ss_pair<KIND>(d_tmem, ad, bd, idesc, accumulate);
               }
@@ -848,13 +901,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     (void)fp8_scale;
     uint32_t tl = 0;
     for (int unit = first_tile; unit < num_units; unit += tile_step, ++tl) {
-      int tile, kb_lo, kb_hi;
-      unit_range(unit, S, num_kb, tile, kb_lo, kb_hi);
+      const Unit u = unit_of<BN>(unit, S, half_from, num_kb);
+      const int tile = u.tile;
       int mb, nb;
       tile_coords(tile, num_m_tiles, num_n_tiles, group_m, mb, nb);
       const uint32_t acc = tl & 1u;
       const uint32_t use = tl >> 1;
-      const int col_base = nb * BN;
+      const int col_base = nb * BN + u.col_off;
+      const int nch = u.width / 32;  // 32-column chunks of this unit
       if constexpr (!kRaw) {
         // Stage this warp's per-column weight scales and bias while the MMA
         // is still running: lane j loads column j of each of the warp's chunks.
@@ -865,7 +919,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < C::kChunksPerWarp; ++i) {
           const int ch = kRope ? 4 * half + i : half + 2 * i;  // chunk of the tile
           const int col = col_base + ch * 32 + lane;
-          const bool in = ch < BN / 32 && col < N;
+          const bool in = ch < nch && col < N;
           float wv = 1.0f, bvv = 0.0f;
           if constexpr (KIND == 0) wv = in ? __ldg(ep.ws + (ep.ws_scalar ? 0 : col)) : 0.0f;
           if (has_bias && in) bvv = OutTraits<OutT>::load(ep.bias, col);
@@ -891,7 +945,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (kRope) {
         // this warp's head: chunks 4 half .. 4 half + 3 of the tile
         const int hcol0 = col_base + half * 128;
-        const bool active = half * 128 < BN && hcol0 < N;
+        const bool active = half * 128 < u.width && hcol0 < N;
         const bool roped = active && hcol0 < ep.rope_cols;
         const uint32_t head_tmem = tmem_base + lane_base + acc * BN + half * 128;
         if (active) {
@@ -963,10 +1017,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // as soon as chunk c's registers are free, so its latency overlaps the
       // arithmetic of chunk c.
       uint32_t r[32];
-      if (half * 32 < BN && col_base + half * 32 < N) {
+      if (half * 32 < u.width && col_base + half * 32 < N) {
         tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + half * 32, r);
       }
-      for (int c = half; c < BN / 32; c += 2) {
+      for (int c = half; c < nch; c += 2) {
         const int col0 = col_base + c * 32;
         if (col0 >= N) break;
         const int ci = (c - half) >> 1;  // this warp's chunk index
@@ -974,7 +1028,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t cur[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) cur[j] = r[j];
-        if (c + 2 < BN / 32 && col0 + 64 < N) {
+        if (c + 2 < nch && col0 + 64 < N) {
           tmem_ld_32x32b_x32(tmem_base + lane_base + acc * BN + (c + 2) * 32, r);
         }
         if (do_reduce) {
@@ -1097,7 +1151,7 @@ __global__ void __launch_bounds__(128) gemm_simt_kernel(const uint8_t* __restric
     }
     const bool has_resid = ep.residual != nullptr;
     const float res = has_resid ? OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(m) * ep.ldr + n) : 0.0f;
-    const float rs = has_resid ? OutTraits<OutT>::load(ep.rscale, n) : 0.0f;
+    const float rs = has_resid ? OutTraits<OutT>::load(ep.rscale, rscale_row(ep, m) + n) : 0.0f;
     y = finish_one<OutT>(y, res, rs, has_resid, ep.act);
     if constexpr (std::is_same<OutT, float>::value) {
       static_cast<float*>(out)[o] = y;
@@ -1152,6 +1206,8 @@ EpilogueParams to_params(const GemmArgs& g) {
     ep.residual = g.epi->residual;
     ep.ldr = g.epi->ldr;
     ep.rscale = g.epi->residual_scale;
+    ep.rscale_rows = g.epi->residual_scale_rows;
+    ep.ld_rscale = g.N;
     ep.dq_order = g.epi->dequant_order;
     ep.act = g.epi->activation;
   }
@@ -1177,8 +1233,9 @@ EpilogueParams to_params(const GemmArgs& g) {
 // mw / sk: the split-K scratch map and pointers (SPLIT only; otherwise the
 // output map stands in for the unused map parameter).
 template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG, bool SPLIT = false>
-int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& md,
-              const CUtensorMap& mw, SplitArgs sk, int group_m, int max_ctas, cudaStream_t stream) {
+int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb,
+              const CUtensorMap& mbh, const CUtensorMap& md, const CUtensorMap& mw, SplitArgs sk,
+              int group_m, int max_ctas, cudaStream_t stream) {
   // The same configuration the kernel lays its shared memory out with: the
   // block-scaled kind adds scale-factor bytes to every stage.
   using C = Cfg<BN, OutT, CG, KIND, SPLIT>;
@@ -1200,32 +1257,36 @@ int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb, c
   const int tiles = num_m * num_n;
   const int sms = device_sm_count();
   if (!SPLIT) sk.splits = 1;
+  if (SPLIT || CG != 1 || BN != 256 || sk.half_from > tiles) sk.half_from = tiles;
+  const int64_t all_units = sk.splits > 1 ? static_cast<int64_t>(tiles) * sk.splits
+                                          : sk.half_from + 2ll * (tiles - sk.half_from);
   int units = static_cast<int>(
-      std::min<int64_t>(static_cast<int64_t>(tiles) * sk.splits,
-                        (max_ctas > 0 ? max_ctas : sms) / CG));  // CTAs or CTA pairs
+      std::min<int64_t>(all_units, (max_ctas > 0 ? max_ctas : sms) / CG));  // CTAs or CTA pairs
   if (units < 1) units = 1;
   const EpilogueParams ep = to_params(g);
   const int Mi = static_cast<int>(g.M), Ni = static_cast<int>(g.N), Ki = static_cast<int>(g.K);
-  cudaError_t e;
-  if constexpr (CG == 1) {
-    kern<<<units, kThreads, C::kSmemBytes, stream>>>(ma, mb, md, mw, Mi, Ni, Ki, num_m, num_n,
-                                                    group_m, ep, sk);
-    e = cudaGetLastError();
-  } else {
-    cudaLaunchConfig_t lc{};
-    lc.gridDim = dim3(static_cast<unsigned>(units * 2));
-    lc.blockDim = dim3(kThreads);
-    lc.dynamicSmemBytes = C::kSmemBytes;
-    lc.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
-    e = cudaLaunchKernelEx(&lc, kern, ma, mb, md, mw, Mi, Ni, Ki, num_m, num_n, group_m, ep, sk);
+  // Programmatic stream serialization: the grid may launch while the kernel
+  // before it (the quantiser, which triggers early) is still running; the
+  // kernel waits for it (griddep_wait) before reading anything it wrote.
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(static_cast<unsigned>(units * CG));
+  lc.blockDim = dim3(kThreads);
+  lc.dynamicSmemBytes = C::kSmemBytes;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  if constexpr (CG == 2) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    lc.numAttrs = 2;
   }
+  const cudaError_t e = cudaLaunchKernelEx(&lc, kern, ma, mb, mbh, md, mw, Mi, Ni, Ki, num_m,
+                                           num_n, group_m, ep, sk);
   if (e != cudaSuccess) {
     set_error("tcgen05 GEMM launch failed: %s", cudaGetErrorString(e));
     return W8A8_ERR_ACCELERATOR;
@@ -1253,7 +1314,7 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, const GemmPlan& plan, cudaStream
   if (!tc_ok) return launch_simt<KIND, OutT>(g, stream);
   const int bn = plan.bn, cg = plan.cg, group_m = plan.group_m, max_ctas = plan.max_ctas;
   const int splits = plan.splits;
-  CUtensorMap ma, mb, md, mw;
+  CUtensorMap ma, mb, mbh, md, mw;
   bool ok = make_map_2d(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.a, g.K, g.M, g.lda, kBK, kBM,
                         CU_TENSOR_MAP_SWIZZLE_128B);
   if (g.b_tiled) {
@@ -1272,7 +1333,14 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, const GemmPlan& plan, cudaStream
   else dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   ok = ok && make_map_2d(&md, dt, static_cast<int>(sizeof(OutT)), g.out, g.N, g.M, g.ldo, 32, 32,
                          sizeof(OutT) == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
-  SplitArgs sk{nullptr, nullptr, 1};
+  SplitArgs sk{nullptr, nullptr, 1, static_cast<int>(plan.half_from)};
+  if (plan.half_from < plan.tiles) {
+    // half-width units: 128-row boxes of B
+    ok = ok && make_map_2d(&mbh, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.b, g.K, g.N, g.ldb, kBK, 128,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    mbh = mb;
+  }
   if (splits > 1) {
     // int32 [tiles * 128, bn] partial sums, then the arrival counters;
     // reductions in 32-row x 16-column boxes
@@ -1296,42 +1364,34 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, const GemmPlan& plan, cudaStream
     if constexpr (A == kActRmsRope) {
       // int8 with bf16 output only (checked by gemm_launch); one CTA per tile
       if constexpr (KIND == 0 && std::is_same<OutT, __nv_bfloat16>::value) {
-        if (splits > 1) {
-          if (bn == 128) {
-            return launch_tc<KIND, 128, OutT, O, A, 1, true>(g, ma, mb, md, mw, sk, group_m,
-                                                             max_ctas, stream);
-          }
-          return launch_tc<KIND, 256, OutT, O, A, 1, true>(g, ma, mb, md, mw, sk, group_m, max_ctas,
-                                                           stream);
+        if (splits > 1) {  // split-K runs 128-column tiles
+          return launch_tc<KIND, 128, OutT, O, A, 1, true>(g, ma, mb, mbh, md, mw, sk, group_m,
+                                                           max_ctas, stream);
         }
         if (bn == 128) {
-          return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
+          return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas, stream);
         }
-        return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
+        return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas, stream);
       } else {
         set_error("the RMSNorm + RoPE epilogue needs int8 operands and bf16 output");
         return W8A8_ERR_VALUE;
       }
     } else if constexpr (KIND == 2) {
-      return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
+      return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas, stream);
     } else {
       if constexpr (KIND == 0 && !std::is_same<OutT, int32_t>::value) {
-        if (splits > 1) {
-          if (bn == 128) {
-            return launch_tc<KIND, 128, OutT, O, A, 1, true>(g, ma, mb, md, mw, sk, group_m,
-                                                             max_ctas, stream);
-          }
-          return launch_tc<KIND, 256, OutT, O, A, 1, true>(g, ma, mb, md, mw, sk, group_m, max_ctas,
-                                                           stream);
+        if (splits > 1) {  // split-K runs 128-column tiles
+          return launch_tc<KIND, 128, OutT, O, A, 1, true>(g, ma, mb, mbh, md, mw, sk, group_m,
+                                                           max_ctas, stream);
         }
       }
       if (bn == 128) {
-        return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
+        return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas, stream);
       }
       if (cg == 2) {
-        return launch_tc<KIND, 256, OutT, O, A, 2>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
+        return launch_tc<KIND, 256, OutT, O, A, 2>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas, stream);
       }
-      return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, md, mw, sk, group_m, max_ctas, stream);
+      return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas, stream);
     }
   };
   using I0 = std::integral_constant<int, 0>;
@@ -1449,6 +1509,17 @@ int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& p) {
   }
   p.bn = bn;
   p.cg = cg;
+  p.tiles = ((g.M + kBM * cg - 1) / (kBM * cg)) * ((g.N + bn - 1) / bn);
+  // A partial last wave of 1-CTA 256-column tiles that fills at most half of
+  // the persistent CTAs runs as half-width units, twice as many, each half the
+  // work (5600 x 3072 -> 12288: 2112 tiles on 148 SMs, the last 40 run as 80
+  // units of 128 x 128).  No partial sums: each unit owns its columns.
+  p.half_from = p.tiles;
+  if (p.splits == 1 && bn == 256 && cg == 1 && !g.b_tiled && g.kind != 2) {
+    const int64_t P = std::min<int64_t>(p.tiles, p.max_ctas > 0 ? p.max_ctas : sms);
+    const int64_t R = p.tiles % P;
+    if (p.tiles > P && R > 0 && 2 * R <= P) p.half_from = p.tiles - R;
+  }
   return 0;
 }
 

@@ -120,7 +120,7 @@ __device__ __forceinline__ float epi_value(int32_t acc, int m, int n, float xs, 
   float y = dequant_one<OutT>(static_cast<float>(acc), xs, ws, b, has_bias, ep.dq_order);
   const bool has_resid = ep.residual != nullptr;
   const float res = has_resid ? OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(m) * ep.ldr + n) : 0.0f;
-  const float rs = has_resid ? OutTraits<OutT>::load(ep.rscale, n) : 0.0f;
+  const float rs = has_resid ? OutTraits<OutT>::load(ep.rscale, rscale_row(ep, m) + n) : 0.0f;
   return finish_one<OutT>(y, res, rs, has_resid, ep.act);
 }
 
@@ -293,8 +293,10 @@ __global__ void __launch_bounds__(256) quantize_fp8_tensor_kernel(const T* __res
   }
 }
 
-EpilogueParams params_of(const w8a8_epilogue_t* e) {
+EpilogueParams params_of(const w8a8_epilogue_t* e, int64_t N) {
   EpilogueParams ep{};
+  ep.rscale_rows = e->residual_scale_rows;
+  ep.ld_rscale = N;
   ep.ws = e->ws;
   ep.ws_scalar = e->ws_numel == 1 ? 1 : 0;
   ep.bias = e->bias;
@@ -323,7 +325,7 @@ int launch_gemv_t(const InT* x, const float* xs, const int8_t* w, const w8a8_epi
   if (smem > 48 * 1024) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   }
-  kern<<<grid, kGemvThreads, smem, stream>>>(x, xs, w, params_of(epi), out, N, K, scale_mode, q_out,
+  kern<<<grid, kGemvThreads, smem, stream>>>(x, xs, w, params_of(epi, N), out, N, K, scale_mode, q_out,
                                              xs_out);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -390,7 +392,7 @@ int linear_small_launch(const void* x, int x_dtype, const int8_t* w, const w8a8_
 int dequant_launch(const int32_t* acc, const float* xs, const w8a8_epilogue_t* epi, void* out,
                    int out_dtype, int64_t M, int64_t N, cudaStream_t stream) {
   if (M == 0 || N == 0) return 0;
-  const EpilogueParams ep = params_of(epi);
+  const EpilogueParams ep = params_of(epi, N);
   const int64_t total = M * N;
   int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, device_sm_count() * 16));
   switch (out_dtype) {

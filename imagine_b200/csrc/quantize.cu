@@ -16,6 +16,7 @@
 #include <type_traits>
 
 #include "quant_common.cuh"
+#include "sm100_ptx.cuh"
 #include "w8a8_internal.h"
 
 namespace w8a8 {
@@ -87,6 +88,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
   constexpr int kGroupThreads = WPR * 32;
   constexpr int kRowsPerCta = kQuantThreads / kGroupThreads;
   __shared__ float red[kQuantThreads / 32];
+  griddep_launch_dependents();  // the GEMM that reads q may start its prologue
 
   const int group = threadIdx.x / kGroupThreads;
   const int gt = threadIdx.x % kGroupThreads;

@@ -68,6 +68,8 @@ struct GemmPlan {
   int splits;              // > 1: every tile is cut into this many K ranges
   int64_t split_tiles;     // tiles cut in K
   int64_t workspace_need;  // scratch bytes the split tiles use (0 without splits)
+  int64_t tiles;           // output tiles of bn columns
+  int64_t half_from;       // tiles from here on run as two 128-column units
 };
 // tc_ok: the operands suit the tcgen05 path.  Returns 0 or an error code.
 int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& plan);

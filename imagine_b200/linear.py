@@ -505,7 +505,34 @@ def quantize_weight(weight: torch.Tensor, convrot: bool = False, convrot_groupsi
 # --------------------------------------------------------------------------
 # a3 / a4 / a5 / a6
 # --------------------------------------------------------------------------
-def _epilogue(weight_scale, bias, residual, residual_scale, dequant, output_act, n, ldr):
+def _residual_scale(scale, lead, n, dtype, dev):
+    """The residual scale as the epilogue reads it, with the broadcasting of the
+    reference's ``residual.addcmul(out, scale)`` (inference/src/int8_linear.rs:
+    99-111) against an output of shape (*lead, n).  Returns (table, rows_per):
+    one [N] row for every output row (rows_per 0); a per-sample gate [B, 1, N]
+    over an output [B, S, N] as a [B, N] table with rows_per = S (the model's
+    gated residual, inference/src/models/qwen_image21/numeric.rs:110-126); any
+    other broadcastable shape expanded to one row per output row (rows_per 1)."""
+    scale = scale.to(device=dev, dtype=dtype)
+    if scale.numel() == n:
+        return scale.reshape(-1).contiguous(), 0
+    full = (*lead, n)
+    try:
+        shape = torch.broadcast_shapes(tuple(scale.shape), full)
+    except RuntimeError as e:
+        raise ValueError(f"residual_scale of shape {tuple(scale.shape)} does not broadcast "
+                         f"against the output {full}: {e}") from None
+    if shape != full:
+        raise ValueError(f"residual_scale of shape {tuple(scale.shape)} broadcasts the output "
+                         f"{full} to {shape}")
+    s = scale.reshape((1,) * (len(full) - scale.dim()) + tuple(scale.shape))
+    if len(lead) >= 2 and s.shape[-2] == 1 and tuple(s.shape[:-2]) == tuple(lead[:-1]):
+        return s.reshape(-1, n).contiguous(), lead[-1]
+    return scale.expand(full).reshape(-1, n).contiguous(), 1
+
+
+def _epilogue(weight_scale, bias, residual, residual_scale, dequant, output_act, n, ldr,
+              residual_scale_rows=0):
     ep = N.Epilogue()
     ep.ws = weight_scale.data_ptr()
     ep.ws_numel = weight_scale.numel()
@@ -513,6 +540,7 @@ def _epilogue(weight_scale, bias, residual, residual_scale, dequant, output_act,
     ep.residual = residual.data_ptr() if residual is not None else None
     ep.ldr = ldr if residual is not None else 0
     ep.residual_scale = residual_scale.data_ptr() if residual_scale is not None else None
+    ep.residual_scale_rows = residual_scale_rows if residual is not None else 0
     if dequant not in DEQUANT:
         raise ValueError(f"unknown dequant order {dequant!r}")
     ep.dequant_order = DEQUANT[dequant]
@@ -758,13 +786,12 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
         raise ValueError("pre-tiled weights need K > 0")
     b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
     r = rs = None
+    rs_rows = 0
     if residual is not None:
         r = residual.to(device=dev, dtype=out_dtype).reshape(m, n).contiguous()
-        rs = residual_scale.to(device=dev, dtype=out_dtype).reshape(-1).contiguous()
-        if rs.numel() != n:
-            raise ValueError("residual_scale must have N elements")
+        rs, rs_rows = _residual_scale(residual_scale, tuple(lead), n, out_dtype, dev)
     out = torch.empty((m, n), dtype=out_dtype, device=dev)
-    ep = _epilogue(ws, b, r, rs, dequant, output_act, n, n)
+    ep = _epilogue(ws, b, r, rs, dequant, output_act, n, n, rs_rows)
     stream = _stream(dev)
     if fused:
         q, xs = quantize_int8_rowwise_convrot(x2, 256 if convrot else 0, input_act, input_act_weight,
@@ -930,9 +957,10 @@ def int8_gemv(q, w, x_scale, weight_scale, bias=None, out_dtype=torch.bfloat16, 
     xs = x_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
     b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
     r = residual.to(device=dev, dtype=out_dtype).reshape(m, n).contiguous() if residual is not None else None
-    rs = residual_scale.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if residual is not None else None
+    rs, rs_rows = (_residual_scale(residual_scale, (m,), n, out_dtype, dev) if residual is not None
+                   else (None, 0))
     out = torch.empty((m, n), dtype=out_dtype, device=dev)
-    ep = _epilogue(ws, b, r, rs, dequant, None, n, n)
+    ep = _epilogue(ws, b, r, rs, dequant, None, n, n, rs_rows)
     N.check(N.LIB.w8a8_gemv_dequant(_vp(q.contiguous()), _vp(w.contiguous()), _vp(xs),
                                     ctypes.byref(ep), _vp(out), _code(out_dtype), m, n, k,
                                     _stream(dev)))

@@ -76,6 +76,12 @@ typedef struct w8a8_epilogue {
   const void* residual_scale; /* [N] in the output dtype; required with residual */
   int32_t dequant_order;      /* W8A8_DQ_* */
   int32_t activation;         /* W8A8_ACT_* */
+  /* 0: residual_scale is one [N] row for every output row.  g > 0:
+   * residual_scale is [ceil(M / g), N] and output row m uses row m / g: the
+   * model's gated residual, a per-sample gate [B, 1, N] over B samples of g
+   * tokens (inference/src/models/qwen_image21/numeric.rs:110-126), which the
+   * reference's residual addcmul broadcasts (inference/src/int8_linear.rs:99-111). */
+  int64_t residual_scale_rows;
 } w8a8_epilogue_t;
 
 /* Optional GEMM launch configuration (what the autotuner selects).  A NULL

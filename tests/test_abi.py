@@ -18,7 +18,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert N.LIB.w8a8_abi_version() == 100
+    assert N.LIB.w8a8_abi_version() == 101
 
 
 def test_header_compiles_as_c():
@@ -89,3 +89,28 @@ def test_python_errors_map_to_exceptions():
         N.check(N.ERR_OOM)
     with pytest.raises(N.W8A8Error):
         N.check(N.ERR_ACCELERATOR)
+
+
+def test_residual_scale_broadcasting():
+    """The host side of the gated residual: how a residual_scale broadcast
+    against the output becomes the table and rows-per-row the epilogue reads."""
+    import torch
+    from imagine_b200.linear import _residual_scale
+
+    n = 8
+    cpu = torch.device("cpu")
+    t, rows = _residual_scale(torch.ones(n), (2, 5), n, torch.float32, cpu)
+    assert t.shape == (n,) and rows == 0
+    t, rows = _residual_scale(torch.ones(1, 1, n), (2, 5), n, torch.float32, cpu)
+    assert t.shape == (n,) and rows == 0
+    gate = torch.arange(2 * n, dtype=torch.float32).reshape(2, 1, n)
+    t, rows = _residual_scale(gate, (2, 5), n, torch.float32, cpu)
+    assert rows == 5 and torch.equal(t, gate.reshape(2, n))
+    full = torch.randn(2, 5, n)
+    t, rows = _residual_scale(full, (2, 5), n, torch.float32, cpu)
+    assert rows == 1 and torch.equal(t, full.reshape(10, n))
+    col = torch.randn(5, 1)  # broadcast along N: expanded to one row per output row
+    t, rows = _residual_scale(col, (2, 5), n, torch.float32, cpu)
+    assert rows == 1 and torch.equal(t, col.expand(2, 5, n).reshape(10, n))
+    with pytest.raises(ValueError):
+        _residual_scale(torch.ones(3, 1, n), (2, 5), n, torch.float32, cpu)

@@ -258,6 +258,50 @@ def test_residual_epilogue():
     assert_rms_close(y, ref)
 
 
+@pytest.mark.parametrize("k", [512, 520, 3072])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_gated_residual_epilogue(k, out_dtype):
+    """The model's gated residual (inference/src/models/qwen_image21/numeric.rs:
+    110-126) fused into the linear: x [2, S, K], residual [2, S, N] and a
+    per-sample gate [2, 1, N] that the reference's addcmul broadcasts
+    (inference/src/int8_linear.rs:99-111).  K = 520 takes the CUDA-core path;
+    S = 300 puts the sample boundary inside a warp's 32 rows; S = 128 at
+    K = 3072 is a few-row shape that takes split-K."""
+    g = torch.Generator().manual_seed(k)
+    b_, n = 2, 384
+    s_ = 128 if k == 3072 else 300
+    x = torch.randn(b_, s_, k, generator=g).to(torch.bfloat16)
+    wq = _rand_i8(g, n, k)
+    ws = torch.rand(n, generator=g) * 1e-3
+    bias = (torch.randn(n, generator=g) * 0.1).to(out_dtype)
+    r = torch.randn(b_, s_, n, generator=g).to(out_dtype)
+    for gate in (torch.randn(b_, 1, n, generator=g).to(out_dtype),      # per sample
+                 torch.randn(b_, s_, n, generator=g).to(out_dtype)):    # per row
+        y = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), bias.to(cuda()),
+                            out_dtype=out_dtype, residual=r.to(cuda()), residual_scale=gate.to(cuda()))
+        ref = O.int8_linear(x, wq, ws, bias, out_dtype=out_dtype, residual=r, residual_scale=gate)
+        assert y.shape == (b_, s_, n)
+        assert_rms_close(y, ref)
+    no_device_error()
+
+
+def test_gated_residual_small_m():
+    """Two rows (the fused quantise + GEMV launch), one per sample."""
+    g = torch.Generator().manual_seed(77)
+    k, n = 3072, 1024
+    x = torch.randn(2, 1, k, generator=g).to(torch.bfloat16)
+    wq = _rand_i8(g, n, k)
+    ws = torch.rand(n, generator=g) * 1e-3
+    r = torch.randn(2, 1, n, generator=g).to(torch.bfloat16)
+    gate = torch.randn(2, 1, n, generator=g).to(torch.bfloat16)
+    y = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), None, residual=r.to(cuda()),
+                        residual_scale=gate.to(cuda()), scale_mode="kitchen", dequant="chained")
+    ref = O.int8_linear(x, wq, ws, None, out_dtype=torch.bfloat16, residual=r, residual_scale=gate,
+                        dequant="chained")
+    assert_rms_close(y, ref, tol=0.02)
+    no_device_error()
+
+
 def test_headline_shape_properties():
     """5600 x 3072 -> 12288 (the MLP-up headline): exact int32 row checksums over
     the whole output, exact rows on a random sample, and the GELU epilogue on
@@ -281,6 +325,57 @@ def test_headline_shape_properties():
     y = W().int8_linear(xd, wq.to(cuda()), ws.to(cuda()), None, output_act="gelu_tanh")
     ref = O.int8_linear(x[rows], wq, ws, None, out_dtype=torch.bfloat16, output_act="gelu_tanh")
     assert_rms_close(y[rows.to(cuda())], ref)
+    no_device_error()
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_half_width_tail_units(out_dtype):
+    """1280 x 512 -> 4096: 160 tiles of 128 x 256 on 148 SMs, so the last 12
+    run as 24 half-width units.  Against the same GEMM on 160 CTAs (every tile
+    whole, one wave): bit-identical for int32 and every output dtype; the
+    oracle on the rows of the half-width tiles."""
+    sms = torch.cuda.get_device_properties(cuda()).multi_processor_count
+    if sms != 148:
+        pytest.skip("tile counts chosen for 148 SMs")
+    g = torch.Generator().manual_seed(41)
+    m, k, n = 1280, 512, 4096
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.02).to(out_dtype)
+    wq, ws = O.quantize_weight(w)
+    xd, wqd, wsd, bd = x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda())
+    whole_cfg = (256, 8, 160, 1)
+    for act in (None, "gelu_tanh"):
+        y = W().int8_linear(xd, wqd, wsd, bd, out_dtype=out_dtype, output_act=act)
+        y_whole = W().int8_linear(xd, wqd, wsd, bd, out_dtype=out_dtype, output_act=act,
+                                  config=whole_cfg)
+        assert torch.equal(y.view(torch.uint8), y_whole.view(torch.uint8))
+    qd, _ = W().quantize_int8_rowwise(xd)
+    assert torch.equal(W().int8_gemm_s32(qd, wqd), W().int8_gemm_s32(qd, wqd, config=whole_cfg))
+    # tile order is grouped by 8 row blocks: the last 12 tiles lie in rows 1024..1279
+    rows = torch.arange(1024, 1280, 8)
+    y = W().int8_linear(xd, wqd, wsd, bd, out_dtype=out_dtype)
+    ref = O.int8_linear(x[rows], wq, ws, b, out_dtype=out_dtype)
+    assert np.array_equal(_b(y[rows.to(cuda())]), _b(ref))
+    no_device_error()
+
+
+def test_half_width_tail_units_fp8():
+    sms = torch.cuda.get_device_properties(cuda()).multi_processor_count
+    if sms != 148:
+        pytest.skip("tile counts chosen for 148 SMs")
+    g = torch.Generator().manual_seed(43)
+    m, k, n = 1280, 512, 4096
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    sa = (x.abs().max().float() / 448).reshape(1)
+    sw = (w.abs().max().float() / 448).reshape(1)
+    aq = W().quantize_per_tensor_fp8(x.to(cuda()), sa.to(cuda()))
+    wq = W().quantize_per_tensor_fp8(w.to(cuda()), sw.to(cuda()))
+    y = W().fp8_linear(aq, sa.to(cuda()), wq, sw.to(cuda()), None)
+    rows = torch.arange(1024, 1280, 4)
+    assert_rms_close(y[rows.to(cuda())],
+                     O.fp8_linear_exact(aq.cpu()[rows], sa, wq.cpu(), sw, None, out_dtype=torch.float32))
     no_device_error()
 
 
