@@ -1482,13 +1482,17 @@ int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& p) {
   p.split_tiles = 0;
   p.workspace_need = 0;
   // Split-K (int8 with a dequant epilogue, scratch given or asked about):
-  // explicit split_k > 1, or 128 x 128 tiles that leave SMs idle (few rows):
-  // every 128-column tile is cut into `splits` K ranges, keeping at least 4
-  // K-blocks (512 bytes of K) per split.  Large GEMMs run every tile whole:
-  // cutting only the trailing, partial wave of tiles in K measured slower on
-  // B200 (5600 x 3072 -> 3072: 48 us whole, 114 us with its last 84 tiles cut
-  // in five), because the TMA add-reductions of the int32 partials into L2
-  // sustain under 1 TB/s.
+  // explicit split_k > 1, or 128 x 128 tiles that leave SMs idle (few rows)
+  // with a K loop long enough to pay for the partials' round trip: every
+  // 128-column tile is cut into `splits` K ranges of at least 16 K-blocks
+  // (2 KiB of K).  Measured on B200: 256 x 12288 -> 3072 in 30.7 us split in
+  // three against 36.9 us whole, but 256 x 3072 -> 3072 in 22.5 us split
+  // against 16.4 us whole.  Large GEMMs run every tile whole: cutting only the
+  // trailing, partial wave of tiles in K measured slower (5600 x 3072 -> 3072:
+  // 48 us whole, 114 us with its last 84 tiles cut in five), because the TMA
+  // add-reductions of the int32 partials into L2 sustain under 1 TB/s.  (One
+  // slot per split with plain stores, summed by the last split, measured
+  // slower still for the few-row shapes: 34.8 and 41.0 us.)
   if (g.kind == 0 && g.out_dtype != W8A8_S32 && tc_ok && g.N % 4 == 0 && g.split_k != 1) {
     const int num_kb = static_cast<int>((g.K + kBK - 1) / kBK);
     const int64_t tiles128 = ((g.M + kBM - 1) / kBM) * ((g.N + 127) / 128);
@@ -1497,7 +1501,7 @@ int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& p) {
       full = std::min(g.split_k, num_kb);
     } else {
       const int64_t fill = sms / std::max<int64_t>(1, tiles128);
-      full = static_cast<int>(std::min<int64_t>(fill, std::min(8, num_kb / 4)));
+      full = static_cast<int>(std::min<int64_t>(fill, std::min(8, num_kb / 16)));
     }
     if (full > 1) {
       p.splits = full;

@@ -258,7 +258,7 @@ def test_residual_epilogue():
     assert_rms_close(y, ref)
 
 
-@pytest.mark.parametrize("k", [512, 520, 3072])
+@pytest.mark.parametrize("k", [512, 520, 6144])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
 def test_gated_residual_epilogue(k, out_dtype):
     """The model's gated residual (inference/src/models/qwen_image21/numeric.rs:
@@ -266,10 +266,10 @@ def test_gated_residual_epilogue(k, out_dtype):
     per-sample gate [2, 1, N] that the reference's addcmul broadcasts
     (inference/src/int8_linear.rs:99-111).  K = 520 takes the CUDA-core path;
     S = 300 puts the sample boundary inside a warp's 32 rows; S = 128 at
-    K = 3072 is a few-row shape that takes split-K."""
+    K = 6144 is a few-row shape that takes split-K."""
     g = torch.Generator().manual_seed(k)
     b_, n = 2, 384
-    s_ = 128 if k == 3072 else 300
+    s_ = 128 if k == 6144 else 300
     x = torch.randn(b_, s_, k, generator=g).to(torch.bfloat16)
     wq = _rand_i8(g, n, k)
     ws = torch.rand(n, generator=g) * 1e-3
