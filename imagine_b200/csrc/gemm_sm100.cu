@@ -1385,6 +1385,12 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, const GemmPlan& plan, cudaStream
                                                            max_ctas, stream);
         }
       }
+      if constexpr (KIND == 0) {
+        if (bn == 64) {
+          return launch_tc<KIND, 64, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas,
+                                                    stream);
+        }
+      }
       if (bn == 128) {
         return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas, stream);
       }
@@ -1440,17 +1446,25 @@ int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& p) {
   const int out_bytes = g.out_dtype == W8A8_F32 || g.out_dtype == W8A8_S32 ? 4 : 2;
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
   int bn = g.cfg && g.cfg->block_n ? g.cfg->block_n : 0;
-  if (bn != 0 && bn != 128 && bn != 256) {
-    set_error("block_n must be 128 or 256, got %d", bn);
+  if (bn != 0 && bn != 64 && bn != 128 && bn != 256) {
+    set_error("block_n must be 64, 128 or 256, got %d", bn);
+    return W8A8_ERR_VALUE;
+  }
+  if (bn == 64 && (g.kind != 0 || g.rms_rope)) {
+    set_error("64-column tiles are built for the int8 GEMM without the RoPE epilogue");
     return W8A8_ERR_VALUE;
   }
   const int sms = device_sm_count();
   if (bn == 0) {
     // 256-column tiles when they alone fill every SM; otherwise the 128-column
     // tiles' extra parallelism wins (measured on B200: 256 x 12288 -> 3072
-    // runs 27% faster with 128-column tiles, 5600 x 3072 -> 3072 50% slower).
+    // runs 27% faster with 128-column tiles, 5600 x 3072 -> 3072 50% slower);
+    // and when even 128-column tiles leave half of the SMs idle (few rows),
+    // 64-column tiles run on twice as many.
     const long long tiles256 = ((g.M + kBM - 1) / kBM) * ((g.N + 255) / 256);
+    const long long tiles128 = ((g.M + kBM - 1) / kBM) * ((g.N + 127) / 128);
     bn = tiles256 >= sms && g.N >= 256 ? 256 : 128;
+    if (bn == 128 && 2 * tiles128 <= sms && g.kind == 0 && !g.rms_rope && !g.b_tiled) bn = 64;
   }
   p.group_m = g.cfg && g.cfg->group_m > 0 ? g.cfg->group_m : 8;
   p.max_ctas = g.cfg ? g.cfg->max_ctas : 0;
@@ -1477,17 +1491,17 @@ int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& p) {
     cg = 1;
   }
   if (g.rms_rope) cg = 1;  // heads of 128 columns per epilogue warp half, 1-CTA tiles
-  if (bn == 128) cg = 1;   // pairs are built for 256-column tiles
+  if (bn != 256) cg = 1;   // pairs are built for 256-column tiles
   p.splits = 1;
   p.split_tiles = 0;
   p.workspace_need = 0;
   // Split-K (int8 with a dequant epilogue, scratch given or asked about):
   // explicit split_k > 1, or 128 x 128 tiles that leave SMs idle (few rows)
   // with a K loop long enough to pay for the partials' round trip: every
-  // 128-column tile is cut into `splits` K ranges of at least 16 K-blocks
-  // (2 KiB of K).  Measured on B200: 256 x 12288 -> 3072 in 30.7 us split in
-  // three against 36.9 us whole, but 256 x 3072 -> 3072 in 22.5 us split
-  // against 16.4 us whole.  Large GEMMs run every tile whole: cutting only the
+  // 128-column tile is cut into `splits` K ranges of at least 32 K-blocks
+  // (4 KiB of K).  Measured on B200: 256 x 12288 -> 3072 in 30.7 us split in
+  // three against 36.9 us whole, but 256 x 6144 -> 3072 in 25.6 us split in
+  // three against 22.5-23.5 us whole, 256 x 3072 -> 3072 22.5 against 16.4 us.  Large GEMMs run every tile whole: cutting only the
   // trailing, partial wave of tiles in K measured slower (5600 x 3072 -> 3072:
   // 48 us whole, 114 us with its last 84 tiles cut in five), because the TMA
   // add-reductions of the int32 partials into L2 sustain under 1 TB/s.  (One
@@ -1501,7 +1515,7 @@ int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& p) {
       full = std::min(g.split_k, num_kb);
     } else {
       const int64_t fill = sms / std::max<int64_t>(1, tiles128);
-      full = static_cast<int>(std::min<int64_t>(fill, std::min(8, num_kb / 16)));
+      full = static_cast<int>(std::min<int64_t>(fill, std::min(8, num_kb / 32)));
     }
     if (full > 1) {
       p.splits = full;

@@ -114,9 +114,9 @@ def _rand_i8(g, *shape):
     return torch.randint(-128, 128, shape, generator=g, dtype=torch.int8)
 
 
-# (block_n, cta_group): heuristic, 128-column tiles, 256-column 1-CTA tiles,
-# 256x256 tiles on CTA pairs (2-SM MMA)
-TILE_CONFIGS = [(0, 0), (128, 1), (256, 1), (256, 2)]
+# (block_n, cta_group): heuristic, 64- and 128-column tiles, 256-column 1-CTA
+# tiles, 256x256 tiles on CTA pairs (2-SM MMA)
+TILE_CONFIGS = [(0, 0), (64, 1), (128, 1), (256, 1), (256, 2)]
 
 
 @pytest.mark.parametrize("m,k,n", GEMM_SHAPES)
@@ -145,6 +145,28 @@ def test_int8_linear_eager_order_bit_exact(m, k, n, out_dtype, cg):
     ref = O.int8_linear(x, wq, ws, b, out_dtype=out_dtype)
     no_device_error()
     assert np.array_equal(_b(y), _b(ref))
+
+
+@pytest.mark.parametrize("m,k,n", [(256, 3072, 3072), (200, 1024, 520), (64, 512, 96)])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_few_row_64_column_tiles_bit_exact(m, k, n, out_dtype):
+    """Few-row shapes whose 128-column tiles would leave most SMs idle run on
+    64-column tiles (the default there, and asked for explicitly here too):
+    bit-exact against the oracle, with GELU and an N tail."""
+    g = torch.Generator().manual_seed(m + k + n + 1)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    wq, ws = O.quantize_weight(w)
+    b = (torch.randn(n, generator=g) * 0.02).to(out_dtype)
+    ref = O.int8_linear(x, wq, ws, b, out_dtype=out_dtype)
+    for cfg in (None, (64, 8, 0, 1)):
+        y = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda()),
+                            out_dtype=out_dtype, config=cfg)
+        assert np.array_equal(_b(y), _b(ref))
+    yg = W().int8_linear(x.to(cuda()), wq.to(cuda()), ws.to(cuda()), b.to(cuda()),
+                         out_dtype=out_dtype, output_act="gelu_tanh", config=(64, 8, 0, 1))
+    assert_rms_close(yg, O.int8_linear(x, wq, ws, b, out_dtype=out_dtype, output_act="gelu_tanh"))
+    no_device_error()
 
 
 @pytest.mark.parametrize("name", [n for n in MAN["kitchen_eager"] if n.startswith("linear/")
@@ -258,7 +280,7 @@ def test_residual_epilogue():
     assert_rms_close(y, ref)
 
 
-@pytest.mark.parametrize("k", [512, 520, 6144])
+@pytest.mark.parametrize("k", [512, 520, 12288])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
 def test_gated_residual_epilogue(k, out_dtype):
     """The model's gated residual (inference/src/models/qwen_image21/numeric.rs:
@@ -266,10 +288,10 @@ def test_gated_residual_epilogue(k, out_dtype):
     per-sample gate [2, 1, N] that the reference's addcmul broadcasts
     (inference/src/int8_linear.rs:99-111).  K = 520 takes the CUDA-core path;
     S = 300 puts the sample boundary inside a warp's 32 rows; S = 128 at
-    K = 6144 is a few-row shape that takes split-K."""
+    K = 12288 is a few-row shape that takes split-K."""
     g = torch.Generator().manual_seed(k)
     b_, n = 2, 384
-    s_ = 128 if k == 6144 else 300
+    s_ = 128 if k == 12288 else 300
     x = torch.randn(b_, s_, k, generator=g).to(torch.bfloat16)
     wq = _rand_i8(g, n, k)
     ws = torch.rand(n, generator=g) * 1e-3
