@@ -22,6 +22,7 @@ ERR_VALUE = -20
 ERR_INDEX = -21
 
 F32, F16, BF16, S32, S8, E4M3 = 0, 1, 2, 3, 4, 5
+MAX_RANKS, PEER_FLAG_WORDS = 8, 32
 SCALE_EAGER, SCALE_KITCHEN = 0, 1
 DQ_EAGER, DQ_SCALE_PRODUCT, DQ_CHAINED = 0, 1, 2
 ACT_NONE, ACT_GELU_TANH = 0, 1
@@ -84,6 +85,11 @@ SIGNATURES = {
     "w8a8_rope_freqs_rows_bytes": (_i64, [_i64]),
     "w8a8_rope_freqs_rows": (_i32, [_vp, _i64, _i64, _vp, _vp]),
     "w8a8_gemm_splitk_workspace_bytes": (_i64, [_i64, _i64]),
+    "w8a8_peer_barrier": (_i32, [_vp, _i32, _i32, ctypes.c_uint, _vp]),
+    "w8a8_gemm_dequant_allgather": (_i32, [_vp, _i64, _vp, _i64, _vp, _EP, _vp, _i32, _i64, _i64,
+                                           _i64, _i64, _i64, _vp, _i32, _i32, ctypes.c_uint,
+                                           _CFG, _vp]),
+    "w8a8_allgather_wait": (_i32, [_vp, _i32, _i32, ctypes.c_uint, _vp]),
     "w8a8_gemm_auto_workspace_bytes": (_i64, [_i64, _i64, _i64, _CFG]),
     "w8a8_weight_tiles_bytes": (_i64, [_i64, _i64]),
     "w8a8_pack_weight_tiles": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),

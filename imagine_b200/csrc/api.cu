@@ -299,6 +299,82 @@ int w8a8_rope_freqs_rows(const float* freqs, int64_t freq_rows, int64_t rows, fl
   return finish(rope_freqs_rows_launch(freqs, freq_rows, rows, out, static_cast<cudaStream_t>(stream)));
 }
 
+namespace {
+int check_peers(unsigned* const* flags, int rank, int world) {
+  if (world < 2 || world > W8A8_MAX_RANKS) {
+    return fail(W8A8_ERR_VALUE, "world must be 2..%d, got %d", W8A8_MAX_RANKS, world);
+  }
+  if (rank < 0 || rank >= world) return fail(W8A8_ERR_VALUE, "rank %d outside 0..%d", rank, world - 1);
+  if (!flags) return fail(W8A8_ERR_VALUE, "NULL flag pointer array");
+  for (int r = 0; r < world; ++r) {
+    if (!flags[r] || (reinterpret_cast<uintptr_t>(flags[r]) & 3u)) {
+      return fail(W8A8_ERR_VALUE, "flag block of rank %d is NULL or misaligned", r);
+    }
+  }
+  return 0;
+}
+}  // namespace
+
+int w8a8_peer_barrier(unsigned* const* flags, int rank, int world, unsigned epoch, void* stream) {
+  if (int rc = check_peers(flags, rank, world)) return rc;
+  if (epoch == 0) return fail(W8A8_ERR_VALUE, "epoch must be nonzero");
+  return finish(peer_flags_launch(flags, rank, world, epoch, 0, 1, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_allgather_wait(unsigned* const* flags, int rank, int world, unsigned epoch, void* stream) {
+  if (int rc = check_peers(flags, rank, world)) return rc;
+  if (epoch == 0) return fail(W8A8_ERR_VALUE, "epoch must be nonzero");
+  return finish(peer_flags_launch(flags, rank, world, epoch, W8A8_MAX_RANKS, 0,
+                                  static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_gemm_dequant_allgather(const int8_t* q, int64_t ldq, const int8_t* w_shard, int64_t ldw,
+                                const float* xs, const w8a8_epilogue_t* epi, void* const* outs,
+                                int out_dtype, int64_t ldo, int64_t col_offset, int64_t M,
+                                int64_t N_shard, int64_t K, unsigned* const* flags, int rank,
+                                int world, unsigned epoch, const w8a8_gemm_config_t* cfg,
+                                void* stream) {
+  if (M < 0 || N_shard < 0 || K < 0 || col_offset < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (int rc = check_epilogue(epi, N_shard, true)) return rc;
+  if (int rc = check_peers(flags, rank, world)) return rc;
+  if (epoch == 0) return fail(W8A8_ERR_VALUE, "epoch must be nonzero");
+  if (!outs) return fail(W8A8_ERR_VALUE, "NULL output pointer array");
+  for (int r = 0; r < world; ++r) {
+    if (!outs[r]) return fail(W8A8_ERR_VALUE, "output of rank %d is NULL", r);
+  }
+  if (ldo < col_offset + N_shard) return fail(W8A8_ERR_VALUE, "ldo smaller than the shard's last column");
+  if (M == 0 || N_shard == 0) return finish(0);
+  if (!q || !w_shard || !xs) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldq < K || ldw < K) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  const int esz = out_dtype == W8A8_F32 ? 4 : 2;
+  GemmArgs g{};
+  g.kind = 0;
+  g.a = q;
+  g.lda = ldq;
+  g.b = w_shard;
+  g.ldb = ldw;
+  g.xs = xs;
+  g.epi = epi;
+  g.out = static_cast<uint8_t*>(outs[rank]) + col_offset * esz;
+  g.out_dtype = out_dtype;
+  g.ldo = ldo;
+  g.M = M;
+  g.N = N_shard;
+  g.K = K;
+  g.cfg = cfg;
+  g.split_k = 1;
+  g.ag_world = world;
+  g.ag_rank = rank;
+  for (int r = 0; r < world; ++r) {
+    g.ag_out[r] = outs[r];
+    g.ag_flags[r] = flags[r];
+  }
+  g.ag_col_off = col_offset;
+  g.ag_epoch = epoch;
+  return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
 int w8a8_row_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,
                     float* amax, void* stream) {
   if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");

@@ -21,6 +21,10 @@ enum DequantOrder : int { kDqEager = 0, kDqScaleProduct = 1, kDqChained = 2 };
 // QKV projection's epilogue; GEMM with 256-column tiles and bf16 output only)
 enum OutputAct : int { kActNone = 0, kActGeluTanh = 1, kActRmsRope = 2 };
 
+// Ranks of a fused column-parallel all-gather (one GPU each, one NVLink domain;
+// W8A8_MAX_RANKS of the public header).
+constexpr int kMaxRanks = 8;
+
 template <typename T>
 struct OutTraits;
 template <>
@@ -96,6 +100,19 @@ struct EpilogueParams {
   const float* rope_f;
   int rope_cols;
   float rope_eps;
+  // Column-parallel all-gather fused into the epilogue (n_ranks > 1): every
+  // finished output chunk is also written to each peer's output buffer
+  // (peer_out[r], row stride ld_peer, this shard's columns from peer_col_off);
+  // the last CTA to finish then writes `epoch` into slot `rank` of every peer's
+  // flag array (peer_flags[r]).  cta_count: this rank's CTA arrival counter.
+  int n_ranks;
+  int rank;
+  void* peer_out[kMaxRanks];
+  unsigned* peer_flags[kMaxRanks];
+  int64_t ld_peer;
+  int64_t peer_col_off;
+  unsigned* cta_count;
+  unsigned epoch;
 };
 
 // Value of one output element before the optional residual, already rounded

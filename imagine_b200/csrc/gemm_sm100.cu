@@ -347,6 +347,36 @@ __device__ __forceinline__ Unit unit_of(int unit, int S, int half_from, int num_
   return u;
 }
 
+// Fused column-parallel all-gather: the staged 32 x 32 chunk (row0.., col0..
+// in this shard's columns) copied from the warp's staging tile to every peer's
+// output buffer with 16-byte P2P stores over NVLink.  A row of the chunk is
+// 64 B (2-byte outputs, 64B swizzle) or 128 B (4-byte, 128B swizzle); lanes
+// cover whole rows, so each store instruction writes 8 or 4 row segments.
+// Shard widths are multiples of 8 columns, so a 16-byte piece is wholly
+// inside or outside the shard.
+template <int ESZ>
+__device__ __forceinline__ void peer_copy_chunk(const uint8_t* st, const EpilogueParams& ep,
+                                                int col0, int row0, int M, int N, int lane) {
+  constexpr int kRowBytes = 32 * ESZ;           // 64 or 128
+  constexpr int kPieces = kRowBytes / 16;       // 16-byte pieces per row: 4 or 8
+  constexpr int kRowsPerPass = 32 / kPieces;    // 8 or 4
+  const int piece = lane % kPieces;
+  const int col = col0 + piece * (16 / ESZ);
+  if (col >= N) return;
+#pragma unroll
+  for (int pass = 0; pass < 32 / kRowsPerPass; ++pass) {
+    const int r = pass * kRowsPerPass + lane / kPieces;
+    if (row0 + r >= M) break;
+    const int phys = ESZ == 2 ? (piece ^ ((r >> 1) & 3)) : (piece ^ (r & 7));
+    const uint4 v = *reinterpret_cast<const uint4*>(st + r * kRowBytes + phys * 16);
+    const int64_t off = (static_cast<int64_t>(row0 + r) * ep.ld_peer + ep.peer_col_off + col) * ESZ;
+    for (int p = 0; p < ep.n_ranks; ++p) {
+      if (p == ep.rank) continue;
+      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(ep.peer_out[p]) + off) = v;
+    }
+  }
+}
+
 // Dequant epilogue of one 32 x 32 chunk (lane = row) from its raw 32-bit
 // accumulators, staged in `st` and TMA-stored to (col0, row0) of the output.
 template <int KIND, typename OutT, int ORDER, int ACT>
@@ -470,6 +500,9 @@ __device__ __forceinline__ void finish_chunk(const uint32_t (&cur)[32], const fl
   if (lane == 0 && row0 < M) {
     tma_store_2d(tmD, st, col0, row0);
     tma_store_commit();
+  }
+  if constexpr (!kRaw) {
+    if (ep.n_ranks > 1) peer_copy_chunk<static_cast<int>(sizeof(OutT))>(st, ep, col0, row0, M, N, lane);
   }
 }
 
@@ -1077,6 +1110,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (lane == 0) tma_store_wait_all<0>();
+    if constexpr (!kRaw) {
+      if (ep.n_ranks > 1) {
+        // Fused all-gather: this CTA's P2P stores are published, then it counts
+        // itself in; the last CTA of the grid writes this call's epoch into
+        // slot `rank` of every peer's done flags.
+        __threadfence_system();
+        named_bar_sync(1, kEpiWarps * 32);
+        if (threadIdx.x == 0) {
+          __threadfence_system();
+          const unsigned prev = atomicAdd(ep.cta_count, 1u);
+          if (prev == gridDim.x - 1) {
+            __threadfence_system();
+            for (int p = 0; p < ep.n_ranks; ++p) {
+              if (p != ep.rank) st_release_sys(ep.peer_flags[p] + kMaxRanks + ep.rank, ep.epoch);
+            }
+            *ep.cta_count = 0u;  // every CTA of this call has arrived
+          }
+        }
+      }
+    }
   }
 
   __syncthreads();
@@ -1215,6 +1268,18 @@ EpilogueParams to_params(const GemmArgs& g) {
   ep.sfb = static_cast<const uint8_t*>(g.sfb);
   ep.sf_ncb = static_cast<int>((g.K + 127) / 128);
   ep.b_tiles_kb = g.b_tiled ? static_cast<int>((g.K + kBK - 1) / kBK) : 0;
+  ep.n_ranks = g.ag_world > 1 ? g.ag_world : 1;
+  if (ep.n_ranks > 1) {
+    ep.rank = g.ag_rank;
+    for (int r = 0; r < g.ag_world; ++r) {
+      ep.peer_out[r] = g.ag_out[r];
+      ep.peer_flags[r] = g.ag_flags[r];
+    }
+    ep.ld_peer = g.ldo;
+    ep.peer_col_off = g.ag_col_off;
+    ep.cta_count = g.ag_flags[g.ag_rank] + 2 * kMaxRanks;
+    ep.epoch = g.ag_epoch;
+  }
   if (g.rms_rope) {
     ep.act = kActRmsRope;
     ep.rope_w = g.rope_w;
@@ -1292,6 +1357,38 @@ int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb,
     return W8A8_ERR_ACCELERATOR;
   }
   return 0;
+}
+
+static_assert(kMaxRanks == W8A8_MAX_RANKS && 2 * kMaxRanks + 1 <= W8A8_PEER_FLAG_WORDS,
+              "flag block layout");
+
+struct PeerFlags {
+  unsigned* flags[kMaxRanks];
+};
+
+// Flag block of a fused all-gather rank (uint32): [0, 8) ready slots, one per
+// peer, [8, 16) done slots, [16] the rank's CTA arrival counter.
+//
+// peer_barrier: every rank writes `epoch` into its slot of each peer's ready
+// flags, then waits until all peers' slots of its own block hold it (no rank
+// writes into another's output before all have finished reading the previous
+// call's).  peer_done_wait: waits until every peer's GEMM has written `epoch`
+// into the done slots.  Each wait gives up after kSpinLimitNs, records
+// kDevTimeoutPeer and returns.
+__global__ void __launch_bounds__(32) peer_flags_kernel(unsigned* mine, PeerFlags peers, int rank,
+                                                        int world, unsigned epoch, int base,
+                                                        int signal) {
+  const int p = threadIdx.x;
+  if (p >= world || p == rank) return;
+  if (signal) st_release_sys(peers.flags[p] + base + rank, epoch);
+  const uint64_t t0 = globaltimer_ns();
+  while (static_cast<int>(ld_acquire_sys(mine + base + p) - epoch) < 0) {
+    if (globaltimer_ns() - t0 > kSpinLimitNs) {
+      atomicCAS(&g_w8a8_device_error, 0, kDevTimeoutPeer);
+      return;
+    }
+    __nanosleep(256);
+  }
 }
 
 template <int KIND, typename OutT>
@@ -1442,6 +1539,19 @@ int64_t splitk_workspace_bytes(int64_t M, int64_t N) {
   return splitk_acc_bytes(tiles128, 128) + tiles128 * kEpiWarps * 4;
 }
 
+int peer_flags_launch(unsigned* const* flags, int rank, int world, unsigned epoch, int base,
+                      int signal, cudaStream_t stream) {
+  PeerFlags pf{};
+  for (int r = 0; r < world; ++r) pf.flags[r] = flags[r];
+  peer_flags_kernel<<<1, 32, 0, stream>>>(flags[rank], pf, rank, world, epoch, base, signal);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("peer flag kernel launch failed: %s", cudaGetErrorString(e));
+    return W8A8_ERR_ACCELERATOR;
+  }
+  return 0;
+}
+
 int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& p) {
   const int out_bytes = g.out_dtype == W8A8_F32 || g.out_dtype == W8A8_S32 ? 4 : 2;
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
@@ -1572,6 +1682,20 @@ int gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
       set_error("RoPE needs a 16-byte aligned norm weight and rotations");
       return W8A8_ERR_VALUE;
     }
+  }
+  if (g.ag_world > 1) {
+    const int esz = out_bytes;
+    if (!(g.kind == 0 && tc_ok && !g.rms_rope && !g.b_tiled && g.out_dtype != W8A8_S32 &&
+          g.ag_world <= kMaxRanks && g.ag_rank >= 0 && g.ag_rank < g.ag_world &&
+          g.N % 8 == 0 && g.ldo % 8 == 0 && g.ag_col_off % 8 == 0 && esz >= 2 &&
+          !(g.epi && g.epi->residual))) {
+      set_error("the fused all-gather needs int8 codes, a floating output without residual, "
+                "2..%d ranks, K %% 16 == 0, 16-byte aligned operands and N_shard, ldo and the "
+                "column offset multiples of 8", kMaxRanks);
+      return W8A8_ERR_VALUE;
+    }
+    g.split_k = 1;
+    g.workspace = nullptr;
   }
   if (!g.workspace) g.split_k = 1;
   GemmPlan plan{};

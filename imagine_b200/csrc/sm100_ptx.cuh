@@ -24,6 +24,7 @@ enum DeviceError : int {
   kDevTimeoutTmemFull = 3,  // epilogue waited too long for an accumulator
   kDevTimeoutTmemEmpty = 4, // MMA issuer waited too long for a free accumulator
   kDevBadScaleBlock = 5,    // an MXFP8 scale block outside the caller's buffers
+  kDevTimeoutPeer = 6,      // a peer GPU's flag did not arrive (fused all-gather)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -46,6 +47,21 @@ __device__ __forceinline__ void griddep_launch_dependents() {
 }
 __device__ __forceinline__ void griddep_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- peers
+// Flags between GPUs: release / acquire at system scope.
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Barrier among the first n threads of the CTA (id 0 is __syncthreads').
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
 // ---------------------------------------------------------------- mbarrier

@@ -60,8 +60,21 @@ struct GemmArgs {
   const float* rope_f;  // row-blocked rotations (w8a8_rope_freqs_rows)
   int64_t rope_cols;
   float rope_eps;
+  // column-parallel all-gather fused into the epilogue (ag_world > 1); `out`
+  // is this rank's buffer at its shard's first column
+  int ag_world;
+  int ag_rank;
+  void* ag_out[W8A8_MAX_RANKS];
+  unsigned* ag_flags[W8A8_MAX_RANKS];
+  int64_t ag_col_off;
+  unsigned ag_epoch;
 };
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);
+// Fused all-gather flags (gemm_sm100.cu): base 0 with signal = the barrier on
+// the ready slots; base W8A8_MAX_RANKS without signal = the wait for the
+// peers' GEMMs.
+int peer_flags_launch(unsigned* const* flags, int rank, int world, unsigned epoch, int base,
+                      int signal, cudaStream_t stream);
 // Tile shape and split-K layout gemm_launch uses for a GEMM.
 struct GemmPlan {
   int bn, cg, group_m, max_ctas;

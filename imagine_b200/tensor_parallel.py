@@ -7,7 +7,10 @@ placement plan.  Both linears are bit-identical to the single-GPU operator:
 * ``ColumnParallelInt8Linear`` shards W along N.  Every rank quantises the full
   activation (identical codes on every rank), computes its N-slice, and
   optionally all-gathers the slices.  Used for QKV, MLP-up and the AdaLN
-  modulation GEMV.
+  modulation GEMV.  With ``fused=True`` the all-gather is not a collective
+  after the GEMM: the GEMM's epilogue writes every finished output chunk into
+  all ranks' outputs over NVLink (w8a8_gemm_dequant_allgather), on buffers
+  that every rank maps (torch's symmetric memory, used as plumbing).
 * ``RowParallelInt8Linear`` shards W and the activation along K.  The per-token
   scale needs the absmax of the whole row, so ranks all-reduce(MAX) their
   shard's row absmax first; each rank then quantises its shard with the full
@@ -21,6 +24,7 @@ libw8a8 C ABI.  Collectives go through ``torch.distributed`` (NCCL on GPUs).
 """
 from __future__ import annotations
 
+import ctypes
 from typing import List, Optional, Tuple
 
 import torch
@@ -63,6 +67,48 @@ def shard_slice(total: int, rank: int, world: int) -> slice:
     return slice(start, start + sizes[rank])
 
 
+class _PeerBuffers:
+    """Peer-mapped output buffer and flag block of one fused column-parallel
+    linear, on every rank of `group` (rendezvous is collective: every rank
+    makes the same calls in the same order)."""
+
+    def __init__(self, group, device):
+        import torch.distributed._symmetric_memory as symm
+
+        from . import _native as N
+
+        self.symm = symm
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.flags = symm.empty(N.PEER_FLAG_WORDS, dtype=torch.int32, device=device)
+        self.flags.zero_()
+        handle = symm.rendezvous(self.flags, self.group)
+        self.flag_ptrs = (ctypes.c_void_p * self.world)(*handle.buffer_ptrs)
+        self._keep = [handle]
+        self.out = None
+        self.out_ptrs = None
+        self.epoch = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(self.group)  # every flag block is zero before any rank signals
+
+    def output(self, m: int, n: int, dtype: torch.dtype, device) -> torch.Tensor:
+        if self.out is None or self.out.shape[0] < m or self.out.shape[1] != n or \
+                self.out.dtype != dtype:
+            # a peer may still be writing into the old buffer: finish first
+            torch.cuda.synchronize(device)
+            dist.barrier(self.group)
+            buf = self.symm.empty(max(m, 1), n, dtype=dtype, device=device)
+            handle = self.symm.rendezvous(buf, self.group)
+            self.out_ptrs = (ctypes.c_void_p * self.world)(*handle.buffer_ptrs)
+            self._keep.append((buf, handle))
+            self.out = buf
+        return self.out[:m]
+
+    def next_epoch(self) -> int:
+        self.epoch = self.epoch % 0xFFFFFFFF + 1  # never 0
+        return self.epoch
+
+
 def _world(group) -> Tuple[int, int]:
     if not dist.is_available() or not dist.is_initialized():
         return 0, 1
@@ -74,11 +120,13 @@ class ColumnParallelInt8Linear:
 
     def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor,
                  bias: Optional[torch.Tensor] = None, *, group=None, gather_output: bool = True,
-                 backend=None, **linear_kwargs):
+                 backend=None, fused: bool = False, **linear_kwargs):
         self.group = group
         self.rank, self.world = _world(group)
         n = weight.shape[0]
+        self.n = n
         sl = shard_slice(n, self.rank, self.world)
+        self.col_offset = sl.start
         self.sizes = split_sizes(n, self.world)
         self.weight = weight[sl].contiguous()
         ws = weight_scale.reshape(-1)
@@ -87,8 +135,48 @@ class ColumnParallelInt8Linear:
         self.gather_output = gather_output
         self.backend = backend or NativeBackend()
         self.kw = linear_kwargs
+        self.fused = (fused and gather_output and self.world > 1 and
+                      all(sz % 8 == 0 for sz in self.sizes) and n % 8 == 0 and
+                      set(linear_kwargs) <= {"dequant", "scale_mode", "output_act"})
+        self._peers = None
+
+    def _fused_call(self, x: torch.Tensor, out_dtype) -> torch.Tensor:
+        """One launch per rank: quantise x, then the GEMM whose epilogue writes
+        this rank's columns into every rank's output (see the module doc).  The
+        result is a view of the layer's peer-mapped buffer, valid until the
+        layer's next call."""
+        from . import _native as N
+        from .linear import _code, _epilogue, _stream, _vp, quantize_int8_rowwise
+
+        dev = x.device
+        if self._peers is None:
+            self._peers = _PeerBuffers(self.group, dev)
+        pb = self._peers
+        lead = x.shape[:-1]
+        k = x.shape[-1]
+        x2 = x.reshape(-1, k)
+        m = x2.shape[0]
+        y = pb.output(m, self.n, out_dtype, dev)
+        epoch = pb.next_epoch()
+        stream = _stream(dev)
+        if m > 0:
+            N.check(N.LIB.w8a8_peer_barrier(pb.flag_ptrs, self.rank, self.world, epoch, stream))
+            q, xs = quantize_int8_rowwise(x2, scale_mode=self.kw.get("scale_mode", "eager"))
+            ws = self.weight_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+            b = (self.bias.to(device=dev, dtype=out_dtype).contiguous()
+                 if self.bias is not None else None)
+            ep = _epilogue(ws, b, None, None, self.kw.get("dequant", "eager"),
+                           self.kw.get("output_act"), self.weight.shape[0], self.weight.shape[0])
+            N.check(N.LIB.w8a8_gemm_dequant_allgather(
+                _vp(q), k, _vp(self.weight), k, _vp(xs.reshape(-1)), ctypes.byref(ep),
+                pb.out_ptrs, _code(out_dtype), self.n, self.col_offset, m,
+                self.weight.shape[0], k, pb.flag_ptrs, self.rank, self.world, epoch, None, stream))
+            N.check(N.LIB.w8a8_allgather_wait(pb.flag_ptrs, self.rank, self.world, epoch, stream))
+        return y.reshape(*lead, self.n)
 
     def __call__(self, x: torch.Tensor, out_dtype=None) -> torch.Tensor:
+        if self.fused:
+            return self._fused_call(x, out_dtype or x.dtype)
         y = self.backend.linear(x, self.weight, self.weight_scale, self.bias,
                                 out_dtype or x.dtype, **self.kw)
         if not self.gather_output or self.world == 1:

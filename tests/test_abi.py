@@ -114,3 +114,23 @@ def test_residual_scale_broadcasting():
     assert rows == 1 and torch.equal(t, col.expand(2, 5, n).reshape(10, n))
     with pytest.raises(ValueError):
         _residual_scale(torch.ones(3, 1, n), (2, 5), n, torch.float32, cpu)
+
+
+def test_fused_allgather_argument_errors():
+    """The fused column-parallel entry points refuse bad ranks and pointers on
+    the host, before any launch."""
+    flags = (ctypes.c_void_p * 2)(0x1000, 0x2000)
+    assert N.LIB.w8a8_peer_barrier(flags, 0, 1, 1, None) == N.ERR_VALUE  # one rank
+    assert N.LIB.w8a8_peer_barrier(flags, 2, 2, 1, None) == N.ERR_VALUE  # rank outside
+    assert N.LIB.w8a8_allgather_wait(flags, 0, 9, 1, None) == N.ERR_VALUE  # too many ranks
+    assert N.LIB.w8a8_allgather_wait(flags, 0, 2, 0, None) == N.ERR_VALUE  # epoch 0
+    null_flags = (ctypes.c_void_p * 2)(0x1000, 0)
+    assert N.LIB.w8a8_peer_barrier(null_flags, 0, 2, 1, None) == N.ERR_VALUE
+    ep = N.Epilogue()
+    ep.ws = 0x3000
+    ep.ws_numel = 1
+    outs = (ctypes.c_void_p * 2)(0x4000, 0x5000)
+    # the shard's last column beyond ldo
+    rc = N.LIB.w8a8_gemm_dequant_allgather(0x6000, 64, 0x7000, 64, 0x8000, ctypes.byref(ep), outs,
+                                           N.BF16, 128, 64, 16, 128, 64, flags, 0, 2, 1, None, None)
+    assert rc == N.ERR_VALUE and b"ldo" in N.LIB.w8a8_last_error()

@@ -1,6 +1,7 @@
-"""Tensor-parallel linears on 2 GPUs over NCCL with the native kernels: both
-forms must equal the single-GPU int8_linear bit for bit.  Skips on boxes with
-fewer than two GPUs."""
+"""Tensor-parallel linears on 2 GPUs with the native kernels: the NCCL forms
+(column- and row-parallel) and the column-parallel linear whose all-gather is
+fused into the GEMM epilogue (peer stores over NVLink) must all equal the
+single-GPU int8_linear bit for bit.  Skips on boxes with fewer than two GPUs."""
 import os
 import socket
 
@@ -43,9 +44,22 @@ def _worker(rank, world, port, q):
         row = TP.RowParallelInt8Linear(wq, ws, b)
         y_col = col(x)
         y_row = row(row.shard_input(x))
+        # the all-gather fused into the GEMM (peer stores over NVLink): two
+        # calls with different inputs (epochs 1 and 2), and the GELU epilogue
+        fused = TP.ColumnParallelInt8Linear(wq, ws, b, fused=True)
+        fused_gelu = TP.ColumnParallelInt8Linear(wq, ws, b, fused=True, output_act="gelu_tanh")
+        assert fused.fused and fused_gelu.fused
+        x2 = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+        ok_fused = True
+        for xi in (x, x2, x):
+            want = W.int8_linear(xi, wq, ws, b)
+            ok_fused &= torch.equal(fused(xi).view(torch.int16), want.view(torch.int16))
+            want = W.int8_linear(xi, wq, ws, b, output_act="gelu_tanh")
+            ok_fused &= torch.equal(fused_gelu(xi).view(torch.int16), want.view(torch.int16))
         torch.cuda.synchronize()
+        ok_fused &= W.device_error() == 0
         q.put((rank, torch.equal(y_col.view(torch.int16), ref.view(torch.int16)),
-               torch.equal(y_row.view(torch.int16), ref.view(torch.int16))))
+               torch.equal(y_row.view(torch.int16), ref.view(torch.int16)), bool(ok_fused)))
     finally:
         dist.destroy_process_group()
 
@@ -65,5 +79,5 @@ def test_tensor_parallel_nccl_bit_exact():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, col_ok, row_ok in results:
-        assert col_ok and row_ok, (rank, col_ok, row_ok)
+    for rank, col_ok, row_ok, fused_ok in results:
+        assert col_ok and row_ok and fused_ok, (rank, col_ok, row_ok, fused_ok)
