@@ -85,11 +85,13 @@ SIGNATURES = {
     "w8a8_rope_freqs_rows_bytes": (_i64, [_i64]),
     "w8a8_rope_freqs_rows": (_i32, [_vp, _i64, _i64, _vp, _vp]),
     "w8a8_gemm_splitk_workspace_bytes": (_i64, [_i64, _i64]),
+    "w8a8_allgather_recv_bytes": (_i64, [_i64, _i64, _i32, _i32]),
     "w8a8_peer_barrier": (_i32, [_vp, _i32, _i32, ctypes.c_uint, _vp]),
     "w8a8_gemm_dequant_allgather": (_i32, [_vp, _i64, _vp, _i64, _vp, _EP, _vp, _i32, _i64, _i64,
-                                           _i64, _i64, _i64, _vp, _i32, _i32, ctypes.c_uint,
+                                           _i64, _i64, _vp, _vp, _i32, _i32, ctypes.c_uint,
                                            _CFG, _vp]),
-    "w8a8_allgather_wait": (_i32, [_vp, _i32, _i32, ctypes.c_uint, _vp]),
+    "w8a8_allgather_finish": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _i32, _i32,
+                                     ctypes.c_uint, _vp]),
     "w8a8_gemm_auto_workspace_bytes": (_i64, [_i64, _i64, _i64, _CFG]),
     "w8a8_weight_tiles_bytes": (_i64, [_i64, _i64]),
     "w8a8_pack_weight_tiles": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),

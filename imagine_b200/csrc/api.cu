@@ -321,31 +321,31 @@ int w8a8_peer_barrier(unsigned* const* flags, int rank, int world, unsigned epoc
   return finish(peer_flags_launch(flags, rank, world, epoch, 0, 1, static_cast<cudaStream_t>(stream)));
 }
 
-int w8a8_allgather_wait(unsigned* const* flags, int rank, int world, unsigned epoch, void* stream) {
-  if (int rc = check_peers(flags, rank, world)) return rc;
-  if (epoch == 0) return fail(W8A8_ERR_VALUE, "epoch must be nonzero");
-  return finish(peer_flags_launch(flags, rank, world, epoch, W8A8_MAX_RANKS, 0,
-                                  static_cast<cudaStream_t>(stream)));
+int64_t w8a8_allgather_recv_bytes(int64_t M, int64_t N_shard, int out_dtype, int world) {
+  if (M < 0 || N_shard < 0 || world < 1) return fail(W8A8_ERR_VALUE, "negative shape");
+  const int64_t esz = out_dtype == W8A8_F32 ? 4 : 2;
+  return static_cast<int64_t>(world) * ((M + 31) / 32) * ((N_shard + 31) / 32) * 32 * 32 * esz;
 }
 
 int w8a8_gemm_dequant_allgather(const int8_t* q, int64_t ldq, const int8_t* w_shard, int64_t ldw,
-                                const float* xs, const w8a8_epilogue_t* epi, void* const* outs,
-                                int out_dtype, int64_t ldo, int64_t col_offset, int64_t M,
-                                int64_t N_shard, int64_t K, unsigned* const* flags, int rank,
-                                int world, unsigned epoch, const w8a8_gemm_config_t* cfg,
-                                void* stream) {
-  if (M < 0 || N_shard < 0 || K < 0 || col_offset < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+                                const float* xs, const w8a8_epilogue_t* epi, void* out,
+                                int out_dtype, int64_t ldo, int64_t M, int64_t N_shard, int64_t K,
+                                void* const* recvs, unsigned* const* flags, int rank, int world,
+                                unsigned epoch, const w8a8_gemm_config_t* cfg, void* stream) {
+  if (M < 0 || N_shard < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
   if (int rc = check_epilogue(epi, N_shard, true)) return rc;
   if (int rc = check_peers(flags, rank, world)) return rc;
   if (epoch == 0) return fail(W8A8_ERR_VALUE, "epoch must be nonzero");
-  if (!outs) return fail(W8A8_ERR_VALUE, "NULL output pointer array");
+  if (!recvs) return fail(W8A8_ERR_VALUE, "NULL receive buffer array");
   for (int r = 0; r < world; ++r) {
-    if (!outs[r]) return fail(W8A8_ERR_VALUE, "output of rank %d is NULL", r);
+    if (!recvs[r] || (reinterpret_cast<uintptr_t>(recvs[r]) & 15u)) {
+      return fail(W8A8_ERR_VALUE, "receive buffer of rank %d is NULL or not 16-byte aligned", r);
+    }
   }
-  if (ldo < col_offset + N_shard) return fail(W8A8_ERR_VALUE, "ldo smaller than the shard's last column");
+  if (ldo < world * N_shard) return fail(W8A8_ERR_VALUE, "ldo smaller than world * N_shard");
   if (M == 0 || N_shard == 0) return finish(0);
-  if (!q || !w_shard || !xs) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (!q || !w_shard || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
   if (ldq < K || ldw < K) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
   const int esz = out_dtype == W8A8_F32 ? 4 : 2;
   GemmArgs g{};
@@ -356,7 +356,7 @@ int w8a8_gemm_dequant_allgather(const int8_t* q, int64_t ldq, const int8_t* w_sh
   g.ldb = ldw;
   g.xs = xs;
   g.epi = epi;
-  g.out = static_cast<uint8_t*>(outs[rank]) + col_offset * esz;
+  g.out = static_cast<uint8_t*>(out) + static_cast<int64_t>(rank) * N_shard * esz;
   g.out_dtype = out_dtype;
   g.ldo = ldo;
   g.M = M;
@@ -367,12 +367,27 @@ int w8a8_gemm_dequant_allgather(const int8_t* q, int64_t ldq, const int8_t* w_sh
   g.ag_world = world;
   g.ag_rank = rank;
   for (int r = 0; r < world; ++r) {
-    g.ag_out[r] = outs[r];
+    g.ag_recv[r] = recvs[r];
     g.ag_flags[r] = flags[r];
   }
-  g.ag_col_off = col_offset;
   g.ag_epoch = epoch;
   return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_allgather_finish(void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N_shard,
+                          void* const* recvs, unsigned* const* flags, int rank, int world,
+                          unsigned epoch, void* stream) {
+  if (M < 0 || N_shard < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (int rc = check_peers(flags, rank, world)) return rc;
+  if (epoch == 0) return fail(W8A8_ERR_VALUE, "epoch must be nonzero");
+  if (!recvs || !recvs[rank] || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldo < world * N_shard || N_shard % 8 || ldo % 8) {
+    return fail(W8A8_ERR_VALUE, "ldo must be >= world * N_shard, both multiples of 8");
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (int rc = peer_flags_launch(flags, rank, world, epoch, W8A8_MAX_RANKS, 0, st)) return finish(rc);
+  return finish(allgather_unpack_launch(recvs[rank], out, out_dtype, ldo, M, N_shard, rank, world, st));
 }
 
 int w8a8_row_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,

@@ -101,16 +101,18 @@ struct EpilogueParams {
   int rope_cols;
   float rope_eps;
   // Column-parallel all-gather fused into the epilogue (n_ranks > 1): every
-  // finished output chunk is also written to each peer's output buffer
-  // (peer_out[r], row stride ld_peer, this shard's columns from peer_col_off);
-  // the last CTA to finish then writes `epoch` into slot `rank` of every peer's
-  // flag array (peer_flags[r]).  cta_count: this rank's CTA arrival counter.
+  // finished 32 x 32 output chunk, as staged (swizzled rows), is also copied
+  // whole into slot `chunk` of this rank's region of each peer's receive
+  // buffer (peer_recv[r] + (rank * chunks + chunk) * chunk bytes, chunk =
+  // (row0 / 32) * chunk_cols + col0 / 32); the last CTA to finish then writes
+  // `epoch` into slot `rank` of every peer's flag array (peer_flags[r]).
+  // cta_count: this rank's CTA arrival counter.
   int n_ranks;
   int rank;
-  void* peer_out[kMaxRanks];
+  uint8_t* peer_recv[kMaxRanks];
   unsigned* peer_flags[kMaxRanks];
-  int64_t ld_peer;
-  int64_t peer_col_off;
+  int64_t chunks;      // chunks of one shard: ceil(M / 32) * chunk_cols
+  int chunk_cols;      // ceil(N_shard / 32)
   unsigned* cta_count;
   unsigned epoch;
 };

@@ -347,36 +347,6 @@ __device__ __forceinline__ Unit unit_of(int unit, int S, int half_from, int num_
   return u;
 }
 
-// Fused column-parallel all-gather: the staged 32 x 32 chunk (row0.., col0..
-// in this shard's columns) copied from the warp's staging tile to every peer's
-// output buffer with 16-byte P2P stores over NVLink.  A row of the chunk is
-// 64 B (2-byte outputs, 64B swizzle) or 128 B (4-byte, 128B swizzle); lanes
-// cover whole rows, so each store instruction writes 8 or 4 row segments.
-// Shard widths are multiples of 8 columns, so a 16-byte piece is wholly
-// inside or outside the shard.
-template <int ESZ>
-__device__ __forceinline__ void peer_copy_chunk(const uint8_t* st, const EpilogueParams& ep,
-                                                int col0, int row0, int M, int N, int lane) {
-  constexpr int kRowBytes = 32 * ESZ;           // 64 or 128
-  constexpr int kPieces = kRowBytes / 16;       // 16-byte pieces per row: 4 or 8
-  constexpr int kRowsPerPass = 32 / kPieces;    // 8 or 4
-  const int piece = lane % kPieces;
-  const int col = col0 + piece * (16 / ESZ);
-  if (col >= N) return;
-#pragma unroll
-  for (int pass = 0; pass < 32 / kRowsPerPass; ++pass) {
-    const int r = pass * kRowsPerPass + lane / kPieces;
-    if (row0 + r >= M) break;
-    const int phys = ESZ == 2 ? (piece ^ ((r >> 1) & 3)) : (piece ^ (r & 7));
-    const uint4 v = *reinterpret_cast<const uint4*>(st + r * kRowBytes + phys * 16);
-    const int64_t off = (static_cast<int64_t>(row0 + r) * ep.ld_peer + ep.peer_col_off + col) * ESZ;
-    for (int p = 0; p < ep.n_ranks; ++p) {
-      if (p == ep.rank) continue;
-      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(ep.peer_out[p]) + off) = v;
-    }
-  }
-}
-
 // Dequant epilogue of one 32 x 32 chunk (lane = row) from its raw 32-bit
 // accumulators, staged in `st` and TMA-stored to (col0, row0) of the output.
 template <int KIND, typename OutT, int ORDER, int ACT>
@@ -499,10 +469,19 @@ __device__ __forceinline__ void finish_chunk(const uint32_t (&cur)[32], const fl
   __syncwarp();
   if (lane == 0 && row0 < M) {
     tma_store_2d(tmD, st, col0, row0);
+    if constexpr (!kRaw) {
+      // fused all-gather: the staged chunk, whole and contiguous, into this
+      // rank's region of every peer's receive buffer
+      if (ep.n_ranks > 1) {
+        constexpr uint32_t kChunkBytes = 32 * 32 * sizeof(OutT);
+        const int64_t slot = static_cast<int64_t>(ep.rank) * ep.chunks +
+                             static_cast<int64_t>(row0 >> 5) * ep.chunk_cols + (col0 >> 5);
+        for (int p = 0; p < ep.n_ranks; ++p) {
+          if (p != ep.rank) bulk_store(ep.peer_recv[p] + slot * kChunkBytes, st, kChunkBytes);
+        }
+      }
+    }
     tma_store_commit();
-  }
-  if constexpr (!kRaw) {
-    if (ep.n_ranks > 1) peer_copy_chunk<static_cast<int>(sizeof(OutT))>(st, ep, col0, row0, M, N, lane);
   }
 }
 
@@ -1112,9 +1091,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) tma_store_wait_all<0>();
     if constexpr (!kRaw) {
       if (ep.n_ranks > 1) {
-        // Fused all-gather: this CTA's P2P stores are published, then it counts
-        // itself in; the last CTA of the grid writes this call's epoch into
-        // slot `rank` of every peer's done flags.
+        // Fused all-gather: this CTA's peer copies are complete (each warp's
+        // bulk groups waited above) and published, then it counts itself in;
+        // the last CTA of the grid writes this call's epoch into slot `rank`
+        // of every peer's done flags.
+        fence_proxy_async_global();
         __threadfence_system();
         named_bar_sync(1, kEpiWarps * 32);
         if (threadIdx.x == 0) {
@@ -1272,11 +1253,11 @@ EpilogueParams to_params(const GemmArgs& g) {
   if (ep.n_ranks > 1) {
     ep.rank = g.ag_rank;
     for (int r = 0; r < g.ag_world; ++r) {
-      ep.peer_out[r] = g.ag_out[r];
+      ep.peer_recv[r] = static_cast<uint8_t*>(g.ag_recv[r]);
       ep.peer_flags[r] = g.ag_flags[r];
     }
-    ep.ld_peer = g.ldo;
-    ep.peer_col_off = g.ag_col_off;
+    ep.chunk_cols = static_cast<int>((g.N + 31) / 32);
+    ep.chunks = (g.M + 31) / 32 * ep.chunk_cols;
     ep.cta_count = g.ag_flags[g.ag_rank] + 2 * kMaxRanks;
     ep.epoch = g.ag_epoch;
   }
@@ -1388,6 +1369,41 @@ __global__ void __launch_bounds__(32) peer_flags_kernel(unsigned* mine, PeerFlag
       return;
     }
     __nanosleep(256);
+  }
+}
+
+// The peers' chunks in this rank's receive buffer (each as its epilogue
+// staged it: 32 rows of 32 * ESZ bytes in 16-byte pieces, swizzled like the
+// staging tile) into the output at columns p * N_shard: one warp per chunk,
+// lanes covering whole rows of it.
+template <int ESZ>
+__global__ void __launch_bounds__(256) allgather_unpack_kernel(
+    const uint8_t* __restrict__ recv, uint8_t* __restrict__ out, int64_t ldo, int M, int N_shard,
+    int rank, int world, int64_t chunks, int chunk_cols) {
+  constexpr int kRowBytes = 32 * ESZ;
+  constexpr int kPieces = kRowBytes / 16;
+  constexpr int kRowsPerPass = 32 / kPieces;
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (wid >= static_cast<int64_t>(world - 1) * chunks) return;
+  int p = static_cast<int>(wid / chunks);
+  if (p >= rank) ++p;  // the peers, skipping this rank
+  const int64_t c = wid - static_cast<int64_t>(wid / chunks) * chunks;
+  const int rb = static_cast<int>(c / chunk_cols);
+  const int cb = static_cast<int>(c - static_cast<int64_t>(rb) * chunk_cols);
+  const int piece = lane % kPieces;
+  const int col = cb * 32 + piece * (16 / ESZ);  // shard column (N_shard % 8 == 0)
+  if (col >= N_shard) return;
+  const uint8_t* src = recv + (static_cast<int64_t>(p) * chunks + c) * 32 * kRowBytes;
+#pragma unroll
+  for (int pass = 0; pass < 32 / kRowsPerPass; ++pass) {
+    const int r = pass * kRowsPerPass + lane / kPieces;
+    const int row = rb * 32 + r;
+    if (row >= M) break;
+    const int phys = ESZ == 2 ? (piece ^ ((r >> 1) & 3)) : (piece ^ (r & 7));
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src + r * kRowBytes + phys * 16));
+    *reinterpret_cast<uint4*>(
+        out + (static_cast<int64_t>(row) * ldo + static_cast<int64_t>(p) * N_shard + col) * ESZ) = v;
   }
 }
 
@@ -1552,6 +1568,32 @@ int peer_flags_launch(unsigned* const* flags, int rank, int world, unsigned epoc
   return 0;
 }
 
+int allgather_unpack_launch(const void* recv, void* out, int out_dtype, int64_t ldo, int64_t M,
+                            int64_t N_shard, int rank, int world, cudaStream_t stream) {
+  const int chunk_cols = static_cast<int>((N_shard + 31) / 32);
+  const int64_t chunks = (M + 31) / 32 * chunk_cols;
+  const int64_t warps = static_cast<int64_t>(world - 1) * chunks;
+  if (warps == 0) return 0;
+  const unsigned grid = static_cast<unsigned>((warps + 7) / 8);
+  const auto* r = static_cast<const uint8_t*>(recv);
+  auto* o = static_cast<uint8_t*>(out);
+  if (out_dtype == W8A8_F32) {
+    allgather_unpack_kernel<4><<<grid, 256, 0, stream>>>(r, o, ldo, static_cast<int>(M),
+                                                         static_cast<int>(N_shard), rank, world,
+                                                         chunks, chunk_cols);
+  } else {
+    allgather_unpack_kernel<2><<<grid, 256, 0, stream>>>(r, o, ldo, static_cast<int>(M),
+                                                         static_cast<int>(N_shard), rank, world,
+                                                         chunks, chunk_cols);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("all-gather unpack launch failed: %s", cudaGetErrorString(e));
+    return W8A8_ERR_ACCELERATOR;
+  }
+  return 0;
+}
+
 int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& p) {
   const int out_bytes = g.out_dtype == W8A8_F32 || g.out_dtype == W8A8_S32 ? 4 : 2;
   auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
@@ -1687,11 +1729,11 @@ int gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
     const int esz = out_bytes;
     if (!(g.kind == 0 && tc_ok && !g.rms_rope && !g.b_tiled && g.out_dtype != W8A8_S32 &&
           g.ag_world <= kMaxRanks && g.ag_rank >= 0 && g.ag_rank < g.ag_world &&
-          g.N % 8 == 0 && g.ldo % 8 == 0 && g.ag_col_off % 8 == 0 && esz >= 2 &&
+          g.N % 8 == 0 && g.ldo % 8 == 0 && esz >= 2 &&
           !(g.epi && g.epi->residual))) {
       set_error("the fused all-gather needs int8 codes, a floating output without residual, "
-                "2..%d ranks, K %% 16 == 0, 16-byte aligned operands and N_shard, ldo and the "
-                "column offset multiples of 8", kMaxRanks);
+                "2..%d ranks, K %% 16 == 0, 16-byte aligned operands and N_shard and ldo "
+                "multiples of 8", kMaxRanks);
       return W8A8_ERR_VALUE;
     }
     g.split_k = 1;

@@ -187,6 +187,14 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* smem_
       : "memory");
 }
 
+// Untiled bulk copy shared -> global (16-byte aligned addresses, size a
+// multiple of 16), in the thread's current bulk group.
+__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_store_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

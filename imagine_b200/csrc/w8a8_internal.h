@@ -61,12 +61,12 @@ struct GemmArgs {
   int64_t rope_cols;
   float rope_eps;
   // column-parallel all-gather fused into the epilogue (ag_world > 1); `out`
-  // is this rank's buffer at its shard's first column
+  // is this rank's output at its shard's first column, ag_recv[r] rank r's
+  // receive buffer
   int ag_world;
   int ag_rank;
-  void* ag_out[W8A8_MAX_RANKS];
+  void* ag_recv[W8A8_MAX_RANKS];
   unsigned* ag_flags[W8A8_MAX_RANKS];
-  int64_t ag_col_off;
   unsigned ag_epoch;
 };
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);
@@ -75,6 +75,10 @@ int gemm_launch(const GemmArgs& args, cudaStream_t stream);
 // peers' GEMMs.
 int peer_flags_launch(unsigned* const* flags, int rank, int world, unsigned epoch, int base,
                       int signal, cudaStream_t stream);
+// The peers' chunks in this rank's receive buffer into its output [M, ldo]
+// (rank r's shard at columns r * N_shard).
+int allgather_unpack_launch(const void* recv, void* out, int out_dtype, int64_t ldo, int64_t M,
+                            int64_t N_shard, int rank, int world, cudaStream_t stream);
 // Tile shape and split-K layout gemm_launch uses for a GEMM.
 struct GemmPlan {
   int bn, cg, group_m, max_ctas;

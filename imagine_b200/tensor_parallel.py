@@ -8,9 +8,10 @@ placement plan.  Both linears are bit-identical to the single-GPU operator:
   activation (identical codes on every rank), computes its N-slice, and
   optionally all-gathers the slices.  Used for QKV, MLP-up and the AdaLN
   modulation GEMV.  With ``fused=True`` the all-gather is not a collective
-  after the GEMM: the GEMM's epilogue writes every finished output chunk into
-  all ranks' outputs over NVLink (w8a8_gemm_dequant_allgather), on buffers
-  that every rank maps (torch's symmetric memory, used as plumbing).
+  after the GEMM: the GEMM's epilogue copies every finished output chunk into
+  every peer's receive buffer over NVLink (w8a8_gemm_dequant_allgather), which
+  every rank maps (torch's symmetric memory, used as plumbing), and each rank
+  then places its peers' chunks (w8a8_allgather_finish).
 * ``RowParallelInt8Linear`` shards W and the activation along K.  The per-token
   scale needs the absmax of the whole row, so ranks all-reduce(MAX) their
   shard's row absmax first; each rank then quantises its shard with the full
@@ -68,7 +69,7 @@ def shard_slice(total: int, rank: int, world: int) -> slice:
 
 
 class _PeerBuffers:
-    """Peer-mapped output buffer and flag block of one fused column-parallel
+    """Peer-mapped receive buffer and flag block of one fused column-parallel
     linear, on every rank of `group` (rendezvous is collective: every rank
     makes the same calls in the same order)."""
 
@@ -85,24 +86,22 @@ class _PeerBuffers:
         handle = symm.rendezvous(self.flags, self.group)
         self.flag_ptrs = (ctypes.c_void_p * self.world)(*handle.buffer_ptrs)
         self._keep = [handle]
-        self.out = None
-        self.out_ptrs = None
+        self.recv = None
+        self.recv_ptrs = None
         self.epoch = 0
         torch.cuda.synchronize(device)
         dist.barrier(self.group)  # every flag block is zero before any rank signals
 
-    def output(self, m: int, n: int, dtype: torch.dtype, device) -> torch.Tensor:
-        if self.out is None or self.out.shape[0] < m or self.out.shape[1] != n or \
-                self.out.dtype != dtype:
+    def receive(self, nbytes: int, device) -> None:
+        if self.recv is None or self.recv.numel() < nbytes:
             # a peer may still be writing into the old buffer: finish first
             torch.cuda.synchronize(device)
             dist.barrier(self.group)
-            buf = self.symm.empty(max(m, 1), n, dtype=dtype, device=device)
+            buf = self.symm.empty(max(nbytes, 16), dtype=torch.uint8, device=device)
             handle = self.symm.rendezvous(buf, self.group)
-            self.out_ptrs = (ctypes.c_void_p * self.world)(*handle.buffer_ptrs)
+            self.recv_ptrs = (ctypes.c_void_p * self.world)(*handle.buffer_ptrs)
             self._keep.append((buf, handle))
-            self.out = buf
-        return self.out[:m]
+            self.recv = buf
 
     def next_epoch(self) -> int:
         self.epoch = self.epoch % 0xFFFFFFFF + 1  # never 0
@@ -136,15 +135,14 @@ class ColumnParallelInt8Linear:
         self.backend = backend or NativeBackend()
         self.kw = linear_kwargs
         self.fused = (fused and gather_output and self.world > 1 and
-                      all(sz % 8 == 0 for sz in self.sizes) and n % 8 == 0 and
+                      len(set(self.sizes)) == 1 and self.sizes[0] % 8 == 0 and
                       set(linear_kwargs) <= {"dequant", "scale_mode", "output_act"})
         self._peers = None
 
     def _fused_call(self, x: torch.Tensor, out_dtype) -> torch.Tensor:
-        """One launch per rank: quantise x, then the GEMM whose epilogue writes
-        this rank's columns into every rank's output (see the module doc).  The
-        result is a view of the layer's peer-mapped buffer, valid until the
-        layer's next call."""
+        """Quantise x, then the GEMM whose epilogue also sends this rank's
+        chunks to every peer, then this rank's copy of the peers' chunks (see
+        the module doc)."""
         from . import _native as N
         from .linear import _code, _epilogue, _stream, _vp, quantize_int8_rowwise
 
@@ -156,22 +154,25 @@ class ColumnParallelInt8Linear:
         k = x.shape[-1]
         x2 = x.reshape(-1, k)
         m = x2.shape[0]
-        y = pb.output(m, self.n, out_dtype, dev)
+        ns = self.weight.shape[0]
+        y = torch.empty((m, self.n), dtype=out_dtype, device=dev)
+        if m == 0:
+            return y.reshape(*lead, self.n)
+        pb.receive(int(N.LIB.w8a8_allgather_recv_bytes(m, ns, _code(out_dtype), self.world)), dev)
         epoch = pb.next_epoch()
         stream = _stream(dev)
-        if m > 0:
-            N.check(N.LIB.w8a8_peer_barrier(pb.flag_ptrs, self.rank, self.world, epoch, stream))
-            q, xs = quantize_int8_rowwise(x2, scale_mode=self.kw.get("scale_mode", "eager"))
-            ws = self.weight_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
-            b = (self.bias.to(device=dev, dtype=out_dtype).contiguous()
-                 if self.bias is not None else None)
-            ep = _epilogue(ws, b, None, None, self.kw.get("dequant", "eager"),
-                           self.kw.get("output_act"), self.weight.shape[0], self.weight.shape[0])
-            N.check(N.LIB.w8a8_gemm_dequant_allgather(
-                _vp(q), k, _vp(self.weight), k, _vp(xs.reshape(-1)), ctypes.byref(ep),
-                pb.out_ptrs, _code(out_dtype), self.n, self.col_offset, m,
-                self.weight.shape[0], k, pb.flag_ptrs, self.rank, self.world, epoch, None, stream))
-            N.check(N.LIB.w8a8_allgather_wait(pb.flag_ptrs, self.rank, self.world, epoch, stream))
+        N.check(N.LIB.w8a8_peer_barrier(pb.flag_ptrs, self.rank, self.world, epoch, stream))
+        q, xs = quantize_int8_rowwise(x2, scale_mode=self.kw.get("scale_mode", "eager"))
+        ws = self.weight_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+        b = self.bias.to(device=dev, dtype=out_dtype).contiguous() if self.bias is not None else None
+        ep = _epilogue(ws, b, None, None, self.kw.get("dequant", "eager"),
+                       self.kw.get("output_act"), ns, ns)
+        N.check(N.LIB.w8a8_gemm_dequant_allgather(
+            _vp(q), k, _vp(self.weight), k, _vp(xs.reshape(-1)), ctypes.byref(ep), _vp(y),
+            _code(out_dtype), self.n, m, ns, k, pb.recv_ptrs, pb.flag_ptrs, self.rank, self.world,
+            epoch, None, stream))
+        N.check(N.LIB.w8a8_allgather_finish(_vp(y), _code(out_dtype), self.n, m, ns, pb.recv_ptrs,
+                                            pb.flag_ptrs, self.rank, self.world, epoch, stream))
         return y.reshape(*lead, self.n)
 
     def __call__(self, x: torch.Tensor, out_dtype=None) -> torch.Tensor:

@@ -230,35 +230,40 @@ int w8a8_rope_freqs_rows(const float* freqs, int64_t freq_rows, int64_t rows, fl
 
 /* ---- column-parallel linear with the all-gather fused into the GEMM -------
  * No reference counterpart (the reference runs on one GPU).  Ranks of one
- * NVLink domain (one process per GPU) each hold an N-shard of the weight
+ * NVLink domain (one process per GPU) each hold an equal N-shard of the weight
  * ([N_shard, K], with its ws / bias shard in `epi`) and the same activation
- * codes; every rank ends with the whole [M, N] output.  Instead of a GEMM
- * followed by an all-gather collective, each finished output chunk is written
- * by the GEMM's epilogue both to this rank's output and, with 16-byte P2P
- * stores over NVLink, to every peer's output (columns col_offset ..
- * col_offset + N_shard), so the exchange overlaps the math tile by tile.
- *   outs[r]:  rank r's output buffer [M, ldo] (bf16 / f16 / f32), mapped into
- *             this process (peer pointers, e.g. symmetric memory);
+ * codes; every rank ends with the whole [M, N] output, rank r's shard at
+ * columns r * N_shard.  Instead of a GEMM followed by an all-gather
+ * collective, the GEMM's epilogue writes each finished 32 x 32 output chunk to
+ * this rank's output and also copies it, whole and contiguous, into this
+ * rank's region of every peer's receive buffer over NVLink, so the exchange
+ * overlaps the math tile by tile; w8a8_allgather_finish then waits for the
+ * peers and places their chunks into the output.
+ *   recvs[r]: rank r's receive buffer, w8a8_allgather_recv_bytes(M, N_shard,
+ *             out_dtype, world) bytes, 16-byte aligned, mapped into this
+ *             process (peer pointers, e.g. symmetric memory);
  *   flags[r]: rank r's flag block of W8A8_PEER_FLAG_WORDS uint32, zeroed once
  *             before first use, likewise mapped;
  *   epoch:    one more on every call (the same on all ranks, never 0).
  * Per call, on every rank, in stream order: w8a8_peer_barrier (no rank writes
- * into another's output before all are done with the previous call's), the
- * quantiser, w8a8_gemm_dequant_allgather, then w8a8_allgather_wait before
- * anything reads the output.  The GEMM's last CTA to finish signals the
- * peers; the waits are bounded (2 s) and record a device error on timeout.
- * N_shard, ldo and col_offset multiples of 8; K % 16 == 0; 2 to 8 ranks;
- * int8 codes; no residual; one launch per rank with identical shapes. */
+ * into another's receive buffer before all are done with the previous
+ * call's), the quantiser, w8a8_gemm_dequant_allgather, w8a8_allgather_finish.
+ * The GEMM's last CTA to finish signals the peers; the waits are bounded (2 s)
+ * and record a device error on timeout.  N_shard and ldo (>= world * N_shard)
+ * multiples of 8; K % 16 == 0; 2 to 8 ranks; int8 codes; no residual; one
+ * launch per rank with identical shapes. */
 #define W8A8_MAX_RANKS 8
 #define W8A8_PEER_FLAG_WORDS 32
+int64_t w8a8_allgather_recv_bytes(int64_t M, int64_t N_shard, int out_dtype, int world);
 int w8a8_peer_barrier(unsigned* const* flags, int rank, int world, unsigned epoch, void* stream);
 int w8a8_gemm_dequant_allgather(const int8_t* q, int64_t ldq, const int8_t* w_shard, int64_t ldw,
-                                const float* xs, const w8a8_epilogue_t* epi, void* const* outs,
-                                int out_dtype, int64_t ldo, int64_t col_offset, int64_t M,
-                                int64_t N_shard, int64_t K, unsigned* const* flags, int rank,
-                                int world, unsigned epoch, const w8a8_gemm_config_t* cfg,
-                                void* stream);
-int w8a8_allgather_wait(unsigned* const* flags, int rank, int world, unsigned epoch, void* stream);
+                                const float* xs, const w8a8_epilogue_t* epi, void* out,
+                                int out_dtype, int64_t ldo, int64_t M, int64_t N_shard, int64_t K,
+                                void* const* recvs, unsigned* const* flags, int rank, int world,
+                                unsigned epoch, const w8a8_gemm_config_t* cfg, void* stream);
+int w8a8_allgather_finish(void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N_shard,
+                          void* const* recvs, unsigned* const* flags, int rank, int world,
+                          unsigned epoch, void* stream);
 
 /* ---- row-parallel (K-sharded) quantisation --------------------------------
  * No reference counterpart: the reference runs on one GPU.  A K-sharded

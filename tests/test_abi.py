@@ -122,15 +122,20 @@ def test_fused_allgather_argument_errors():
     flags = (ctypes.c_void_p * 2)(0x1000, 0x2000)
     assert N.LIB.w8a8_peer_barrier(flags, 0, 1, 1, None) == N.ERR_VALUE  # one rank
     assert N.LIB.w8a8_peer_barrier(flags, 2, 2, 1, None) == N.ERR_VALUE  # rank outside
-    assert N.LIB.w8a8_allgather_wait(flags, 0, 9, 1, None) == N.ERR_VALUE  # too many ranks
-    assert N.LIB.w8a8_allgather_wait(flags, 0, 2, 0, None) == N.ERR_VALUE  # epoch 0
+    recvs = (ctypes.c_void_p * 2)(0x4000, 0x5000)
+    assert N.LIB.w8a8_allgather_finish(0x9000, N.BF16, 256, 16, 128, recvs, flags, 0, 9, 1,
+                                       None) == N.ERR_VALUE  # too many ranks
+    assert N.LIB.w8a8_allgather_finish(0x9000, N.BF16, 256, 16, 128, recvs, flags, 0, 2, 0,
+                                       None) == N.ERR_VALUE  # epoch 0
     null_flags = (ctypes.c_void_p * 2)(0x1000, 0)
     assert N.LIB.w8a8_peer_barrier(null_flags, 0, 2, 1, None) == N.ERR_VALUE
     ep = N.Epilogue()
     ep.ws = 0x3000
     ep.ws_numel = 1
-    outs = (ctypes.c_void_p * 2)(0x4000, 0x5000)
-    # the shard's last column beyond ldo
-    rc = N.LIB.w8a8_gemm_dequant_allgather(0x6000, 64, 0x7000, 64, 0x8000, ctypes.byref(ep), outs,
-                                           N.BF16, 128, 64, 16, 128, 64, flags, 0, 2, 1, None, None)
+    # the output's row is narrower than world * N_shard
+    rc = N.LIB.w8a8_gemm_dequant_allgather(0x6000, 64, 0x7000, 64, 0x8000, ctypes.byref(ep), 0x9000,
+                                           N.BF16, 128, 16, 128, 64, recvs, flags, 0, 2, 1, None,
+                                           None)
     assert rc == N.ERR_VALUE and b"ldo" in N.LIB.w8a8_last_error()
+    # a receive buffer: every shard's 32 x 32 chunks, for every rank
+    assert N.LIB.w8a8_allgather_recv_bytes(40, 72, N.BF16, 2) == 2 * 2 * 3 * 2048
