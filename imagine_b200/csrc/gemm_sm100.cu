@@ -680,6 +680,10 @@ __device__ __forceinline__ void splitk_take_chunk(const SplitArgs& sk, int srow,
 // Half-width units (tiles from sk.half_from on, CG = 1, BN = 256, no split-K)
 // load 128 rows of B through tmBh and issue N = 128 MMAs into the first 128
 // columns of the accumulator.
+//
+// KIND 2 (MXFP8) with CG = 2 (BN = 128: 256 x 128 pair tiles, each CTA two
+// 128-column accumulators plus its scale blocks in TMEM): tmBh and tmW, unused
+// by that kind, are the scale-factor maps of A and B.
 template <int KIND, int BN, typename OutT, int ORDER, int ACT, int CG, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -688,6 +692,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       int num_n_tiles, int group_m, EpilogueParams ep, SplitArgs sk) {
   using C = Cfg<BN, OutT, CG, KIND, SPLIT>;
   static_assert(!SPLIT || (CG == 1 && KIND == 0), "split-K is built for the 1-CTA int8 GEMM");
+  static_assert(KIND != 2 || CG == 1 || BN == 128, "MXFP8 pairs run 256 x 128 tiles");
   constexpr bool kRaw = std::is_same<OutT, int32_t>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -732,9 +737,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kProducerWarp && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (half_from < num_tiles) tma_prefetch_desc(&tmBh);
+    if (half_from < num_tiles || (KIND == 2 && CG == 2)) tma_prefetch_desc(&tmBh);
     if constexpr (!kRaw) tma_prefetch_desc(&tmD);
-    if constexpr (SPLIT) tma_prefetch_desc(&tmW);
+    if constexpr (SPLIT || (KIND == 2 && CG == 2)) tma_prefetch_desc(&tmW);
   }
   if (warp == kMmaWarp) {
     tmem_alloc<C::kTmemCols, CG>(tmem_slot);
@@ -806,10 +811,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           } else {
             // both CTAs' bytes are counted on the leader's barrier
-            if (leader) mbar_arrive_expect_tx(&full[s], 2 * C::kStageBytes);
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * (C::kStageBytes + C::kSFBytes));
             const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
             tma_load_2d_pair(sA + s * C::kABytes, &tmA, bar, kb * kBK, a_row);
             tma_load_2d_pair(sB + s * C::kBBytes, &tmB, bar, kb * kBK, b_row);
+            if constexpr (KIND == 2) {
+              // scale blocks as two 256-byte rows of the [blocks * 2, 256]
+              // maps (tmBh: A, tmW: B): this CTA's 128-row block of A and
+              // the tile's 128-column block of B; blocks past the buffers'
+              // ends read as zeros (rows past M / N, never stored)
+              uint8_t* sf = sSF + s * C::kSFBytes;
+              const int a_blk = mb * CG + static_cast<int>(rank);
+              tma_load_2d_pair(sf, &tmBh, bar, 0, (a_blk * ep.sf_ncb + kb) * 2);
+              tma_load_2d_pair(sf + 512, &tmW, bar, 0, (nb * ep.sf_ncb + kb) * 2);
+            }
           }
         }
       }
@@ -850,16 +865,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             // four K=32 MMAs each pick their K sub-block with sf_id
             const uint32_t sf_tmem = tmem_base + C::kSFCol0 + s * C::kSFCols;
             const uint32_t sf_smem = smem_u32(sSF + s * C::kSFBytes);
-            tmem_cp_32x128b_x4(sf_tmem, smem_desc_sf(sf_smem));
+            tmem_cp_32x128b_x4<CG>(sf_tmem, smem_desc_sf(sf_smem));
 #pragma unroll
             for (int j = 0; j < BN / 128; ++j) {
-              tmem_cp_32x128b_x4(sf_tmem + 4 * (1 + j), smem_desc_sf(sf_smem + 512 * (1 + j)));
+              tmem_cp_32x128b_x4<CG>(sf_tmem + 4 * (1 + j), smem_desc_sf(sf_smem + 512 * (1 + j)));
             }
 #pragma unroll
             for (int k = 0; k < kBK / kUmmaK; ++k) {
-              umma_mx(d_tmem, smem_desc_k_sw128(a0 + k * kUmmaK), smem_desc_k_sw128(b0 + k * kUmmaK),
-                      make_idesc_mx(kBM, BN, static_cast<uint32_t>(k)), sf_tmem, sf_tmem + 4,
-                      (kb != kb_lo || k != 0) ? 1u : 0u);
+              umma_mx<CG>(d_tmem, smem_desc_k_sw128(a0 + k * kUmmaK),
+                          smem_desc_k_sw128(b0 + k * kUmmaK),
+                          make_idesc_mx(kBM * CG, BN, static_cast<uint32_t>(k)), sf_tmem,
+                          sf_tmem + 4, (kb != kb_lo || k != 0) ? 1u : 0u);
             }
           } else {
 #pragma unroll
@@ -1454,7 +1470,16 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, const GemmPlan& plan, cudaStream
   } else {
     mbh = mb;
   }
-  if (splits > 1) {
+  if (KIND == 2 && cg == 2) {
+    // MXFP8 pairs: the blocked scales (512 bytes per 128-row block and 128
+    // K elements) as [blocks * 2, 256] byte maps, one block per 256 x 2 box
+    const int64_t ncb = (g.K + 127) / 128;
+    const int64_t a_rows = (g.M + 127) / 128 * ncb * 2, b_rows = (g.N + 127) / 128 * ncb * 2;
+    ok = ok && make_map_2d(&mbh, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.sfa, 256, a_rows, 256, 256, 2,
+                           CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok = ok && make_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.sfb, 256, b_rows, 256, 256, 2,
+                           CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else if (splits > 1) {
     // int32 [tiles * 128, bn] partial sums, then the arrival counters;
     // reductions in 32-row x 16-column boxes
     sk.acc = static_cast<int32_t*>(g.workspace);
@@ -1490,6 +1515,10 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, const GemmPlan& plan, cudaStream
         return W8A8_ERR_VALUE;
       }
     } else if constexpr (KIND == 2) {
+      if (cg == 2) {
+        return launch_tc<KIND, 128, OutT, O, A, 2>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas,
+                                                   stream);
+      }
       return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas, stream);
     } else {
       if constexpr (KIND == 0 && !std::is_same<OutT, int32_t>::value) {
@@ -1764,9 +1793,15 @@ int gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
     }
   } else if (g.kind == 2) {
     const bool mx_ok = tc_ok && g.K % 32 == 0 && a16(g.sfa) && a16(g.sfb);
-    GemmPlan mx_plan = plan;  // 128-column tiles, one CTA per tile
+    // 128-column tiles: two 256-column accumulators would fill all 512 TMEM
+    // columns and leave none for the block scales.  One CTA per tile unless
+    // pairs (256 x 128 tiles, each SM loading half of B) are asked for: on
+    // B200 the pairs measured 4-8% slower (5600 x 3072 -> 3072: 93.3 against
+    // 89.1 us; -> 12288: 314 against 292 us; 5600 x 12288 -> 3072: 333
+    // against 306 us).
+    GemmPlan mx_plan = plan;
     mx_plan.bn = 128;
-    mx_plan.cg = 1;
+    mx_plan.cg = g.cfg && g.cfg->cta_group ? g.cfg->cta_group : 1;
     switch (g.out_dtype) {
       case W8A8_BF16: return dispatch_out<2, __nv_bfloat16>(g, mx_ok, mx_plan, stream);
       case W8A8_F16: return dispatch_out<2, __half>(g, mx_ok, mx_plan, stream);

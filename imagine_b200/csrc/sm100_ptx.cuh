@@ -319,23 +319,43 @@ __device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, u
 }
 
 // Block-scaled MMA, kind::mxf8f6f4 (e4m3 x e4m3, one e8m0 scale per 32 K
-// elements per row), scale factors read from TMEM.
+// elements per row), scale factors read from TMEM.  CG = 2: the pair's MMA,
+// issued by the leader; each CTA's TMEM holds the scales of its own 128 rows
+// of A and of all N columns of B at the same addresses.
+template <int CG = 1>
 __device__ __forceinline__ void umma_mx(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
-          d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
-      : "memory");
+  if constexpr (CG == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+            d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+        : "memory");
+  }
 }
 
 // Shared -> TMEM copy of a 32 x 16 B block, replicated into the four 32-lane
-// quadrants (the scale-factor layout of a 128-row block).
+// quadrants (the scale-factor layout of a 128-row block).  CG = 2 (issued by
+// the pair's leader): each CTA's block, at the same shared-memory offset, into
+// its own TMEM at the same address.
+template <int CG = 1>
 __device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
-               : "memory");
+  if constexpr (CG == 1) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+                 : "memory");
+  } else {
+    asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+                 : "memory");
+  }
 }
 
 // Descriptor of a 32-row x 16-byte shared-memory block with no swizzle: 8-row

@@ -117,7 +117,7 @@ def main():
         elif a.kernel == "mxfp8_gemm":
             aq, asf = W.quantize_mxfp8(x)
             bq, bsf = W.quantize_mxfp8(w)
-            run(lambda: W.mxfp8_linear(aq, asf, bq, bsf, b, out_dtype=torch.bfloat16))
+            run(lambda: W.mxfp8_linear(aq, asf, bq, bsf, b, out_dtype=torch.bfloat16, config=cfg))
         elif a.kernel in ("gemm", "gemm_gelu", "gemv"):
             act = "gelu_tanh" if a.kernel == "gemm_gelu" else None
             if a.time and a.kernel != "gemv":

@@ -486,8 +486,12 @@ def test_mxfp8_quantize_random(dt, m, k):
     assert np.array_equal(_b(p), _b(po))
 
 
-@pytest.mark.parametrize("m,k,n", [(300, 3072, 256), (130, 160, 264), (128, 256, 128)])
-def test_mxfp8_linear(m, k, n):
+@pytest.mark.parametrize("cta_group", [1, 2])
+@pytest.mark.parametrize("m,k,n", [(300, 3072, 256), (130, 160, 264), (128, 256, 128),
+                                   (1000, 1024, 640)])
+def test_mxfp8_linear(m, k, n, cta_group):
+    """One CTA per 128 x 128 tile, and CTA pairs (256 x 128 tiles; rows of the
+    last pair past M, columns past N)."""
     g = torch.Generator().manual_seed(m + k + n)
     x = torch.randn(m, k, generator=g)
     x = torch.where(torch.rand(m, k, generator=g) < 0.01, x * 20, x).to(torch.bfloat16)
@@ -495,7 +499,7 @@ def test_mxfp8_linear(m, k, n):
     b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16)
     aq, asf = W().quantize_mxfp8(x.to(cuda()))
     wq, wsf = W().quantize_mxfp8(w.to(cuda()))
-    y = W().mxfp8_linear(aq, asf, wq, wsf, b.to(cuda()))
+    y = W().mxfp8_linear(aq, asf, wq, wsf, b.to(cuda()), config=(0, 8, 0, cta_group))
     no_device_error()
     ref = O.mxfp8_linear(aq.cpu(), asf.cpu(), wq.cpu(), wsf.cpu(), b, out_dtype=torch.float32)
     assert_rms_close(y, ref)
