@@ -26,6 +26,7 @@ MAX_RANKS, PEER_FLAG_WORDS = 8, 32
 SCALE_EAGER, SCALE_KITCHEN = 0, 1
 DQ_EAGER, DQ_SCALE_PRODUCT, DQ_CHAINED = 0, 1, 2
 ACT_NONE, ACT_GELU_TANH = 0, 1
+STEP_DENOISED, STEP_EULER, STEP_ER_SDE, STEP_CHURN = 0, 1, 2, 3
 
 
 class Epilogue(ctypes.Structure):
@@ -39,6 +40,18 @@ class Epilogue(ctypes.Structure):
         ("dequant_order", ctypes.c_int32),
         ("activation", ctypes.c_int32),
         ("residual_scale_rows", ctypes.c_int64),
+    ]
+
+
+class SamplerStep(ctypes.Structure):
+    _fields_ = [
+        ("mode", ctypes.c_int32),
+        ("stage", ctypes.c_int32),
+        ("last", ctypes.c_int32),
+        ("has_noise", ctypes.c_int32),
+        ("cfg_scale", ctypes.c_float),
+        ("s_noise", ctypes.c_float),
+        ("denoised_input", ctypes.c_int32),
     ]
 
 
@@ -109,6 +122,8 @@ SIGNATURES = {
     "w8a8_fp8_gemm": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _CFG, _vp]),
     "w8a8_quantize_mxfp8": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "w8a8_mxfp8_gemm": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _CFG, _vp]),
+    "w8a8_sampler_step": (_i32, [_vp, _vp, _vp, _i32, _i64, _vp, ctypes.POINTER(SamplerStep), _vp,
+                                 _vp, _vp, _vp, _vp]),
 }
 
 

@@ -24,7 +24,7 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libw8a8.so")
 
 SOURCES = ["api.cu", "quantize.cu", "convrot.cu", "gemm_sm100.cu", "gemm_splitk_static.cu", "gemv.cu",
-           "mxfp8.cu", "rope.cu"]
+           "mxfp8.cu", "rope.cu", "sampler.cu"]
 HEADERS = ["sm100_ptx.cuh", "epilogue.cuh", "quant_common.cuh", "w8a8_internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

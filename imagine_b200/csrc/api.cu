@@ -104,7 +104,7 @@ const char* w8a8_last_error(void) { return g_last_error; }
 
 int w8a8_last_accelerator_code(void) { return g_last_accel; }
 
-int w8a8_abi_version(void) { return 101; }
+int w8a8_abi_version(void) { return 102; }
 
 int w8a8_device_error(void* stream) {
   int v = 0;
@@ -388,6 +388,42 @@ int w8a8_allgather_finish(void* out, int out_dtype, int64_t ldo, int64_t M, int6
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (int rc = peer_flags_launch(flags, rank, world, epoch, W8A8_MAX_RANKS, 0, st)) return finish(rc);
   return finish(allgather_unpack_launch(recvs[rank], out, out_dtype, ldo, M, N_shard, rank, world, st));
+}
+
+int w8a8_sampler_step(float* x, const void* out_cond, const void* out_uncond, int out_dtype,
+                      int64_t n, const float* coef, const w8a8_sampler_step_t* step,
+                      float* denoised, float* old_denoised, float* old_derivative,
+                      const float* noise, void* stream) {
+  if (n < 0) return fail(W8A8_ERR_VALUE, "negative size");
+  if (!step) return fail(W8A8_ERR_VALUE, "NULL step description");
+  if (step->mode < W8A8_STEP_DENOISED || step->mode > W8A8_STEP_CHURN) {
+    return fail(W8A8_ERR_VALUE, "unknown sampler step mode %d", step->mode);
+  }
+  if (!is_float_dtype(out_dtype)) {
+    return fail(W8A8_ERR_VALUE, "model output dtype code %d is not floating", out_dtype);
+  }
+  if (n == 0) return finish(0);
+  if (!x || !coef) return fail(W8A8_ERR_VALUE, "NULL latent or coefficient pointer");
+  const int mode = step->mode;
+  if (mode != W8A8_STEP_CHURN && !out_cond) return fail(W8A8_ERR_VALUE, "NULL model output");
+  if (mode == W8A8_STEP_DENOISED && !denoised) return fail(W8A8_ERR_VALUE, "NULL denoised output");
+  if (mode == W8A8_STEP_ER_SDE) {
+    if (step->stage < 1 || step->stage > 3) {
+      return fail(W8A8_ERR_VALUE, "ER-SDE stage must be 1..3, got %d", step->stage);
+    }
+    if (!old_denoised) return fail(W8A8_ERR_VALUE, "ER-SDE needs the old_denoised buffer");
+    if (!step->last && step->stage >= 2 && !old_derivative) {
+      return fail(W8A8_ERR_VALUE, "ER-SDE stage >= 2 needs the old_derivative buffer");
+    }
+    if (!step->last && step->has_noise && !noise) return fail(W8A8_ERR_VALUE, "NULL noise");
+  }
+  if (mode == W8A8_STEP_CHURN && !noise) return fail(W8A8_ERR_VALUE, "NULL noise");
+  if (step->denoised_input && out_uncond) {
+    return fail(W8A8_ERR_VALUE, "a denoised model output has no unconditional branch");
+  }
+  return finish(sampler_step_launch(x, out_cond, out_uncond, out_dtype, n, coef, *step, denoised,
+                                    old_denoised, old_derivative, noise,
+                                    static_cast<cudaStream_t>(stream)));
 }
 
 int w8a8_row_absmax(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,

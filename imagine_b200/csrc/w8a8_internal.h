@@ -79,6 +79,11 @@ int peer_flags_launch(unsigned* const* flags, int rank, int world, unsigned epoc
 // (rank r's shard at columns r * N_shard).
 int allgather_unpack_launch(const void* recv, void* out, int out_dtype, int64_t ldo, int64_t M,
                             int64_t N_shard, int rank, int world, cudaStream_t stream);
+// The fused sampler step (flow parameterisation, CFG, Euler / ER-SDE update).
+int sampler_step_launch(float* x, const void* out_cond, const void* out_uncond, int out_dtype,
+                        int64_t n, const float* coef, const w8a8_sampler_step_t& step,
+                        float* denoised, float* old_denoised, float* old_derivative,
+                        const float* noise, cudaStream_t stream);
 // Tile shape and split-K layout gemm_launch uses for a GEMM.
 struct GemmPlan {
   int bn, cg, group_m, max_ctas;

@@ -432,6 +432,60 @@ int w8a8_mxfp8_gemm(const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
                     const uint8_t* b_scales, const void* bias, void* out, int out_dtype, int64_t M,
                     int64_t N, int64_t K, const w8a8_gemm_config_t* cfg, void* stream);
 
+/* ---- sampler step: flow parameterisation + CFG combine + Euler / ER-SDE ----
+ *
+ * One elementwise pass per denoising step over the fp32 latent x [n]:
+ *   denoised = cfg_combine(x - out_cond * sigma, x - out_uncond * sigma, scale)
+ * (the flow / CONST parameterisation, inference/src/models/qwen_image21/
+ * sampling.rs:165-167 and denoiser.rs:135; the full-area aggregation of
+ * cfg.rs:145-207, whose x1 / +0 / /(1e-37 + 1) steps only normalise the sign
+ * of zeros; cfg_combine sampling.rs:178-180), then the sampler's update of x:
+ *   EULER  (sampling.rs:231-277): x += ((x - denoised) / sigma_hat) * dt
+ *   ER_SDE (er_sde.rs:60-134): the stage 1-3 update with the multistep state
+ *          old_denoised / old_derivative (updated in place) and the noise term
+ *   CHURN  (sampling.rs:244-253): x += (noise * s_noise) * coef[0], before the
+ *          model runs at sigma_hat
+ *   DENOISED: only writes `denoised`.
+ * Every fp32 operation rounds once, in ATen's order (no FMA contraction), so
+ * with the same per-step scalars the result equals the reference's tensor
+ * operations bit for bit.
+ *
+ * out_cond / out_uncond: the model outputs (f32, f16 or bf16 code in
+ * out_dtype), [n] each; out_uncond NULL when the negative branch is skipped
+ * (CFG = 1 shortcut, cfg.rs:136-144: uncond reads as zeros).
+ * coef: device fp32 array of the step's scalars (1 for DENOISED and CHURN,
+ * 3 for EULER, 9 for ER_SDE), computed with the
+ * reference's 0-dim tensor operations on the sigmas' device:
+ *   [0] the model's sigma (timestep)
+ *   EULER:  [1] sigma_hat, [2] dt = sigma_next - sigma_hat
+ *   ER_SDE: [1] r_alpha * r, [2] alpha_t * (1 - r), [3] the stage-2
+ *           coefficient alpha_t * (dt + integral * noise_scaler(t)),
+ *           [4] s - lambda[i-1], [5] the stage-3 coefficient, [6] (s -
+ *           lambda[i-2]) / 2, [7] alpha_t, [8] the noise deviation
+ *   CHURN:  [0] (sigma_hat^2 - sigma^2)^0.5
+ * denoised: optional output [n] (NULL: not written).  noise: [n] fp32 (ER_SDE
+ * with has_noise, CHURN). */
+#define W8A8_STEP_DENOISED 0
+#define W8A8_STEP_EULER 1
+#define W8A8_STEP_ER_SDE 2
+#define W8A8_STEP_CHURN 3
+typedef struct {
+  int mode;        /* W8A8_STEP_* */
+  int stage;       /* ER_SDE: min(max_stage, i + 1), 1..3 */
+  int last;        /* ER_SDE: the next sigma is 0, x becomes denoised */
+  int has_noise;   /* ER_SDE: settings.noise > 0 */
+  float cfg_scale; /* the CFG scale as fp32 (ATen's mul by a double scalar) */
+  float s_noise;   /* ER_SDE / CHURN: settings.noise as fp32 */
+  int denoised_input; /* 1: out_cond already is the denoised prediction (an
+                         execution whose denoise() returns it, no flow
+                         parameterisation or CFG); out_uncond must be NULL */
+} w8a8_sampler_step_t;
+
+int w8a8_sampler_step(float* x, const void* out_cond, const void* out_uncond, int out_dtype,
+                      int64_t n, const float* coef, const w8a8_sampler_step_t* step,
+                      float* denoised, float* old_denoised, float* old_derivative,
+                      const float* noise, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -18,7 +18,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert N.LIB.w8a8_abi_version() == 101
+    assert N.LIB.w8a8_abi_version() == 102
 
 
 def test_header_compiles_as_c():
