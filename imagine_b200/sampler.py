@@ -125,6 +125,31 @@ def sampler_step(x: torch.Tensor, out_cond: Optional[torch.Tensor], out_uncond: 
         _vp(same("noise", noise, torch.float32)), _stream(dev)))
 
 
+def cfg_parallel_model(branch_model: Callable[[torch.Tensor, torch.Tensor, int], torch.Tensor],
+                       group=None) -> Model:
+    """A ``Model`` whose two CFG branches run on the two ranks of ``group``:
+    rank 0 evaluates the conditional branch, rank 1 the unconditional one
+    (``branch_model(x, timestep, branch)``), and one all-gather of the outputs
+    gives every rank both, so each rank's sampler step computes the same latent.
+    The reference batches the two branches on one device instead
+    (cfg.rs:170-200); the combine that follows is the same.  Under the CFG = 1
+    shortcut both ranks evaluate the conditional branch and nothing is
+    exchanged."""
+    import torch.distributed as dist
+
+    def model(x, timestep, with_uncond):
+        if not with_uncond:
+            return branch_model(x, timestep, 0), None
+        if dist.get_world_size(group) != 2:
+            raise ValueError("CFG-parallel sampling runs on a group of two ranks")
+        mine = branch_model(x, timestep, dist.get_rank(group)).contiguous()
+        both = [torch.empty_like(mine), torch.empty_like(mine)]
+        dist.all_gather(both, mine, group=group)
+        return both[0], both[1]
+
+    return model
+
+
 # ---------------------------------------------------------------- Euler
 @dataclass
 class EulerSettings:

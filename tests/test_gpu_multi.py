@@ -1,7 +1,8 @@
 """Tensor-parallel linears on 2 GPUs with the native kernels: the NCCL forms
 (column- and row-parallel) and the column-parallel linear whose all-gather is
-fused into the GEMM epilogue (peer stores over NVLink) must all equal the
-single-GPU int8_linear bit for bit.  Skips on boxes with fewer than two GPUs."""
+fused into the GEMM epilogue (chunk copies over NVLink) must all equal the
+single-GPU int8_linear bit for bit; CFG-parallel sampling (one branch per GPU)
+must give the single-GPU latent.  Skips on boxes with fewer than two GPUs."""
 import os
 import socket
 
@@ -58,6 +59,28 @@ def _worker(rank, world, port, q):
             ok_fused &= torch.equal(fused_gelu(xi).view(torch.int16), want.view(torch.int16))
         torch.cuda.synchronize()
         ok_fused &= W.device_error() == 0
+        # CFG-parallel sampling: rank r evaluates branch r, one all-gather of
+        # the outputs, then the fused ER-SDE step on every rank -- the same
+        # latent as both branches on one GPU
+        from imagine_b200 import sampler as SM
+
+        def branch(xx, ts, bb):
+            t = ts.reshape(-1, 1, 1, 1)
+            return (xx.mul(0.61).add(t.mul(0.5)) if bb == 0 else xx.mul(-0.23).sub(t)).to(
+                torch.bfloat16)
+
+        def noises():
+            gg = torch.Generator().manual_seed(9)
+            return lambda xx: torch.randn(xx.shape, generator=gg).to(dev)
+
+        x0 = torch.randn(2, 16, 28, 50, generator=torch.Generator().manual_seed(5))
+        sig = SM.FluxSampling().simple(6)
+        y_par = SM.sample_er_sde(x0.to(dev), sig, SM.FluxSampling(), SM.cfg_parallel_model(branch),
+                                 3.0, noise_like=noises())
+        y_one = SM.sample_er_sde(x0.to(dev), sig, SM.FluxSampling(),
+                                 lambda xx, ts, wu: (branch(xx, ts, 0), branch(xx, ts, 1)), 3.0,
+                                 noise_like=noises())
+        ok_fused &= torch.equal(y_par, y_one)
         q.put((rank, torch.equal(y_col.view(torch.int16), ref.view(torch.int16)),
                torch.equal(y_row.view(torch.int16), ref.view(torch.int16)), bool(ok_fused)))
     finally:

@@ -87,3 +87,50 @@ def test_split_and_placement():
     plan = TP.cfg_placement(world=4, samples=2)
     assert plan == [[(0, 0)], [(0, 1)], [(1, 0)], [(1, 1)]]
     assert TP.cfg_placement(world=1, samples=1) == [[(0, 0), (0, 1)]]
+
+
+def _cfg_parallel_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    from imagine_b200.sampler import cfg_parallel_model
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    try:
+        calls = []
+
+        def branch(x, ts, b):
+            calls.append(b)
+            return x.mul(0.5 if b == 0 else -2.0).add(ts.view(-1, 1, 1, 1))
+
+        model = cfg_parallel_model(branch)
+        x = torch.arange(2 * 3 * 4 * 5, dtype=torch.float32).reshape(2, 3, 4, 5)
+        ts = torch.tensor([0.25, 0.25])
+        c, u = model(x, ts, True)
+        c1, u1 = model(x, ts, False)
+        ok = (torch.equal(c, branch(x, ts, 0)) and torch.equal(u, branch(x, ts, 1))
+              and u1 is None and torch.equal(c1, c))
+        q.put((rank, ok, calls[:2]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_cfg_parallel_model_gloo():
+    """Two gloo ranks: rank r evaluates branch r only, both end with both outputs."""
+    import multiprocessing as mp
+    import socket
+
+    ctx = mp.get_context("spawn")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_cfg_parallel_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert [r[1] for r in res] == [True, True]
+    assert res[0][2] == [0, 0] and res[1][2] == [1, 0]  # CFG pass: own branch; shortcut: cond
