@@ -105,6 +105,12 @@ SIGNATURES = {
                                            _CFG, _vp]),
     "w8a8_allgather_finish": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _vp, _i32, _i32,
                                      ctypes.c_uint, _vp]),
+    "w8a8_reduce_scatter_rows": (_i64, [_i64, _i32]),
+    "w8a8_reduce_scatter_recv_bytes": (_i64, [_i64, _i64, _i32]),
+    "w8a8_gemm_s32_reduce_scatter": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _i32,
+                                            _i32, ctypes.c_uint, _CFG, _vp]),
+    "w8a8_reduce_scatter_finish": (_i32, [_vp, _EP, _vp, _i32, _i64, _i64, _i64, _vp, _vp, _vp,
+                                          _i32, _i32, ctypes.c_uint, _vp]),
     "w8a8_gemm_auto_workspace_bytes": (_i64, [_i64, _i64, _i64, _CFG]),
     "w8a8_weight_tiles_bytes": (_i64, [_i64, _i64]),
     "w8a8_pack_weight_tiles": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),

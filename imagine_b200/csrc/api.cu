@@ -390,6 +390,93 @@ int w8a8_allgather_finish(void* out, int out_dtype, int64_t ldo, int64_t M, int6
   return finish(allgather_unpack_launch(recvs[rank], out, out_dtype, ldo, M, N_shard, rank, world, st));
 }
 
+int64_t w8a8_reduce_scatter_rows(int64_t M, int world) {
+  if (M < 0 || world < 1) return fail(W8A8_ERR_VALUE, "negative shape or no ranks");
+  const int64_t per = (M + world - 1) / world;
+  return std::max<int64_t>(32, (per + 31) / 32 * 32);
+}
+
+int64_t w8a8_reduce_scatter_recv_bytes(int64_t M, int64_t N, int world) {
+  const int64_t rows = w8a8_reduce_scatter_rows(M, world);
+  if (rows < 0 || N < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  return static_cast<int64_t>(world) * (rows / 32) * ((N + 31) / 32) * 32 * 32 * 4;
+}
+
+int w8a8_gemm_s32_reduce_scatter(const int8_t* q, int64_t ldq, const int8_t* w_shard, int64_t ldw,
+                                 int64_t M, int64_t N, int64_t K_shard, void* const* recvs,
+                                 unsigned* const* flags, int rank, int world, unsigned epoch,
+                                 const w8a8_gemm_config_t* cfg, void* stream) {
+  if (M < 0 || N < 0 || K_shard < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (int rc = check_peers(flags, rank, world)) return rc;
+  if (epoch == 0) return fail(W8A8_ERR_VALUE, "epoch must be nonzero");
+  if (!recvs) return fail(W8A8_ERR_VALUE, "NULL receive buffer array");
+  for (int r = 0; r < world; ++r) {
+    if (!recvs[r] || (reinterpret_cast<uintptr_t>(recvs[r]) & 15u)) {
+      return fail(W8A8_ERR_VALUE, "receive buffer of rank %d is NULL or not 16-byte aligned", r);
+    }
+  }
+  if (N % 4) return fail(W8A8_ERR_VALUE, "N must be a multiple of 4");
+  if (M == 0 || N == 0) return finish(0);
+  if (!q || !w_shard) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
+  if (ldq < K_shard || ldw < K_shard) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  GemmArgs g{};
+  g.kind = 0;
+  g.a = q;
+  g.lda = ldq;
+  g.b = w_shard;
+  g.ldb = ldw;
+  g.out = recvs[rank];  // no [M, N] output: the chunks go to their owners
+  g.out_dtype = W8A8_S32;
+  g.ldo = N;
+  g.M = M;
+  g.N = N;
+  g.K = K_shard;
+  g.cfg = cfg;
+  g.split_k = 1;
+  g.ag_world = world;
+  g.ag_rank = rank;
+  for (int r = 0; r < world; ++r) {
+    g.ag_recv[r] = recvs[r];
+    g.ag_flags[r] = flags[r];
+  }
+  g.ag_epoch = epoch;
+  g.rs_rows = w8a8_reduce_scatter_rows(M, world);
+  return finish(gemm_launch(g, static_cast<cudaStream_t>(stream)));
+}
+
+int w8a8_reduce_scatter_finish(const float* xs, const w8a8_epilogue_t* epi, void* out,
+                               int out_dtype, int64_t ldo, int64_t M, int64_t N,
+                               void* const* recvs, void* const* stages, unsigned* const* flags,
+                               int rank, int world, unsigned epoch, void* stream) {
+  if (M < 0 || N < 0) return fail(W8A8_ERR_VALUE, "negative shape");
+  if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
+  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (int rc = check_peers(flags, rank, world)) return rc;
+  if (epoch == 0) return fail(W8A8_ERR_VALUE, "epoch must be nonzero");
+  if (!recvs || !stages || !recvs[rank]) return fail(W8A8_ERR_VALUE, "NULL buffer array");
+  for (int r = 0; r < world; ++r) {
+    if (!stages[r] || (reinterpret_cast<uintptr_t>(stages[r]) & 15u)) {
+      return fail(W8A8_ERR_VALUE, "staging buffer of rank %d is NULL or not 16-byte aligned", r);
+    }
+  }
+  if (N % 8 || ldo % 8 || ldo < N) {
+    return fail(W8A8_ERR_VALUE, "N and ldo must be multiples of 8 with ldo >= N");
+  }
+  if (M > 0 && N > 0 && (!xs || !out || (reinterpret_cast<uintptr_t>(out) & 15u))) {
+    return fail(W8A8_ERR_VALUE, "NULL row scales or a NULL / misaligned output");
+  }
+  const int64_t rows = w8a8_reduce_scatter_rows(M, world);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // every peer's partial chunks have landed (the GEMMs' done flags)
+  if (int rc = peer_flags_launch(flags, rank, world, epoch, W8A8_MAX_RANKS, 0, st)) return finish(rc);
+  if (int rc = rs_reduce_launch(recvs[rank], xs, epi, out, out_dtype, ldo, M, N, rows, stages, flags,
+                                rank, world, epoch, st)) {
+    return finish(rc);
+  }
+  return finish(rs_gather_launch(out, out_dtype, ldo, M, N, rows, stages[rank], flags, rank, world,
+                                 epoch, st));
+}
+
 int w8a8_sampler_step(float* x, const void* out_cond, const void* out_uncond, int out_dtype,
                       int64_t n, const float* coef, const w8a8_sampler_step_t* step,
                       float* denoised, float* old_denoised, float* old_derivative,

@@ -115,6 +115,12 @@ struct EpilogueParams {
   int chunk_cols;      // ceil(N_shard / 32)
   unsigned* cta_count;
   unsigned epoch;
+  // Row-parallel reduce-scatter (int32 output, rs_rows > 0): rank p owns
+  // output rows [p * rs_rows, (p + 1) * rs_rows); every finished int32
+  // partial chunk goes whole, as staged, to its owner's receive buffer at
+  // slot (rank * rs_rows / 32 + (row0 - owner * rs_rows) / 32) * chunk_cols +
+  // col0 / 32 (this rank's own chunks included), instead of an output store.
+  int64_t rs_rows;
 };
 
 // Value of one output element before the optional residual, already rounded
@@ -147,6 +153,21 @@ __device__ __forceinline__ float finish_one(float y, float resid, float rs, bool
   if (act == kActGeluTanh) y = OutTraits<OutT>::round(gelu_tanh(y));
   if (has_resid) y = OutTraits<OutT>::round(__fmaf_rn(y, rs, resid));
   return y;
+}
+
+// The whole epilogue of one element from its int32 accumulator (the CUDA-core
+// paths: GEMV, stand-alone dequant, the row-parallel reduce-scatter finish).
+template <typename OutT>
+__device__ __forceinline__ float epi_value(int32_t acc, int64_t m, int n, float xs,
+                                           const EpilogueParams& ep) {
+  const bool has_bias = ep.bias != nullptr;
+  const float b = has_bias ? OutTraits<OutT>::load(ep.bias, n) : 0.0f;
+  const float ws = __ldg(ep.ws + (ep.ws_scalar ? 0 : n));
+  float y = dequant_one<OutT>(static_cast<float>(acc), xs, ws, b, has_bias, ep.dq_order);
+  const bool has_resid = ep.residual != nullptr;
+  const float res = has_resid ? OutTraits<OutT>::load(ep.residual, m * ep.ldr + n) : 0.0f;
+  const float rs = has_resid ? OutTraits<OutT>::load(ep.rscale, rscale_row(ep, m) + n) : 0.0f;
+  return finish_one<OutT>(y, res, rs, has_resid, ep.act);
 }
 
 }  // namespace w8a8

@@ -468,7 +468,16 @@ __device__ __forceinline__ void finish_chunk(const uint32_t (&cur)[32], const fl
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0 && row0 < M) {
-    tma_store_2d(tmD, st, col0, row0);
+    if (kRaw && ep.rs_rows > 0) {
+      // row-parallel reduce-scatter: the int32 partial chunk to its owner
+      const int owner = static_cast<int>(row0 / ep.rs_rows);
+      const int64_t slot =
+          (static_cast<int64_t>(ep.rank) * (ep.rs_rows >> 5) + ((row0 - owner * ep.rs_rows) >> 5)) *
+              ep.chunk_cols + (col0 >> 5);
+      bulk_store(ep.peer_recv[owner] + slot * (32 * 32 * 4), st, 32 * 32 * 4);
+    } else {
+      tma_store_2d(tmD, st, col0, row0);
+    }
     if constexpr (!kRaw) {
       // fused all-gather: the staged chunk, whole and contiguous, into this
       // rank's region of every peer's receive buffer
@@ -1105,12 +1114,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (lane == 0) tma_store_wait_all<0>();
-    if constexpr (!kRaw) {
+    {
       if (ep.n_ranks > 1) {
-        // Fused all-gather: this CTA's peer copies are complete (each warp's
-        // bulk groups waited above) and published, then it counts itself in;
-        // the last CTA of the grid writes this call's epoch into slot `rank`
-        // of every peer's done flags.
+        // Fused all-gather / reduce-scatter: this CTA's peer copies are
+        // complete (each warp's bulk groups waited above) and published, then
+        // it counts itself in; the last CTA of the grid writes this call's
+        // epoch into slot `rank` of every peer's done flags.
         fence_proxy_async_global();
         __threadfence_system();
         named_bar_sync(1, kEpiWarps * 32);
@@ -1276,6 +1285,7 @@ EpilogueParams to_params(const GemmArgs& g) {
     ep.chunks = (g.M + 31) / 32 * ep.chunk_cols;
     ep.cta_count = g.ag_flags[g.ag_rank] + 2 * kMaxRanks;
     ep.epoch = g.ag_epoch;
+    ep.rs_rows = g.rs_rows;
   }
   if (g.rms_rope) {
     ep.act = kActRmsRope;
@@ -1356,15 +1366,17 @@ int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb,
   return 0;
 }
 
-static_assert(kMaxRanks == W8A8_MAX_RANKS && 2 * kMaxRanks + 1 <= W8A8_PEER_FLAG_WORDS,
+static_assert(kMaxRanks == W8A8_MAX_RANKS && 4 * kMaxRanks <= W8A8_PEER_FLAG_WORDS,
               "flag block layout");
 
 struct PeerFlags {
   unsigned* flags[kMaxRanks];
 };
 
-// Flag block of a fused all-gather rank (uint32): [0, 8) ready slots, one per
-// peer, [8, 16) done slots, [16] the rank's CTA arrival counter.
+// Flag block of a fused all-gather / reduce-scatter rank (uint32): [0, 8)
+// ready slots, one per peer, [8, 16) done slots, [16] the rank's CTA arrival
+// counter for the GEMM, [17] the one for the reduce-scatter finish, [24, 32)
+// the finish's done slots.
 //
 // peer_barrier: every rank writes `epoch` into its slot of each peer's ready
 // flags, then waits until all peers' slots of its own block hold it (no rank
@@ -1420,6 +1432,124 @@ __global__ void __launch_bounds__(256) allgather_unpack_kernel(
     const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src + r * kRowBytes + phys * 16));
     *reinterpret_cast<uint4*>(
         out + (static_cast<int64_t>(row) * ldo + static_cast<int64_t>(p) * N_shard + col) * ESZ) = v;
+  }
+}
+
+struct PeerBytes {
+  uint8_t* p[kMaxRanks];
+};
+
+// Row-parallel reduce-scatter finish, one warp per owned row: sum the int32
+// partial chunks the ranks sent for this row (each chunk as its epilogue
+// staged it: 32 rows of 128 bytes in 16-byte pieces, piece ^= row & 7),
+// apply the dequant epilogue, stage 512 columns at a time in shared memory and
+// write them as 16-byte pieces to this rank's output and to every peer's
+// staging buffer ([M, N], same rows).  Then every CTA publishes and counts
+// itself in at flags[rank][17]; the last one writes `epoch` into slot `rank`
+// of every peer's finish-done flags [24, 32).
+template <typename OutT>
+__global__ void __launch_bounds__(256) rs_reduce_kernel(
+    const uint8_t* __restrict__ recv, const float* __restrict__ xs, EpilogueParams ep,
+    uint8_t* __restrict__ out, int64_t ldo, int M, int N, int64_t rs_rows, int chunk_cols,
+    PeerBytes stages, PeerFlags flags, int rank, int world, unsigned epoch) {
+  constexpr int kEsz = static_cast<int>(sizeof(OutT));
+  constexpr int kSeg = 512;
+  __shared__ __align__(16) uint8_t seg[8][kSeg * kEsz];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t row_lo = static_cast<int64_t>(rank) * rs_rows;
+  const int64_t nrows = (M < row_lo + rs_rows ? M : row_lo + rs_rows) - row_lo;
+  const int64_t slot_rows = rs_rows >> 5;
+  for (int64_t lr = static_cast<int64_t>(blockIdx.x) * 8 + warp; lr < nrows;
+       lr += static_cast<int64_t>(gridDim.x) * 8) {
+    const int64_t row = row_lo + lr;
+    const int64_t rb = lr >> 5;
+    const int r = static_cast<int>(lr & 31);
+    const float xsr = xs[row];
+    const int in_row = r * 128 + ((((lane >> 2) ^ (r & 7)) << 4) | ((lane & 3) << 2));
+    for (int c0 = 0; c0 < N; c0 += kSeg) {
+      const int cend = N < c0 + kSeg ? N : c0 + kSeg;
+      for (int col = c0 + lane; col < cend; col += 32) {
+        const int64_t chunk = rb * chunk_cols + (col >> 5);
+        int32_t v = 0;
+        for (int s = 0; s < world; ++s) {
+          v += __ldcg(reinterpret_cast<const int32_t*>(
+              recv + (static_cast<int64_t>(s) * slot_rows * chunk_cols + chunk) * 4096 + in_row));
+        }
+        const float y = epi_value<OutT>(v, row, col, xsr, ep);
+        OutT* dst = reinterpret_cast<OutT*>(&seg[warp][(col - c0) * kEsz]);
+        if constexpr (std::is_same<OutT, float>::value) {
+          *dst = y;
+        } else if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+          *dst = __float2bfloat16_rn(y);
+        } else {
+          *dst = __float2half_rn(y);
+        }
+      }
+      __syncwarp();
+      const int bytes = (cend - c0) * kEsz;  // a multiple of 16 (N % 8 == 0)
+      for (int o = lane * 16; o < bytes; o += 32 * 16) {
+        const uint4 v4 = *reinterpret_cast<const uint4*>(&seg[warp][o]);
+        *reinterpret_cast<uint4*>(out + (row * ldo + c0) * kEsz + o) = v4;
+        for (int p = 0; p < world; ++p) {
+          if (p != rank) {
+            *reinterpret_cast<uint4*>(stages.p[p] + (row * N + c0) * kEsz + o) = v4;
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned* cnt = flags.flags[rank] + 2 * kMaxRanks + 1;
+    if (atomicAdd(cnt, 1u) == gridDim.x - 1) {
+      __threadfence_system();
+      for (int p = 0; p < world; ++p) {
+        if (p != rank) st_release_sys(flags.flags[p] + 3 * kMaxRanks + rank, epoch);
+      }
+      *cnt = 0u;  // every CTA of this call has arrived
+    }
+  }
+}
+
+// After every peer's finish-done flag holds `epoch` (each CTA's thread 0
+// waits, bounded: on expiry kDevTimeoutPeer and the CTA copies nothing), the
+// rows the peers own go from this rank's staging buffer into its output.
+template <int ESZ>
+__global__ void __launch_bounds__(256) rs_gather_kernel(uint8_t* __restrict__ out, int64_t ldo,
+                                                        int M, int N, int64_t rs_rows,
+                                                        const uint8_t* __restrict__ stage,
+                                                        unsigned* mine, int rank, int world,
+                                                        unsigned epoch) {
+  __shared__ int ready;
+  if (threadIdx.x == 0) {
+    ready = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int p = 0; p < world && ready; ++p) {
+      if (p == rank) continue;
+      while (static_cast<int>(ld_acquire_sys(mine + 3 * kMaxRanks + p) - epoch) < 0) {
+        if (globaltimer_ns() - t0 > kSpinLimitNs) {
+          atomicCAS(&g_w8a8_device_error, 0, kDevTimeoutPeer);
+          ready = 0;
+          break;
+        }
+        __nanosleep(256);
+      }
+    }
+  }
+  __syncthreads();
+  if (!ready) return;
+  const int64_t pieces = static_cast<int64_t>(N) * ESZ / 16;  // per row
+  const int64_t total = static_cast<int64_t>(M) * pieces;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / pieces;
+    if (row / rs_rows == rank) continue;  // this rank's rows are in `out` already
+    const int64_t pc = i - row * pieces;
+    const uint4 v = __ldcg(reinterpret_cast<const uint4*>(stage + (row * N * ESZ) + pc * 16));
+    *reinterpret_cast<uint4*>(out + row * ldo * ESZ + pc * 16) = v;
   }
 }
 
@@ -1597,6 +1727,76 @@ int peer_flags_launch(unsigned* const* flags, int rank, int world, unsigned epoc
   return 0;
 }
 
+int rs_reduce_launch(const void* recv, const float* xs, const w8a8_epilogue_t* epi, void* out,
+                     int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t rs_rows,
+                     void* const* stages, unsigned* const* flags, int rank, int world,
+                     unsigned epoch, cudaStream_t stream) {
+  GemmArgs g{};
+  g.epi = epi;
+  g.N = N;
+  g.M = M;
+  const EpilogueParams ep = to_params(g);
+  PeerBytes st{};
+  PeerFlags fl{};
+  for (int r = 0; r < world; ++r) {
+    st.p[r] = static_cast<uint8_t*>(stages[r]);
+    fl.flags[r] = flags[r];
+  }
+  const int64_t own =
+      std::max<int64_t>(0, std::min<int64_t>(M, (rank + 1) * rs_rows) - rank * rs_rows);
+  const int64_t want = (own + 7) / 8;
+  const unsigned grid = static_cast<unsigned>(
+      std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * 8)));
+  const auto* rv = static_cast<const uint8_t*>(recv);
+  auto* o = static_cast<uint8_t*>(out);
+  const int cc = static_cast<int>((N + 31) / 32);
+  const int Mi = static_cast<int>(M), Ni = static_cast<int>(N);
+  switch (out_dtype) {
+    case W8A8_F32:
+      rs_reduce_kernel<float><<<grid, 256, 0, stream>>>(rv, xs, ep, o, ldo, Mi, Ni, rs_rows, cc, st,
+                                                        fl, rank, world, epoch);
+      break;
+    case W8A8_F16:
+      rs_reduce_kernel<__half><<<grid, 256, 0, stream>>>(rv, xs, ep, o, ldo, Mi, Ni, rs_rows, cc, st,
+                                                         fl, rank, world, epoch);
+      break;
+    default:
+      rs_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(rv, xs, ep, o, ldo, Mi, Ni, rs_rows,
+                                                                cc, st, fl, rank, world, epoch);
+      break;
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("reduce-scatter finish launch failed: %s", cudaGetErrorString(e));
+    return W8A8_ERR_ACCELERATOR;
+  }
+  return 0;
+}
+
+int rs_gather_launch(void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t rs_rows,
+                     const void* stage, unsigned* const* flags, int rank, int world, unsigned epoch,
+                     cudaStream_t stream) {
+  const int esz = out_dtype == W8A8_F32 ? 4 : 2;
+  const int64_t total = M * N * esz / 16;
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(
+      1, std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(device_sm_count()) * 4)));
+  auto* o = static_cast<uint8_t*>(out);
+  const auto* sg = static_cast<const uint8_t*>(stage);
+  if (esz == 4) {
+    rs_gather_kernel<4><<<grid, 256, 0, stream>>>(o, ldo, static_cast<int>(M), static_cast<int>(N),
+                                                  rs_rows, sg, flags[rank], rank, world, epoch);
+  } else {
+    rs_gather_kernel<2><<<grid, 256, 0, stream>>>(o, ldo, static_cast<int>(M), static_cast<int>(N),
+                                                  rs_rows, sg, flags[rank], rank, world, epoch);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("reduce-scatter gather launch failed: %s", cudaGetErrorString(e));
+    return W8A8_ERR_ACCELERATOR;
+  }
+  return 0;
+}
+
 int allgather_unpack_launch(const void* recv, void* out, int out_dtype, int64_t ldo, int64_t M,
                             int64_t N_shard, int rank, int world, cudaStream_t stream) {
   const int chunk_cols = static_cast<int>((N_shard + 31) / 32);
@@ -1754,7 +1954,17 @@ int gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
       return W8A8_ERR_VALUE;
     }
   }
-  if (g.ag_world > 1) {
+  if (g.ag_world > 1 && g.rs_rows > 0) {
+    if (!(g.kind == 0 && tc_ok && !g.b_tiled && g.out_dtype == W8A8_S32 &&
+          g.ag_world <= kMaxRanks && g.ag_rank >= 0 && g.ag_rank < g.ag_world &&
+          g.rs_rows % 32 == 0 && g.N % 4 == 0)) {
+      set_error("the fused reduce-scatter needs int8 codes (K %% 16 == 0, 16-byte aligned), "
+                "2..%d ranks, row blocks of a multiple of 32 rows and N %% 4 == 0", kMaxRanks);
+      return W8A8_ERR_VALUE;
+    }
+    g.split_k = 1;
+    g.workspace = nullptr;
+  } else if (g.ag_world > 1) {
     const int esz = out_bytes;
     if (!(g.kind == 0 && tc_ok && !g.rms_rope && !g.b_tiled && g.out_dtype != W8A8_S32 &&
           g.ag_world <= kMaxRanks && g.ag_rank >= 0 && g.ag_rank < g.ag_world &&

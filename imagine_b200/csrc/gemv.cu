@@ -112,18 +112,6 @@ __device__ __forceinline__ void store_out(void* out, int64_t idx, float y) {
   }
 }
 
-template <typename OutT>
-__device__ __forceinline__ float epi_value(int32_t acc, int m, int n, float xs, const EpilogueParams& ep) {
-  const bool has_bias = ep.bias != nullptr;
-  const float b = has_bias ? OutTraits<OutT>::load(ep.bias, n) : 0.0f;
-  const float ws = __ldg(ep.ws + (ep.ws_scalar ? 0 : n));
-  float y = dequant_one<OutT>(static_cast<float>(acc), xs, ws, b, has_bias, ep.dq_order);
-  const bool has_resid = ep.residual != nullptr;
-  const float res = has_resid ? OutTraits<OutT>::load(ep.residual, static_cast<int64_t>(m) * ep.ldr + n) : 0.0f;
-  const float rs = has_resid ? OutTraits<OutT>::load(ep.rscale, rscale_row(ep, m) + n) : 0.0f;
-  return finish_one<OutT>(y, res, rs, has_resid, ep.act);
-}
-
 // One kernel for both the pre-quantised GEMV (InT = int8_t: x are codes, xs
 // given) and the fused quantise + GEMV (InT = a float type).
 template <int M, typename InT, typename OutT, bool kVec>

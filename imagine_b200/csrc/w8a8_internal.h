@@ -68,6 +68,9 @@ struct GemmArgs {
   void* ag_recv[W8A8_MAX_RANKS];
   unsigned* ag_flags[W8A8_MAX_RANKS];
   unsigned ag_epoch;
+  // row-parallel reduce-scatter of the int32 partials (rs_rows > 0, with the
+  // ag_* peers and an S32 output): rank r owns rows [r * rs_rows, ...)
+  int64_t rs_rows;
 };
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);
 // Fused all-gather flags (gemm_sm100.cu): base 0 with signal = the barrier on
@@ -79,6 +82,17 @@ int peer_flags_launch(unsigned* const* flags, int rank, int world, unsigned epoc
 // (rank r's shard at columns r * N_shard).
 int allgather_unpack_launch(const void* recv, void* out, int out_dtype, int64_t ldo, int64_t M,
                             int64_t N_shard, int rank, int world, cudaStream_t stream);
+// Row-parallel reduce-scatter finish: sum the owned rows' int32 partials, the
+// dequant epilogue, own rows to `out` and to every peer's staging buffer, then
+// (last CTA) the done flags at [24, 32).  rs_gather: wait for every peer's
+// rows, copy them from this rank's staging buffer into `out`.
+int rs_reduce_launch(const void* recv, const float* xs, const w8a8_epilogue_t* epi, void* out,
+                     int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t rs_rows,
+                     void* const* stages, unsigned* const* flags, int rank, int world,
+                     unsigned epoch, cudaStream_t stream);
+int rs_gather_launch(void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t rs_rows,
+                     const void* stage, unsigned* const* flags, int rank, int world, unsigned epoch,
+                     cudaStream_t stream);
 // The fused sampler step (flow parameterisation, CFG, Euler / ER-SDE update).
 int sampler_step_launch(float* x, const void* out_cond, const void* out_uncond, int out_dtype,
                         int64_t n, const float* coef, const w8a8_sampler_step_t& step,

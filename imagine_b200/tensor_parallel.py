@@ -86,22 +86,29 @@ class _PeerBuffers:
         handle = symm.rendezvous(self.flags, self.group)
         self.flag_ptrs = (ctypes.c_void_p * self.world)(*handle.buffer_ptrs)
         self._keep = [handle]
-        self.recv = None
         self.recv_ptrs = None
         self.epoch = 0
         torch.cuda.synchronize(device)
         dist.barrier(self.group)  # every flag block is zero before any rank signals
 
-    def receive(self, nbytes: int, device) -> None:
-        if self.recv is None or self.recv.numel() < nbytes:
+    def _mapped(self, attr: str, nbytes: int, device):
+        """A peer-mapped byte buffer of at least `nbytes` under `attr`, and the
+        array of every rank's pointer to it (collective on first use and on
+        growth)."""
+        cur = getattr(self, attr, None)
+        if cur is None or cur[0].numel() < nbytes:
             # a peer may still be writing into the old buffer: finish first
             torch.cuda.synchronize(device)
             dist.barrier(self.group)
             buf = self.symm.empty(max(nbytes, 16), dtype=torch.uint8, device=device)
             handle = self.symm.rendezvous(buf, self.group)
-            self.recv_ptrs = (ctypes.c_void_p * self.world)(*handle.buffer_ptrs)
+            ptrs = (ctypes.c_void_p * self.world)(*handle.buffer_ptrs)
             self._keep.append((buf, handle))
-            self.recv = buf
+            setattr(self, attr, (buf, ptrs))
+        return getattr(self, attr)[1]
+
+    def receive(self, nbytes: int, device) -> None:
+        self.recv_ptrs = self._mapped("_recv", nbytes, device)
 
     def next_epoch(self) -> int:
         self.epoch = self.epoch % 0xFFFFFFFF + 1  # never 0
@@ -198,11 +205,22 @@ class ColumnParallelInt8Linear:
 
 
 class RowParallelInt8Linear:
-    """W [N, K] int8 sharded along K; the input arrives sharded along K."""
+    """W [N, K] int8 sharded along K; the input arrives sharded along K.
+
+    Each rank quantises its K-slice with the full rows' scales (an all-reduce
+    MAX of the per-row absmax) and computes an exact int32 partial product.
+    With ``fused=False`` an NCCL all-reduce SUM of the partials follows, then
+    the dequant epilogue.  With ``fused=True`` the reduction is no collective
+    after the GEMM: the GEMM's epilogue sends every finished int32 partial
+    chunk to the rank that owns its rows (w8a8_gemm_s32_reduce_scatter), and
+    each rank sums its rows, applies the epilogue and hands its rows to the
+    others (w8a8_reduce_scatter_finish), over buffers every rank maps (torch's
+    symmetric memory, used as plumbing).  Both equal the single-GPU linear bit
+    for bit."""
 
     def __init__(self, weight: torch.Tensor, weight_scale: torch.Tensor,
                  bias: Optional[torch.Tensor] = None, *, group=None, backend=None,
-                 dequant: str = "eager", scale_mode: str = "eager"):
+                 dequant: str = "eager", scale_mode: str = "eager", fused: bool = False):
         self.group = group
         self.rank, self.world = _world(group)
         k = weight.shape[1]
@@ -213,6 +231,9 @@ class RowParallelInt8Linear:
         self.backend = backend or NativeBackend()
         self.dequant = dequant
         self.scale_mode = scale_mode
+        self.fused = (fused and self.world > 1 and weight.shape[0] % 8 == 0
+                      and isinstance(self.backend, NativeBackend))
+        self._peers = None
 
     def shard_input(self, x_full: torch.Tensor) -> torch.Tensor:
         return x_full[..., self.k_slice].contiguous()
@@ -225,11 +246,47 @@ class RowParallelInt8Linear:
         if self.world > 1:
             dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)
         q, xs = self.backend.quantize_given_absmax(x2, amax, scale_mode=self.scale_mode)
+        if self.fused and x2.shape[0] > 0:
+            return self._fused_call(q, xs, out_dtype).reshape(*lead, -1)
         acc = self.backend.gemm_s32(q, self.weight)
         if self.world > 1:
             dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.group)
         y = self.backend.dequant(acc, xs, self.weight_scale, self.bias, out_dtype, dequant=self.dequant)
         return y.reshape(*lead, -1)
+
+    def _fused_call(self, q: torch.Tensor, xs: torch.Tensor, out_dtype) -> torch.Tensor:
+        """The GEMM with the reduce-scatter in its epilogue, then the finish (see
+        the class doc).  The ready barrier comes first so that no rank writes
+        into a peer's buffers before that peer has consumed the previous
+        call's."""
+        from . import _native as N
+        from .linear import _code, _epilogue, _stream, _vp
+
+        dev = q.device
+        m, k = q.shape
+        n = self.weight.shape[0]
+        if self._peers is None:
+            self._peers = _PeerBuffers(self.group, dev)
+        pb = self._peers
+        recvs = pb._mapped("_rs_recv", int(N.LIB.w8a8_reduce_scatter_recv_bytes(m, n, self.world)),
+                           dev)
+        esz = torch.empty((), dtype=out_dtype).element_size()
+        stages = pb._mapped("_rs_stage", m * n * esz, dev)
+        y = torch.empty((m, n), dtype=out_dtype, device=dev)
+        epoch = pb.next_epoch()
+        stream = _stream(dev)
+        N.check(N.LIB.w8a8_peer_barrier(pb.flag_ptrs, self.rank, self.world, epoch, stream))
+        N.check(N.LIB.w8a8_gemm_s32_reduce_scatter(_vp(q), k, _vp(self.weight), k, m, n, k, recvs,
+                                                   pb.flag_ptrs, self.rank, self.world, epoch,
+                                                   None, stream))
+        ws = self.weight_scale.to(device=dev, dtype=torch.float32).contiguous()
+        b = self.bias.to(device=dev, dtype=out_dtype).contiguous() if self.bias is not None else None
+        ep = _epilogue(ws, b, None, None, self.dequant, None, n, n)
+        N.check(N.LIB.w8a8_reduce_scatter_finish(_vp(xs.reshape(-1)), ctypes.byref(ep), _vp(y),
+                                                 _code(out_dtype), n, m, n, recvs, stages,
+                                                 pb.flag_ptrs, self.rank, self.world, epoch,
+                                                 stream))
+        return y
 
 
 def cfg_placement(world: int, samples: int, branches: int = 2) -> List[List[Tuple[int, int]]]:

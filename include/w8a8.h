@@ -432,6 +432,42 @@ int w8a8_mxfp8_gemm(const uint8_t* a, const uint8_t* a_scales, const uint8_t* b,
                     const uint8_t* b_scales, const void* bias, void* out, int out_dtype, int64_t M,
                     int64_t N, int64_t K, const w8a8_gemm_config_t* cfg, void* stream);
 
+/* ---- row-parallel linear with the reduce-scatter fused into the GEMM ------
+ *
+ * No reference counterpart (the reference runs on one GPU).  The K-sharded
+ * (row-parallel) linear: each of `world` ranks holds codes q [M, K_shard]
+ * quantised with the full rows' scales xs (w8a8_row_absmax, a MAX across
+ * ranks, w8a8_quantize_rowwise_given_absmax) and W [:, K_shard].  Instead of
+ * an int32 GEMM followed by an all-reduce:
+ *   w8a8_gemm_s32_reduce_scatter: the GEMM's epilogue copies every finished
+ *     32 x 32 int32 partial chunk, whole, into the receive buffer of the rank
+ *     that owns those rows (rank r owns rows [r * R, (r + 1) * R), R =
+ *     w8a8_reduce_scatter_rows(M, world)), over NVLink while the math runs;
+ *     its last CTA then writes `epoch` into every peer's done flags.
+ *   w8a8_reduce_scatter_finish: waits for the peers' partials, sums them
+ *     (exact int32), applies the epilogue (dequant order, bias, GELU,
+ *     residual: `epi` as for w8a8_gemm_dequant) to the owned rows, writes them
+ *     to `out` [M, ldo] and to every peer's staging buffer, then waits for the
+ *     peers' rows and copies them into `out`.
+ * The result equals the single-GPU linear bit for bit.
+ *   recvs[r]:  rank r's receive buffer, w8a8_reduce_scatter_recv_bytes(M, N,
+ *              world) bytes;  stages[r]: rank r's staging buffer, M * N *
+ *              sizeof(out dtype) bytes;  flags[r]: its 32-word flag block
+ *              (zeroed once) -- all mapped into this process (CUDA VMM or
+ *              symmetric memory), 16-byte aligned.
+ * Per call on every rank: w8a8_peer_barrier, the quantiser,
+ * w8a8_gemm_s32_reduce_scatter, w8a8_reduce_scatter_finish (same epoch). */
+int64_t w8a8_reduce_scatter_rows(int64_t M, int world);
+int64_t w8a8_reduce_scatter_recv_bytes(int64_t M, int64_t N, int world);
+int w8a8_gemm_s32_reduce_scatter(const int8_t* q, int64_t ldq, const int8_t* w_shard, int64_t ldw,
+                                 int64_t M, int64_t N, int64_t K_shard, void* const* recvs,
+                                 unsigned* const* flags, int rank, int world, unsigned epoch,
+                                 const w8a8_gemm_config_t* cfg, void* stream);
+int w8a8_reduce_scatter_finish(const float* xs, const w8a8_epilogue_t* epi, void* out,
+                               int out_dtype, int64_t ldo, int64_t M, int64_t N,
+                               void* const* recvs, void* const* stages, unsigned* const* flags,
+                               int rank, int world, unsigned epoch, void* stream);
+
 /* ---- sampler step: flow parameterisation + CFG combine + Euler / ER-SDE ----
  *
  * One elementwise pass per denoising step over the fp32 latent x [n]:

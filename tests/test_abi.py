@@ -139,3 +139,17 @@ def test_fused_allgather_argument_errors():
     assert rc == N.ERR_VALUE and b"ldo" in N.LIB.w8a8_last_error()
     # a receive buffer: every shard's 32 x 32 chunks, for every rank
     assert N.LIB.w8a8_allgather_recv_bytes(40, 72, N.BF16, 2) == 2 * 2 * 3 * 2048
+    # row-parallel reduce-scatter: owned row blocks of a multiple of 32 rows,
+    # one int32 chunk slot per sender, owned row block and column block
+    assert N.LIB.w8a8_reduce_scatter_rows(600, 2) == 320
+    assert N.LIB.w8a8_reduce_scatter_rows(10, 4) == 32
+    assert N.LIB.w8a8_reduce_scatter_recv_bytes(600, 1536, 2) == 2 * 10 * 48 * 4096
+    rc = N.LIB.w8a8_gemm_s32_reduce_scatter(0x6000, 64, 0x7000, 64, 16, 130, 64, recvs, flags, 0, 2,
+                                            1, None, None)
+    assert rc == N.ERR_VALUE and b"multiple of 4" in N.LIB.w8a8_last_error()
+    assert N.LIB.w8a8_gemm_s32_reduce_scatter(0x6000, 64, 0x7000, 64, 16, 128, 64, recvs, flags, 0,
+                                              9, 1, None, None) == N.ERR_VALUE  # too many ranks
+    stages = (ctypes.c_void_p * 2)(0x8000, 0x9000)
+    rc = N.LIB.w8a8_reduce_scatter_finish(0xa000, ctypes.byref(ep), 0xb000, N.BF16, 100, 16, 128,
+                                          recvs, stages, flags, 0, 2, 1, None)
+    assert rc == N.ERR_VALUE and b"ldo" in N.LIB.w8a8_last_error()

@@ -1,6 +1,7 @@
 """Tensor-parallel linears on 2 GPUs with the native kernels: the NCCL forms
 (column- and row-parallel) and the column-parallel linear whose all-gather is
-fused into the GEMM epilogue (chunk copies over NVLink) must all equal the
+fused into the GEMM epilogue (chunk copies over NVLink) and the row-parallel
+linear whose reduce-scatter is fused into the GEMM epilogue must all equal the
 single-GPU int8_linear bit for bit; CFG-parallel sampling (one branch per GPU)
 must give the single-GPU latent.  Skips on boxes with fewer than two GPUs."""
 import os
@@ -57,6 +58,19 @@ def _worker(rank, world, port, q):
             ok_fused &= torch.equal(fused(xi).view(torch.int16), want.view(torch.int16))
             want = W.int8_linear(xi, wq, ws, b, output_act="gelu_tanh")
             ok_fused &= torch.equal(fused_gelu(xi).view(torch.int16), want.view(torch.int16))
+        torch.cuda.synchronize()
+        ok_fused &= W.device_error() == 0
+        # the all-reduce fused into the row-parallel GEMM (int32 partial chunks
+        # sent to their rows' owners, summed there, rows handed back): three
+        # calls, bf16 and fp32 outputs
+        rowf = TP.RowParallelInt8Linear(wq, ws, b, fused=True)
+        assert rowf.fused
+        for xi in (x, x2, x):
+            want = W.int8_linear(xi, wq, ws, b)
+            ok_fused &= torch.equal(rowf(rowf.shard_input(xi)).view(torch.int16),
+                                    want.view(torch.int16))
+        want32 = W.int8_linear(x2, wq, ws, b.float(), out_dtype=torch.float32)
+        ok_fused &= torch.equal(rowf(rowf.shard_input(x2), out_dtype=torch.float32), want32)
         torch.cuda.synchronize()
         ok_fused &= W.device_error() == 0
         # CFG-parallel sampling: rank r evaluates branch r, one all-gather of
