@@ -22,7 +22,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", choices=["gemm", "gemm_gelu", "gemm_s32", "quantize", "convrot",
                                                        "gemv", "fp8_gemm", "mxfp8_gemm", "rms_rope",
-                                                       "gemm_rope"],
+                                                       "gemm_rope", "sampler_euler", "sampler_er_sde"],
                     required=True)
     ap.add_argument("--m", type=int, default=5600)
     ap.add_argument("--k", type=int, default=3072)
@@ -66,7 +66,24 @@ def main():
             else:
                 fn()
 
-    if a.kernel == "quantize":
+    if a.kernel.startswith("sampler_"):
+        # one fused sampler step over an fp32 latent of --m x --k elements with
+        # bf16 branch outputs (ER-SDE: stage 3 with noise)
+        from imagine_b200 import _native as NAT
+        from imagine_b200 import sampler as SM
+        shape = (a.m, a.k)
+        lat = torch.randn(shape, generator=g).to(dev)
+        oc = torch.randn(shape, generator=g).to(torch.bfloat16).to(dev)
+        ou = torch.randn(shape, generator=g).to(torch.bfloat16).to(dev)
+        coef = (torch.rand(9, generator=g) + 0.5).to(dev)
+        if a.kernel == "sampler_euler":
+            run(lambda: SM.sampler_step(lat, oc, ou, coef, NAT.STEP_EULER, cfg_scale=2.5))
+        else:
+            od, odr = torch.zeros_like(lat), torch.zeros_like(lat)
+            nz = torch.randn(shape, generator=g).to(dev)
+            run(lambda: SM.sampler_step(lat, oc, ou, coef, NAT.STEP_ER_SDE, cfg_scale=2.5, stage=3,
+                                        old_denoised=od, old_derivative=odr, noise=nz))
+    elif a.kernel == "quantize":
         run(lambda: W.quantize_int8_rowwise(x))
     elif a.kernel == "convrot":
         run(lambda: W.quantize_int8_rowwise_convrot(x, 256))
@@ -166,6 +183,11 @@ def main():
         elif a.kernel == "gemv":
             nbytes = a.n * a.k + 2 * (a.m * a.k + a.m * a.n) + 4 * a.n
             msg += f" GB/s={nbytes / t / 1e6:.1f}"
+        elif a.kernel.startswith("sampler_"):
+            # algorithmic bytes per element: Euler x in/out 8 + two bf16
+            # outputs 4; ER-SDE stage 3 with noise adds history in/out 16 and noise 4
+            per = 12 if a.kernel == "sampler_euler" else 32
+            msg += f" GB/s={a.m * a.k * per / t / 1e6:.1f}"
         elif a.kernel not in ("quantize", "convrot", "rms_rope"):
             msg += f" TOPS={ops / t / 1e9:.1f}"
         else:
