@@ -1439,8 +1439,8 @@ struct PeerBytes {
   uint8_t* p[kMaxRanks];
 };
 
-// Row-parallel reduce-scatter finish, one warp per owned row: sum the int32
-// partial chunks the ranks sent for this row (each chunk as its epilogue
+// Row-parallel reduce-scatter finish, one warp per (owned row, 512 columns):
+// sum the int32 partial chunks the ranks sent for those columns (each chunk as its epilogue
 // staged it: 32 rows of 128 bytes in 16-byte pieces, piece ^= row & 7),
 // apply the dequant epilogue, stage 512 columns at a time in shared memory and
 // write them as 16-byte pieces to this rank's output and to every peer's
@@ -1460,23 +1460,40 @@ __global__ void __launch_bounds__(256) rs_reduce_kernel(
   const int64_t row_lo = static_cast<int64_t>(rank) * rs_rows;
   const int64_t nrows = (M < row_lo + rs_rows ? M : row_lo + rs_rows) - row_lo;
   const int64_t slot_rows = rs_rows >> 5;
-  for (int64_t lr = static_cast<int64_t>(blockIdx.x) * 8 + warp; lr < nrows;
-       lr += static_cast<int64_t>(gridDim.x) * 8) {
+  const int nseg = (N + kSeg - 1) / kSeg;
+  // work item = (owned row, 512-column segment), one per warp; a lane's 16
+  // columns of every sender are loaded back to back (32 loads in flight for
+  // two ranks) before the epilogue runs on them
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * 8 + warp; item < nrows * nseg;
+       item += static_cast<int64_t>(gridDim.x) * 8) {
+    const int64_t lr = item / nseg;
+    const int c0 = static_cast<int>(item - lr * nseg) * kSeg;
+    const int cend = N < c0 + kSeg ? N : c0 + kSeg;
     const int64_t row = row_lo + lr;
     const int64_t rb = lr >> 5;
     const int r = static_cast<int>(lr & 31);
-    const float xsr = xs[row];
     const int in_row = r * 128 + ((((lane >> 2) ^ (r & 7)) << 4) | ((lane & 3) << 2));
-    for (int c0 = 0; c0 < N; c0 += kSeg) {
-      const int cend = N < c0 + kSeg ? N : c0 + kSeg;
-      for (int col = c0 + lane; col < cend; col += 32) {
-        const int64_t chunk = rb * chunk_cols + (col >> 5);
-        int32_t v = 0;
-        for (int s = 0; s < world; ++s) {
-          v += __ldcg(reinterpret_cast<const int32_t*>(
-              recv + (static_cast<int64_t>(s) * slot_rows * chunk_cols + chunk) * 4096 + in_row));
+    int32_t v[kSeg / 32];
+#pragma unroll
+    for (int i = 0; i < kSeg / 32; ++i) v[i] = 0;
+    for (int s = 0; s < world; ++s) {
+      // chunk (rb, c0 / 32 + i) of sender s, this lane's element of row r
+      const uint8_t* base =
+          recv + ((static_cast<int64_t>(s) * slot_rows + rb) * chunk_cols + (c0 >> 5)) * 4096 +
+          in_row;
+#pragma unroll
+      for (int i = 0; i < kSeg / 32; ++i) {
+        if (c0 + lane + 32 * i < cend) {
+          v[i] += __ldcg(reinterpret_cast<const int32_t*>(base + static_cast<int64_t>(i) * 4096));
         }
-        const float y = epi_value<OutT>(v, row, col, xsr, ep);
+      }
+    }
+    const float xsr = xs[row];
+#pragma unroll
+    for (int i = 0; i < kSeg / 32; ++i) {
+      const int col = c0 + lane + 32 * i;
+      if (col < cend) {
+        const float y = epi_value<OutT>(v[i], row, col, xsr, ep);
         OutT* dst = reinterpret_cast<OutT*>(&seg[warp][(col - c0) * kEsz]);
         if constexpr (std::is_same<OutT, float>::value) {
           *dst = y;
@@ -1486,19 +1503,19 @@ __global__ void __launch_bounds__(256) rs_reduce_kernel(
           *dst = __float2half_rn(y);
         }
       }
-      __syncwarp();
-      const int bytes = (cend - c0) * kEsz;  // a multiple of 16 (N % 8 == 0)
-      for (int o = lane * 16; o < bytes; o += 32 * 16) {
-        const uint4 v4 = *reinterpret_cast<const uint4*>(&seg[warp][o]);
-        *reinterpret_cast<uint4*>(out + (row * ldo + c0) * kEsz + o) = v4;
-        for (int p = 0; p < world; ++p) {
-          if (p != rank) {
-            *reinterpret_cast<uint4*>(stages.p[p] + (row * N + c0) * kEsz + o) = v4;
-          }
+    }
+    __syncwarp();
+    const int bytes = (cend - c0) * kEsz;  // a multiple of 16 (N % 8 == 0)
+    for (int o = lane * 16; o < bytes; o += 32 * 16) {
+      const uint4 v4 = *reinterpret_cast<const uint4*>(&seg[warp][o]);
+      *reinterpret_cast<uint4*>(out + (row * ldo + c0) * kEsz + o) = v4;
+      for (int p = 0; p < world; ++p) {
+        if (p != rank) {
+          *reinterpret_cast<uint4*>(stages.p[p] + (row * N + c0) * kEsz + o) = v4;
         }
       }
-      __syncwarp();
     }
+    __syncwarp();
   }
   __threadfence_system();
   __syncthreads();
@@ -1744,7 +1761,7 @@ int rs_reduce_launch(const void* recv, const float* xs, const w8a8_epilogue_t* e
   }
   const int64_t own =
       std::max<int64_t>(0, std::min<int64_t>(M, (rank + 1) * rs_rows) - rank * rs_rows);
-  const int64_t want = (own + 7) / 8;
+  const int64_t want = (own * ((N + 511) / 512) + 7) / 8;
   const unsigned grid = static_cast<unsigned>(
       std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(device_sm_count()) * 8)));
   const auto* rv = static_cast<const uint8_t*>(recv);
