@@ -134,3 +134,48 @@ def test_cfg_parallel_model_gloo():
         p.join(timeout=60)
     assert [r[1] for r in res] == [True, True]
     assert res[0][2] == [0, 0] and res[1][2] == [1, 0]  # CFG pass: own branch; shortcut: cond
+
+
+def _peer_failure_worker(rank, world, port, q):
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    from imagine_b200.sampler import cfg_parallel_model
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        os._exit(0)  # this rank dies between steps: it never reaches the exchange
+    model = cfg_parallel_model(lambda x, ts, b: x * (b + 1))
+    t0 = time.time()
+    try:
+        model(torch.ones(2, 3), torch.ones(2), True)
+        q.put((rank, "no error", time.time() - t0))
+    except Exception as e:  # the exchange must end with an error, not hang
+        q.put((rank, type(e).__name__, time.time() - t0))
+
+
+def test_cfg_parallel_peer_failure_gloo():
+    """A rank that exits before the CFG exchange: the surviving rank's all-gather
+    ends with an error within the process group's timeout instead of waiting
+    for good."""
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_peer_failure_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    rank, what, elapsed = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert rank == 0 and what != "no error", what
+    assert elapsed < 60
