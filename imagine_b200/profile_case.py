@@ -22,7 +22,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", choices=["gemm", "gemm_gelu", "gemm_s32", "quantize", "convrot",
                                                        "gemv", "fp8_gemm", "mxfp8_gemm", "rms_rope",
-                                                       "gemm_rope", "sampler_euler", "sampler_er_sde"],
+                                                       "gemm_rope", "sampler_euler", "sampler_er_sde", "gemv_q"],
                     required=True)
     ap.add_argument("--m", type=int, default=5600)
     ap.add_argument("--k", type=int, default=3072)
@@ -135,6 +135,10 @@ def main():
             aq, asf = W.quantize_mxfp8(x)
             bq, bsf = W.quantize_mxfp8(w)
             run(lambda: W.mxfp8_linear(aq, asf, bq, bsf, b, out_dtype=torch.bfloat16, config=cfg))
+        elif a.kernel == "gemv_q":
+            # the GEMV alone, on activation codes quantised beforehand
+            q, xs = W.quantize_int8_rowwise(x)
+            run(lambda: W.int8_gemv(q, wq, xs, ws, b))
         elif a.kernel in ("gemm", "gemm_gelu", "gemv"):
             act = "gelu_tanh" if a.kernel == "gemm_gelu" else None
             if a.time and a.kernel != "gemv":
@@ -180,7 +184,7 @@ def main():
         if a.kernel == "rms_rope":
             nbytes = 2 * 2 * a.m * a.k * 2 + a.m * 64 * 16
             msg += f" GB/s={nbytes / t / 1e6:.1f}"
-        elif a.kernel == "gemv":
+        elif a.kernel in ("gemv", "gemv_q"):
             nbytes = a.n * a.k + 2 * (a.m * a.k + a.m * a.n) + 4 * a.n
             msg += f" GB/s={nbytes / t / 1e6:.1f}"
         elif a.kernel.startswith("sampler_"):
