@@ -132,9 +132,9 @@ __device__ __forceinline__ void rms_rope_heads(const T* x, T* out, const float (
   }
 }
 
-// One warp per token: lane l owns elements [EPL l, EPL l + EPL) of every
+// One warp per token and tensor: lane l owns elements [EPL l, EPL l + EPL) of every
 // head, loads the rotations of its EPL/2 pairs once, then walks the heads of
-// q and of k.
+// q (or, in the next warp, of k).
 template <typename T, int EPL>
 __global__ void __launch_bounds__(kRopeWarps * 32) rms_rope_kernel(
     const T* __restrict__ q, const T* __restrict__ k, T* __restrict__ q_out, T* __restrict__ k_out,
@@ -142,18 +142,22 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rms_rope_kernel(
     const float* __restrict__ freqs, int64_t freq_rows, const T* __restrict__ q_scale,
     const T* __restrict__ k_scale, float eps, int vec) {
   const int lane = threadIdx.x & 31;
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * kRopeWarps + (threadIdx.x >> 5);
+  // warp w: token w / per, q (even w) or k (odd w) when both are given
+  const int per = k ? 2 : 1;
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * kRopeWarps + (threadIdx.x >> 5);
+  const int64_t t = w / per;
   if (t >= rows) return;
+  const bool is_k = per == 2 && (w & 1);
   const float4* fr = reinterpret_cast<const float4*>(freqs + (t % freq_rows) * (2 * D));
   float4 f[EPL / 2];
 #pragma unroll
   for (int j = 0; j < EPL / 2; ++j) f[j] = __ldg(fr + (EPL * lane) / 2 + j);
   float wv[EPL];
-  load_row<T, EPL>(q_scale + EPL * lane, vec != 0, wv);
-  rms_rope_heads<T, EPL>(q + t * ldq, q_out + t * ldqo, wv, f, eps, heads, D, lane, vec != 0);
-  if (k) {
-    load_row<T, EPL>(k_scale + EPL * lane, vec != 0, wv);
+  load_row<T, EPL>((is_k ? k_scale : q_scale) + EPL * lane, vec != 0, wv);
+  if (is_k) {
     rms_rope_heads<T, EPL>(k + t * ldk, k_out + t * ldko, wv, f, eps, heads, D, lane, vec != 0);
+  } else {
+    rms_rope_heads<T, EPL>(q + t * ldq, q_out + t * ldqo, wv, f, eps, heads, D, lane, vec != 0);
   }
 }
 
@@ -169,7 +173,8 @@ int launch_rope(const void* q, const void* k, void* q_out, void* k_out, int64_t 
                        (!k || ((ldk * static_cast<int64_t>(sizeof(T))) % 8 == 0 &&
                                (ldko * static_cast<int64_t>(sizeof(T))) % 8 == 0));
   const int vec = row_vec && a8(q) && a8(q_out) && a8(q_scale) && (!k || (a8(k) && a8(k_out) && a8(k_scale)));
-  const dim3 grid(static_cast<unsigned>((rows + kRopeWarps - 1) / kRopeWarps));
+  const int64_t warps = rows * (k ? 2 : 1);  // one warp per token and tensor
+  const dim3 grid(static_cast<unsigned>((warps + kRopeWarps - 1) / kRopeWarps));
   const T* qp = static_cast<const T*>(q);
   const T* kp = static_cast<const T*>(k);
   T* qo = static_cast<T*>(q_out);
