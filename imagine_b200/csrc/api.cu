@@ -201,6 +201,13 @@ int w8a8_quantize_rowwise_modulated(const void* x, int x_dtype, int64_t rows, in
   if (rows > 0x7fffffffLL) return fail(W8A8_ERR_VALUE, "rows must be <= INT_MAX");
   if (!x || !q || !scale) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
   if (ldx < cols || ldq < cols) return fail(W8A8_ERR_VALUE, "row stride smaller than the row");
+  if (group != 256) {
+    // no rotation: the plain quantiser's row-in-registers layout when it fits
+    const int rc = quantize_modulated_vec_launch(x, x_dtype, rows, cols, ldx, mode + 5, norm_w, eps,
+                                                 mod_scale, mod_shift, mod_group, q, ldq, scale,
+                                                 scale_mode, static_cast<cudaStream_t>(stream));
+    if (rc != -1) return finish(rc);
+  }
   return finish(quantize_act_rot_launch(x, x_dtype, rows, cols, ldx, group == 256 ? 1 : 0, mode + 5,
                                         norm_w, eps, mod_scale, mod_shift, mod_group, q, ldq, scale,
                                         scale_mode, static_cast<cudaStream_t>(stream)));

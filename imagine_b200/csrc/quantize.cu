@@ -269,6 +269,248 @@ int launch_quant(const void* x, int64_t ldx, int8_t* q, int64_t ldq, float* scal
   return 0;
 }
 
+
+// ---- modulation (without ConvRot) + quantiser in the row-in-registers layout
+// of quantize_rowwise_vec_kernel: a group of WPR warps owns one row of 16-bit
+// values, each thread up to MAXV 16-byte vectors of it.  ACT: 5 x (1 + s),
+// 6 rms_norm(x, w) (1 + s), 7 layer_norm(x) (1 + s) + shift, 8 rms_norm(x)
+// (1 + s) + shift; the per-element arithmetic and its roundings to T are
+// those of the ConvRot kernel's modulation step (the reference's ATen
+// sequence, inference/src/backend_eager.rs:176-197 and
+// inference/src/backend_bindings.rs:329-405, or with `kitchen` its CUDA
+// adaln, KSRC backends/cuda/ops/adaln.cu:103-190); only the order in which
+// the row statistics are summed differs.
+template <typename T, int WPR, int MAXV, int ACT>
+__global__ void __launch_bounds__(kQuantThreads) quantize_modulated_vec_kernel(
+    const T* __restrict__ x, int64_t ldx, const T* __restrict__ msc, const T* __restrict__ msh,
+    const T* __restrict__ nw, int64_t mgroup, float eps, int8_t* __restrict__ q, int64_t ldq,
+    float* __restrict__ scales, int rows, int cols, int kitchen) {
+  static_assert(sizeof(T) == 2, "16-bit inputs");
+  constexpr int kPer = 8;
+  constexpr int kGroupThreads = WPR * 32;
+  constexpr int kRowsPerCta = kQuantThreads / kGroupThreads;
+  __shared__ float red[kQuantThreads / 32];
+  griddep_launch_dependents();  // the GEMM that reads q may start its prologue
+  const int group = threadIdx.x / kGroupThreads;
+  const int gt = threadIdx.x % kGroupThreads;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int row = blockIdx.x * kRowsPerCta + group;
+  const bool live = row < rows;
+  const int nvec = cols / kPer;
+  // sum (or max) over the row's WPR warps; every thread of the CTA calls it
+  auto row_reduce = [&](float v, bool is_max) -> float {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float t = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmaxf(v, t) : __fadd_rn(v, t);
+    }
+    __syncthreads();  // red[] may still be read by the previous reduction
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float r = red[group * WPR];
+#pragma unroll
+    for (int w = 1; w < WPR; ++w) {
+      r = is_max ? fmaxf(r, red[group * WPR + w]) : __fadd_rn(r, red[group * WPR + w]);
+    }
+    return r;
+  };
+  auto elem = [](const uint4& u, int e) -> float {
+    return QuantTraits<T>::to_f(reinterpret_cast<const T*>(&u)[e]);
+  };
+
+  const uint4* xrow = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(live ? row : 0) * ldx);
+  uint4 v[MAXV];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = gt + i * kGroupThreads;
+    v[i] = make_uint4(0, 0, 0, 0);
+    if (live && vi < nvec) v[i] = __ldg(xrow + vi);
+  }
+  // row statistics
+  float mean = 0.0f, rstd = 1.0f;
+  if constexpr (ACT != 5) {
+    float sum = 0.0f, sumsq = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+#pragma unroll
+      for (int e = 0; e < kPer; ++e) {
+        const float f = elem(v[i], e);  // zero past the row's end
+        if constexpr (ACT == 7) sum = __fadd_rn(sum, f);
+        sumsq = __fmaf_rn(f, f, sumsq);
+      }
+    }
+    const float kf = static_cast<float>(cols);
+    if constexpr (ACT == 7) {
+      const float inv_k = 1.0f / kf;
+      mean = row_reduce(sum, false) * inv_k;
+      if (kitchen) {
+        const float s2 = row_reduce(sumsq, false);
+        rstd = rsqrtf(fmaxf(s2 * inv_k - mean * mean, 0.0f) + eps);
+      } else {
+        float dev = 0.0f;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+          const int vi = gt + i * kGroupThreads;
+          if (vi < nvec) {
+#pragma unroll
+            for (int e = 0; e < kPer; ++e) {
+              const float d = __fsub_rn(elem(v[i], e), mean);
+              dev = __fmaf_rn(d, d, dev);
+            }
+          }
+        }
+        rstd = rsqrtf(row_reduce(dev, false) * inv_k + eps);
+      }
+    } else {
+      rstd = rsqrtf(row_reduce(sumsq, false) / kf + eps);
+    }
+  }
+  // modulated values, rounded to T as the reference materialises them, and
+  // their absmax
+  const int64_t mrow = (static_cast<int64_t>(live ? row : 0) / mgroup) * cols;
+  const uint4* srow = reinterpret_cast<const uint4*>(msc + mrow);
+  const uint4* hrow = reinterpret_cast<const uint4*>(msh ? msh + mrow : msc);
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = gt + i * kGroupThreads;
+    if (live && vi < nvec) {
+      const uint4 sv = __ldg(srow + vi);
+      uint4 hv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
+      if constexpr (ACT == 7 || ACT == 8) hv = __ldg(hrow + vi);
+      if constexpr (ACT == 6) wv = __ldg(reinterpret_cast<const uint4*>(nw) + vi);
+      T out[kPer];
+#pragma unroll
+      for (int e = 0; e < kPer; ++e) {
+        const float xv = elem(v[i], e);
+        const float one_s = QuantTraits<T>::round_t(__fadd_rn(1.0f, elem(sv, e)));
+        float y;
+        if constexpr (ACT == 5) {
+          y = __fmul_rn(xv, one_s);
+        } else if constexpr (ACT == 6) {
+          const float nrm = QuantTraits<T>::round_t(__fmul_rn(__fmul_rn(xv, rstd), elem(wv, e)));
+          y = __fmul_rn(nrm, one_s);
+        } else {
+          const float nrm = __fmul_rn(__fsub_rn(xv, mean), rstd);
+          if (kitchen) {
+            y = __fmaf_rn(nrm, __fadd_rn(1.0f, elem(sv, e)), elem(hv, e));
+          } else {
+            const float t = QuantTraits<T>::round_t(__fmul_rn(QuantTraits<T>::round_t(nrm), one_s));
+            y = __fadd_rn(t, elem(hv, e));
+          }
+        }
+        const float yt = QuantTraits<T>::round_t(y);
+        amax = fmaxf(amax, fabsf(yt));
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+          out[e] = __float2bfloat16_rn(yt);  // exact: yt is a bf16 value
+        } else {
+          out[e] = __float2half_rn(yt);
+        }
+      }
+      v[i] = *reinterpret_cast<const uint4*>(out);
+    }
+  }
+  amax = row_reduce(amax, true);
+  if (!live) return;
+  const float scale = quant_row_scale<T>(kitchen ? amax : QuantTraits<T>::round_t(amax), kitchen);
+  if (gt == 0) scales[row] = scale;
+  const float div = quant_divisor<T>(scale);
+  const float recip = __frcp_rn(div);
+  int8_t* qrow = q + static_cast<int64_t>(row) * ldq;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = gt + i * kGroupThreads;
+    if (vi >= nvec) continue;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      reinterpret_cast<uint2*>(qrow)[vi] = quant8_bf16(v[i], div, recip);
+    } else {
+      uint32_t packed[2];
+#pragma unroll
+      for (int w = 0; w < 2; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int qv = quant_code<T>(elem(v[i], w * 4 + j), div, recip);
+          word |= (static_cast<uint32_t>(qv) & 0xFFu) << (8 * j);
+        }
+        packed[w] = word;
+      }
+      reinterpret_cast<uint2*>(qrow)[vi] = make_uint2(packed[0], packed[1]);
+    }
+  }
+}
+
+template <typename T, int ACT>
+int launch_modulated_t(const void* x, int64_t ldx, const void* msc, const void* msh,
+                       const void* nw, int64_t mgroup, float eps, int8_t* q, int64_t ldq,
+                       float* scales, int rows, int cols, int kitchen, cudaStream_t stream) {
+  const int nvec = cols / 8;
+  int wpr = 0;
+  for (int w : {1, 2, 4, 8}) {
+    if (nvec <= w * 32 * 4) {
+      wpr = w;
+      break;
+    }
+  }
+  if (!wpr) return -1;  // more than 8192 columns: the ConvRot-layout kernel
+  auto go = [&](auto kernel, int rows_per_cta) {
+    kernel<<<(rows + rows_per_cta - 1) / rows_per_cta, kQuantThreads, 0, stream>>>(
+        static_cast<const T*>(x), ldx, static_cast<const T*>(msc), static_cast<const T*>(msh),
+        static_cast<const T*>(nw), mgroup, eps, q, ldq, scales, rows, cols, kitchen);
+  };
+  switch (wpr) {
+    case 1: go(quantize_modulated_vec_kernel<T, 1, 4, ACT>, 8); break;
+    case 2: go(quantize_modulated_vec_kernel<T, 2, 4, ACT>, 4); break;
+    case 4: go(quantize_modulated_vec_kernel<T, 4, 4, ACT>, 2); break;
+    default: go(quantize_modulated_vec_kernel<T, 8, 4, ACT>, 1); break;
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("modulated quantiser launch failed: %s", cudaGetErrorString(e));
+    return W8A8_ERR_ACCELERATOR;
+  }
+  return 0;
+}
+
+template <typename T>
+int launch_modulated(int act, const void* x, int64_t ldx, const void* msc, const void* msh,
+                     const void* nw, int64_t mgroup, float eps, int8_t* q, int64_t ldq,
+                     float* scales, int rows, int cols, int kitchen, cudaStream_t stream) {
+  switch (act) {
+    case 5: return launch_modulated_t<T, 5>(x, ldx, msc, msh, nw, mgroup, eps, q, ldq, scales, rows, cols, kitchen, stream);
+    case 6: return launch_modulated_t<T, 6>(x, ldx, msc, msh, nw, mgroup, eps, q, ldq, scales, rows, cols, kitchen, stream);
+    case 7: return launch_modulated_t<T, 7>(x, ldx, msc, msh, nw, mgroup, eps, q, ldq, scales, rows, cols, kitchen, stream);
+    case 8: return launch_modulated_t<T, 8>(x, ldx, msc, msh, nw, mgroup, eps, q, ldq, scales, rows, cols, kitchen, stream);
+    default: return -1;
+  }
+}
+
+}  // namespace
+
+int quantize_modulated_vec_launch(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                                  int64_t ldx, int act, const void* norm_w, float eps,
+                                  const void* mod_scale, const void* mod_shift, int64_t mod_group,
+                                  int8_t* q, int64_t ldq, float* scales, int scale_mode,
+                                  cudaStream_t stream) {
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if ((x_dtype != W8A8_BF16 && x_dtype != W8A8_F16) || cols % 8 || ldx % 8 || ldq % 8 ||
+      rows > 0x7fffffffLL || !a16(x) || !a16(q) || !a16(mod_scale) ||
+      (mod_shift && !a16(mod_shift)) || (norm_w && !a16(norm_w))) {
+    return -1;
+  }
+  const int km = scale_mode == W8A8_SCALE_KITCHEN ? 1 : 0;
+  const int64_t g = mod_group > 0 ? mod_group : 1;
+  if (x_dtype == W8A8_BF16) {
+    return launch_modulated<__nv_bfloat16>(act, x, ldx, mod_scale, mod_shift, norm_w, g, eps, q, ldq,
+                                           scales, static_cast<int>(rows), static_cast<int>(cols),
+                                           km, stream);
+  }
+  return launch_modulated<__half>(act, x, ldx, mod_scale, mod_shift, norm_w, g, eps, q, ldq, scales,
+                                  static_cast<int>(rows), static_cast<int>(cols), km, stream);
+}
+
+namespace {
 }  // namespace
 
 int quantize_rowwise_launch(const void* x, int x_dtype, int64_t rows, int64_t cols, int64_t ldx,

@@ -93,6 +93,14 @@ int rs_reduce_launch(const void* recv, const float* xs, const w8a8_epilogue_t* e
 int rs_gather_launch(void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t rs_rows,
                      const void* stage, unsigned* const* flags, int rank, int world, unsigned epoch,
                      cudaStream_t stream);
+// Modulation (act 5..8) + quantiser without ConvRot for 16-bit rows of at
+// most 8192 columns in the plain quantiser's layout; -1: not handled here
+// (the ConvRot-layout kernel takes the call).
+int quantize_modulated_vec_launch(const void* x, int x_dtype, int64_t rows, int64_t cols,
+                                  int64_t ldx, int act, const void* norm_w, float eps,
+                                  const void* mod_scale, const void* mod_shift, int64_t mod_group,
+                                  int8_t* q, int64_t ldq, float* scales, int scale_mode,
+                                  cudaStream_t stream);
 // The fused sampler step (flow parameterisation, CFG, Euler / ER-SDE update).
 int sampler_step_launch(float* x, const void* out_cond, const void* out_uncond, int out_dtype,
                         int64_t n, const float* coef, const w8a8_sampler_step_t& step,
