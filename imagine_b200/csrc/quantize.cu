@@ -372,10 +372,60 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_modulated_vec_kernel(
   const uint4* srow = reinterpret_cast<const uint4*>(msc + mrow);
   const uint4* hrow = reinterpret_cast<const uint4*>(msh ? msh + mrow : msc);
   float amax = 0.0f;
+  // bf16 rows (all modulations but the kitchen-numerics (rms) AdaLN, whose
+  // shift is an FMA): the same per-element operations and roundings as the
+  // loop below, two elements per f32x2 instruction and per paired bf16
+  // conversion
+  constexpr bool kPairedAdaLN = std::is_same<T, __nv_bfloat16>::value;
+  const bool paired = kPairedAdaLN && (ACT == 5 || ACT == 6 || !kitchen);
+  if constexpr (kPairedAdaLN) {
+    if (paired) {
+      auto rne2 = [](uint64_t p) -> uint32_t {  // two RN bf16 roundings, packed
+        const __nv_bfloat162 b = __floats2bfloat162_rn(lo(p), hi(p));
+        return *reinterpret_cast<const uint32_t*>(&b);
+      };
+      auto unpack2 = [](uint32_t w) -> uint64_t {
+        return pk(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+      };
+      const uint64_t mean2 = pk(mean, mean), rstd2 = pk(rstd, rstd), one2 = pk(1.0f, 1.0f);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int vi = gt + i * kGroupThreads;
+        if (live && vi < nvec) {
+          const uint4 sv = __ldg(srow + vi);
+          uint4 hv = make_uint4(0, 0, 0, 0), nv = make_uint4(0, 0, 0, 0);
+          if constexpr (ACT == 7 || ACT == 8) hv = __ldg(hrow + vi);
+          if constexpr (ACT == 6) nv = __ldg(reinterpret_cast<const uint4*>(nw) + vi);
+          const uint32_t xw[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+          const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+          const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+          const uint32_t nwv[4] = {nv.x, nv.y, nv.z, nv.w};
+          uint32_t ow[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t one_s = unpack2(rne2(add2(one2, unpack2(sw[k]))));
+            if constexpr (ACT == 5) {
+              ow[k] = rne2(mul2(unpack2(xw[k]), one_s));
+            } else if constexpr (ACT == 6) {
+              const uint64_t nrm =
+                  unpack2(rne2(mul2(mul2(unpack2(xw[k]), rstd2), unpack2(nwv[k]))));
+              ow[k] = rne2(mul2(nrm, one_s));
+            } else {
+              const uint64_t nrm = mul2(sub2(unpack2(xw[k]), mean2), rstd2);
+              const uint64_t t = unpack2(rne2(mul2(unpack2(rne2(nrm)), one_s)));
+              ow[k] = rne2(add2(t, unpack2(hw[k])));
+            }
+          }
+          v[i] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          amax = fmaxf(amax, vec_absmax<__nv_bfloat16>(v[i]));
+        }
+      }
+    }
+  }
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int vi = gt + i * kGroupThreads;
-    if (live && vi < nvec) {
+    if (!paired && live && vi < nvec) {
       const uint4 sv = __ldg(srow + vi);
       uint4 hv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
       if constexpr (ACT == 7 || ACT == 8) hv = __ldg(hrow + vi);
