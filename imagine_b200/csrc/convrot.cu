@@ -388,6 +388,37 @@ __device__ __forceinline__ void act_rot_row(
           load16<T>(mod.scale, mrow + col, vec_in, sc);
           if constexpr (ACT == kInAdaLN || ACT == kInRmsAdaLN) load16<T>(mod.shift, mrow + col, vec_in, sh);
           if constexpr (ACT == kInRmsModScale) load16<T>(act_w, col, vec_in, w);
+          if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+            if (ACT == kInModScale || ACT == kInRmsModScale || !kitchen_mode) {
+              // bf16: the same operations and roundings as the scalar loop
+              // below, two elements per f32x2 instruction and per paired
+              // bf16 conversion
+              auto rne2 = [](uint64_t p) -> uint64_t {
+                const __nv_bfloat162 b = __floats2bfloat162_rn(lo(p), hi(p));
+                const uint32_t w = *reinterpret_cast<const uint32_t*>(&b);
+                return pk(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+              };
+              const uint64_t one2 = pk(1.0f, 1.0f), mean2 = pk(mean, mean), rstd2 = pk(rstd, rstd);
+#pragma unroll
+              for (int j = 0; j < 16; j += 2) {
+                const uint64_t xp = pk(v[i][h][j], v[i][h][j + 1]);
+                const uint64_t one_s = rne2(add2(one2, pk(sc[j], sc[j + 1])));
+                uint64_t y;
+                if constexpr (ACT == kInModScale) {
+                  y = mul2(xp, one_s);
+                } else if constexpr (ACT == kInRmsModScale) {
+                  y = mul2(rne2(mul2(mul2(xp, rstd2), pk(w[j], w[j + 1]))), one_s);
+                } else {
+                  const uint64_t nrm = mul2(sub2(xp, mean2), rstd2);
+                  y = add2(rne2(mul2(rne2(nrm), one_s)), pk(sh[j], sh[j + 1]));
+                }
+                y = rne2(y);
+                v[i][h][j] = lo(y);
+                v[i][h][j + 1] = hi(y);
+              }
+              continue;
+            }
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float xv = v[i][h][j];
