@@ -13,7 +13,14 @@ N > 1 runs under torchrun, one rank per GPU; every rank runs its own linear
 (independent CFG branches / seeds: weak scaling, no data-path collective) and
 the job's value is the sum of all ranks' work over the slowest rank's time.
 ``--impl reference`` times the reference's LibTorch CPU path (the oracle's
-restatement of inference/src/int8_linear.rs:198-277) on the host cores.
+restatement of inference/src/int8_linear.rs:198-277) on the host cores, all
+5600 rows per step.
+
+After the linear, the line's ``dit_step`` object times the metric's second
+half: one denoising step of the 60-block MMDiT at 1600x896 with CFG batch 2
+(imagine_b200.mmdit): both branches batched on one GPU; on 2 GPUs one branch
+per GPU; on 4 / 8 GPUs a branch per half of the GPUs, tensor-parallel inside
+it (strong scaling: the step's work is fixed).
 """
 from __future__ import annotations
 
@@ -248,30 +255,131 @@ def run_ours(args, rank, world, local_rank):
                 e2e_ms=e2e_ms, clocks=clocks, x_host=x_host, wq=wq, ws=ws, bias=bias)
 
 
-def cpu_baseline(rows: int = 256, reps: int = 3):
-    """The reference's LibTorch CPU path (oracle restatement of
-    inference/src/int8_linear.rs:198-277) on a bounded sample: `rows` of the
-    5600 tokens through the full 3072 -> 12288 linear, all host threads."""
+def cpu_case(m: int = M, k: int = K, n: int = N, act="gelu_tanh"):
+    """One call of the reference's LibTorch CPU path (the oracle's restatement
+    of inference/src/int8_linear.rs:198-277, whose int32 product reads the
+    transposed weight view with no copy, as the reference's ``accumulate``
+    does for aligned K and N) on the full workload -- all m rows of the
+    k -> n linear: quantise, int32 _int_mm, dequant, bias, optional GELU --
+    on every host thread.  Returns the call (inputs made once)."""
     from oracle import eager as O
 
     torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(0)
-    x = torch.randn(rows, K, generator=g).to(torch.bfloat16)
-    w = (torch.randn(N, K, generator=torch.Generator().manual_seed(1)) * 0.02).to(torch.bfloat16)
-    b = (torch.randn(N, generator=torch.Generator().manual_seed(2)) * 0.02).to(torch.bfloat16)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=torch.Generator().manual_seed(1)) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, generator=torch.Generator().manual_seed(2)) * 0.02).to(torch.bfloat16)
     wq, ws = O.quantize_weight(w)
-    O.int8_linear(x[:16], wq, ws, b, output_act="gelu_tanh")  # warm-up
+    return lambda: O.int8_linear(x, wq, ws, b, output_act=act)
+
+
+def cpu_baseline(m: int = M, k: int = K, n: int = N, act="gelu_tanh", reps: int = 5):
+    """``cpu_case`` timed: median of ``reps`` calls after one warm-up call."""
+    call = cpu_case(m, k, n, act)
+    call()  # warm-up
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
-        O.int8_linear(x, wq, ws, b, output_act="gelu_tanh")
+        call()
         times.append(time.perf_counter() - t0)
     sec = statistics.median(times)
-    return {"value": 2.0 * rows * N * K / sec / 1e12, "unit": "TOPS",
+    return {"value": 2.0 * m * n * k / sec / 1e12, "unit": "TOPS",
             "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{rows} of {M} rows through the full {K}->{N} linear (quantise, int32 "
-                      f"_int_mm, dequant, bias, gelu), median of {reps}",
-            "seconds_per_sample": sec}
+            "sample": f"{m} of {m} rows through the full {k}->{n} linear (quantise, int32 "
+                      f"_int_mm, dequant, bias{', gelu' if act else ''}), median of {reps} after "
+                      f"1 warm-up",
+            "seconds_per_sample": sec, "cpu": _cpu_model()}
+
+
+def _cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ---------------------------------------------------------------------------
+# The DiT step: 60 MMDiT blocks at 1600x896, CFG batch 2 (the metric's
+# second half), one Euler step of the sampler per timed step.
+# ---------------------------------------------------------------------------
+DIT_TEXT = 256
+DIT_LATENT = (16, 112, 200)
+
+
+def run_dit(args, rank, world, local_rank):
+    from imagine_b200 import mmdit as MD
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = MD.MMDiTConfig(blocks=args.dit_blocks)
+    pl = MD.placement(world, rank)
+    groups = MD.ProcessGroups(pl)
+    ops = MD.NativeOps()
+    t0 = time.perf_counter()
+    params = MD.random_params(cfg, ops, dev, seed=1234, tp_rank=pl.tp_rank, tp_world=pl.tp)
+    torch.cuda.synchronize()
+    init_s = time.perf_counter() - t0
+    dit = MD.MMDiT(params, ops, groups.tp_group)
+    g = torch.Generator().manual_seed(77)
+    lat = torch.randn(1, *DIT_LATENT, generator=g)
+    ctx_c = torch.randn(1, DIT_TEXT, cfg.context_dim, generator=g).to(torch.bfloat16).to(dev)
+    ctx_u = torch.randn(1, DIT_TEXT, cfg.context_dim, generator=g).to(torch.bfloat16).to(dev)
+    loop = MD.DenoiseLoop(MD.cfg_model(dit, pl, groups, ctx_c, ctx_u), lat.to(dev), steps=40,
+                          cfg_scale=2.5)
+    warm = max(3, args.dit_warmup)
+    for i in range(warm):
+        loop.step(i)
+    torch.cuda.synchronize()
+    steps = args.dit_steps
+    stream = torch.cuda.current_stream(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.05)
+    ev[0].record(stream)
+    for i in range(steps):
+        loop.step(warm + i)
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = ev[0].elapsed_time(ev[1]) / steps
+    finite = bool(torch.isfinite(loop.x).all())
+    if world > 1:
+        t = torch.tensor([ms, 0.0 if finite else 1.0], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, finite = float(t[0]), float(t[1]) == 0.0
+    import imagine_b200 as W
+
+    if W.device_error() != 0:
+        raise RuntimeError("device error during the DiT step")
+    rows = 2 * (DIT_LATENT[1] // 2) * (DIT_LATENT[2] // 2) + 2 * DIT_TEXT
+    lin_ops = rows * 2.0 * cfg.hidden * (3 * cfg.hidden + cfg.hidden + 2 * cfg.mlp_hidden) \
+        * cfg.blocks
+    seq = (DIT_LATENT[1] // 2) * (DIT_LATENT[2] // 2) + DIT_TEXT
+    attn_flops = 4.0 * 2 * seq * seq * cfg.hidden * cfg.blocks
+    return {"ms": ms, "unit": "ms per denoising step", "n_gpus": world, "steps": steps,
+            "warmup": warm, "scaling": "strong", "blocks": cfg.blocks,
+            "model": "Qwen-Image MMDiT (synthesised): hidden 3072, 24x128 heads, GELU-tanh MLP "
+                     "12288, per-block AdaLN 3072->18432, random-init int8 weights",
+            "workload": "1600x896 (latent 16x112x200 -> 5600 image tokens) + 256 text tokens, "
+                        "CFG batch 2 (scale 2.5), Euler flow sampler, 40-step schedule",
+            "placement": pl.describe(),
+            "attention": "torch scaled_dot_product_attention, bf16 (cuDNN backend first)",
+            "linear_tops_per_step": lin_ops / 1e12, "attention_tflop_per_step": attn_flops / 1e12,
+            "achieved_tops": (lin_ops + attn_flops) / (ms * 1e-3) / 1e12,
+            "weights_gb_per_rank": params.weight_bytes / 1e9, "init_s": init_s,
+            "finite": finite, "clocks": clocks,
+            "est_40_step_s": 40 * ms / 1e3}
 
 
 def main():
@@ -281,6 +389,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dit-blocks", type=int, default=60,
+                    help="blocks of the DiT step timed after the linear (0: skip it)")
+    ap.add_argument("--dit-steps", type=int, default=5)
+    ap.add_argument("--dit-warmup", type=int, default=3)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -291,20 +403,23 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
+        call = cpu_case()
         steps = []
-        base = None
         for _ in range(args.warmup + args.steps):
-            base = cpu_baseline(rows=64, reps=1)
-            steps.append(base["seconds_per_sample"])
+            t0 = time.perf_counter()
+            call()
+            steps.append(time.perf_counter() - t0)
         sec = statistics.median(steps[args.warmup:])
-        value = 2.0 * 64 * N * K / sec / 1e12
+        value = OPS / sec / 1e12
         line = {"metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
                 "data": "synthetic", "config": WORKLOAD, "impl": "reference",
-                "cpu_baseline": {"value": value, "unit": "TOPS", "cores": base["cores"],
-                                 "kind": "port",
-                                 "sample": "64 of 5600 rows per step through the full linear"},
+                "cpu_baseline": {"value": value, "unit": "TOPS", "cores": torch.get_num_threads(),
+                                 "kind": "port", "cpu": _cpu_model(),
+                                 "sample": f"{M} of {M} rows per step through the full {K}->{N} "
+                                           "linear (quantise, int32 _int_mm, dequant, bias, gelu); "
+                                           "each step one full call, median over the timed steps"},
                 "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
@@ -315,6 +430,9 @@ def main():
             "nccl", device_id=torch.device("cuda", local_rank),
             timeout=__import__("datetime").timedelta(seconds=120))
     r = run_ours(args, rank, world, local_rank)
+    dit = None
+    if args.dit_blocks > 0:
+        dit = run_dit(args, rank, world, local_rank)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -350,8 +468,14 @@ def main():
         "gpu_launches": 2 * args.steps,
         "clocks": r["clocks"],
     }
+    if dit is not None:
+        line["dit_step"] = dit
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_baseline().items() if k != "seconds_per_sample"}
+        # BASELINE.json config 1 (the reference's CPU case): 5600 x 3072 -> 3072
+        c1 = cpu_baseline(M, K, 3072, act=None)
+        line["cpu_baseline"]["config1_5600x3072x3072"] = {
+            "value": c1["value"], "unit": "TOPS", "sample": c1["sample"]}
     print(json.dumps(line))
 
 

@@ -1939,14 +1939,20 @@ int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& p) {
   return 0;
 }
 
+bool gemm_tc_ok(const GemmArgs& g) {
+  const int out_bytes = g.out_dtype == W8A8_F32 || g.out_dtype == W8A8_S32 ? 4 : 2;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return g.K > 0 && g.K % 16 == 0 && g.lda % 16 == 0 && g.ldb % 16 == 0 && a16(g.a) &&
+         a16(g.b) && a16(g.out) && (g.ldo * out_bytes) % 16 == 0 && g.M < (1ll << 31) &&
+         g.N < (1ll << 31) && g.K < (1ll << 31);
+}
+
 int gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
   GemmArgs g = g_in;  // split_k is cleared below when no scratch is given
   if (g.M == 0 || g.N == 0) return 0;
   const int out_bytes = g.out_dtype == W8A8_F32 || g.out_dtype == W8A8_S32 ? 4 : 2;
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  const bool tc_ok = g.K > 0 && g.K % 16 == 0 && g.lda % 16 == 0 && g.ldb % 16 == 0 &&
-                     a16(g.a) && a16(g.b) && a16(g.out) && (g.ldo * out_bytes) % 16 == 0 &&
-                     g.M < (1ll << 31) && g.N < (1ll << 31) && g.K < (1ll << 31);
+  const bool tc_ok = gemm_tc_ok(g);
   if (g.rms_rope) {
     // heads of 128 columns, one per epilogue warp half: the 1-CTA tcgen05 GEMM
     if (!(g.kind == 0 && g.out_dtype == W8A8_BF16 && tc_ok && !g.b_tiled)) {

@@ -13,9 +13,12 @@
 //
 // Set-up: the first call on a device (with that device current) looks up the
 // array's device address with cudaGetSymbolAddress and caches it per device;
-// make that first call before any stream capture.  Every call, from every
-// thread and stream, shares the one array per device, so calls that overlap
-// on the GPU race with each other.
+// make that first call before any stream capture.  The cached address is not
+// looked up again: after cudaDeviceReset in the host process it is stale, so
+// a process that resets a device must not call this entry point again.
+// Every call, from every thread and stream, shares the one array per device,
+// so calls that overlap on the GPU race with each other.  Only calls whose
+// GEMM splits use (and clear) the array; the others run without scratch.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -70,19 +73,31 @@ int static_scratch(void** out) {
 }  // namespace
 
 int gemm_splitk_static_launch(GemmArgs g, cudaStream_t stream) {
-  const int64_t need = splitk_workspace_bytes(g.M, g.N);
+  if (g.M == 0 || g.N == 0) return 0;
+  // Plan first: a GEMM that does not split (split_k = 1, or a shape the
+  // automatic policy runs whole) needs no scratch at all, whatever its size.
+  GemmPlan plan{};
+  if (int rc = plan_gemm(g, gemm_tc_ok(g), plan)) return rc;
+  if (plan.splits <= 1) {
+    g.split_k = 1;
+    g.workspace = nullptr;
+    g.workspace_bytes = 0;
+    return gemm_launch(g, stream);
+  }
+  const int64_t need = plan.workspace_need;
   if (need > kStaticScratchBytes) {
-    set_error("M=%lld x N=%lld needs %lld bytes of split-K scratch; the static scratch holds %lld "
-              "bytes (64 KiB per 128 x 128 output tile plus one counter per tile and epilogue "
-              "warp)",
-              static_cast<long long>(g.M), static_cast<long long>(g.N),
+    set_error("M=%lld x N=%lld split %d ways needs %lld bytes of split-K scratch; the static "
+              "scratch holds %lld bytes (64 KiB per 128 x 128 output tile plus one counter per "
+              "tile and epilogue warp)",
+              static_cast<long long>(g.M), static_cast<long long>(g.N), plan.splits,
               static_cast<long long>(need), static_cast<long long>(kStaticScratchBytes));
     return W8A8_ERR_VALUE;
   }
   void* ptr = nullptr;
   if (int rc = static_scratch(&ptr)) return rc;
   // The partial sums and counters must start at zero.  A completed call
-  // leaves them zero, but a call that gave up (device error) may not have.
+  // leaves them zero, but a call that gave up (device error) may not have,
+  // so the part this call uses is cleared on its stream first.
   cudaError_t e = cudaMemsetAsync(ptr, 0, static_cast<size_t>(need), stream);
   if (e != cudaSuccess) {
     set_error("clearing the static split-K scratch failed: %s", cudaGetErrorString(e));

@@ -117,6 +117,8 @@ struct GemmPlan {
 };
 // tc_ok: the operands suit the tcgen05 path.  Returns 0 or an error code.
 int plan_gemm(const GemmArgs& g, bool tc_ok, GemmPlan& plan);
+// Whether the operands suit the tcgen05 path (K % 16, 16-byte aligned rows).
+bool gemm_tc_ok(const GemmArgs& g);
 // Split-K scratch: int32 partial sums [tiles * 128, bn], then one arrival
 // counter per (tile, epilogue warp).
 int64_t splitk_acc_bytes(int64_t split_tiles, int bn);

@@ -418,7 +418,8 @@ def int8_linear_rms_rope(x: torch.Tensor, weight: torch.Tensor, weight_scale: to
                          bias: Optional[torch.Tensor], norm_weight: torch.Tensor,
                          freqs_cis: torch.Tensor, epsilon: float = 1e-6,
                          rope_cols: Optional[int] = None, *, dequant: str = "eager",
-                         scale_mode: str = "eager", split_k: Optional[int] = None, config=None):
+                         scale_mode: str = "eager", split_k: Optional[int] = None, config=None,
+                         modulation: Optional[tuple] = None):
     """The Q (or K) projection with its RMSNorm + RoPE fused into the GEMM
     epilogue: ``rms_rope(int8_linear(x, weight, ...))`` of the reference's
     attention (inference/src/models/qwen_image21/dit.rs:427-429, 486-505) for
@@ -427,7 +428,9 @@ def int8_linear_rms_rope(x: torch.Tensor, weight: torch.Tensor, weight_scale: to
     every head, or [rope_cols] per column (q_norm then k_norm for a fused QKV
     weight) -- and rotated by ``freqs_cis`` [S, 64, 2, 2] (row r of x uses
     position r % S); later columns (v) get the plain epilogue.  Returns
-    [..., N] bf16."""
+    [..., N] bf16.  ``modulation=(scale, shift, eps, rms)`` quantises
+    ``norm(x)(1 + scale) + shift`` instead of x (the AdaLN step before an
+    MMDiT block's QKV projection), in the same pass as the quantiser."""
     _cuda("x", x)
     dev = x.device
     _cuda("weight", weight, dev)
@@ -453,18 +456,36 @@ def int8_linear_rms_rope(x: torch.Tensor, weight: torch.Tensor, weight_scale: to
     if not x2.is_contiguous():
         x2 = x2.contiguous()
     m = x2.shape[0]
-    fr = rope_freqs_rows(freqs_cis, m) if rope_cols and m > 0 else None
+    if m == 0:
+        return torch.empty((*lead, n), dtype=torch.bfloat16, device=dev)
+    stream = _stream(dev)
+    if modulation is None:
+        q = torch.empty((m, k), dtype=torch.int8, device=dev)
+        xs = torch.empty((m,), dtype=torch.float32, device=dev)
+        N.check(N.LIB.w8a8_quantize_rowwise(_vp(x2), _code(x2.dtype), m, k, k, _vp(q), k, _vp(xs),
+                                            SCALE_MODE[scale_mode], 0, 0, stream))
+    else:
+        scale, shift, eps_mod, rms = modulation
+        q, xs = quantize_int8_rowwise_modulated(x2.reshape(*lead, k), "rms_adaln" if rms else "adaln",
+                                                scale, shift, None, eps_mod,
+                                                scale_mode=scale_mode)
+        q = q.reshape(m, k)
+        xs = xs.reshape(m)
+    return _rms_rope_gemm(q, xs, lead, weight, ws, bias, nw, freqs_cis, epsilon, rope_cols,
+                          dequant, split_k, config, stream)
+
+
+def _rms_rope_gemm(q, xs, lead, weight, ws, bias, nw, freqs_cis, epsilon, rope_cols, dequant,
+                   split_k, config, stream):
+    """The GEMM with the RMSNorm + RoPE epilogue on quantised rows q [M, K]."""
+    dev = q.device
+    m, k = q.shape
+    n = weight.shape[0]
+    fr = rope_freqs_rows(freqs_cis, m) if rope_cols else None
     w = weight if weight.is_contiguous() else weight.contiguous()
     b = bias.to(device=dev, dtype=torch.bfloat16).reshape(-1).contiguous() if bias is not None else None
     out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
-    if m == 0:
-        return out.reshape(*lead, n)
     ep = _epilogue(ws, b, None, None, dequant, None, n, n)
-    stream = _stream(dev)
-    q = torch.empty((m, k), dtype=torch.int8, device=dev)
-    xs = torch.empty((m,), dtype=torch.float32, device=dev)
-    N.check(N.LIB.w8a8_quantize_rowwise(_vp(x2), _code(x2.dtype), m, k, k, _vp(q), k, _vp(xs),
-                                        SCALE_MODE[scale_mode], 0, 0, stream))
     cfg = _config(config)
     cfg = cfg if isinstance(cfg, N.GemmConfig) else None
     if split_k is None:
@@ -930,19 +951,34 @@ def int8_gemm_s32(q: torch.Tensor, w: torch.Tensor, config=None) -> torch.Tensor
 
 
 def dequantize_int8_linear(acc, x_scale, weight_scale, bias=None, out_dtype=torch.bfloat16, *,
-                           dequant="chained"):
-    """``dequantize_int8_linear`` replacement (native/comfy-port/kitchen/int8_linear.cu:517-583)."""
+                           dequant="chained", residual=None, residual_scale=None, lead=None):
+    """``dequantize_int8_linear`` replacement (native/comfy-port/kitchen/int8_linear.cu:517-583).
+
+    ``residual`` / ``residual_scale`` add the residual epilogue of
+    ``int8_linear`` (``residual + y * residual_scale``, broadcast as there
+    against an output of shape ``(*lead, N)``; ``lead`` defaults to (M,)).
+    Returns [M, N], or ``(*lead, N)`` when ``lead`` is given."""
     _cuda("acc", acc)
     dev = acc.device
     m, n = acc.shape
+    if residual is not None and residual_scale is None:
+        raise ValueError("dequantize_int8_linear: residual requires residual_scale")
+    lead = tuple(lead) if lead is not None else None
+    if lead is not None and math.prod(lead) != m:
+        raise ValueError(f"lead {lead} does not hold the {m} accumulator rows")
     ws = weight_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
     xs = x_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
     b = bias.to(device=dev, dtype=out_dtype).reshape(-1).contiguous() if bias is not None else None
+    r = rs = None
+    rs_rows = 0
+    if residual is not None:
+        r = residual.to(device=dev, dtype=out_dtype).reshape(m, n).contiguous()
+        rs, rs_rows = _residual_scale(residual_scale, lead or (m,), n, out_dtype, dev)
     out = torch.empty((m, n), dtype=out_dtype, device=dev)
-    ep = _epilogue(ws, b, None, None, dequant, None, n, n)
+    ep = _epilogue(ws, b, r, rs, dequant, None, n, n, rs_rows)
     N.check(N.LIB.w8a8_dequantize_linear(_vp(acc.contiguous()), _vp(xs), ctypes.byref(ep), _vp(out),
                                          _code(out_dtype), m, n, _stream(dev)))
-    return out
+    return out.reshape(*lead, n) if lead is not None else out
 
 
 def int8_gemv(q, w, x_scale, weight_scale, bias=None, out_dtype=torch.bfloat16, residual=None,

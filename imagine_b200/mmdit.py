@@ -1,0 +1,607 @@
+"""The MMDiT joint block and the denoising step over the W8A8 linear family.
+
+The BASELINE model is the original Qwen-Image MMDiT: 60 joint blocks of
+hidden 3072, 24 heads x 128, a GELU-tanh MLP of 12288 and a per-block,
+per-stream AdaLN modulation 3072 -> 18432.  No code for it exists in the
+reference (its Qwen-Image 2.1 DiT is single-stream, hidden 4096), so it is
+assembled here from the reference's operators and model steps:
+
+* per stream (image, text): AdaLN (``modulated_norm``,
+  inference/src/models/qwen_image21/numeric.rs:63-108) fused into the QKV
+  projection's quantiser, with the per-head Q/K RMSNorm + RoPE
+  (``rms_rope``, dit.rs:486-505) fused into its GEMM epilogue;
+* joint attention over the text tokens followed by the image tokens (the
+  sequence order of ``assemble_sequence``, geometry.rs:143-230), bf16
+  scaled-dot-product attention;
+* the out-projection and MLP-down with the gated residual
+  (``gated_residual``, numeric.rs:110-126) in their GEMM epilogues;
+* AdaLN fused into MLP-up's quantiser, GELU-tanh in its epilogue;
+* the block loop of ``DiT::forward_original`` (dit.rs:567-757): text
+  projection, timestep embedding (numeric.rs:22-50), 3-axis RoPE
+  (geometry.rs:65-110), final AdaLN + projection.
+
+The modulation linears of all blocks read the same SiLU(temb) row, so their
+weights are stored as one [blocks * 6 * hidden, hidden] matrix per stream and
+run as ONE M <= 2 GEMV per stream per step.
+
+Every numeric step goes through an ``ops`` object.  ``NativeOps`` is libw8a8
+(imagine_b200.linear) plus torch's scaled-dot-product attention; the tests
+run the same model code over a CPU oracle for parity.
+
+Multi-GPU (one process per GPU):
+
+* CFG: the two branches of a CFG step are independent until the combine.
+  With 2 or more ranks, ranks [0, W/2) run the conditional branch and
+  [W/2, W) the unconditional one; one all-gather between the rank pairs
+  (r, r + W/2) gives every rank both predictions (``cfg_model``).
+* Tensor parallelism inside a branch (W/2 > 1 ranks): heads are split across
+  the ranks of a branch.  QKV and MLP-up are column-parallel (no exchange);
+  the out-projection and MLP-down are row-parallel: an all-reduce MAX of the
+  row absmax (so every rank quantises its K-slice with the full row's scale),
+  an int32 GEMM on the slice, an all-reduce SUM of the exact int32 partials,
+  then the dequant + bias + gated-residual epilogue.  The modulation GEMV is
+  split by output rows and all-gathered once per step.  Results equal the
+  single-GPU model's bit for bit.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, fields
+from typing import List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+@dataclass(frozen=True)
+class MMDiTConfig:
+    hidden: int = 3072
+    heads: int = 24
+    head_dim: int = 128
+    mlp_hidden: int = 12288
+    blocks: int = 60
+    latent_channels: int = 16
+    patch: int = 2
+    context_dim: int = 3072
+    time_dim: int = 256
+    eps: float = 1e-6
+    axes: Tuple[int, int, int] = (16, 56, 56)
+    theta: float = 10000.0
+
+    @property
+    def in_channels(self) -> int:
+        return self.latent_channels * self.patch * self.patch
+
+    @property
+    def mod_dim(self) -> int:
+        return 6 * self.hidden
+
+
+# --------------------------------------------------------------------------
+# positions, timestep embedding, patches
+# --------------------------------------------------------------------------
+def sequence_ids(text_tokens: int, h: int, w: int, device=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Position ids [S, 3] of the text tokens and of the h x w image patches,
+    as ``assemble_sequence`` builds them for one image and no references
+    (inference/src/models/qwen_image21/geometry.rs:143-230): text token i at
+    (i, i, i); the image after it at frame index ``text_tokens`` and centred
+    row / column indices."""
+    txt = torch.arange(text_tokens, dtype=torch.float32, device=device).unsqueeze(1).expand(text_tokens, 3)
+    hh = torch.arange(h, dtype=torch.float32, device=device) - (h - h // 2)
+    ww = torch.arange(w, dtype=torch.float32, device=device) - (w - w // 2)
+    img = torch.stack([torch.full((h, w), float(text_tokens), device=device),
+                       hh.unsqueeze(1).expand(h, w), ww.unsqueeze(0).expand(h, w)], -1)
+    return txt.contiguous(), img.reshape(h * w, 3).contiguous()
+
+
+def rope_freqs(ids: torch.Tensor, axes=(16, 56, 56), theta: float = 10000.0) -> torch.Tensor:
+    """Rotations [S, sum(axes) / 2, 2, 2] (fp32) for position ids [S, 3]
+    (``PositionEncoding::forward``, geometry.rs:65-110): per axis of width d,
+    omega_j = 1 / theta^(j * 2 / d) in float64, angle = pos * omega, and the
+    2 x 2 block [[cos, -sin], [sin, cos]]; the axes concatenated along the
+    pairs."""
+    parts = []
+    for axis, dim in enumerate(axes):
+        if dim % 2:
+            raise ValueError("every RoPE axis needs an even width")
+        scale = torch.linspace(0.0, (dim - 2) / dim, dim // 2, dtype=torch.float64, device=ids.device)
+        omega = torch.pow(theta, scale).reciprocal()
+        ang = torch.einsum("n,d->nd", ids[:, axis].to(torch.float32).double(), omega)
+        c, s = torch.cos(ang), torch.sin(ang)
+        parts.append(torch.stack([c, -s, s, c], -1).reshape(ids.shape[0], dim // 2, 2, 2).float())
+    return torch.cat(parts, dim=1).contiguous()
+
+
+def timestep_embedding(t: torch.Tensor, dim: int = 256, max_period: float = 10000.0,
+                       time_factor: float = 1000.0) -> torch.Tensor:
+    """inference/src/models/qwen_image21/numeric.rs:22-50 (fp32)."""
+    t = t.to(torch.float32) * time_factor
+    half = dim // 2
+    freq = torch.exp(torch.arange(half, dtype=torch.float32, device=t.device)
+                     * -math.log(max_period) / half)
+    args = t.unsqueeze(1) * freq.unsqueeze(0)
+    out = torch.cat([torch.cos(args), torch.sin(args)], -1)
+    if dim % 2:
+        out = torch.cat([out, torch.zeros_like(out[:, :1])], -1)
+    return out
+
+
+def round_timesteps(t: torch.Tensor, dtype=torch.bfloat16) -> torch.Tensor:
+    """numeric.rs:15-20: t * 1000 in the model dtype, / 1000."""
+    return (t * 1000).to(dtype).div(1000).to(dtype)
+
+
+def patchify(x: torch.Tensor, p: int) -> torch.Tensor:
+    """[B, C, H, W] -> [B, (H/p)(W/p), C p p] (channel, then patch row, then
+    patch column)."""
+    b, c, h, w = x.shape
+    x = x.reshape(b, c, h // p, p, w // p, p).permute(0, 2, 4, 1, 3, 5)
+    return x.reshape(b, (h // p) * (w // p), c * p * p)
+
+
+def unpatchify(x: torch.Tensor, p: int, c: int, h: int, w: int) -> torch.Tensor:
+    b = x.shape[0]
+    x = x.reshape(b, h // p, w // p, c, p, p).permute(0, 3, 1, 4, 2, 5)
+    return x.reshape(b, c, h, w)
+
+
+# --------------------------------------------------------------------------
+# parameters
+# --------------------------------------------------------------------------
+@dataclass
+class Int8Params:
+    """One quantised linear: int8 w [N, K], fp32 per-output-channel ws [N],
+    bf16 bias [N] (or None)."""
+    w: torch.Tensor
+    ws: torch.Tensor
+    b: Optional[torch.Tensor]
+
+    def to(self, device) -> "Int8Params":
+        return Int8Params(self.w.to(device), self.ws.to(device),
+                          None if self.b is None else self.b.to(device))
+
+
+@dataclass
+class StreamParams:
+    """One stream of a joint block on one rank: QKV rows are this rank's heads
+    (q rows, then k rows, then v rows), ``qk_norm`` the per-column RMSNorm
+    weight of the q and k columns, ``out`` / ``down`` this rank's K-slice
+    (all output channels), ``up`` this rank's output rows."""
+    qkv: Int8Params
+    qk_norm: torch.Tensor
+    out: Int8Params
+    up: Int8Params
+    down: Int8Params
+
+
+@dataclass
+class BlockParams:
+    img: StreamParams
+    txt: StreamParams
+
+
+@dataclass
+class MMDiTParams:
+    cfg: MMDiTConfig
+    tp_rank: int
+    tp_world: int
+    blocks: List[BlockParams]
+    mod_img: Int8Params   # this rank's rows of [blocks * 6 * hidden, hidden]
+    mod_txt: Int8Params
+    time1: Int8Params     # [hidden, time_dim]
+    time2: Int8Params     # [hidden, hidden]
+    img_in: Int8Params    # [hidden, in_channels]
+    txt_norm: torch.Tensor  # bf16 [context_dim]
+    txt_in: Int8Params    # [hidden, context_dim]
+    norm_out: Int8Params  # [2 * hidden, hidden]: scale rows, then shift rows
+    proj_out: Int8Params  # [in_channels, hidden]
+
+    def to(self, device) -> "MMDiTParams":
+        def mv(v):
+            if isinstance(v, (Int8Params, StreamParams, BlockParams)):
+                return type(v)(**{f.name: mv(getattr(v, f.name)) for f in fields(v)})
+            if isinstance(v, torch.Tensor):
+                return v.to(device)
+            if isinstance(v, list):
+                return [mv(e) for e in v]
+            return v
+        return MMDiTParams(**{f.name: mv(getattr(self, f.name)) for f in fields(self)})
+
+    @property
+    def weight_bytes(self) -> int:
+        total = 0
+
+        def acc(v):
+            nonlocal total
+            if isinstance(v, torch.Tensor):
+                total += v.numel() * v.element_size()
+            elif isinstance(v, (Int8Params, StreamParams, BlockParams)):
+                for f in fields(v):
+                    acc(getattr(v, f.name))
+            elif isinstance(v, list):
+                for e in v:
+                    acc(e)
+        for f in fields(self):
+            acc(getattr(self, f.name))
+        return total
+
+
+def _shard(total: int, rank: int, world: int) -> slice:
+    if total % world:
+        raise ValueError(f"{total} does not split evenly over {world} ranks")
+    n = total // world
+    return slice(rank * n, (rank + 1) * n)
+
+
+class _Init:
+    """Seeded random-init weights ~ N(0, 0.02) (bf16), quantised per output
+    channel by ``ops.quantize_weight``; every rank draws the full matrix from
+    the same seed and keeps its slice, so shards equal the single-GPU
+    weights' slices exactly."""
+
+    def __init__(self, ops, device, seed: int):
+        self.ops = ops
+        self.device = torch.device(device)
+        self.gen = torch.Generator(device=self.device)
+        self.gen.manual_seed(seed)
+
+    def randn(self, *shape, std=0.02):
+        return (torch.randn(*shape, generator=self.gen, device=self.device) * std).to(torch.bfloat16)
+
+    def linear(self, n, k, rows: Optional[slice] = None, cols: Optional[slice] = None,
+               bias=True) -> Int8Params:
+        w = self.randn(n, k)
+        b = self.randn(n) if bias else None
+        q, ws = self.ops.quantize_weight(w)
+        del w
+        ws = ws.reshape(-1)
+        if rows is not None:
+            q, ws = q[rows], ws[rows]
+            b = b[rows] if b is not None else None
+        if cols is not None:
+            q = q[:, cols]
+        return Int8Params(q.contiguous(), ws.contiguous(), None if b is None else b.contiguous())
+
+
+def random_params(cfg: MMDiTConfig, ops, device, seed: int = 0, tp_rank: int = 0,
+                  tp_world: int = 1) -> MMDiTParams:
+    """Random-init weights of the architecture ``cfg`` (this rank's shards)."""
+    if cfg.heads % tp_world:
+        raise ValueError(f"{cfg.heads} heads do not split over {tp_world} ranks")
+    init = _Init(ops, device, seed)
+    hd = cfg.heads * cfg.head_dim
+    if hd != cfg.hidden:
+        raise ValueError("hidden must equal heads * head_dim")
+    heads = _shard(hd, tp_rank, tp_world)
+    qkv_rows = [slice(i * hd + heads.start, i * hd + heads.stop) for i in range(3)]
+    mlp_rows = _shard(cfg.mlp_hidden, tp_rank, tp_world)
+
+    def stream():
+        w = init.randn(3 * hd, cfg.hidden)
+        b = init.randn(3 * hd)
+        q, ws = ops.quantize_weight(w)
+        del w
+        ws = ws.reshape(-1)
+        qkv = Int8Params(torch.cat([q[r] for r in qkv_rows]).contiguous(),
+                         torch.cat([ws[r] for r in qkv_rows]).contiguous(),
+                         torch.cat([b[r] for r in qkv_rows]).contiguous())
+        qn = 1.0 + init.randn(cfg.head_dim, std=0.05).float()
+        kn = 1.0 + init.randn(cfg.head_dim, std=0.05).float()
+        local_heads = cfg.heads // tp_world
+        norm = torch.cat([qn.repeat(local_heads), kn.repeat(local_heads)]).to(torch.bfloat16)
+        out = init.linear(cfg.hidden, hd, cols=heads)
+        up = init.linear(cfg.mlp_hidden, cfg.hidden, rows=mlp_rows)
+        down = init.linear(cfg.hidden, cfg.mlp_hidden, cols=mlp_rows)
+        return StreamParams(qkv, norm.contiguous(), out, up, down)
+
+    blocks = []
+    for _ in range(cfg.blocks):
+        img = stream()
+        txt = stream()
+        blocks.append(BlockParams(img, txt))
+    mod_rows = _shard(cfg.blocks * cfg.mod_dim, tp_rank, tp_world)
+    mod_img = init.linear(cfg.blocks * cfg.mod_dim, cfg.hidden, rows=mod_rows)
+    mod_txt = init.linear(cfg.blocks * cfg.mod_dim, cfg.hidden, rows=mod_rows)
+    return MMDiTParams(
+        cfg=cfg, tp_rank=tp_rank, tp_world=tp_world, blocks=blocks, mod_img=mod_img,
+        mod_txt=mod_txt, time1=init.linear(cfg.hidden, cfg.time_dim),
+        time2=init.linear(cfg.hidden, cfg.hidden), img_in=init.linear(cfg.hidden, cfg.in_channels),
+        txt_norm=(1.0 + init.randn(cfg.context_dim, std=0.05).float()).to(torch.bfloat16),
+        txt_in=init.linear(cfg.hidden, cfg.context_dim),
+        norm_out=init.linear(2 * cfg.hidden, cfg.hidden),
+        proj_out=init.linear(cfg.in_channels, cfg.hidden))
+
+
+# --------------------------------------------------------------------------
+# native operators
+# --------------------------------------------------------------------------
+class NativeOps:
+    """The model's numeric steps on libw8a8 (imagine_b200.linear); attention
+    is torch's scaled-dot-product attention in bf16 (the library has no
+    attention kernel; the reference's own model calls its attention
+    routes the same way, dit.rs:506-515)."""
+
+    def __init__(self, attention_backends=None):
+        from torch.nn.attention import SDPBackend
+
+        from . import linear
+
+        self.L = linear
+        # cuDNN's fused attention first: on B200 it runs the joint attention
+        # of the 1600x896 step (B 2, 24 heads, 5856 tokens) in 0.58 ms
+        # (1.46 PFLOP/s) against 2.13 ms for torch's flash kernel
+        self.attention_backends = attention_backends or [
+            SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION,
+            SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
+
+    def quantize_weight(self, w):
+        return self.L.quantize_weight(w)
+
+    def linear(self, x, p: Int8Params, act=None, residual=None, gate=None, input_norm=None,
+               eps=1e-6):
+        if input_norm is not None:
+            return self.L.int8_linear(x, p.w, p.ws, p.b, torch.bfloat16, input_act="rms_norm",
+                                      input_act_weight=input_norm, input_act_eps=eps,
+                                      output_act=act)
+        return self.L.int8_linear(x, p.w, p.ws, p.b, torch.bfloat16, residual=residual,
+                                  residual_scale=gate, output_act=act)
+
+    def adaln_linear(self, x, scale, shift, p: Int8Params, act=None, eps=1e-6):
+        return self.L.adaln_int8_linear(x, scale, shift, p.w, p.ws, p.b, torch.bfloat16, eps=eps,
+                                        output_act=act)
+
+    def adaln_qkv_rope(self, x, scale, shift, p: Int8Params, norm_w, freqs, rope_cols, eps=1e-6):
+        return self.L.int8_linear_rms_rope(x, p.w, p.ws, p.b, norm_w, freqs, eps, rope_cols,
+                                           modulation=(scale, shift, eps, False))
+
+    def row_absmax(self, x):
+        return self.L.row_absmax(x).reshape(-1).contiguous()
+
+    def quantize_given_absmax(self, x, amax):
+        q, s = self.L.quantize_int8_rowwise_given_absmax(x, amax)
+        return q, s.reshape(-1)
+
+    def gemm_s32(self, q, w):
+        return self.L.int8_gemm_s32(q, w)
+
+    def dequant(self, acc, xs, p: Int8Params, residual=None, gate=None, lead=None):
+        # the eager dequant order: the one int8_linear (the 1-GPU path) uses
+        return self.L.dequantize_int8_linear(acc, xs, p.ws, p.b, torch.bfloat16, dequant="eager",
+                                             residual=residual, residual_scale=gate, lead=lead)
+
+    def joint_attention(self, qkv_t, qkv_i, heads: int, head_dim: int):
+        """Joint attention of [text; image] tokens.  qkv_*: [B, S, 3 * heads *
+        head_dim] (q, k, v columns).  Returns the text and image outputs
+        [B, S, heads * head_dim]."""
+        b, st, _ = qkv_t.shape
+        c = heads * head_dim
+        joint = torch.cat([qkv_t, qkv_i], dim=1)
+        q, k, v = (joint[..., i * c:(i + 1) * c].unflatten(-1, (heads, head_dim)).transpose(1, 2)
+                   for i in range(3))
+        if self.attention_backends:
+            from torch.nn.attention import sdpa_kernel
+
+            with sdpa_kernel(self.attention_backends, set_priority=True):
+                o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+        else:
+            o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+        o = o.transpose(1, 2).reshape(b, -1, c)
+        return o[:, :st], o[:, st:]
+
+    def silu(self, x):
+        return torch.nn.functional.silu(x)
+
+
+# --------------------------------------------------------------------------
+# the model
+# --------------------------------------------------------------------------
+class MMDiT:
+    """The MMDiT forward on one rank of a tensor-parallel group (``tp_group``
+    None: one GPU)."""
+
+    def __init__(self, params: MMDiTParams, ops, tp_group=None):
+        self.p = params
+        self.cfg = params.cfg
+        self.ops = ops
+        self.tp_group = tp_group
+        self.tp = params.tp_world
+        if self.tp > 1 and (tp_group is None or dist.get_world_size(tp_group) != self.tp):
+            raise ValueError("the parameters are sharded; pass their tensor-parallel group")
+        self._freqs = {}
+
+    # -- helpers -------------------------------------------------------------
+    def freqs(self, text_tokens: int, h: int, w: int, device):
+        key = (text_tokens, h, w, str(device))
+        if key not in self._freqs:
+            ids_t, ids_i = sequence_ids(text_tokens, h, w, device)
+            self._freqs[key] = (rope_freqs(ids_t, self.cfg.axes, self.cfg.theta),
+                                rope_freqs(ids_i, self.cfg.axes, self.cfg.theta))
+        return self._freqs[key]
+
+    def _row_parallel(self, x, p: Int8Params, residual, gate):
+        """x [B, S, K/tp] (this rank's K-slice) -> [B, S, N] with the gated
+        residual, equal to the single-GPU linear bit for bit."""
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, x.shape[-1])
+        if self.tp == 1:
+            return self.ops.linear(x2.reshape(*lead, -1), p, residual=residual, gate=gate)
+        amax = self.ops.row_absmax(x2)
+        dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.tp_group)
+        q, xs = self.ops.quantize_given_absmax(x2, amax)
+        acc = self.ops.gemm_s32(q, p.w)
+        dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.tp_group)
+        return self.ops.dequant(acc, xs, p, residual=residual, gate=gate, lead=lead)
+
+    def _gather_cols(self, y):
+        """All-gather a [B, N/tp] row-shard of the modulation output."""
+        if self.tp == 1:
+            return y
+        parts = [torch.empty_like(y) for _ in range(self.tp)]
+        dist.all_gather(parts, y.contiguous(), group=self.tp_group)
+        return torch.cat(parts, dim=-1)
+
+    # -- one joint block -------------------------------------------------------
+    def block(self, bp: BlockParams, img, txt, mod_i, mod_t, freqs_t, freqs_i):
+        cfg = self.cfg
+        b = img.shape[0]
+        hl = cfg.heads // self.tp
+        c = hl * cfg.head_dim
+        sh1i, sc1i, g1i, sh2i, sc2i, g2i = mod_i.reshape(b, 6, 1, cfg.hidden).unbind(1)
+        sh1t, sc1t, g1t, sh2t, sc2t, g2t = mod_t.reshape(b, 6, 1, cfg.hidden).unbind(1)
+        ops = self.ops
+        qkv_i = ops.adaln_qkv_rope(img, sc1i, sh1i, bp.img.qkv, bp.img.qk_norm, freqs_i, 2 * c,
+                                   cfg.eps)
+        qkv_t = ops.adaln_qkv_rope(txt, sc1t, sh1t, bp.txt.qkv, bp.txt.qk_norm, freqs_t, 2 * c,
+                                   cfg.eps)
+        o_t, o_i = ops.joint_attention(qkv_t.reshape(b, -1, 3 * c), qkv_i.reshape(b, -1, 3 * c),
+                                       hl, cfg.head_dim)
+        img = self._row_parallel(o_i, bp.img.out, img, g1i)
+        txt = self._row_parallel(o_t, bp.txt.out, txt, g1t)
+        h_i = ops.adaln_linear(img, sc2i, sh2i, bp.img.up, act="gelu_tanh", eps=cfg.eps)
+        img = self._row_parallel(h_i, bp.img.down, img, g2i)
+        h_t = ops.adaln_linear(txt, sc2t, sh2t, bp.txt.up, act="gelu_tanh", eps=cfg.eps)
+        txt = self._row_parallel(h_t, bp.txt.down, txt, g2t)
+        return img, txt
+
+    # -- the forward -------------------------------------------------------------
+    def embed(self, latent, t, context):
+        """Input projections and the modulation rows of every block."""
+        cfg, p, ops = self.cfg, self.p, self.ops
+        b, _, h, w = latent.shape
+        img = patchify(latent.to(torch.bfloat16), cfg.patch)
+        img = ops.linear(img, p.img_in)
+        txt = ops.linear(context.to(torch.bfloat16), p.txt_in, input_norm=p.txt_norm, eps=cfg.eps)
+        emb = timestep_embedding(round_timesteps(t).float(), cfg.time_dim).to(torch.bfloat16)
+        temb = ops.linear(ops.silu(ops.linear(emb, p.time1)), p.time2)
+        s = ops.silu(temb)
+        mods_i = self._gather_cols(ops.linear(s, p.mod_img))
+        mods_t = self._gather_cols(ops.linear(s, p.mod_txt))
+        return img, txt, s, mods_i, mods_t
+
+    def forward(self, latent: torch.Tensor, t: torch.Tensor, context: torch.Tensor,
+                blocks: Optional[int] = None) -> torch.Tensor:
+        """latent [B, C, H, W], t [B] (sigma in [0, 1]), context [B, S_txt,
+        context_dim] -> the velocity prediction [B, C, H, W] (bf16)."""
+        cfg, p, ops = self.cfg, self.p, self.ops
+        b, c, h, w = latent.shape
+        img, txt, s, mods_i, mods_t = self.embed(latent, t, context)
+        freqs_t, freqs_i = self.freqs(txt.shape[1], h // cfg.patch, w // cfg.patch, latent.device)
+        n = len(p.blocks) if blocks is None else blocks
+        md = cfg.mod_dim
+        for i, bp in enumerate(p.blocks[:n]):
+            img, txt = self.block(bp, img, txt, mods_i[:, i * md:(i + 1) * md],
+                                  mods_t[:, i * md:(i + 1) * md], freqs_t, freqs_i)
+        scale, shift = ops.linear(s, p.norm_out).reshape(b, 2, 1, cfg.hidden).unbind(1)
+        out = ops.adaln_linear(img, scale, shift, p.proj_out, eps=cfg.eps)
+        return unpatchify(out, cfg.patch, c, h, w)
+
+
+# --------------------------------------------------------------------------
+# placement and the denoising step
+# --------------------------------------------------------------------------
+@dataclass
+class Placement:
+    """Where a CFG step runs: ``world`` ranks, ``branches`` CFG branches per
+    rank (2: both batched on each rank; 1: one branch per rank group), the
+    tensor-parallel width and this rank's branch and TP rank."""
+    world: int
+    rank: int
+    tp: int
+    branch: int
+    tp_rank: int
+
+    @property
+    def batched(self) -> bool:
+        return self.world == 1
+
+    def describe(self) -> str:
+        if self.world == 1:
+            return "1 GPU: both CFG branches batched (B = 2)"
+        if self.tp == 1:
+            return f"{self.world} GPUs: one CFG branch per GPU, predictions all-gathered"
+        return (f"{self.world} GPUs: CFG branch per group of {self.tp} GPUs x {self.tp}-way tensor "
+                "parallel (column-parallel QKV / MLP-up, row-parallel out / MLP-down with int32 "
+                "all-reduce), predictions all-gathered")
+
+
+def placement(world: int, rank: int) -> Placement:
+    """1 rank: both branches batched.  W >= 2 (even): ranks [0, W/2) run the
+    conditional branch, [W/2, W) the unconditional one, each branch over W/2
+    tensor-parallel ranks."""
+    if world == 1:
+        return Placement(1, 0, 1, 0, 0)
+    if world % 2:
+        raise ValueError("CFG placement needs an even number of ranks")
+    tp = world // 2
+    return Placement(world, rank, tp, rank // tp, rank % tp)
+
+
+class ProcessGroups:
+    """The tensor-parallel group of this rank's branch and the CFG pair group
+    (r, r + W/2); every rank creates every group in the same order."""
+
+    def __init__(self, pl: Placement, backend=None):
+        self.tp_group = None
+        self.cfg_group = None
+        if pl.world == 1:
+            return
+        for br in range(2):
+            ranks = list(range(br * pl.tp, (br + 1) * pl.tp))
+            g = dist.new_group(ranks, backend=backend) if pl.tp > 1 else None
+            if br == pl.branch:
+                self.tp_group = g
+        for r in range(pl.tp):
+            g = dist.new_group([r, r + pl.tp], backend=backend)
+            if r == pl.tp_rank:
+                self.cfg_group = g
+
+
+def cfg_model(dit: MMDiT, pl: Placement, groups: ProcessGroups, context_cond: torch.Tensor,
+              context_uncond: torch.Tensor):
+    """The sampler's ``Model`` (imagine_b200.sampler): ``model(x, timestep,
+    with_uncond)`` -> (conditional, unconditional) predictions.  On one GPU
+    the branches run as one batch of 2 (the reference's batched CFG,
+    inference/src/models/qwen_image21/cfg.rs:136-207); on 2+ GPUs each rank
+    group runs its branch and the pair all-gather exchanges the outputs."""
+
+    def model(x, timestep, with_uncond):
+        xb = x.to(torch.bfloat16)
+        if not with_uncond:
+            return dit.forward(xb, timestep, context_cond), None
+        if pl.batched:
+            out = dit.forward(torch.cat([xb, xb]), torch.cat([timestep, timestep]),
+                              torch.cat([context_cond, context_uncond]))
+            n = x.shape[0]
+            return out[:n], out[n:]
+        ctx = context_cond if pl.branch == 0 else context_uncond
+        mine = dit.forward(xb, timestep, ctx).contiguous()
+        both = [torch.empty_like(mine), torch.empty_like(mine)]
+        dist.all_gather(both, mine, group=groups.cfg_group)
+        return both[0], both[1]
+
+    return model
+
+
+class DenoiseLoop:
+    """The Euler CFG loop of the sampler (inference/src/models/qwen_image21/
+    sampling.rs:231-277) around ``cfg_model``, one step at a time:
+    ``step(i)`` runs the model on both branches and the fused sampler step
+    (imagine_b200.sampler) on the latent ``x``."""
+
+    def __init__(self, model, x: torch.Tensor, steps: int = 40, cfg_scale: float = 2.5,
+                 shift: float = 0.69):
+        from . import sampler as S
+
+        self.S = S
+        self.model = model
+        self.x = x.to(torch.float32).contiguous().clone()
+        self.cfg_scale = cfg_scale
+        sigmas = S.FluxSampling(shift).simple(steps).to(self.x.device)
+        self.rows = [r for _, _, r in S.euler_coefficients(sigmas)]
+        self.s_in = torch.ones(self.x.shape[0], dtype=torch.float32, device=self.x.device)
+
+    def step(self, i: int) -> None:
+        row = self.rows[i % len(self.rows)]
+        out_c, out_u = self.model(self.x, row[0].mul(self.s_in), True)
+        self.S.sampler_step(self.x, out_c.contiguous(), out_u.contiguous(), row,
+                            self.S.N.STEP_EULER, cfg_scale=self.cfg_scale)

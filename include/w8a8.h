@@ -350,14 +350,18 @@ int w8a8_gemm_dequant_tiled(const int8_t* q, int64_t ldq, const int8_t* tiles, c
  * w8a8_gemm_dequant_splitk minus the workspace, returns the same results, and
  * allocates nothing: its scratch is an array of
  * W8A8_SPLITK_STATIC_SCRATCH_BYTES (8 MiB) built into the library, one per
- * device.  Shapes whose scratch (w8a8_gemm_splitk_workspace_bytes(M, N):
- * 64 KiB per 128 x 128 output tile plus counters, e.g. up to 512 x 3072 or
- * 256 x 6144) does not fit are rejected with W8A8_ERR_VALUE and a message.  The first call on a
- * device, with that device current, looks the array up
- * (cudaGetSymbolAddress); make it before any stream capture.  Each call clears
- * the part of the array it uses on `stream` before the GEMM.  All calls share
- * the array: calls that overlap on the GPU (other streams, other threads)
- * race with each other. */
+ * device.  A GEMM that does not split (split_k = 1, or split_k = 0 on a shape
+ * the automatic policy runs whole) uses no scratch and runs at any size.  A
+ * GEMM that splits and whose scratch (64 KiB per 128 x 128 output tile plus
+ * counters, e.g. up to 512 x 3072 or 256 x 6144) does not fit is rejected
+ * with W8A8_ERR_VALUE and a message.  The first call on a device, with that
+ * device current, looks the array up (cudaGetSymbolAddress) and caches the
+ * address; make it before any stream capture, and do not call this entry
+ * point again on a device after cudaDeviceReset in the same process (the
+ * cached address is stale then).  A splitting call clears the part of the
+ * array it uses on `stream` before the GEMM.  All calls share the array:
+ * calls that overlap on the GPU (other streams, other threads) race with
+ * each other. */
 #define W8A8_SPLITK_STATIC_SCRATCH_BYTES (8ll << 20)
 int w8a8_gemm_dequant_splitk_static(const int8_t* q, int64_t ldq, const int8_t* w, int64_t ldw,
                                     const float* xs, const w8a8_epilogue_t* epi, void* out,

@@ -163,12 +163,15 @@ def int8_accumulate(a: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
 
     The reference pads K and N to multiples of 8 and calls ``_int_mm``; zero
     padding does not change an integer sum, so the result is the exact product
-    (|sum| < 2^31 for K < 2^17).
+    (|sum| < 2^31 for K < 2^17).  Like the reference, no copy is made when K
+    and N are already aligned: ``_int_mm`` then reads the transposed view of W.
     """
     m, k = a.shape
     n = w.shape[0]
     if m == 0 or n == 0 or k == 0:
         return torch.zeros((m, n), dtype=torch.int32)
+    if k % 8 == 0 and n % 8 == 0 and m > 16:
+        return torch._int_mm(a.contiguous(), w.t())
     pk = (k + 7) // 8 * 8
     pn = (n + 7) // 8 * 8
     a_p = torch.zeros((max(m, 17), pk), dtype=torch.int8)

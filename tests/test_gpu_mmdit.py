@@ -1,0 +1,140 @@
+"""The MMDiT harness on libw8a8 (imagine_b200.mmdit.NativeOps) against the
+same model code over the CPU oracle, and the full-size block and step.
+
+Tolerance: the native model and the oracle differ by bf16 rounding of the
+fused steps (the AdaLN modulation and RMSNorm + RoPE are computed in fp32
+inside the kernels, the oracle rounds every eager operation to bf16),
+bf16 attention against fp32 softmax attention, and the +-1 code flips such
+differences cause in the next quantiser.  The bar: the RMS of the difference
+is at most 2% of the compared tensor's RMS for one block (3% for the whole
+two-block forward, whose final projection sums the block's differences), and
+99% of the elements differ by at most 4x that bound (no heavy tail)."""
+import pytest
+import torch
+
+from imagine_b200 import mmdit as M
+
+pytestmark = pytest.mark.gpu
+
+SMALL = M.MMDiTConfig(blocks=2)  # full width, two blocks
+
+
+def cuda():
+    return torch.device("cuda", 0)
+
+
+def _close(got, want, rel=0.02, tail=4.0):
+    got = got.float().cpu()
+    want = want.float().cpu()
+    rms = want.pow(2).mean().sqrt().item()
+    diff = (got - want).abs().flatten()
+    err = diff.pow(2).mean().sqrt().item()
+    p99 = diff.kthvalue(max(1, int(0.99 * diff.numel()))).values.item()
+    print(f"rms {rms:.4g}: RMS difference {err / rms:.4%}, 99th percentile {p99 / rms:.4%}")
+    assert err <= rel * rms, f"RMS difference {err:.4g} > {rel} x RMS {rms:.4g}"
+    assert p99 <= tail * rel * rms, f"99th percentile difference {p99:.4g} > {tail * rel} x RMS"
+
+
+def _inputs(cfg, b, h, w, st, seed=3):
+    g = torch.Generator().manual_seed(seed)
+    lat = torch.randn(b, cfg.latent_channels, h, w, generator=g).to(torch.bfloat16)
+    ctx = torch.randn(b, st, cfg.context_dim, generator=g).to(torch.bfloat16)
+    t = torch.rand(b, generator=g)
+    return lat, ctx, t
+
+
+@pytest.fixture(scope="module")
+def small_models():
+    from tests._mmdit_oracle import OracleOps
+
+    native = M.NativeOps()
+    params = M.random_params(SMALL, native, cuda(), seed=11)
+    return M.MMDiT(params, native), M.MMDiT(params.to("cpu"), OracleOps())
+
+
+def test_block_matches_oracle(small_models):
+    """One joint block at full width (B = 2, 8 x 16 image patches + 32 text
+    tokens): the image and text streams against the oracle block."""
+    nat, orc = small_models
+    lat, ctx, t = _inputs(SMALL, 2, 16, 32, 32)
+    img, txt, s, mi, mt = nat.embed(lat.to(cuda()), t.to(cuda()), ctx.to(cuda()))
+    img_o, txt_o, s_o, mi_o, mt_o = orc.embed(lat, t, ctx)
+    _close(img, img_o)
+    _close(txt, txt_o)
+    _close(mi, mi_o)
+    # the block on identical inputs (the native embedding fed to both)
+    ft, fi = nat.freqs(32, 8, 16, cuda())
+    md = SMALL.mod_dim
+    bi, bt = nat.block(nat.p.blocks[0], img, txt, mi[:, :md], mt[:, :md], ft, fi)
+    oi, ot = orc.block(orc.p.blocks[0], img.cpu(), txt.cpu(), mi[:, :md].cpu(), mt[:, :md].cpu(),
+                       ft.cpu(), fi.cpu())
+    _close(bi, oi)
+    _close(bt, ot)
+
+
+def test_forward_matches_oracle(small_models):
+    """The whole two-block forward (embedding, blocks, final AdaLN +
+    projection)."""
+    nat, orc = small_models
+    lat, ctx, t = _inputs(SMALL, 2, 16, 32, 32, seed=4)
+    got = nat.forward(lat.to(cuda()), t.to(cuda()), ctx.to(cuda()))
+    want = orc.forward(lat, t, ctx)
+    _close(got, want, rel=0.03)
+
+
+def test_fused_qkv_rope_equals_unfused_native():
+    """The AdaLN-fused QKV with the RMSNorm + RoPE epilogue equals the
+    stand-alone modulated linear followed by the stand-alone rms_rope kernel
+    within one bf16 step per rotated pair (the epilogue normalises the fp32
+    accumulator before its bf16 rounding)."""
+    import imagine_b200 as W
+
+    g = torch.Generator().manual_seed(9)
+    b, s, k, heads = 2, 96, 3072, 24
+    x = torch.randn(b, s, k, generator=g).to(torch.bfloat16).to(cuda())
+    sc = (torch.randn(b, 1, k, generator=g) * 0.3).to(torch.bfloat16).to(cuda())
+    sh = (torch.randn(b, 1, k, generator=g) * 0.3).to(torch.bfloat16).to(cuda())
+    wq, ws = W.quantize_weight((torch.randn(3 * k, k, generator=g) * 0.02).to(torch.bfloat16).to(cuda()))
+    bias = (torch.randn(3 * k, generator=g) * 0.02).to(torch.bfloat16).to(cuda())
+    nw = (1 + 0.05 * torch.randn(2 * k, generator=g)).to(torch.bfloat16).to(cuda())
+    ids = torch.stack([torch.arange(s, dtype=torch.float32)] * 3, -1)
+    f = M.rope_freqs(ids).to(cuda())
+    fused = W.int8_linear_rms_rope(x, wq, ws, bias, nw, f, 1e-6, 2 * k,
+                                   modulation=(sc, sh, 1e-6, False))
+    y = W.adaln_int8_linear(x, sc, sh, wq, ws, bias, torch.bfloat16)
+    qk = y[..., : 2 * k].reshape(b, s, 2 * heads, 128)
+    qo, ko = W.rms_rope(qk[:, :, :heads].contiguous(), qk[:, :, heads:].contiguous(), f,
+                        nw[:128], nw[k:k + 128])
+    ref = torch.cat([qo.reshape(b, s, k), ko.reshape(b, s, k), y[..., 2 * k:]], -1)
+    assert torch.equal(fused[..., 2 * k:].view(torch.int16), ref[..., 2 * k:].view(torch.int16))
+    _close(fused[..., : 2 * k], ref[..., : 2 * k], rel=0.01)
+
+
+def test_full_size_block_and_step():
+    """The BASELINE block (hidden 3072, 24 x 128, GELU 12288; B = 2, 5600
+    image + 256 text tokens): one joint block keeps finite, non-degenerate
+    streams, and one CFG Euler step of a 2-block model moves the latent."""
+    cfg = M.MMDiTConfig(blocks=2)
+    nat = M.NativeOps()
+    model = M.MMDiT(M.random_params(cfg, nat, cuda(), seed=2), nat)
+    lat, ctx, t = _inputs(cfg, 1, 112, 200, 256, seed=6)
+    lat, ctx, t = lat.to(cuda()), ctx.to(cuda()), t.to(cuda())
+    lat2, ctx2 = torch.cat([lat, lat]), torch.cat([ctx, -ctx])
+    img, txt, s, mi, mt = model.embed(lat2, torch.cat([t, t]), ctx2)
+    assert img.shape == (2, 5600, 3072) and txt.shape == (2, 256, 3072)
+    ft, fi = model.freqs(256, 56, 100, cuda())
+    md = cfg.mod_dim
+    bi, bt = model.block(model.p.blocks[0], img, txt, mi[:, :md], mt[:, :md], ft, fi)
+    for a, b in ((bi, img), (bt, txt)):
+        assert torch.isfinite(a.float()).all()
+        assert (a - b).float().abs().mean() > 1e-3
+    loop = M.DenoiseLoop(M.cfg_model(model, M.placement(1, 0), M.ProcessGroups(M.placement(1, 0)),
+                                     ctx, -ctx), lat.float(), steps=40)
+    x0 = loop.x.clone()
+    loop.step(0)
+    torch.cuda.synchronize()
+    assert torch.isfinite(loop.x).all()
+    assert (loop.x - x0).abs().mean() > 1e-4
+    import imagine_b200 as W
+
+    assert W.device_error() == 0
