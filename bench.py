@@ -310,34 +310,15 @@ DIT_TEXT = 256
 DIT_LATENT = (16, 112, 200)
 
 
-def run_dit(args, rank, world, local_rank):
-    from imagine_b200 import mmdit as MD
-
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    cfg = MD.MMDiTConfig(blocks=args.dit_blocks)
-    pl = MD.placement(world, rank)
-    groups = MD.ProcessGroups(pl)
-    ops = MD.NativeOps()
-    t0 = time.perf_counter()
-    params = MD.random_params(cfg, ops, dev, seed=1234, tp_rank=pl.tp_rank, tp_world=pl.tp)
-    torch.cuda.synchronize()
-    init_s = time.perf_counter() - t0
-    dit = MD.MMDiT(params, ops, groups.tp_group)
-    g = torch.Generator().manual_seed(77)
-    lat = torch.randn(1, *DIT_LATENT, generator=g)
-    ctx_c = torch.randn(1, DIT_TEXT, cfg.context_dim, generator=g).to(torch.bfloat16).to(dev)
-    ctx_u = torch.randn(1, DIT_TEXT, cfg.context_dim, generator=g).to(torch.bfloat16).to(dev)
-    loop = MD.DenoiseLoop(MD.cfg_model(dit, pl, groups, ctx_c, ctx_u), lat.to(dev), steps=40,
-                          cfg_scale=2.5)
-    warm = max(3, args.dit_warmup)
+def _time_loop(loop, warm, steps, rank, world, local_rank, dev, clocks=False):
+    """Max over ranks of the device time of ``steps`` denoising steps after
+    ``warm`` untimed ones (barrier + synchronize on both sides)."""
     for i in range(warm):
         loop.step(i)
     torch.cuda.synchronize()
-    steps = args.dit_steps
     stream = torch.cuda.current_stream(dev)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-    sampler = ClockSampler(local_rank) if rank == 0 else None
+    sampler = ClockSampler(local_rank) if rank == 0 and clocks else None
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -351,13 +332,53 @@ def run_dit(args, rank, world, local_rank):
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    clocks = sampler.stop() if sampler else None
+    samples = sampler.stop() if sampler else None
     ms = ev[0].elapsed_time(ev[1]) / steps
     finite = bool(torch.isfinite(loop.x).all())
     if world > 1:
         t = torch.tensor([ms, 0.0 if finite else 1.0], dtype=torch.float64, device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms, finite = float(t[0]), float(t[1]) == 0.0
+    return ms, finite, samples
+
+
+def run_dit(args, rank, world, local_rank):
+    from imagine_b200 import mmdit as MD
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = MD.MMDiTConfig(blocks=args.dit_blocks)
+    pl = MD.placement(world, rank)
+    groups = MD.ProcessGroups(pl)
+    ops = MD.NativeOps()
+    t0 = time.perf_counter()
+    params = MD.random_params(cfg, ops, dev, seed=1234, tp_rank=pl.tp_rank, tp_world=pl.tp)
+    torch.cuda.synchronize()
+    init_s = time.perf_counter() - t0
+    g = torch.Generator().manual_seed(77)
+    lat = torch.randn(1, *DIT_LATENT, generator=g).to(dev)
+    ctx_c = torch.randn(1, DIT_TEXT, cfg.context_dim, generator=g).to(torch.bfloat16).to(dev)
+    ctx_u = torch.randn(1, DIT_TEXT, cfg.context_dim, generator=g).to(torch.bfloat16).to(dev)
+    warm = max(3, args.dit_warmup)
+    steps = args.dit_steps
+    # the headline form: the forward captured once as a CUDA graph and
+    # replayed every step (tensor-parallel reductions through NCCL, which
+    # the graph holds)
+    dit = MD.MMDiT(params, ops, groups.tp_group)
+    cap = MD.CapturedModel(dit, pl, groups, ctx_c, ctx_u, (1, *DIT_LATENT), dev)
+    try:
+        cap.capture()
+        loop = MD.DenoiseLoop(cap, lat, steps=40, cfg_scale=2.5)
+        ms, finite, clocks = _time_loop(loop, warm, steps, rank, world, local_rank, dev, clocks=True)
+    finally:
+        cap.release()
+    # the same steps launched eagerly from Python (tensor-parallel reductions
+    # fused into the GEMMs over peer memory)
+    eager = MD.MMDiT(params, ops, groups.tp_group, fused_tp=pl.tp > 1)
+    loop = MD.DenoiseLoop(MD.cfg_model(eager, pl, groups, ctx_c, ctx_u), lat, steps=40,
+                          cfg_scale=2.5)
+    eager_ms, eager_finite, _ = _time_loop(loop, warm, steps, rank, world, local_rank, dev)
+    finite = finite and eager_finite
     import imagine_b200 as W
 
     if W.device_error() != 0:
@@ -374,6 +395,12 @@ def run_dit(args, rank, world, local_rank):
             "workload": "1600x896 (latent 16x112x200 -> 5600 image tokens) + 256 text tokens, "
                         "CFG batch 2 (scale 2.5), Euler flow sampler, 40-step schedule",
             "placement": pl.describe(),
+            "launch": "the forward of both branches captured once as a CUDA graph, replayed per "
+                      "step (with its NCCL collectives); the sampler step a separate kernel",
+            "eager_ms": eager_ms,
+            "eager": "the same step launched from Python per kernel" + (
+                "" if pl.tp == 1 else ", row-parallel reductions fused into the GEMM "
+                "(peer-memory reduce-scatter)"),
             "attention": "torch scaled_dot_product_attention, bf16 (cuDNN backend first)",
             "linear_tops_per_step": lin_ops / 1e12, "attention_tflop_per_step": attn_flops / 1e12,
             "achieved_tops": (lin_ops + attn_flops) / (ms * 1e-3) / 1e12,

@@ -391,6 +391,52 @@ class NativeOps:
     def silu(self, x):
         return torch.nn.functional.silu(x)
 
+    def row_parallel_fused(self, q, xs, p: Int8Params, group, residual=None, gate=None, lead=None):
+        """The row-parallel linear's int32 GEMM with the reduce-scatter in its
+        epilogue (w8a8_gemm_s32_reduce_scatter: each finished partial chunk
+        goes to the rank that owns its rows over NVLink), then the finish
+        (w8a8_reduce_scatter_finish: the owner sums its rows, applies the
+        dequant + bias + gated-residual epilogue and hands its rows to the
+        others).  Equals all-reduce(int32) followed by ``dequant`` bit for
+        bit."""
+        import ctypes
+
+        from . import _native as N
+        from .tensor_parallel import _PeerBuffers
+
+        L = self.L
+        dev = q.device
+        key = (id(group), dev.index)
+        peers = getattr(self, "_peers", None)
+        if peers is None:
+            peers = self._peers = {}
+        pb = peers.get(key)
+        if pb is None:
+            pb = peers[key] = _PeerBuffers(group, dev)
+        m, k = q.shape
+        n = p.w.shape[0]
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        recvs = pb._mapped("_rs_recv", int(N.LIB.w8a8_reduce_scatter_recv_bytes(m, n, world)), dev)
+        stages = pb._mapped("_rs_stage", m * n * 2, dev)
+        lead = tuple(lead) if lead is not None else (m,)
+        r = rs = None
+        rs_rows = 0
+        if residual is not None:
+            r = residual.reshape(m, n).contiguous()
+            rs, rs_rows = L._residual_scale(gate, lead, n, torch.bfloat16, dev)
+        b = p.b.contiguous() if p.b is not None else None
+        ep = L._epilogue(p.ws, b, r, rs, "eager", None, n, n, rs_rows)
+        y = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        epoch = pb.next_epoch()
+        stream = L._stream(dev)
+        N.check(N.LIB.w8a8_peer_barrier(pb.flag_ptrs, rank, world, epoch, stream))
+        N.check(N.LIB.w8a8_gemm_s32_reduce_scatter(L._vp(q), k, L._vp(p.w), k, m, n, k, recvs,
+                                                   pb.flag_ptrs, rank, world, epoch, None, stream))
+        N.check(N.LIB.w8a8_reduce_scatter_finish(L._vp(xs), ctypes.byref(ep), L._vp(y), N.BF16, n,
+                                                 m, n, recvs, stages, pb.flag_ptrs, rank, world,
+                                                 epoch, stream))
+        return y.reshape(*lead, n)
+
 
 # --------------------------------------------------------------------------
 # the model
@@ -399,12 +445,15 @@ class MMDiT:
     """The MMDiT forward on one rank of a tensor-parallel group (``tp_group``
     None: one GPU)."""
 
-    def __init__(self, params: MMDiTParams, ops, tp_group=None):
+    def __init__(self, params: MMDiTParams, ops, tp_group=None, fused_tp: bool = False):
         self.p = params
         self.cfg = params.cfg
         self.ops = ops
         self.tp_group = tp_group
         self.tp = params.tp_world
+        # row-parallel reduction fused into the GEMM (peer memory) instead of
+        # an NCCL all-reduce of the int32 partials
+        self.fused_tp = fused_tp and self.tp > 1 and hasattr(ops, "row_parallel_fused")
         if self.tp > 1 and (tp_group is None or dist.get_world_size(tp_group) != self.tp):
             raise ValueError("the parameters are sharded; pass their tensor-parallel group")
         self._freqs = {}
@@ -428,6 +477,9 @@ class MMDiT:
         amax = self.ops.row_absmax(x2)
         dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.tp_group)
         q, xs = self.ops.quantize_given_absmax(x2, amax)
+        if self.fused_tp:
+            return self.ops.row_parallel_fused(q, xs, p, self.tp_group, residual=residual,
+                                               gate=gate, lead=lead)
         acc = self.ops.gemm_s32(q, p.w)
         dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=self.tp_group)
         return self.ops.dequant(acc, xs, p, residual=residual, gate=gate, lead=lead)
@@ -580,6 +632,56 @@ def cfg_model(dit: MMDiT, pl: Placement, groups: ProcessGroups, context_cond: to
         return both[0], both[1]
 
     return model
+
+
+class CapturedModel:
+    """``cfg_model`` replayed from one CUDA graph per call: the whole forward
+    of both CFG branches (every block's kernels and, across GPUs, its NCCL
+    collectives) is captured once and replayed, so a step costs one graph
+    launch on the host instead of ~40 launches per block.  Inputs are copied
+    into static buffers; the returned predictions are static buffers too,
+    valid until the next call.  The fused peer-memory reductions number their
+    exchanges on the host and cannot be replayed; a model built with
+    ``fused_tp`` is refused."""
+
+    def __init__(self, dit: MMDiT, pl: Placement, groups: ProcessGroups,
+                 context_cond: torch.Tensor, context_uncond: torch.Tensor, x_shape, device):
+        if dit.fused_tp:
+            raise ValueError("the fused tensor-parallel reductions cannot be replayed from a graph")
+        self.fn = cfg_model(dit, pl, groups, context_cond, context_uncond)
+        self.x = torch.zeros(x_shape, dtype=torch.float32, device=device)
+        self.t = torch.full((x_shape[0],), 0.5, dtype=torch.float32, device=device)
+        self.graph = None
+        self.out = None
+
+    def capture(self, warmup: int = 2) -> None:
+        side = torch.cuda.Stream(self.x.device)
+        side.wait_stream(torch.cuda.current_stream(self.x.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.fn(self.x, self.t, True)
+        torch.cuda.current_stream(self.x.device).wait_stream(side)
+        torch.cuda.synchronize(self.x.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = self.fn(self.x, self.t, True)
+        torch.cuda.synchronize(self.x.device)
+
+    def __call__(self, x, timestep, with_uncond):
+        if not with_uncond:
+            raise ValueError("the captured model runs both CFG branches")
+        if self.graph is None:
+            self.capture()
+        self.x.copy_(x)
+        self.t.copy_(timestep)
+        self.graph.replay()
+        return self.out
+
+    def release(self) -> None:
+        """Drop the graph (and the collectives it holds) before the process
+        group is destroyed."""
+        self.graph = None
+        self.out = None
 
 
 class DenoiseLoop:

@@ -96,7 +96,11 @@ def test_fused_qkv_rope_equals_unfused_native():
     sh = (torch.randn(b, 1, k, generator=g) * 0.3).to(torch.bfloat16).to(cuda())
     wq, ws = W.quantize_weight((torch.randn(3 * k, k, generator=g) * 0.02).to(torch.bfloat16).to(cuda()))
     bias = (torch.randn(3 * k, generator=g) * 0.02).to(torch.bfloat16).to(cuda())
-    nw = (1 + 0.05 * torch.randn(2 * k, generator=g)).to(torch.bfloat16).to(cuda())
+    # one RMSNorm weight shared by the q heads, one by the k heads, laid out
+    # per column as the model's fused QKV weight holds them
+    qn = 1 + 0.05 * torch.randn(128, generator=g)
+    kn = 1 + 0.05 * torch.randn(128, generator=g)
+    nw = torch.cat([qn.repeat(heads), kn.repeat(heads)]).to(torch.bfloat16).to(cuda())
     ids = torch.stack([torch.arange(s, dtype=torch.float32)] * 3, -1)
     f = M.rope_freqs(ids).to(cuda())
     fused = W.int8_linear_rms_rope(x, wq, ws, bias, nw, f, 1e-6, 2 * k,
@@ -138,3 +142,27 @@ def test_full_size_block_and_step():
     import imagine_b200 as W
 
     assert W.device_error() == 0
+
+
+def test_captured_step_equals_eager():
+    """The forward replayed from one CUDA graph equals the eagerly launched
+    forward bit for bit, on two calls with different latents and timesteps
+    (the second replay reads the static inputs the first one left)."""
+    cfg = M.MMDiTConfig(blocks=2)
+    nat = M.NativeOps()
+    model = M.MMDiT(M.random_params(cfg, nat, cuda(), seed=8), nat)
+    lat, ctx, _ = _inputs(cfg, 1, 16, 32, 32, seed=12)
+    ctx_c, ctx_u = ctx.to(cuda()), (-ctx).to(cuda())
+    pl = M.placement(1, 0)
+    groups = M.ProcessGroups(pl)
+    eager = M.cfg_model(model, pl, groups, ctx_c, ctx_u)
+    cap = M.CapturedModel(model, pl, groups, ctx_c, ctx_u, tuple(lat.shape), cuda())
+    g = torch.Generator().manual_seed(13)
+    for tval in (0.9, 0.35):
+        x = torch.randn(lat.shape, generator=g).to(cuda())
+        t = torch.full((1,), tval, device=cuda())
+        ec, eu = eager(x, t, True)
+        gc, gu = cap(x, t, True)
+        assert torch.equal(gc.view(torch.int16), ec.view(torch.int16))
+        assert torch.equal(gu.view(torch.int16), eu.view(torch.int16))
+    cap.release()
