@@ -310,6 +310,80 @@ DIT_TEXT = 256
 DIT_LATENT = (16, 112, 200)
 
 
+def run_tp_linears(args, rank, world, local_rank):
+    """The tensor-parallel forms of the MMDiT's linears across all ranks
+    (imagine_b200.tensor_parallel): MLP-up 5600 x 3072 -> 12288 + GELU
+    column-parallel (N split; every rank ends with the whole output) and
+    MLP-down 5600 x 12288 -> 3072 row-parallel (K split; exact int32 partial
+    sums reduced), each with the exchange fused into the GEMM over peer
+    memory and with NCCL after the GEMM.  Per form: median over timed calls
+    of the max over ranks, L2 flushed before each call; bit equality with the
+    one-GPU linear checked on every rank."""
+    import imagine_b200 as W
+    from imagine_b200 import _native as NAT
+    from imagine_b200 import tensor_parallel as TP
+
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator().manual_seed(0)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    clean = torch.ones_like(flush)
+    out = {}
+
+    def timed(layer, x, ref, steps=10, warm=4):
+        for _ in range(warm):
+            layer(x)
+        torch.cuda.synchronize()
+        times = []
+        y = None
+        for _ in range(steps):
+            flush.zero_()
+            clean.sum()
+            torch.distributed.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            y = layer(x)
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        t = torch.tensor([statistics.median(times),
+                          0.0 if torch.equal(y.view(torch.int16), ref.view(torch.int16)) else 1.0],
+                         dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return {"ms": float(t[0]), "bit_exact_vs_1gpu": float(t[1]) == 0.0}
+
+    for name, (m, k, n, act) in {"mlp_up_column_parallel": (M, K, N, "gelu_tanh"),
+                                 "mlp_down_row_parallel": (M, N, K, None)}.items():
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        wq, ws = W.quantize_weight(w)
+        ref = W.int8_linear(x, wq, ws, b, output_act=act)
+        ops = 2.0 * m * n * k
+        if act:
+            forms = {"fused_peer_stores": TP.ColumnParallelInt8Linear(wq, ws, b, output_act=act,
+                                                                      fused=True),
+                     "nccl_all_gather": TP.ColumnParallelInt8Linear(wq, ws, b, output_act=act)}
+            xin = x
+            nvlink = m * (n - n // world) * 2
+        else:
+            forms = {"fused_reduce_scatter": TP.RowParallelInt8Linear(wq, ws, b, fused=True),
+                     "nccl_all_reduce": TP.RowParallelInt8Linear(wq, ws, b)}
+            xin = forms["nccl_all_reduce"].shard_input(x)
+            rows = int(NAT.LIB.w8a8_reduce_scatter_rows(m, world))
+            nvlink = (m - min(m, rows)) * n * 4 + min(m, rows) * n * 2 * (world - 1)
+        res = {"M": m, "K": k, "N": n, "nvlink_bytes_sent_per_rank": nvlink}
+        for fname, layer in forms.items():
+            r = timed(layer, xin, ref)
+            r["TOPS"] = ops / (r["ms"] * 1e-3) / 1e12
+            res[fname] = r
+        out[name] = res
+        forms.clear()
+        del x, w, wq, ws, ref
+    if W.device_error() != 0:
+        raise RuntimeError("device error in the tensor-parallel linears")
+    return out
+
+
 def _time_loop(loop, warm, steps, rank, world, local_rank, dev, clocks=False):
     """Max over ranks of the device time of ``steps`` denoising steps after
     ``warm`` untimed ones (barrier + synchronize on both sides)."""
@@ -457,6 +531,7 @@ def main():
             "nccl", device_id=torch.device("cuda", local_rank),
             timeout=__import__("datetime").timedelta(seconds=120))
     r = run_ours(args, rank, world, local_rank)
+    tp = run_tp_linears(args, rank, world, local_rank) if world > 1 else None
     dit = None
     if args.dit_blocks > 0:
         dit = run_dit(args, rank, world, local_rank)
@@ -495,6 +570,8 @@ def main():
         "gpu_launches": 2 * args.steps,
         "clocks": r["clocks"],
     }
+    if tp is not None:
+        line["tp_linears"] = tp
     if dit is not None:
         line["dit_step"] = dit
     if not args.no_cpu_baseline:

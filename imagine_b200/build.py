@@ -90,7 +90,9 @@ def build_shim(force: bool = False) -> str:
     import torch
 
     src = os.path.join(CSRC, "kitchen_shim.cpp")
-    deps = [src, os.path.join(ROOT, "include", "w8a8.h"), LIB]
+    fwd = os.path.join(CSRC, "kitchen_forward.cpp")
+    deps = [src, fwd, os.path.join(CSRC, "kitchen_forward.h"), os.path.join(ROOT, "include", "w8a8.h"),
+            LIB]
     if not force and os.path.exists(SHIM) and os.path.getmtime(SHIM) >= _newest(deps):
         return SHIM
     tdir = os.path.dirname(torch.__file__)
@@ -102,7 +104,8 @@ def build_shim(force: bool = False) -> str:
     cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared",
            f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-fvisibility=hidden",
            "-I", tinc, "-I", os.path.join(tinc, "torch", "csrc", "api", "include"), "-I", cuda_inc,
-           src, "-o", tmp, "-L", PKG, "-l:libw8a8.so", "-L", tlib, "-lc10", "-lc10_cuda", "-ltorch_cpu",
+           src, fwd, "-o", tmp, "-L", PKG, "-l:libw8a8.so", "-L", tlib, "-lc10", "-lc10_cuda",
+           "-ltorch_cpu", "-ldl",
            f"-Wl,-rpath,$ORIGIN:{tlib}"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:

@@ -85,6 +85,7 @@ struct EpilogueParams {
   int vec_ws;              // 1 if ws is 16-byte aligned (vector loads allowed)
   int vec_bias;            // 1 if bias is 16-byte aligned
   int vec_rscale;          // 1 if rscale is 16-byte aligned
+  int vec_resid;           // 1 if residual rows are 16-byte aligned (base and ldr)
   const uint8_t* sfa;      // MXFP8: e8m0 scales of A, blocked layout
   const uint8_t* sfb;      // MXFP8: e8m0 scales of B, blocked layout
   int sf_ncb;              // MXFP8: 4-wide column blocks per scale row = ceil(K / 128)

@@ -4,12 +4,16 @@
 // point, imagine_kitchen_call(name, KitchenArg*, n, int64_t* result)
 // (inference/native/bridge.hpp:5-6, 29; inference/native/bridge.cpp:421-441),
 // whose arguments are borrowed at::Tensor* handles, integers, doubles and
-// bools.  This library exports the same three symbols (imagine_kitchen_call,
-// imagine_last_error, imagine_last_accelerator_code) and maps the kernel
-// names the crate calls onto libw8a8's plain C entry points, so the crate can
-// load it through IMAGINE_KITCHEN_LIBRARY unchanged.  Error classes follow the
-// bridge: 0 ok, -1 runtime, -20 ValueError, -21 IndexError (and libw8a8's -9 /
-// -10 pass through).
+// bools, and its FP8 linear through imagine_fp8_scaled_mm
+// (inference/native/bridge.cpp:401-413).  This file implements those two, and
+// imagine_last_error / imagine_last_accelerator_code, on libw8a8's plain C
+// entry points; kitchen_forward.cpp passes every other function of the
+// bridge, and every kernel name imagine_kitchen_call does not map, through to
+// the reference's own bridge library (IMAGINE_KITCHEN_FALLBACK_LIBRARY), so
+// the crate can load this library through IMAGINE_KITCHEN_LIBRARY with every
+// symbol it resolves present.  Error classes follow the bridge: 0 ok, -1
+// runtime, -20 ValueError, -21 IndexError (and libw8a8's -9 / -10 pass
+// through).
 //
 // Names and argument lists (call sites in inference/src/cuda_linear.rs and
 // inference/src/convrot.rs):
@@ -36,6 +40,7 @@
 #include <string>
 
 #include "../../include/w8a8.h"
+#include "kitchen_forward.h"
 
 extern "C" {
 struct KitchenArg {
@@ -54,6 +59,10 @@ thread_local int g_accel = 0;
 struct ValueError : std::invalid_argument {
   using std::invalid_argument::invalid_argument;
 };
+
+// A kernel name (or an fp8_scaled_mm form) this library does not run itself:
+// forwarded to the reference bridge library.
+struct NotNative {};
 
 class Args {
  public:
@@ -260,10 +269,51 @@ int64_t dispatch(const char* name, const Args& a) {
         q.size(-1), a.tensor(2).data_ptr<float>(), W8A8_SCALE_KITCHEN, stream_of(a.integer(9))));
     return 0;
   }
-  throw std::runtime_error("Unknown Kitchen kernel");
+  throw NotNative{};
+}
+
+// at::_scaled_mm_v2 TensorWise on e4m3 operands (bridge.cpp:401-413): a
+// [M, K] e4m3 (made contiguous, as there), b [K, N] e4m3 column-major (the
+// transposed view of a row-major [N, K] weight), fp32 scalar scales, optional
+// bias [N], output dtype `kind` (an at::ScalarType code).  Forms the tcgen05
+// kernel does not take -- other scalings, an fp8 or default (kind < 0)
+// output, a row-major b -- are not native.
+at::Tensor fp8_scaled_mm(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor& sa,
+                         const at::Tensor& sb, const at::Tensor* bias, int64_t kind) {
+  if (kind < 0) throw NotNative{};
+  const auto out_type = static_cast<at::ScalarType>(kind);
+  if (out_type != at::kBFloat16 && out_type != at::kHalf && out_type != at::kFloat) throw NotNative{};
+  if (a_in.scalar_type() != at::kFloat8_e4m3fn || b.scalar_type() != at::kFloat8_e4m3fn ||
+      a_in.dim() != 2 || b.dim() != 2 || sa.numel() != 1 || sb.numel() != 1 ||
+      sa.scalar_type() != at::kFloat || sb.scalar_type() != at::kFloat || !a_in.is_cuda()) {
+    throw NotNative{};
+  }
+  const int64_t m = a_in.size(0), k = a_in.size(1), n = b.size(1);
+  if (b.size(0) != k) throw ValueError("mat1 and mat2 shapes cannot be multiplied");
+  // b column-major: b.t() is a row-major [N, K] weight
+  if (!(b.stride(0) == 1 && (b.stride(1) == k || n == 1))) throw NotNative{};
+  if (bias && (bias->numel() != n || bias->scalar_type() != out_type || !bias->is_contiguous())) {
+    throw NotNative{};
+  }
+  const at::Tensor a = a_in.contiguous();
+  at::Tensor out = at::empty({m, n}, a.options().dtype(out_type));
+  const int code = out_type == at::kBFloat16 ? W8A8_BF16 : out_type == at::kHalf ? W8A8_F16 : W8A8_F32;
+  void* stream = reinterpret_cast<void*>(c10::cuda::getCurrentCUDAStream(a.device().index()).stream());
+  rc_or_throw(w8a8_fp8_gemm(static_cast<const uint8_t*>(a.data_ptr()),
+                            static_cast<const uint8_t*>(b.data_ptr()), sa.data_ptr<float>(),
+                            sb.data_ptr<float>(), bias ? bias->data_ptr() : nullptr, out.data_ptr(),
+                            code, m, n, k, nullptr, stream));
+  return out;
 }
 
 }  // namespace
+
+namespace kitchen_forward {
+void set_error(const std::string& message, int accelerator_code) {
+  g_error = message;
+  g_accel = accelerator_code;
+}
+}  // namespace kitchen_forward
 
 extern "C" {
 
@@ -285,7 +335,21 @@ __attribute__((visibility("default"))) int imagine_kitchen_call(const char* name
         break;
       }
     }
-    *result = dispatch(name, Args(args, n, name));
+    try {
+      *result = dispatch(name, Args(args, n, name));
+    } catch (const NotNative&) {
+      using Fn = int (*)(const char*, const KitchenArg*, size_t, int64_t*);
+      auto f = reinterpret_cast<Fn>(kitchen_forward::symbol("imagine_kitchen_call"));
+      if (!f) {
+        kitchen_forward::missing((std::string("imagine_kitchen_call(\"") + name + "\")").c_str());
+        g_error = "Unknown Kitchen kernel " + std::string(name) + " (" + g_error + ")";
+        return W8A8_ERR_RUNTIME;
+      }
+      const int rc = f(name, args, n, result);
+      if (rc != 0) kitchen_forward::copy_fallback_error();
+      else g_error.clear();
+      return rc;
+    }
     g_error.clear();
     return 0;
   } catch (const std::invalid_argument& e) {
@@ -303,6 +367,51 @@ __attribute__((visibility("default"))) int imagine_kitchen_call(const char* name
   }
 }
 
+__attribute__((visibility("default"))) int imagine_fp8_scaled_mm(const void* a, const void* b,
+                                                                const void* sa, const void* sb,
+                                                                const void* bias, int64_t kind,
+                                                                void** output) {
+  try {
+    if (!a || !b || !sa || !sb || !output) throw std::runtime_error("Null bridge argument");
+    const auto& at_a = *static_cast<const at::Tensor*>(a);
+    c10::optional<c10::cuda::CUDAGuard> guard;
+    if (at_a.is_cuda()) guard.emplace(at_a.device());
+    try {
+      *output = new at::Tensor(fp8_scaled_mm(at_a, *static_cast<const at::Tensor*>(b),
+                                             *static_cast<const at::Tensor*>(sa),
+                                             *static_cast<const at::Tensor*>(sb),
+                                             static_cast<const at::Tensor*>(bias), kind));
+    } catch (const NotNative&) {
+      using Fn = int (*)(const void*, const void*, const void*, const void*, const void*, int64_t,
+                         void**);
+      auto f = reinterpret_cast<Fn>(kitchen_forward::symbol("imagine_fp8_scaled_mm"));
+      if (!f) return kitchen_forward::missing("imagine_fp8_scaled_mm (this scaling / output form)");
+      const int rc = f(a, b, sa, sb, bias, kind, output);
+      if (rc != 0) kitchen_forward::copy_fallback_error();
+      else g_error.clear();
+      return rc;
+    }
+    g_error.clear();
+    return 0;
+  } catch (const std::invalid_argument& e) {
+    g_error = e.what();
+    return W8A8_ERR_VALUE;
+  } catch (const std::out_of_range& e) {
+    g_error = e.what();
+    return W8A8_ERR_INDEX;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return W8A8_ERR_RUNTIME;
+  } catch (...) {
+    g_error = "Unknown native exception";
+    return W8A8_ERR_RUNTIME;
+  }
+}
+
+// dtype code of imagine_w8a8_tensor_view for float8_e4m3fn (libw8a8 itself
+// takes e4m3 data as bytes and has no code for it)
+constexpr int64_t kViewE4M3 = 5;
+
 // Test and host convenience: a borrowed at::Tensor handle over existing
 // device memory (the reference bridge's imagine_tensor_* family plays this
 // role for the crate), and its release.
@@ -317,6 +426,7 @@ __attribute__((visibility("default"))) int imagine_w8a8_tensor_view(
       case W8A8_BF16: st = at::kBFloat16; break;
       case W8A8_S32: st = at::kInt; break;
       case W8A8_S8: st = at::kChar; break;
+      case kViewE4M3: st = at::kFloat8_e4m3fn; break;
       default: throw ValueError("unsupported dtype code " + std::to_string(dtype));
     }
     auto opts = at::TensorOptions().dtype(st).device(at::Device(at::kCUDA, static_cast<int>(device)));
@@ -336,6 +446,27 @@ __attribute__((visibility("default"))) int imagine_w8a8_tensor_view(
 
 __attribute__((visibility("default"))) void imagine_w8a8_tensor_free(void* t) {
   delete static_cast<at::Tensor*>(t);
+}
+
+// Test and host convenience: data pointer, element count and libw8a8 dtype
+// code (-1 for others) of an at::Tensor handle (e.g. one a bridge call
+// returned).
+__attribute__((visibility("default"))) int imagine_w8a8_tensor_info(const void* t, void** data,
+                                                                   int64_t* numel,
+                                                                   int64_t* dtype) {
+  if (!t || !data || !numel || !dtype) return W8A8_ERR_VALUE;
+  const auto& x = *static_cast<const at::Tensor*>(t);
+  *data = x.data_ptr();
+  *numel = x.numel();
+  switch (x.scalar_type()) {
+    case at::kFloat: *dtype = W8A8_F32; break;
+    case at::kHalf: *dtype = W8A8_F16; break;
+    case at::kBFloat16: *dtype = W8A8_BF16; break;
+    case at::kInt: *dtype = W8A8_S32; break;
+    case at::kChar: *dtype = W8A8_S8; break;
+    default: *dtype = -1; break;
+  }
+  return 0;
 }
 
 }  // extern "C"

@@ -476,15 +476,22 @@ def int8_linear_rms_rope(x: torch.Tensor, weight: torch.Tensor, weight_scale: to
 
 
 def _rms_rope_gemm(q, xs, lead, weight, ws, bias, nw, freqs_cis, epsilon, rope_cols, dequant,
-                   split_k, config, stream):
-    """The GEMM with the RMSNorm + RoPE epilogue on quantised rows q [M, K]."""
+                   split_k, config, stream, out=None):
+    """The GEMM with the RMSNorm + RoPE epilogue on quantised rows q [M, K];
+    ``out``: an [M, N] bf16 view with unit column stride to write into (any
+    row stride), else a new tensor."""
     dev = q.device
     m, k = q.shape
     n = weight.shape[0]
     fr = rope_freqs_rows(freqs_cis, m) if rope_cols else None
     w = weight if weight.is_contiguous() else weight.contiguous()
     b = bias.to(device=dev, dtype=torch.bfloat16).reshape(-1).contiguous() if bias is not None else None
-    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    elif (out.shape != (m, n) or out.dtype != torch.bfloat16 or out.stride(1) != 1
+          or out.device != dev):
+        raise ValueError(f"out must be a bf16 [{m}, {n}] view with unit column stride")
+    ldo = out.stride(0)
     ep = _epilogue(ws, b, None, None, dequant, None, n, n)
     cfg = _config(config)
     cfg = cfg if isinstance(cfg, N.GemmConfig) else None
@@ -496,11 +503,11 @@ def _rms_rope_gemm(q, xs, lead, weight, ws, bias, nw, freqs_cis, epsilon, rope_c
         nbytes = 0
     scratch = _splitk_scratch(dev, nbytes) if nbytes > 0 else None
     N.check(N.LIB.w8a8_gemm_dequant_rms_rope(
-        _vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep), _vp(out), n, m, n, k, rope_cols,
+        _vp(q), k, _vp(w), k, _vp(xs), ctypes.byref(ep), _vp(out), ldo, m, n, k, rope_cols,
         _vp(nw), 1 if nw.numel() != 128 else 0, _vp(fr), float(epsilon),
         int(split_k or 0) if scratch is not None else 1, _vp(scratch),
         scratch.numel() if scratch is not None else 0, _cfg_ptr(cfg), stream))
-    return out.reshape(*lead, n)
+    return out.reshape(*lead, n) if lead is not None else out
 
 
 def quantize_weight(weight: torch.Tensor, convrot: bool = False, convrot_groupsize: int = 256, *,
@@ -798,10 +805,16 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
         shape = x.shape
         x = torch.matmul(x.reshape(-1, k // convrot_groupsize, convrot_groupsize), h).reshape(shape)
     lead = x.shape[:-1]
-    x2 = x.reshape(-1, x.shape[-1])
-    if not x2.is_contiguous():
+    # [B, S, K] whose samples' rows are each contiguous but not adjacent (a
+    # slice of a longer sequence): the plain quantiser reads each sample's
+    # rows in place instead of a gathered copy
+    per_sample = (not fused and x.dim() == 3 and not x.is_contiguous() and x.stride(-1) == 1
+                  and x.stride(1) == x.shape[-1] and x.shape[0] * x.shape[1] > 2
+                  and x.shape[-1] > 0)
+    x2 = x if per_sample else x.reshape(-1, x.shape[-1])
+    if not per_sample and not x2.is_contiguous():
         x2 = x2.contiguous()
-    m = x2.shape[0]
+    m = x.shape[0] * x.shape[1] if per_sample else x2.shape[0]
     w = weight if weight.is_contiguous() else weight.contiguous()
     if tiled and k == 0:
         raise ValueError("pre-tiled weights need K > 0")
@@ -831,7 +844,13 @@ def int8_linear(x: torch.Tensor, weight: torch.Tensor, weight_scale: torch.Tenso
     else:
         q = torch.empty((m, k), dtype=torch.int8, device=dev)
         xs = (torch.empty if k > 0 else torch.zeros)((m,), dtype=torch.float32, device=dev)
-        if m > 0 and k > 0:
+        if per_sample:
+            s_rows = x.shape[1]
+            for i in range(x.shape[0]):
+                N.check(N.LIB.w8a8_quantize_rowwise(
+                    _vp(x[i]), _code(x.dtype), s_rows, k, k, _vp(q[i * s_rows:]), k,
+                    _vp(xs[i * s_rows:]), SCALE_MODE[scale_mode], 0, 0, stream))
+        elif m > 0 and k > 0:
             N.check(N.LIB.w8a8_quantize_rowwise(_vp(x2), _code(x2.dtype), m, k, k, _vp(q), k,
                                                 _vp(xs), SCALE_MODE[scale_mode], 0, 0, stream))
         cfg = _config(config)

@@ -369,13 +369,11 @@ class NativeOps:
         return self.L.dequantize_int8_linear(acc, xs, p.ws, p.b, torch.bfloat16, dequant="eager",
                                              residual=residual, residual_scale=gate, lead=lead)
 
-    def joint_attention(self, qkv_t, qkv_i, heads: int, head_dim: int):
-        """Joint attention of [text; image] tokens.  qkv_*: [B, S, 3 * heads *
-        head_dim] (q, k, v columns).  Returns the text and image outputs
-        [B, S, heads * head_dim]."""
-        b, st, _ = qkv_t.shape
+    def attention(self, joint, heads: int, head_dim: int):
+        """Attention over a joint sequence: joint [B, S, 3 * heads * head_dim]
+        (q, k, v columns, read in place) -> [B, S, heads * head_dim]."""
+        b, s, _ = joint.shape
         c = heads * head_dim
-        joint = torch.cat([qkv_t, qkv_i], dim=1)
         q, k, v = (joint[..., i * c:(i + 1) * c].unflatten(-1, (heads, head_dim)).transpose(1, 2)
                    for i in range(3))
         if self.attention_backends:
@@ -385,8 +383,30 @@ class NativeOps:
                 o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
         else:
             o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
-        o = o.transpose(1, 2).reshape(b, -1, c)
+        return o.transpose(1, 2).reshape(b, s, c)
+
+    def joint_attention(self, qkv_t, qkv_i, heads: int, head_dim: int):
+        """Joint attention of [text; image] tokens.  qkv_*: [B, S, 3 * heads *
+        head_dim] (q, k, v columns).  Returns the text and image outputs
+        [B, S, heads * head_dim]."""
+        st = qkv_t.shape[1]
+        o = self.attention(torch.cat([qkv_t, qkv_i], dim=1), heads, head_dim)
         return o[:, :st], o[:, st:]
+
+    def adaln_qkv_rope_into(self, x, scale, shift, p: Int8Params, norm_w, freqs, rope_cols, outs,
+                            eps=1e-6):
+        """``adaln_qkv_rope`` with sample i's rows written into ``outs[i]``
+        (an [S, N] view, e.g. the sample's rows of a joint q / k / v buffer):
+        one modulated quantiser over all rows, then one GEMM per sample."""
+        b, s, k = x.shape
+        q, xs = self.L.quantize_int8_rowwise_modulated(x, "adaln", scale, shift, None, eps)
+        q = q.reshape(-1, k)
+        xs = xs.reshape(-1)
+        stream = self.L._stream(x.device)
+        for i, o in enumerate(outs):
+            self.L._rms_rope_gemm(q[i * s:(i + 1) * s], xs[i * s:(i + 1) * s], None, p.w, p.ws,
+                                  p.b, norm_w, freqs, eps, rope_cols, "eager", None, None, stream,
+                                  out=o)
 
     def silu(self, x):
         return torch.nn.functional.silu(x)
@@ -468,12 +488,13 @@ class MMDiT:
         return self._freqs[key]
 
     def _row_parallel(self, x, p: Int8Params, residual, gate):
-        """x [B, S, K/tp] (this rank's K-slice) -> [B, S, N] with the gated
-        residual, equal to the single-GPU linear bit for bit."""
+        """x [B, S, K/tp] (this rank's K-slice; a sample's rows contiguous,
+        samples possibly apart) -> [B, S, N] with the gated residual, equal to
+        the single-GPU linear bit for bit."""
         lead = x.shape[:-1]
-        x2 = x.reshape(-1, x.shape[-1])
         if self.tp == 1:
-            return self.ops.linear(x2.reshape(*lead, -1), p, residual=residual, gate=gate)
+            return self.ops.linear(x, p, residual=residual, gate=gate)
+        x2 = x.reshape(-1, x.shape[-1])
         amax = self.ops.row_absmax(x2)
         dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.tp_group)
         q, xs = self.ops.quantize_given_absmax(x2, amax)
@@ -493,20 +514,40 @@ class MMDiT:
         return torch.cat(parts, dim=-1)
 
     # -- one joint block -------------------------------------------------------
+    @staticmethod
+    def _mod_chunks(mod, b, hidden):
+        """shift1, scale1, gate1, shift2, scale2, gate2 as [B, 1, hidden]
+        tensors, from one block's modulation: [6, B, hidden] (contiguous
+        chunks, as ``forward`` lays them out) or [B, 6 * hidden]."""
+        if mod.dim() == 2:
+            mod = mod.reshape(b, 6, hidden).transpose(0, 1).contiguous()
+        return tuple(mod[j].unsqueeze(1) for j in range(6))
+
     def block(self, bp: BlockParams, img, txt, mod_i, mod_t, freqs_t, freqs_i):
         cfg = self.cfg
-        b = img.shape[0]
+        b, si, _ = img.shape
+        st = txt.shape[1]
         hl = cfg.heads // self.tp
         c = hl * cfg.head_dim
-        sh1i, sc1i, g1i, sh2i, sc2i, g2i = mod_i.reshape(b, 6, 1, cfg.hidden).unbind(1)
-        sh1t, sc1t, g1t, sh2t, sc2t, g2t = mod_t.reshape(b, 6, 1, cfg.hidden).unbind(1)
+        sh1i, sc1i, g1i, sh2i, sc2i, g2i = self._mod_chunks(mod_i, b, cfg.hidden)
+        sh1t, sc1t, g1t, sh2t, sc2t, g2t = self._mod_chunks(mod_t, b, cfg.hidden)
         ops = self.ops
-        qkv_i = ops.adaln_qkv_rope(img, sc1i, sh1i, bp.img.qkv, bp.img.qk_norm, freqs_i, 2 * c,
-                                   cfg.eps)
-        qkv_t = ops.adaln_qkv_rope(txt, sc1t, sh1t, bp.txt.qkv, bp.txt.qk_norm, freqs_t, 2 * c,
-                                   cfg.eps)
-        o_t, o_i = ops.joint_attention(qkv_t.reshape(b, -1, 3 * c), qkv_i.reshape(b, -1, 3 * c),
-                                       hl, cfg.head_dim)
+        if hasattr(ops, "adaln_qkv_rope_into"):
+            # q / k / v of [text; image] written by the projections into one
+            # joint buffer that attention reads in place
+            joint = torch.empty((b, st + si, 3 * c), dtype=torch.bfloat16, device=img.device)
+            ops.adaln_qkv_rope_into(txt, sc1t, sh1t, bp.txt.qkv, bp.txt.qk_norm, freqs_t, 2 * c,
+                                    [joint[i, :st] for i in range(b)], cfg.eps)
+            ops.adaln_qkv_rope_into(img, sc1i, sh1i, bp.img.qkv, bp.img.qk_norm, freqs_i, 2 * c,
+                                    [joint[i, st:] for i in range(b)], cfg.eps)
+        else:
+            qkv_i = ops.adaln_qkv_rope(img, sc1i, sh1i, bp.img.qkv, bp.img.qk_norm, freqs_i, 2 * c,
+                                       cfg.eps)
+            qkv_t = ops.adaln_qkv_rope(txt, sc1t, sh1t, bp.txt.qkv, bp.txt.qk_norm, freqs_t, 2 * c,
+                                       cfg.eps)
+            joint = torch.cat([qkv_t.reshape(b, st, 3 * c), qkv_i.reshape(b, si, 3 * c)], dim=1)
+        o = ops.attention(joint, hl, cfg.head_dim)
+        o_t, o_i = o[:, :st], o[:, st:]
         img = self._row_parallel(o_i, bp.img.out, img, g1i)
         txt = self._row_parallel(o_t, bp.txt.out, txt, g1t)
         h_i = ops.adaln_linear(img, sc2i, sh2i, bp.img.up, act="gelu_tanh", eps=cfg.eps)
@@ -539,10 +580,13 @@ class MMDiT:
         img, txt, s, mods_i, mods_t = self.embed(latent, t, context)
         freqs_t, freqs_i = self.freqs(txt.shape[1], h // cfg.patch, w // cfg.patch, latent.device)
         n = len(p.blocks) if blocks is None else blocks
-        md = cfg.mod_dim
+        # every block's six modulation rows as contiguous [B, hidden] chunks
+        # (one copy per stream and step): [blocks, 6, B, hidden]
+        nb = mods_i.shape[1] // cfg.mod_dim
+        mods_i = mods_i.reshape(b, nb, 6, cfg.hidden).permute(1, 2, 0, 3).contiguous()
+        mods_t = mods_t.reshape(b, nb, 6, cfg.hidden).permute(1, 2, 0, 3).contiguous()
         for i, bp in enumerate(p.blocks[:n]):
-            img, txt = self.block(bp, img, txt, mods_i[:, i * md:(i + 1) * md],
-                                  mods_t[:, i * md:(i + 1) * md], freqs_t, freqs_i)
+            img, txt = self.block(bp, img, txt, mods_i[i], mods_t[i], freqs_t, freqs_i)
         scale, shift = ops.linear(s, p.norm_out).reshape(b, 2, 1, cfg.hidden).unbind(1)
         out = ops.adaln_linear(img, scale, shift, p.proj_out, eps=cfg.eps)
         return unpatchify(out, cfg.patch, c, h, w)

@@ -65,15 +65,14 @@ class OracleOps:
             y = y.reshape(*lead, -1)
         return O.apply_residual(y, residual, gate)
 
-    def joint_attention(self, qkv_t, qkv_i, heads, head_dim):
-        b, st, _ = qkv_t.shape
+    def attention(self, joint, heads, head_dim):
+        b = joint.shape[0]
         c = heads * head_dim
-        joint = torch.cat([qkv_t, qkv_i], dim=1).float()
+        joint = joint.float()
         q, k, v = (joint[..., i * c:(i + 1) * c].unflatten(-1, (heads, head_dim)).transpose(1, 2)
                    for i in range(3))
         a = torch.softmax(q @ k.transpose(-1, -2) / head_dim ** 0.5, dim=-1)
-        o = (a @ v).transpose(1, 2).reshape(b, -1, c).to(torch.bfloat16)
-        return o[:, :st], o[:, st:]
+        return (a @ v).transpose(1, 2).reshape(b, -1, c).to(torch.bfloat16)
 
     def silu(self, x):
         return torch.nn.functional.silu(x)

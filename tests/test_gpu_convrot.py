@@ -176,6 +176,60 @@ def test_modulated_quantiser(mode, rotate, smode, dtype):
     assert W().device_error() == 0
 
 
+def _strided(x2, pad):
+    """x2 [rows, k] as a view with row stride k + pad."""
+    rows, k = x2.shape
+    wide = torch.zeros(rows, k + pad, dtype=x2.dtype, device=x2.device)
+    wide[:, :k] = x2
+    return wide[:, :k]
+
+
+@pytest.mark.parametrize("k", [512, 2048, 6144, 12288])
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("smode", ["eager", "kitchen"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_modulated_quantiser_widths(k, mode, smode, dtype):
+    """The no-rotation modulated quantiser at every row width class: one warp
+    per row (K <= 1024), two (<= 2048), eight (<= 8192), and rows over 8192
+    columns, which take the ConvRot kernel without rotation -- against the C
+    restatement with the bars of test_modulated_quantiser.  A row stride that
+    is not a multiple of 8 elements (no 16-byte rows) also takes the ConvRot
+    kernel: for ``scale`` (no row statistic) its codes and scales equal the
+    aligned call's bit for bit; the normalising modes sum the row's
+    statistics in another order there, so they are held to the same bars
+    against the C restatement."""
+    b, s = 2, 24
+    x, sc, sh, w = _mod_inputs(mode, b, s, k, dtype, 60 + k)
+    x2 = x.reshape(-1, k).to(cuda())
+    args = (mode, sc.to(cuda()), sh.to(cuda()) if sh is not None else None,
+            w.to(cuda()) if w is not None else None, 1e-6, False)
+    q, xs = W().quantize_int8_rowwise_modulated(x2, *args, scale_mode=smode)
+    rq, rs = _cref.quantize_modulated(x.reshape(-1, k), mode, sc, sh, w, 1e-6, False,
+                                      kitchen=(smode == "kitchen"))
+    ulp = {torch.bfloat16: 2.0 ** -7, torch.float16: 2.0 ** -10}[dtype]
+    # rows over 8192 columns: rms_norm(x, w) sums 12288 squares in the ConvRot
+    # kernel's order, and the normalised value is rounded to bf16 before and
+    # after the weight, so the row's bf16 maximum can land two ulps from the
+    # restatement's (measured: 0.0099 relative on bf16) and codes near it two
+    # steps
+    ulps = 2 if (k > 8192 and mode == "rms_scale") else 1
+    rel = ((xs.reshape(-1).cpu() - rs).abs() / rs.abs().clamp(min=1e-30)).max().item()
+    assert rel <= 1.01 * ulps * ulp, f"scale relative difference {rel:.3g} > {ulps} ulp {ulp:.3g}"
+    d = (q.cpu().int() - rq.int()).abs()
+    assert d.max().item() <= ulps
+    assert (d == 0).float().mean().item() >= 0.99
+    for pad in (8, 3):
+        qp, xsp = W().quantize_int8_rowwise_modulated(_strided(x2, pad), *args, scale_mode=smode)
+        if pad == 8 or mode == "scale":
+            assert torch.equal(qp, q) and torch.equal(xsp, xs), f"row stride k + {pad}"
+        else:
+            relp = ((xsp.reshape(-1).cpu() - rs).abs() / rs.abs().clamp(min=1e-30)).max().item()
+            assert relp <= 1.01 * ulps * ulp
+            dp = (qp.cpu().int() - rq.int()).abs()
+            assert dp.max().item() <= ulps and (dp == 0).float().mean().item() >= 0.99
+    assert W().device_error() == 0
+
+
 @pytest.mark.parametrize("op", ["modulated", "rms_modulated", "adaln", "rms_adaln",
                                 "adaln_convrot"])
 def test_modulated_linears(op):

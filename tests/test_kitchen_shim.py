@@ -170,3 +170,62 @@ def test_shim_linear_routes_match_c_abi():
                        I(stream)])
         assert rc == -20 and b"group" in lib.imagine_last_error()
     torch.cuda.synchronize()
+
+
+class _CudaArray:
+    """A raw device buffer as a torch tensor (__cuda_array_interface__)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3}
+
+
+@pytest.mark.gpu
+def test_shim_fp8_scaled_mm_matches_c_abi():
+    """imagine_fp8_scaled_mm (bridge.cpp:401-413: _scaled_mm_v2 TensorWise) on
+    the tcgen05 FP8 GEMM: a [M, K] e4m3, b the column-major [K, N] view of a
+    row-major [N, K] weight, scalar fp32 scales, bf16 bias, bf16 output --
+    bit-identical to libw8a8's w8a8_fp8_gemm (imagine_b200.fp8_linear)."""
+    import imagine_b200 as W
+
+    lib = _lib()
+    lib.imagine_fp8_scaled_mm.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64,
+                                                                  ctypes.POINTER(ctypes.c_void_p)]
+    lib.imagine_w8a8_tensor_info.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p),
+                                             ctypes.POINTER(ctypes.c_int64),
+                                             ctypes.POINTER(ctypes.c_int64)]
+    dev = torch.device("cuda", 0)
+    g = torch.Generator().manual_seed(41)
+    m, k, n = 520, 3072, 1024
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    sa = (x.abs().amax().float() / 448.0).reshape(1)
+    sw = (w.abs().amax().float() / 448.0).reshape(1)
+    a8 = W.quantize_per_tensor_fp8(x, sa)
+    w8 = W.quantize_per_tensor_fp8(w, sw)
+    bias = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    want = W.fp8_linear(a8, sa, w8, sw, bias, torch.bfloat16)
+
+    def view(t, code):
+        sizes = (ctypes.c_int64 * t.dim())(*t.shape)
+        strides = (ctypes.c_int64 * t.dim())(*t.stride())
+        out = ctypes.c_void_p()
+        assert lib.imagine_w8a8_tensor_view(ctypes.c_void_p(t.data_ptr()), sizes, strides, t.dim(),
+                                            code, dev.index, ctypes.byref(out)) == 0
+        return out
+
+    handles = [view(a8, 5), view(w8.t(), 5), view(sa, 0), view(sw, 0), view(bias, 2)]
+    out = ctypes.c_void_p()
+    try:
+        rc = lib.imagine_fp8_scaled_mm(*handles, 15, ctypes.byref(out))  # 15: at::kBFloat16
+        assert rc == 0, lib.imagine_last_error()
+        ptr, numel, code = ctypes.c_void_p(), ctypes.c_int64(), ctypes.c_int64()
+        assert lib.imagine_w8a8_tensor_info(out, ctypes.byref(ptr), ctypes.byref(numel),
+                                            ctypes.byref(code)) == 0
+        assert numel.value == m * n and code.value == 2
+        torch.cuda.synchronize()
+        got = torch.as_tensor(_CudaArray(ptr.value, (m, n), "<i2"), device=dev)
+        assert torch.equal(got, want.view(torch.int16))
+    finally:
+        for h in handles + ([out] if out.value else []):
+            lib.imagine_w8a8_tensor_free(h)
