@@ -422,37 +422,54 @@ def run_dit(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     cfg = MD.MMDiTConfig(blocks=args.dit_blocks)
-    pl = MD.placement(world, rank)
-    groups = MD.ProcessGroups(pl)
     ops = MD.NativeOps()
-    t0 = time.perf_counter()
-    params = MD.random_params(cfg, ops, dev, seed=1234, tp_rank=pl.tp_rank, tp_world=pl.tp)
-    torch.cuda.synchronize()
-    init_s = time.perf_counter() - t0
     g = torch.Generator().manual_seed(77)
     lat = torch.randn(1, *DIT_LATENT, generator=g).to(dev)
     ctx_c = torch.randn(1, DIT_TEXT, cfg.context_dim, generator=g).to(torch.bfloat16).to(dev)
     ctx_u = torch.randn(1, DIT_TEXT, cfg.context_dim, generator=g).to(torch.bfloat16).to(dev)
     warm = max(3, args.dit_warmup)
     steps = args.dit_steps
-    # the headline form: the forward captured once as a CUDA graph and
-    # replayed every step (tensor-parallel reductions through NCCL, which
-    # the graph holds)
-    dit = MD.MMDiT(params, ops, groups.tp_group)
-    cap = MD.CapturedModel(dit, pl, groups, ctx_c, ctx_u, (1, *DIT_LATENT), dev)
-    try:
-        cap.capture()
-        loop = MD.DenoiseLoop(cap, lat, steps=40, cfg_scale=2.5)
-        ms, finite, clocks = _time_loop(loop, warm, steps, rank, world, local_rank, dev, clocks=True)
-    finally:
-        cap.release()
-    # the same steps launched eagerly from Python (tensor-parallel reductions
-    # fused into the GEMMs over peer memory)
-    eager = MD.MMDiT(params, ops, groups.tp_group, fused_tp=pl.tp > 1)
-    loop = MD.DenoiseLoop(MD.cfg_model(eager, pl, groups, ctx_c, ctx_u), lat, steps=40,
-                          cfg_scale=2.5)
-    eager_ms, eager_finite, _ = _time_loop(loop, warm, steps, rank, world, local_rank, dev)
-    finite = finite and eager_finite
+
+    def measure(pl, graph, fused_tp=False, clocks=False):
+        groups = MD.ProcessGroups(pl)
+        t0 = time.perf_counter()
+        dit = MD.build_model(cfg, ops, dev, pl, groups, seed=1234, fused_tp=fused_tp)
+        torch.cuda.synchronize()
+        init_s = time.perf_counter() - t0
+        cap = None
+        try:
+            if graph:
+                cap = MD.CapturedModel(dit, pl, groups, ctx_c, ctx_u, (1, *DIT_LATENT), dev)
+                cap.capture()
+                model = cap
+            else:
+                model = MD.cfg_model(dit, pl, groups, ctx_c, ctx_u)
+            loop = MD.DenoiseLoop(model, lat, steps=40, cfg_scale=2.5)
+            ms, finite, clk = _time_loop(loop, warm, steps, rank, world, local_rank, dev,
+                                         clocks=clocks)
+        finally:
+            if cap is not None:
+                cap.release()
+        wbytes = dit.p.weight_bytes
+        del dit
+        torch.cuda.empty_cache()
+        return ms, finite, clk, init_s, wbytes
+
+    # the headline form: image tokens split across the ranks of a branch
+    # (sequence-parallel) on 4+ GPUs; the forward captured once as a CUDA
+    # graph and replayed every step
+    pl = MD.placement(world, rank, "sequence")
+    ms, finite, clocks, init_s, wbytes = measure(pl, graph=True, clocks=True)
+    alternatives = {}
+    e_ms, e_finite, _, _, _ = measure(pl, graph=False)
+    alternatives["same placement, launched eagerly from Python"] = e_ms
+    finite = finite and e_finite
+    if world >= 4:
+        tp = MD.placement(world, rank, "tensor")
+        t_ms, t_finite, _, _, _ = measure(tp, graph=False, fused_tp=True)
+        alternatives[tp.describe() + "; reductions fused into the GEMMs over peer memory, "
+                     "eager"] = t_ms
+        finite = finite and t_finite
     import imagine_b200 as W
 
     if W.device_error() != 0:
@@ -471,14 +488,11 @@ def run_dit(args, rank, world, local_rank):
             "placement": pl.describe(),
             "launch": "the forward of both branches captured once as a CUDA graph, replayed per "
                       "step (with its NCCL collectives); the sampler step a separate kernel",
-            "eager_ms": eager_ms,
-            "eager": "the same step launched from Python per kernel" + (
-                "" if pl.tp == 1 else ", row-parallel reductions fused into the GEMM "
-                "(peer-memory reduce-scatter)"),
+            "alternatives_ms": alternatives,
             "attention": "torch scaled_dot_product_attention, bf16 (cuDNN backend first)",
             "linear_tops_per_step": lin_ops / 1e12, "attention_tflop_per_step": attn_flops / 1e12,
             "achieved_tops": (lin_ops + attn_flops) / (ms * 1e-3) / 1e12,
-            "weights_gb_per_rank": params.weight_bytes / 1e9, "init_s": init_s,
+            "weights_gb_per_rank": wbytes / 1e9, "init_s": init_s,
             "finite": finite, "clocks": clocks,
             "est_40_step_s": 40 * ms / 1e3}
 

@@ -34,7 +34,15 @@ Multi-GPU (one process per GPU):
   With 2 or more ranks, ranks [0, W/2) run the conditional branch and
   [W/2, W) the unconditional one; one all-gather between the rank pairs
   (r, r + W/2) gives every rank both predictions (``cfg_model``).
-* Tensor parallelism inside a branch (W/2 > 1 ranks): heads are split across
+* Sequence parallelism inside a branch (W/2 > 1 ranks, the default): each
+  rank of the branch holds the whole weights and a contiguous share of the
+  image tokens; per block it writes the k / v of its tokens into its slot of
+  a joint k / v buffer, one in-place all-gather fills the others, its
+  queries (all text tokens, its image tokens) attend to the whole sequence,
+  and every linear is row-local.  The text stream (256 tokens) runs on every
+  rank; the modulation GEMV is split by output rows and all-gathered once
+  per step; the final image rows are all-gathered.
+* Tensor parallelism inside a branch (the alternative): heads are split across
   the ranks of a branch.  QKV and MLP-up are column-parallel (no exchange);
   the out-projection and MLP-down are row-parallel: an all-reduce MAX of the
   row absmax (so every rank quantises its K-slice with the full row's scale),
@@ -372,18 +380,47 @@ class NativeOps:
     def attention(self, joint, heads: int, head_dim: int):
         """Attention over a joint sequence: joint [B, S, 3 * heads * head_dim]
         (q, k, v columns, read in place) -> [B, S, heads * head_dim]."""
-        b, s, _ = joint.shape
         c = heads * head_dim
-        q, k, v = (joint[..., i * c:(i + 1) * c].unflatten(-1, (heads, head_dim)).transpose(1, 2)
-                   for i in range(3))
+        return self.attention_split(joint[..., :c], joint[..., c:], heads, head_dim)
+
+    def attention_split(self, q, kv, heads: int, head_dim: int):
+        """q [B, Sq, C] against kv [B, Skv, 2C] (k columns, then v), both read
+        in place -> [B, Sq, C]."""
+        b, sq, _ = q.shape
+        c = heads * head_dim
+        qh = q.unflatten(-1, (heads, head_dim)).transpose(1, 2)
+        k, v = (kv[..., i * c:(i + 1) * c].unflatten(-1, (heads, head_dim)).transpose(1, 2)
+                for i in range(2))
         if self.attention_backends:
             from torch.nn.attention import sdpa_kernel
 
             with sdpa_kernel(self.attention_backends, set_priority=True):
-                o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+                o = torch.nn.functional.scaled_dot_product_attention(qh, k, v)
         else:
-            o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
-        return o.transpose(1, 2).reshape(b, s, c)
+            o = torch.nn.functional.scaled_dot_product_attention(qh, k, v)
+        return o.transpose(1, 2).reshape(b, sq, c)
+
+    def adaln_qkv_rope_split(self, x, scale, shift, p: Int8Params, norm_w, freqs, q_outs, kv_outs,
+                             eps=1e-6):
+        """``adaln_qkv_rope`` with sample i's q columns written into
+        ``q_outs[i]`` [S, C] and its k, v columns into ``kv_outs[i]`` [S, 2C]:
+        one modulated quantiser over all rows, then per sample the q rows of
+        the weight (RMSNorm + RoPE on every column) and its k, v rows (RMSNorm
+        + RoPE on the k columns)."""
+        b, s, k = x.shape
+        c = p.w.shape[0] // 3
+        q, xs = self.L.quantize_int8_rowwise_modulated(x, "adaln", scale, shift, None, eps)
+        q = q.reshape(-1, k)
+        xs = xs.reshape(-1)
+        stream = self.L._stream(x.device)
+        halves = ((slice(0, c), q_outs), (slice(c, 3 * c), kv_outs))
+        for i in range(b):
+            rows = slice(i * s, (i + 1) * s)
+            for cols, outs in halves:
+                self.L._rms_rope_gemm(q[rows], xs[rows], None, p.w[cols], p.ws[cols],
+                                      None if p.b is None else p.b[cols],
+                                      norm_w[cols.start:cols.start + c], freqs, eps, c, "eager",
+                                      None, None, stream, out=outs[i])
 
     def joint_attention(self, qkv_t, qkv_i, heads: int, head_dim: int):
         """Joint attention of [text; image] tokens.  qkv_*: [B, S, 3 * heads *
@@ -462,15 +499,25 @@ class NativeOps:
 # the model
 # --------------------------------------------------------------------------
 class MMDiT:
-    """The MMDiT forward on one rank of a tensor-parallel group (``tp_group``
-    None: one GPU)."""
+    """The MMDiT forward on one rank: alone, in a tensor-parallel group
+    (``tp_group``, with the weight shards of ``random_params(tp_rank,
+    tp_world)``) or in a sequence-parallel group (``sp_group``, whole
+    weights)."""
 
-    def __init__(self, params: MMDiTParams, ops, tp_group=None, fused_tp: bool = False):
+    def __init__(self, params: MMDiTParams, ops, tp_group=None, fused_tp: bool = False,
+                 sp_group=None):
         self.p = params
         self.cfg = params.cfg
         self.ops = ops
         self.tp_group = tp_group
         self.tp = params.tp_world
+        # sequence parallelism: this rank's share of the image tokens, whole
+        # weights (one sample per call)
+        self.sp_group = sp_group
+        self.sp = dist.get_world_size(sp_group) if sp_group is not None else 1
+        self.sp_rank = dist.get_rank(sp_group) if sp_group is not None else 0
+        if self.sp > 1 and self.tp > 1:
+            raise ValueError("sequence and tensor parallelism are alternatives here")
         # row-parallel reduction fused into the GEMM (peer memory) instead of
         # an NCCL all-reduce of the int32 partials
         self.fused_tp = fused_tp and self.tp > 1 and hasattr(ops, "row_parallel_fused")
@@ -512,6 +559,20 @@ class MMDiT:
         parts = [torch.empty_like(y) for _ in range(self.tp)]
         dist.all_gather(parts, y.contiguous(), group=self.tp_group)
         return torch.cat(parts, dim=-1)
+
+    def _mod_linear(self, s, p: Int8Params):
+        """The modulation GEMV of every block: on sequence-parallel ranks each
+        computes its share of the output rows and one all-gather joins them."""
+        if self.sp == 1:
+            return self._gather_cols(self.ops.linear(s, p))
+        n = p.w.shape[0]
+        rows = _shard(n, self.sp_rank, self.sp)
+        mine = self.ops.linear(s, Int8Params(p.w[rows], p.ws[rows],
+                                             None if p.b is None else p.b[rows]))
+        b = mine.shape[0]
+        out = torch.empty((self.sp * b, mine.shape[1]), dtype=mine.dtype, device=mine.device)
+        dist.all_gather_into_tensor(out, mine.contiguous(), group=self.sp_group)
+        return out.reshape(self.sp, b, -1).permute(1, 0, 2).reshape(b, n)
 
     # -- one joint block -------------------------------------------------------
     @staticmethod
@@ -556,6 +617,39 @@ class MMDiT:
         txt = self._row_parallel(h_t, bp.txt.down, txt, g2t)
         return img, txt
 
+    def block_sp(self, bp: BlockParams, img, txt, mod_i, mod_t, freqs_t, freqs_i):
+        """One joint block on a sequence-parallel rank: ``img`` [1, S/sp,
+        hidden] is this rank's share of the image tokens (``freqs_i`` their
+        rotations), ``txt`` all text tokens (every rank computes the text
+        stream).  Each rank writes the k, v of its image tokens into its slot
+        of the joint k / v buffer, one in-place all-gather fills the other
+        slots, and its queries (all text tokens and its image tokens) attend
+        to the whole sequence; every linear after that is row-local."""
+        cfg, ops = self.cfg, self.ops
+        b, sl, _ = img.shape
+        if b != 1:
+            raise ValueError("sequence parallelism runs one sample per call")
+        st = txt.shape[1]
+        c = cfg.hidden
+        sh1i, sc1i, g1i, sh2i, sc2i, g2i = self._mod_chunks(mod_i, b, cfg.hidden)
+        sh1t, sc1t, g1t, sh2t, sc2t, g2t = self._mod_chunks(mod_t, b, cfg.hidden)
+        q = torch.empty((1, st + sl, c), dtype=torch.bfloat16, device=img.device)
+        kv = torch.empty((1, st + sl * self.sp, 2 * c), dtype=torch.bfloat16, device=img.device)
+        mine = kv[0, st + self.sp_rank * sl: st + (self.sp_rank + 1) * sl]
+        ops.adaln_qkv_rope_split(txt, sc1t, sh1t, bp.txt.qkv, bp.txt.qk_norm, freqs_t,
+                                 [q[0, :st]], [kv[0, :st]], cfg.eps)
+        ops.adaln_qkv_rope_split(img, sc1i, sh1i, bp.img.qkv, bp.img.qk_norm, freqs_i,
+                                 [q[0, st:]], [mine], cfg.eps)
+        dist.all_gather_into_tensor(kv[0, st:], mine, group=self.sp_group)
+        o = ops.attention_split(q, kv, cfg.heads, cfg.head_dim)
+        img = ops.linear(o[:, st:], bp.img.out, residual=img, gate=g1i)
+        txt = ops.linear(o[:, :st], bp.txt.out, residual=txt, gate=g1t)
+        h_i = ops.adaln_linear(img, sc2i, sh2i, bp.img.up, act="gelu_tanh", eps=cfg.eps)
+        img = ops.linear(h_i, bp.img.down, residual=img, gate=g2i)
+        h_t = ops.adaln_linear(txt, sc2t, sh2t, bp.txt.up, act="gelu_tanh", eps=cfg.eps)
+        txt = ops.linear(h_t, bp.txt.down, residual=txt, gate=g2t)
+        return img, txt
+
     # -- the forward -------------------------------------------------------------
     def embed(self, latent, t, context):
         """Input projections and the modulation rows of every block."""
@@ -567,8 +661,8 @@ class MMDiT:
         emb = timestep_embedding(round_timesteps(t).float(), cfg.time_dim).to(torch.bfloat16)
         temb = ops.linear(ops.silu(ops.linear(emb, p.time1)), p.time2)
         s = ops.silu(temb)
-        mods_i = self._gather_cols(ops.linear(s, p.mod_img))
-        mods_t = self._gather_cols(ops.linear(s, p.mod_txt))
+        mods_i = self._mod_linear(s, p.mod_img)
+        mods_t = self._mod_linear(s, p.mod_txt)
         return img, txt, s, mods_i, mods_t
 
     def forward(self, latent: torch.Tensor, t: torch.Tensor, context: torch.Tensor,
@@ -585,10 +679,22 @@ class MMDiT:
         nb = mods_i.shape[1] // cfg.mod_dim
         mods_i = mods_i.reshape(b, nb, 6, cfg.hidden).permute(1, 2, 0, 3).contiguous()
         mods_t = mods_t.reshape(b, nb, 6, cfg.hidden).permute(1, 2, 0, 3).contiguous()
+        block = self.block
+        if self.sp > 1:
+            # this rank's contiguous share of the image tokens
+            mine = _shard(img.shape[1], self.sp_rank, self.sp)
+            img = img[:, mine].contiguous()
+            freqs_i = freqs_i[mine]
+            block = self.block_sp
         for i, bp in enumerate(p.blocks[:n]):
-            img, txt = self.block(bp, img, txt, mods_i[i], mods_t[i], freqs_t, freqs_i)
+            img, txt = block(bp, img, txt, mods_i[i], mods_t[i], freqs_t, freqs_i)
         scale, shift = ops.linear(s, p.norm_out).reshape(b, 2, 1, cfg.hidden).unbind(1)
         out = ops.adaln_linear(img, scale, shift, p.proj_out, eps=cfg.eps)
+        if self.sp > 1:
+            full = torch.empty((self.sp * out.shape[1], out.shape[2]), dtype=out.dtype,
+                               device=out.device)
+            dist.all_gather_into_tensor(full, out[0].contiguous(), group=self.sp_group)
+            out = full.reshape(1, -1, out.shape[-1])
         return unpatchify(out, cfg.patch, c, h, w)
 
 
@@ -597,44 +703,63 @@ class MMDiT:
 # --------------------------------------------------------------------------
 @dataclass
 class Placement:
-    """Where a CFG step runs: ``world`` ranks, ``branches`` CFG branches per
-    rank (2: both batched on each rank; 1: one branch per rank group), the
-    tensor-parallel width and this rank's branch and TP rank."""
+    """Where a CFG step runs: ``world`` ranks; one rank (both branches
+    batched) or a branch per group of ``tp`` ranks (``tp`` is the group's
+    width whatever its mode); this rank's branch and rank in the group;
+    ``mode``: how a group of more than one rank splits its branch --
+    "sequence" (image tokens split, whole weights) or "tensor" (heads and
+    MLP columns split)."""
     world: int
     rank: int
     tp: int
     branch: int
     tp_rank: int
+    mode: str = "sequence"
 
     @property
     def batched(self) -> bool:
         return self.world == 1
+
+    @property
+    def tensor_parallel(self) -> bool:
+        return self.tp > 1 and self.mode == "tensor"
+
+    @property
+    def sequence_parallel(self) -> bool:
+        return self.tp > 1 and self.mode == "sequence"
 
     def describe(self) -> str:
         if self.world == 1:
             return "1 GPU: both CFG branches batched (B = 2)"
         if self.tp == 1:
             return f"{self.world} GPUs: one CFG branch per GPU, predictions all-gathered"
+        if self.mode == "sequence":
+            return (f"{self.world} GPUs: CFG branch per group of {self.tp} GPUs, the image tokens "
+                    f"split {self.tp} ways (whole weights; image k / v all-gathered per block, "
+                    "text stream on every rank), predictions all-gathered")
         return (f"{self.world} GPUs: CFG branch per group of {self.tp} GPUs x {self.tp}-way tensor "
-                "parallel (column-parallel QKV / MLP-up, row-parallel out / MLP-down with int32 "
-                "all-reduce), predictions all-gathered")
+                "parallel (column-parallel QKV / MLP-up, row-parallel out / MLP-down with exact "
+                "int32 reductions), predictions all-gathered")
 
 
-def placement(world: int, rank: int) -> Placement:
+def placement(world: int, rank: int, mode: str = "sequence") -> Placement:
     """1 rank: both branches batched.  W >= 2 (even): ranks [0, W/2) run the
     conditional branch, [W/2, W) the unconditional one, each branch over W/2
-    tensor-parallel ranks."""
+    ranks split by ``mode`` ("sequence" or "tensor")."""
+    if mode not in ("sequence", "tensor"):
+        raise ValueError(f"unknown placement mode {mode!r}")
     if world == 1:
-        return Placement(1, 0, 1, 0, 0)
+        return Placement(1, 0, 1, 0, 0, mode)
     if world % 2:
         raise ValueError("CFG placement needs an even number of ranks")
     tp = world // 2
-    return Placement(world, rank, tp, rank // tp, rank % tp)
+    return Placement(world, rank, tp, rank // tp, rank % tp, mode)
 
 
 class ProcessGroups:
-    """The tensor-parallel group of this rank's branch and the CFG pair group
-    (r, r + W/2); every rank creates every group in the same order."""
+    """The group of this rank's branch (``tp_group``, tensor- or
+    sequence-parallel) and the CFG pair group (r, r + W/2); every rank
+    creates every group in the same order."""
 
     def __init__(self, pl: Placement, backend=None):
         self.tp_group = None
@@ -650,6 +775,16 @@ class ProcessGroups:
             g = dist.new_group([r, r + pl.tp], backend=backend)
             if r == pl.tp_rank:
                 self.cfg_group = g
+
+
+def build_model(cfg: MMDiTConfig, ops, device, pl: Placement, groups: ProcessGroups,
+                seed: int = 0, fused_tp: bool = False) -> MMDiT:
+    """Random-init weights and the model of this rank for ``pl``."""
+    if pl.tensor_parallel:
+        params = random_params(cfg, ops, device, seed=seed, tp_rank=pl.tp_rank, tp_world=pl.tp)
+        return MMDiT(params, ops, groups.tp_group, fused_tp=fused_tp)
+    params = random_params(cfg, ops, device, seed=seed)
+    return MMDiT(params, ops, sp_group=groups.tp_group if pl.sequence_parallel else None)
 
 
 def cfg_model(dit: MMDiT, pl: Placement, groups: ProcessGroups, context_cond: torch.Tensor,

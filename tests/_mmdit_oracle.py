@@ -66,13 +66,24 @@ class OracleOps:
         return O.apply_residual(y, residual, gate)
 
     def attention(self, joint, heads, head_dim):
-        b = joint.shape[0]
         c = heads * head_dim
-        joint = joint.float()
-        q, k, v = (joint[..., i * c:(i + 1) * c].unflatten(-1, (heads, head_dim)).transpose(1, 2)
-                   for i in range(3))
-        a = torch.softmax(q @ k.transpose(-1, -2) / head_dim ** 0.5, dim=-1)
+        return self.attention_split(joint[..., :c], joint[..., c:], heads, head_dim)
+
+    def attention_split(self, q, kv, heads, head_dim):
+        b = q.shape[0]
+        c = heads * head_dim
+        qh = q.float().unflatten(-1, (heads, head_dim)).transpose(1, 2)
+        k, v = (kv[..., i * c:(i + 1) * c].float().unflatten(-1, (heads, head_dim)).transpose(1, 2)
+                for i in range(2))
+        a = torch.softmax(qh @ k.transpose(-1, -2) / head_dim ** 0.5, dim=-1)
         return (a @ v).transpose(1, 2).reshape(b, -1, c).to(torch.bfloat16)
+
+    def adaln_qkv_rope_split(self, x, scale, shift, p, norm_w, freqs, q_outs, kv_outs, eps=1e-6):
+        c = p.w.shape[0] // 3
+        y = self.adaln_qkv_rope(x, scale, shift, p, norm_w, freqs, 2 * c, eps)
+        for i in range(x.shape[0]):
+            q_outs[i].copy_(y[i, :, :c])
+            kv_outs[i].copy_(y[i, :, c:])
 
     def silu(self, x):
         return torch.nn.functional.silu(x)

@@ -1,11 +1,13 @@
 """The DiT step's multi-GPU placements on NCCL ranks, one process per GPU:
-CFG branches on separate GPUs (2 GPUs) and CFG x tensor parallelism
-(4 GPUs: 2-way, 8 GPUs: 4-way) against the one-GPU model with both branches
-batched, computed by every rank on its own GPU from the unsharded weights.
+CFG branches on separate GPUs (2 GPUs) and each branch split over 2 (4 GPUs)
+or 4 (8 GPUs) ranks by image tokens or by heads and MLP columns, against the
+one-GPU model with both branches batched, computed by every rank on its own
+GPU from the unsharded weights.
 
 Everything outside attention is bit-identical by construction (row-wise
 quantisers, per-row GEMMs, exact int32 partial sums, the same epilogue); the
-attention kernel is run on fewer heads and one sample per call, so the test
+attention kernel is run on fewer heads, fewer queries and one sample per
+call, so the test
 asserts bit equality of the predictions when the attention kernel itself is
 invariant to that (checked first, on the same GPU), and otherwise holds them
 to 1% of their RMS."""
@@ -40,11 +42,18 @@ def _attention_invariant(dev) -> bool:
     sub_t = torch.cat([qkv_t[1:, :, c] for c in cols], -1)
     sub_i = torch.cat([qkv_i[1:, :, c] for c in cols], -1)
     t_sub, i_sub = ops.joint_attention(sub_t, sub_i, 2, 128)
-    return (torch.equal(t_sub, t_all[1:, :, 256:512]) and
-            torch.equal(i_sub, i_all[1:, :, 256:512]))
+    heads_ok = (torch.equal(t_sub, t_all[1:, :, 256:512]) and
+                torch.equal(i_sub, i_all[1:, :, 256:512]))
+    # the queries of the text tokens and of the second half of the image
+    # tokens against the whole sequence (a sequence-parallel rank's share)
+    joint = torch.cat([qkv_t, qkv_i], dim=1)[1:]
+    mine = torch.cat([joint[:, :32], joint[:, 32 + 256:]], dim=1)
+    o = ops.attention_split(mine[..., :1024].contiguous(), joint[..., 1024:], 8, 128)
+    queries_ok = (torch.equal(o[:, :32], t_all[1:]) and torch.equal(o[:, 32:], i_all[1:, 256:]))
+    return heads_ok and queries_ok
 
 
-def _worker(rank, world, port, q, fused, graph):
+def _worker(rank, world, port, q, mode, fused, graph):
     import torch.distributed as dist
 
     from imagine_b200 import mmdit as M
@@ -59,15 +68,14 @@ def _worker(rank, world, port, q, fused, graph):
     try:
         cfg = M.MMDiTConfig(**CFG_KW)
         ops = M.NativeOps()
-        pl = M.placement(world, rank)
+        pl = M.placement(world, rank, mode)
         groups = M.ProcessGroups(pl)
         g = torch.Generator().manual_seed(21)
         lat = torch.randn(1, 16, 32, 32, generator=g).to(dev)
         ctx_c = torch.randn(1, 64, cfg.context_dim, generator=g).to(torch.bfloat16).to(dev)
         ctx_u = torch.randn(1, 64, cfg.context_dim, generator=g).to(torch.bfloat16).to(dev)
         t = torch.tensor([0.8], device=dev)
-        shard = M.MMDiT(M.random_params(cfg, ops, dev, seed=5, tp_rank=pl.tp_rank,
-                                        tp_world=pl.tp), ops, groups.tp_group, fused_tp=fused)
+        shard = M.build_model(cfg, ops, dev, pl, groups, seed=5, fused_tp=fused)
         if graph:
             cap = M.CapturedModel(shard, pl, groups, ctx_c, ctx_u, tuple(lat.shape), dev)
             oc, ou = (o.clone() for o in cap(lat, t, True))
@@ -93,13 +101,17 @@ def _worker(rank, world, port, q, fused, graph):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,fused,graph", [
-    (2, False, False), (2, False, True), (4, False, False), (4, True, False), (4, False, True),
-    (8, False, False), (8, True, False), (8, False, True)])
-def test_dit_placements_equal_one_gpu(world, fused, graph):
-    """fused: the row-parallel linears reduce through the GEMM's peer-memory
-    reduce-scatter instead of an NCCL all-reduce; graph: the forward (with
-    its NCCL collectives) replayed from a CUDA graph."""
+@pytest.mark.parametrize("world,mode,fused,graph", [
+    (2, "sequence", False, False), (2, "sequence", False, True),
+    (4, "sequence", False, False), (4, "sequence", False, True),
+    (4, "tensor", False, False), (4, "tensor", True, False), (4, "tensor", False, True),
+    (8, "sequence", False, True), (8, "tensor", True, False), (8, "tensor", False, True)])
+def test_dit_placements_equal_one_gpu(world, mode, fused, graph):
+    """mode: a branch's ranks split the image tokens ("sequence") or the heads
+    and MLP columns ("tensor"); fused: the tensor-parallel row-parallel
+    linears reduce through the GEMM's peer-memory reduce-scatter instead of
+    an NCCL all-reduce; graph: the forward (with its NCCL collectives)
+    replayed from a CUDA graph."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
@@ -107,7 +119,7 @@ def test_dit_placements_equal_one_gpu(world, fused, graph):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, fused, graph)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode, fused, graph)) for r in range(world)]
     for p in procs:
         p.start()
     out = [q.get(timeout=600) for _ in range(world)]

@@ -68,6 +68,9 @@ def test_placement(world, expect):
     assert got == expect
     with pytest.raises(ValueError):
         M.placement(3, 0)
+    assert M.placement(4, 1).sequence_parallel and not M.placement(4, 1).tensor_parallel
+    assert M.placement(4, 1, "tensor").tensor_parallel
+    assert not M.placement(2, 1).sequence_parallel and not M.placement(2, 1, "tensor").tensor_parallel
 
 
 def _oracle_model(tp_rank=0, tp_world=1, group=None, cfg=TINY, seed=0):
@@ -109,14 +112,16 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, q, mode):
+    from tests._mmdit_oracle import OracleOps
+
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.set_num_threads(1)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        pl = M.placement(world, rank)
+        pl = M.placement(world, rank, mode)
         groups = M.ProcessGroups(pl)
-        model = _oracle_model(pl.tp_rank, pl.tp, groups.tp_group)
+        model = M.build_model(TINY, OracleOps(), "cpu", pl, groups, seed=0)
         lat, ctx_c, ctx_u = _inputs()
         fn = M.cfg_model(model, pl, groups, ctx_c, ctx_u)
         oc, ou = fn(lat.float(), torch.tensor([0.55]), True)
@@ -126,11 +131,11 @@ def _rank_main(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_multi_rank_step_equals_one_rank(world):
-    """CFG branches on separate ranks (world 2) and CFG x 2-way tensor
-    parallelism (world 4) give the one-rank batched model's predictions bit
-    for bit."""
+@pytest.mark.parametrize("world,mode", [(2, "sequence"), (4, "sequence"), (4, "tensor")])
+def test_multi_rank_step_equals_one_rank(world, mode):
+    """CFG branches on separate ranks (world 2) and, on world 4, each branch
+    split over 2 ranks by image tokens (sequence) or by heads and MLP columns
+    (tensor) give the one-rank batched model's predictions bit for bit."""
     model = _oracle_model()
     lat, ctx_c, ctx_u = _inputs()
     pl = M.placement(1, 0)
@@ -139,7 +144,7 @@ def test_multi_rank_step_equals_one_rank(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
     got = [q.get(timeout=300) for _ in range(world)]
