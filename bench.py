@@ -308,6 +308,9 @@ def _cpu_model() -> str:
 # ---------------------------------------------------------------------------
 DIT_TEXT = 256
 DIT_LATENT = (16, 112, 200)
+# ranks at which the peer-memory (fused) tensor-parallel kernels have been run
+# and checked on B200; bench.py times them only up to this size
+FUSED_MAX_RANKS = 4
 
 
 def run_tp_linears(args, rank, world, local_rank):
@@ -359,15 +362,20 @@ def run_tp_linears(args, rank, world, local_rank):
         wq, ws = W.quantize_weight(w)
         ref = W.int8_linear(x, wq, ws, b, output_act=act)
         ops = 2.0 * m * n * k
+        # the fused forms have run on hardware at 2 and 4 ranks; larger jobs
+        # report the NCCL forms only
+        fused_ok = world <= FUSED_MAX_RANKS
         if act:
-            forms = {"fused_peer_stores": TP.ColumnParallelInt8Linear(wq, ws, b, output_act=act,
-                                                                      fused=True),
-                     "nccl_all_gather": TP.ColumnParallelInt8Linear(wq, ws, b, output_act=act)}
+            forms = {"nccl_all_gather": TP.ColumnParallelInt8Linear(wq, ws, b, output_act=act)}
+            if fused_ok:
+                forms["fused_peer_stores"] = TP.ColumnParallelInt8Linear(wq, ws, b, output_act=act,
+                                                                         fused=True)
             xin = x
             nvlink = m * (n - n // world) * 2
         else:
-            forms = {"fused_reduce_scatter": TP.RowParallelInt8Linear(wq, ws, b, fused=True),
-                     "nccl_all_reduce": TP.RowParallelInt8Linear(wq, ws, b)}
+            forms = {"nccl_all_reduce": TP.RowParallelInt8Linear(wq, ws, b)}
+            if fused_ok:
+                forms["fused_reduce_scatter"] = TP.RowParallelInt8Linear(wq, ws, b, fused=True)
             xin = forms["nccl_all_reduce"].shard_input(x)
             rows = int(NAT.LIB.w8a8_reduce_scatter_rows(m, world))
             nvlink = (m - min(m, rows)) * n * 4 + min(m, rows) * n * 2 * (world - 1)
@@ -464,7 +472,7 @@ def run_dit(args, rank, world, local_rank):
     e_ms, e_finite, _, _, _ = measure(pl, graph=False)
     alternatives["same placement, launched eagerly from Python"] = e_ms
     finite = finite and e_finite
-    if world >= 4:
+    if 4 <= world <= FUSED_MAX_RANKS:
         tp = MD.placement(world, rank, "tensor")
         t_ms, t_finite, _, _, _ = measure(tp, graph=False, fused_tp=True)
         alternatives[tp.describe() + "; reductions fused into the GEMMs over peer memory, "

@@ -5,6 +5,17 @@ ncu summaries under profiles/ were captured with.
     python -m imagine_b200.profile_case --kernel quantize --m 5600 --k 3072
     python -m imagine_b200.profile_case --kernel gemv --m 2 --k 3072 --n 18432
     python -m imagine_b200.profile_case --kernel gemm_rope --m 5600 --k 3072 --n 9216 --rope-cols 6144
+    python -m imagine_b200.profile_case --kernel compare_libraries --iters 20
+
+``compare_libraries`` times, on the same device buffers, this library's
+INT8 / FP8 / MXFP8 GEMMs against the library kernels the reference's sm_100
+routes call: cuBLASLt INT8 through torch._int_mm (the reference's
+``cublas_gemm_int8``, KSRC backends/cuda/ops/cublas_gemm_int8.cu:89-230, then
+its separate dequant), cuBLASLt FP8 TensorWise through torch._scaled_mm
+(``imagine_fp8_scaled_mm``, inference/native/bridge.cpp:401-413) and cuBLASLt
+MXFP8 with e8m0 block scales through torch._scaled_mm (``scaled_mm_mxfp8``,
+inference/src/backend_quant.rs:320-343), at 5600 x 3072 -> 12288 and -> 3072.
+It prints one JSON line.
 
 Inputs are seeded synthetic tensors of the BASELINE distributions; every
 launch is checked for device errors afterwards.
@@ -22,7 +33,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel", choices=["gemm", "gemm_gelu", "gemm_s32", "quantize", "convrot",
                                                        "gemv", "fp8_gemm", "mxfp8_gemm", "rms_rope",
-                                                       "gemm_rope", "sampler_euler", "sampler_er_sde", "gemv_q"],
+                                                       "gemm_rope", "sampler_euler", "sampler_er_sde", "gemv_q",
+                                                       "compare_libraries"],
                     required=True)
     ap.add_argument("--m", type=int, default=5600)
     ap.add_argument("--k", type=int, default=3072)
@@ -66,6 +78,8 @@ def main():
             else:
                 fn()
 
+    if a.kernel == "compare_libraries":
+        return compare_libraries(a, dev, g, flush, clean)
     if a.kernel.startswith("sampler_"):
         # one fused sampler step over an fp32 latent of --m x --k elements with
         # bf16 branch outputs (ER-SDE: stage 3 with noise)
@@ -197,6 +211,88 @@ def main():
         else:
             msg += f" GB/s={(a.m * a.k * 3 + 4 * a.m) / t / 1e6:.1f}"
     print(msg)
+
+
+def _timed(fn, iters, flush, clean):
+    """Median CUDA-event time (ms) of fn over iters calls, L2 flushed before
+    each, after two warm-up calls."""
+    fn()
+    fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        torch.cuda._sleep(200000)
+        flush.zero_()
+        clean.sum()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return sorted(times)[len(times) // 2]
+
+
+def compare_libraries(a, dev, g, flush, clean):
+    import json
+
+    iters = max(a.iters, 5)
+    if flush is None:
+        flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+        clean = torch.ones_like(flush)
+    out = {"l2": "flushed before every call", "iters": iters, "stat": "median ms", "shapes": {}}
+    for m, k, n in ((5600, 3072, 12288), (5600, 3072, 3072)):
+        ops = 2.0 * m * n * k
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(dev)
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        b = (torch.randn(n, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        row = {}
+
+        def rec(name, fn):
+            try:
+                t = _timed(fn, iters, flush, clean)
+                row[name] = {"ms": round(t, 4), "TOPS": round(ops / t / 1e9, 1)}
+            except Exception as e:  # a library form this torch build does not offer
+                row[name] = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:160]}"}
+
+        # INT8: int32 product, and the whole linear (dequant + bias to bf16)
+        wq, ws = W.quantize_weight(w)
+        q, xs = W.quantize_int8_rowwise(x)
+        rec("int8_s32_ours", lambda: W.int8_gemm_s32(q, wq))
+        wt = wq.t()
+        rec("int8_s32_cublaslt_int_mm", lambda: torch._int_mm(q, wt))
+        rec("int8_linear_ours_fused", lambda: W.int8_linear(x, wq, ws, b))
+
+        def cublas_route():
+            qq, sx = W.quantize_int8_rowwise(x)
+            acc = torch._int_mm(qq, wt)
+            return (acc.float() * (sx.reshape(-1, 1) * ws.reshape(1, -1))).to(torch.bfloat16) + b
+        rec("int8_linear_cublaslt_then_aten_dequant", cublas_route)
+        # FP8 per-tensor
+        sa = (x.abs().max().float() / 448).reshape(1)
+        sw = (w.abs().max().float() / 448).reshape(1)
+        a8 = W.quantize_per_tensor_fp8(x, sa)
+        w8 = W.quantize_per_tensor_fp8(w, sw)
+        rec("fp8_tensorwise_ours", lambda: W.fp8_linear(a8, sa, w8, sw, b))
+        sa0, sw0 = sa.reshape(()), sw.reshape(())
+        rec("fp8_tensorwise_cublaslt_scaled_mm",
+            lambda: torch._scaled_mm(a8, w8.t(), sa0, sw0, bias=b, out_dtype=torch.bfloat16))
+        # MXFP8 (32-element blocks, e8m0 scales in the cuBLAS blocked layout)
+        am, asf = W.quantize_mxfp8(x)
+        wm, wsf = W.quantize_mxfp8(w)
+        rec("mxfp8_ours", lambda: W.mxfp8_linear(am, asf, wm, wsf, b))
+        e8 = getattr(torch, "float8_e8m0fnu", None)
+        if e8 is not None:
+            asf8, wsf8 = asf.view(e8), wsf.view(e8)
+            rec("mxfp8_cublaslt_scaled_mm",
+                lambda: torch._scaled_mm(am, wm.t(), asf8, wsf8, bias=b, out_dtype=torch.bfloat16))
+        else:
+            row["mxfp8_cublaslt_scaled_mm"] = {"unavailable": "no float8_e8m0fnu dtype"}
+        out["shapes"][f"{m}x{k}x{n}"] = row
+    err = W.device_error()
+    if err:
+        raise SystemExit(f"device error {err}")
+    print(json.dumps(out))
 
 
 if __name__ == "__main__":

@@ -131,11 +131,13 @@ def _rank_main(rank, world, port, q, mode):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,mode", [(2, "sequence"), (4, "sequence"), (4, "tensor")])
+@pytest.mark.parametrize("world,mode", [(2, "sequence"), (4, "sequence"), (4, "tensor"),
+                                        (8, "sequence")])
 def test_multi_rank_step_equals_one_rank(world, mode):
     """CFG branches on separate ranks (world 2) and, on world 4, each branch
     split over 2 ranks by image tokens (sequence) or by heads and MLP columns
-    (tensor) give the one-rank batched model's predictions bit for bit."""
+    (tensor), and on world 8 the image tokens split 4 ways, give the one-rank
+    batched model's predictions bit for bit."""
     model = _oracle_model()
     lat, ctx_c, ctx_u = _inputs()
     pl = M.placement(1, 0)
