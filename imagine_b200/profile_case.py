@@ -34,7 +34,7 @@ def main():
     ap.add_argument("--kernel", choices=["gemm", "gemm_gelu", "gemm_s32", "quantize", "convrot",
                                                        "gemv", "fp8_gemm", "mxfp8_gemm", "rms_rope",
                                                        "gemm_rope", "sampler_euler", "sampler_er_sde", "gemv_q",
-                                                       "compare_libraries"],
+                                                       "compare_libraries", "modulated", "dit_step"],
                     required=True)
     ap.add_argument("--m", type=int, default=5600)
     ap.add_argument("--k", type=int, default=3072)
@@ -47,6 +47,11 @@ def main():
     ap.add_argument("--tiled", action="store_true", help="GEMM on the pre-tiled weight layout")
     ap.add_argument("--split-k", type=int, default=1,
                     help="GEMM K splits (0: chosen from the SM count, 1: off)")
+    ap.add_argument("--mode", default="adaln",
+                    choices=["scale", "rms_scale", "adaln", "rms_adaln"],
+                    help="modulated: the modulation fused into the quantiser (rows of --m split "
+                         "into two samples)")
+    ap.add_argument("--blocks", type=int, default=60, help="dit_step: MMDiT blocks")
     ap.add_argument("--time", action="store_true",
                     help="time each launch with CUDA events (L2 flushed before each) and print "
                          "the median")
@@ -80,7 +85,46 @@ def main():
 
     if a.kernel == "compare_libraries":
         return compare_libraries(a, dev, g, flush, clean)
-    if a.kernel.startswith("sampler_"):
+    if a.kernel == "dit_step":
+        # --iters eager denoising steps of the MMDiT at 1600x896, both CFG
+        # branches batched on this GPU (the launch list of one step: skip the
+        # set-up and warm-up launches, capture about 25 x --blocks launches)
+        from imagine_b200 import mmdit as MD
+
+        cfg_m = MD.MMDiTConfig(blocks=a.blocks)
+        ops = MD.NativeOps()
+        pl = MD.placement(1, 0)
+        groups = MD.ProcessGroups(pl)
+        dit = MD.build_model(cfg_m, ops, dev, pl, groups, seed=1)
+        lat = torch.randn(1, 16, 112, 200, generator=g).to(dev)
+        cc = torch.randn(1, 256, 3072, generator=g).to(torch.bfloat16).to(dev)
+        cu = torch.randn(1, 256, 3072, generator=g).to(torch.bfloat16).to(dev)
+        loop = MD.DenoiseLoop(MD.cfg_model(dit, pl, groups, cc, cu), lat)
+        step = [0]
+
+        def one():
+            # every step after the first inside the NVTX range "dit_step" (for
+            # ncu --nvtx --nvtx-include dit_step/)
+            if step[0]:
+                torch.cuda.nvtx.range_push("dit_step")
+            loop.step(step[0])
+            if step[0]:
+                torch.cuda.nvtx.range_pop()
+            step[0] += 1
+        run(one)
+        a.m, a.k, a.n = 1, 1, 1
+    elif a.kernel == "modulated":
+        b2 = 2 if a.m % 2 == 0 else 1
+        xm = x.reshape(b2, a.m // b2, a.k)
+        sc = (0.3 * torch.randn(b2, 1, a.k, generator=g)).to(torch.bfloat16).to(dev)
+        sh = (0.3 * torch.randn(b2, 1, a.k, generator=g)).to(torch.bfloat16).to(dev)
+        nw = (1 + 0.1 * torch.randn(a.k, generator=g)).to(torch.bfloat16).to(dev)
+        if a.mode in ("scale", "rms_scale"):
+            sc = sc[:1]
+        run(lambda: W.quantize_int8_rowwise_modulated(
+            xm, a.mode, sc, sh if "adaln" in a.mode else None,
+            nw if a.mode == "rms_scale" else None))
+    elif a.kernel.startswith("sampler_"):
         # one fused sampler step over an fp32 latent of --m x --k elements with
         # bf16 branch outputs (ER-SDE: stage 3 with noise)
         from imagine_b200 import _native as NAT
@@ -206,7 +250,9 @@ def main():
             # outputs 4; ER-SDE stage 3 with noise adds history in/out 16 and noise 4
             per = 12 if a.kernel == "sampler_euler" else 32
             msg += f" GB/s={a.m * a.k * per / t / 1e6:.1f}"
-        elif a.kernel not in ("quantize", "convrot", "rms_rope"):
+        elif a.kernel == "dit_step":
+            msg += f" blocks={a.blocks}"
+        elif a.kernel not in ("quantize", "convrot", "rms_rope", "modulated"):
             msg += f" TOPS={ops / t / 1e9:.1f}"
         else:
             msg += f" GB/s={(a.m * a.k * 3 + 4 * a.m) / t / 1e6:.1f}"
