@@ -1,9 +1,11 @@
-"""Tensor-parallel linears on 2 GPUs with the native kernels: the NCCL forms
-(column- and row-parallel) and the column-parallel linear whose all-gather is
-fused into the GEMM epilogue (chunk copies over NVLink) and the row-parallel
-linear whose reduce-scatter is fused into the GEMM epilogue must all equal the
-single-GPU int8_linear bit for bit; CFG-parallel sampling (one branch per GPU)
-must give the single-GPU latent.  Skips on boxes with fewer than two GPUs."""
+"""Tensor-parallel linears on 2, 4 and 8 GPUs with the native kernels: the NCCL
+forms (column- and row-parallel) and the column-parallel linear whose
+all-gather is fused into the GEMM epilogue (chunk copies over NVLink) and the
+row-parallel linear whose reduce-scatter is fused into the GEMM epilogue must
+all equal the single-GPU int8_linear bit for bit -- including the AdaLN
+modulation linear (2 rows of SiLU(temb), 3072 -> 18432) column-parallel
+through the fused path; on 2 GPUs CFG-parallel sampling (one branch per GPU)
+must give the single-GPU latent.  Each size skips on boxes with fewer GPUs."""
 import os
 import socket
 
@@ -73,6 +75,23 @@ def _worker(rank, world, port, q):
         ok_fused &= torch.equal(rowf(rowf.shard_input(x2), out_dtype=torch.float32), want32)
         torch.cuda.synchronize()
         ok_fused &= W.device_error() == 0
+        # the AdaLN modulation linear: 2 rows (CFG) of SiLU(temb), 3072 -> 18432,
+        # column-parallel with the all-gather fused into the GEMM
+        wm = (torch.randn(18432, k, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        bm = (torch.randn(18432, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        wmq, wms = W.quantize_weight(wm)
+        s_temb = torch.nn.functional.silu(torch.randn(2, k, generator=g).to(torch.bfloat16)).to(dev)
+        modf = TP.ColumnParallelInt8Linear(wmq, wms, bm, fused=True)
+        assert modf.fused
+        want = W.int8_linear(s_temb, wmq, wms, bm)
+        for _ in range(2):
+            ok_fused &= torch.equal(modf(s_temb).view(torch.int16), want.view(torch.int16))
+        torch.cuda.synchronize()
+        ok_fused &= W.device_error() == 0
+        if world != 2:
+            q.put((rank, torch.equal(y_col.view(torch.int16), ref.view(torch.int16)),
+                   torch.equal(y_row.view(torch.int16), ref.view(torch.int16)), bool(ok_fused)))
+            return
         # CFG-parallel sampling: rank r evaluates branch r, one all-gather of
         # the outputs, then the fused ER-SDE step on every rank -- the same
         # latent as both branches on one GPU
@@ -101,11 +120,12 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tensor_parallel_nccl_bit_exact():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel_nccl_bit_exact(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
-    world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
