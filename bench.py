@@ -438,45 +438,55 @@ def run_dit(args, rank, world, local_rank):
     warm = max(3, args.dit_warmup)
     steps = args.dit_steps
 
-    def measure(pl, graph, fused_tp=False, clocks=False):
+    def measure(pl, graph, fused_tp=False, rounds=2):
+        """Best ms per launch mode ("eager", and "graph" when asked) of one
+        placement: one model build, the modes timed in alternation."""
         groups = MD.ProcessGroups(pl)
         t0 = time.perf_counter()
         dit = MD.build_model(cfg, ops, dev, pl, groups, seed=1234, fused_tp=fused_tp)
         torch.cuda.synchronize()
         init_s = time.perf_counter() - t0
+        models = {"eager": MD.cfg_model(dit, pl, groups, ctx_c, ctx_u)}
         cap = None
+        best = {}
+        finite = True
         try:
             if graph:
                 cap = MD.CapturedModel(dit, pl, groups, ctx_c, ctx_u, (1, *DIT_LATENT), dev)
                 cap.capture()
-                model = cap
-            else:
-                model = MD.cfg_model(dit, pl, groups, ctx_c, ctx_u)
-            loop = MD.DenoiseLoop(model, lat, steps=40, cfg_scale=2.5)
-            ms, finite, clk = _time_loop(loop, warm, steps, rank, world, local_rank, dev,
-                                         clocks=clocks)
+                models["graph"] = cap
+            for _ in range(rounds):
+                for mode, model in models.items():
+                    loop = MD.DenoiseLoop(model, lat, steps=40, cfg_scale=2.5)
+                    ms, fin, clk = _time_loop(loop, warm, steps, rank, world, local_rank, dev,
+                                              clocks=True)
+                    finite = finite and fin
+                    if mode not in best or ms < best[mode][0]:
+                        best[mode] = (ms, clk)
         finally:
             if cap is not None:
                 cap.release()
         wbytes = dit.p.weight_bytes
-        del dit
+        del dit, models
         torch.cuda.empty_cache()
-        return ms, finite, clk, init_s, wbytes
+        return best, finite, init_s, wbytes
 
-    # the headline form: image tokens split across the ranks of a branch
-    # (sequence-parallel) on 4+ GPUs; the forward captured once as a CUDA
-    # graph and replayed every step
+    # the headline: on 4+ GPUs the image tokens split across the ranks of a
+    # branch (sequence-parallel); the step launched eagerly and replayed from
+    # one captured CUDA graph, timed in alternation, the faster form reported
     pl = MD.placement(world, rank, "sequence")
-    ms, finite, clocks, init_s, wbytes = measure(pl, graph=True, clocks=True)
-    alternatives = {}
-    e_ms, e_finite, _, _, _ = measure(pl, graph=False)
-    alternatives["same placement, launched eagerly from Python"] = e_ms
-    finite = finite and e_finite
+    best, finite, init_s, wbytes = measure(pl, graph=True)
+    mode = min(best, key=lambda m: best[m][0])
+    ms, clocks = best[mode]
+    launch_desc = {"graph": "the forward of both branches captured once as a CUDA graph and "
+                            "replayed per step (with its NCCL collectives)",
+                   "eager": "the forward launched from Python kernel by kernel"}
+    alternatives = {f"same placement, {launch_desc[m]}": best[m][0] for m in best if m != mode}
     if 4 <= world <= FUSED_MAX_RANKS:
         tp = MD.placement(world, rank, "tensor")
-        t_ms, t_finite, _, _, _ = measure(tp, graph=False, fused_tp=True)
+        tbest, t_finite, _, _ = measure(tp, graph=False, fused_tp=True, rounds=1)
         alternatives[tp.describe() + "; reductions fused into the GEMMs over peer memory, "
-                     "eager"] = t_ms
+                     "launched eagerly"] = tbest["eager"][0]
         finite = finite and t_finite
     import imagine_b200 as W
 
@@ -494,8 +504,8 @@ def run_dit(args, rank, world, local_rank):
             "workload": "1600x896 (latent 16x112x200 -> 5600 image tokens) + 256 text tokens, "
                         "CFG batch 2 (scale 2.5), Euler flow sampler, 40-step schedule",
             "placement": pl.describe(),
-            "launch": "the forward of both branches captured once as a CUDA graph, replayed per "
-                      "step (with its NCCL collectives); the sampler step a separate kernel",
+            "launch": launch_desc[mode] + "; the sampler step one fused kernel; best of "
+                      "2 timed runs per launch form, the forms alternated",
             "alternatives_ms": alternatives,
             "attention": "torch scaled_dot_product_attention, bf16 (cuDNN backend first)",
             "linear_tops_per_step": lin_ops / 1e12, "attention_tflop_per_step": attn_flops / 1e12,
