@@ -23,8 +23,8 @@ ERR_INDEX = -21
 
 F32, F16, BF16, S32, S8, E4M3 = 0, 1, 2, 3, 4, 5
 MAX_RANKS, PEER_FLAG_WORDS = 8, 32
-SCALE_EAGER, SCALE_KITCHEN = 0, 1
-DQ_EAGER, DQ_SCALE_PRODUCT, DQ_CHAINED = 0, 1, 2
+SCALE_EAGER, SCALE_KITCHEN, SCALE_KITCHEN_CUDA = 0, 1, 2
+DQ_EAGER, DQ_SCALE_PRODUCT, DQ_CHAINED, DQ_SEPARATE = 0, 1, 2, 3
 ACT_NONE, ACT_GELU_TANH = 0, 1
 STEP_DENOISED, STEP_EULER, STEP_ER_SDE, STEP_CHURN = 0, 1, 2, 3
 

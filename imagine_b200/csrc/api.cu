@@ -63,7 +63,9 @@ int finish(int rc) {
 
 bool is_float_dtype(int d) { return d == W8A8_F32 || d == W8A8_F16 || d == W8A8_BF16; }
 
-int check_epilogue(const w8a8_epilogue_t* epi, int64_t N, bool need_ws) {
+// cuda_core: the entry point runs the epilogue on CUDA cores (dequant_one),
+// which alone offers W8A8_DQ_SEPARATE.
+int check_epilogue(const w8a8_epilogue_t* epi, int64_t N, bool need_ws, bool cuda_core = false) {
   if (!epi) return fail(W8A8_ERR_VALUE, "epilogue descriptor is NULL");
   if (need_ws) {
     if (!epi->ws) return fail(W8A8_ERR_VALUE, "weight scale pointer is NULL");
@@ -84,7 +86,12 @@ int check_epilogue(const w8a8_epilogue_t* epi, int64_t N, bool need_ws) {
     return fail(W8A8_ERR_VALUE, "residual row stride %lld < N=%lld",
                 static_cast<long long>(epi->ldr), static_cast<long long>(N));
   }
-  if (epi->dequant_order < W8A8_DQ_EAGER || epi->dequant_order > W8A8_DQ_CHAINED) {
+  if (epi->dequant_order == W8A8_DQ_SEPARATE && !cuda_core) {
+    return fail(W8A8_ERR_VALUE,
+                "dequant order SEPARATE is offered by the GEMV, the small linear and the "
+                "stand-alone dequant only");
+  }
+  if (epi->dequant_order < W8A8_DQ_EAGER || epi->dequant_order > W8A8_DQ_SEPARATE) {
     return fail(W8A8_ERR_VALUE, "unknown dequant order %d", epi->dequant_order);
   }
   if (epi->activation != W8A8_ACT_NONE && epi->activation != W8A8_ACT_GELU_TANH) {
@@ -104,7 +111,7 @@ const char* w8a8_last_error(void) { return g_last_error; }
 
 int w8a8_last_accelerator_code(void) { return g_last_accel; }
 
-int w8a8_abi_version(void) { return 102; }
+int w8a8_abi_version(void) { return 103; }
 
 int w8a8_device_error(void* stream) {
   int v = 0;
@@ -122,7 +129,7 @@ int w8a8_quantize_rowwise(const void* x, int x_dtype, int64_t rows, int64_t cols
                           uint64_t seed, void* stream) {
   if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
-  if (scale_mode != W8A8_SCALE_EAGER && scale_mode != W8A8_SCALE_KITCHEN) {
+  if (scale_mode < W8A8_SCALE_EAGER || scale_mode > W8A8_SCALE_KITCHEN_CUDA) {
     return fail(W8A8_ERR_VALUE, "unknown scale mode %d", scale_mode);
   }
   if (rows == 0 || cols == 0) return finish(0);
@@ -142,7 +149,7 @@ int w8a8_quantize_rowwise_convrot(const void* x, int x_dtype, int64_t rows, int6
                                   int scale_mode, void* stream) {
   if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
-  if (scale_mode != W8A8_SCALE_EAGER && scale_mode != W8A8_SCALE_KITCHEN) {
+  if (scale_mode < W8A8_SCALE_EAGER || scale_mode > W8A8_SCALE_KITCHEN_CUDA) {
     return fail(W8A8_ERR_VALUE, "unknown scale mode %d", scale_mode);
   }
   if (group != 0 && group != 256) {
@@ -177,7 +184,7 @@ int w8a8_quantize_rowwise_modulated(const void* x, int x_dtype, int64_t rows, in
                                     float* scale, int scale_mode, void* stream) {
   if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
-  if (scale_mode != W8A8_SCALE_EAGER && scale_mode != W8A8_SCALE_KITCHEN) {
+  if (scale_mode < W8A8_SCALE_EAGER || scale_mode > W8A8_SCALE_KITCHEN_CUDA) {
     return fail(W8A8_ERR_VALUE, "unknown scale mode %d", scale_mode);
   }
   if (mode < W8A8_MOD_SCALE || mode > W8A8_MOD_RMS_ADALN) {
@@ -541,7 +548,7 @@ int w8a8_quantize_rowwise_given_absmax(const void* x, int x_dtype, int64_t rows,
                                        float* scale, int scale_mode, void* stream) {
   if (rows < 0 || cols < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
-  if (scale_mode != W8A8_SCALE_EAGER && scale_mode != W8A8_SCALE_KITCHEN) {
+  if (scale_mode < W8A8_SCALE_EAGER || scale_mode > W8A8_SCALE_KITCHEN_CUDA) {
     return fail(W8A8_ERR_VALUE, "unknown scale mode %d", scale_mode);
   }
   if (rows == 0 || cols == 0) return finish(0);
@@ -740,7 +747,7 @@ int w8a8_dequantize_linear(const int32_t* acc, const float* xs, const w8a8_epilo
                            void* out, int out_dtype, int64_t M, int64_t N, void* stream) {
   if (M < 0 || N < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
-  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (int rc = check_epilogue(epi, N, true, true)) return rc;
   if (M == 0 || N == 0) return finish(0);
   if (!acc || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
   return finish(dequant_launch(acc, xs, epi, out, out_dtype, M, N, static_cast<cudaStream_t>(stream)));
@@ -752,7 +759,7 @@ int w8a8_gemv_dequant(const int8_t* q, const int8_t* w, const float* xs,
   if (M != 1 && M != 2) return fail(W8A8_ERR_VALUE, "GEMV supports M in {1, 2}, got %lld", static_cast<long long>(M));
   if (N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
-  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (int rc = check_epilogue(epi, N, true, true)) return rc;
   if (N == 0) return finish(0);
   if (!q || !w || !xs || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
   return finish(gemv_launch(q, w, xs, epi, out, out_dtype, M, N, K, static_cast<cudaStream_t>(stream)));
@@ -765,10 +772,10 @@ int w8a8_linear_small(const void* x, int x_dtype, const int8_t* w, const w8a8_ep
   if (N < 0 || K < 0) return fail(W8A8_ERR_VALUE, "negative shape");
   if (!is_float_dtype(x_dtype)) return fail(W8A8_ERR_VALUE, "input dtype code %d is not floating", x_dtype);
   if (!is_float_dtype(out_dtype)) return fail(W8A8_ERR_VALUE, "output dtype code %d is not floating", out_dtype);
-  if (scale_mode != W8A8_SCALE_EAGER && scale_mode != W8A8_SCALE_KITCHEN) {
+  if (scale_mode < W8A8_SCALE_EAGER || scale_mode > W8A8_SCALE_KITCHEN_CUDA) {
     return fail(W8A8_ERR_VALUE, "unknown scale mode %d", scale_mode);
   }
-  if (int rc = check_epilogue(epi, N, true)) return rc;
+  if (int rc = check_epilogue(epi, N, true, true)) return rc;
   if (N == 0) return finish(0);
   if (!x || !w || !out) return fail(W8A8_ERR_VALUE, "NULL tensor pointer");
   return finish(linear_small_launch(x, x_dtype, w, epi, scale_mode, q_out, xs_out, out, out_dtype,

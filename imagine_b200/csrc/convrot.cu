@@ -161,6 +161,80 @@ __device__ __forceinline__ float in_silu(float g) { return g / (1.0f + expf(-g))
 
 __device__ __forceinline__ float in_sigmoid(float g) { return 1.0f / (1.0f + expf(-g)); }
 
+// The same activations as the reference's Kitchen CUDA kernels compute them
+// as built (--use_fast_math, native/comfy-port/CMakeLists.txt:30-36): there
+// tanhf is tanh.approx.f32, expf is __expf and a divide is __fdividef (the
+// intrinsic forms give bit-identical outputs to that build's).  Used with the
+// W8A8_SCALE_KITCHEN_CUDA numerics on the rotated route.
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float in_gelu_tanh_fast(float v) {
+  const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+  return 0.5f * v * (1.0f + tanh_fast(inner));
+}
+
+__device__ __forceinline__ float in_silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+__device__ __forceinline__ float in_sigmoid_fast(float g) {
+  return __fdividef(1.0f, 1.0f + __expf(-g));
+}
+
+// Sum of squares of a K-wide row in the order the reference's fused kernel
+// forms it (int8_linear.cu:1239-1248 with block_reduce_sum_f32_t, :141-158):
+// B threads (its block size for this launch, chosen from the row count and K
+// at :1668-1673) each accumulate v*v with FMA over columns t, t + B, ...; a
+// shuffle-down tree (offsets 16 .. 1) within each warp; the same tree over
+// the warp totals, zero-padded to 32.  This CTA's threads emulate the B
+// partial sums in `part` (1024 + 33 floats: the partials, the warp totals
+// and the result) and the trees in registers.
+template <typename T>
+__device__ float sumsq_reference_order(const void* x, int64_t xrow, int K, int rows, float* part) {
+  const int B = rows == 1 ? 512
+              : K == 256 ? 64
+              : K <= 3072 ? 128
+              : K <= 6144 ? 256
+              : K < 12288 ? 512
+              : 1024;
+  for (int t = threadIdx.x; t < B; t += blockDim.x) {
+    float acc = 0.0f;
+    for (int c = t; c < K; c += B) {
+      const float v = Ld<T>::at(x, xrow + c);
+      acc = __fmaf_rn(v, v, acc);
+    }
+    part[t] = acc;
+  }
+  __syncthreads();
+  auto tree32 = [](float* a) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int i = 0; i < o; ++i) a[i] = __fadd_rn(a[i], a[i + o]);
+    }
+    return a[0];
+  };
+  const int warps = B / 32;
+  float w[32];
+  if (static_cast<int>(threadIdx.x) < warps) {
+    for (int i = 0; i < 32; ++i) w[i] = part[32 * threadIdx.x + i];
+    part[1024 + threadIdx.x] = tree32(w);  // warp totals after the B partials
+  }
+  __syncthreads();
+  float result = 0.0f;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 32; ++i) w[i] = i < warps ? part[1024 + i] : 0.0f;
+    result = tree32(w);
+    part[1024 + 32] = result;
+  }
+  __syncthreads();
+  result = part[1024 + 32];
+  __syncthreads();
+  return result;
+}
+
 // Packed pairs (pk / lo / hi / add2 / sub2 / mul2 / fma2, quant_common.cuh):
 // element j of two 256-groups of the row in one 64-bit register pair, so
 // every f32x2 instruction serves both groups.
@@ -188,7 +262,7 @@ __device__ __forceinline__ void h4x2(uint64_t& a, uint64_t& b, uint64_t& c, uint
 // complement): clamp(rne(T(T(v) / div)), -128, 127).
 template <typename T>
 __device__ __forceinline__ void quant_pair(uint64_t p, float div, float recip, uint32_t& c0,
-                                           uint32_t& c1) {
+                                           uint32_t& c1, bool fast) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
     // paired RN conversions; exact quotients by one packed FMA correction
     // (div_exact_short); rne by adding 1.5 * 2^23
@@ -208,8 +282,8 @@ __device__ __forceinline__ void quant_pair(uint64_t p, float div, float recip, u
     c0 = __float_as_uint(lo(t));
     c1 = __float_as_uint(hi(t));
   } else {
-    c0 = static_cast<uint32_t>(quant_code<T>(QuantTraits<T>::round_t(lo(p)), div, recip));
-    c1 = static_cast<uint32_t>(quant_code<T>(QuantTraits<T>::round_t(hi(p)), div, recip));
+    c0 = static_cast<uint32_t>(quant_code<T>(QuantTraits<T>::round_t(lo(p)), div, recip, fast));
+    c1 = static_cast<uint32_t>(quant_code<T>(QuantTraits<T>::round_t(hi(p)), div, recip, fast));
   }
 }
 
@@ -261,6 +335,9 @@ __device__ __forceinline__ void act_rot_row(
   // The activation is T-rounded at each step the ATen sequence rounds, except
   // for the kitchen numerics of the fused ConvRot kernel (fp32 throughout).
   const bool kRound = !ROT || !kitchen_mode;
+  // the Kitchen CUDA build's fast-math activations (rotated route only; the
+  // unrotated route stands for ATen operators, which are not built that way)
+  const bool fast_act = ROT && kitchen_mode == kScaleKitchenCuda;
 
   // v[i][h][j]: element 16 r + j of group 2 (team + i teams) + h
   float v[PPT][2][16];
@@ -281,7 +358,13 @@ __device__ __forceinline__ void act_rot_row(
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             if constexpr (ACT == kInSwiGLU) {
-              f[j] = rt<T>(rt<T>(in_silu(gate[j]), kRound) * up[j], kRound);
+              const float sg = fast_act ? in_silu_fast(gate[j]) : in_silu(gate[j]);
+              f[j] = rt<T>(rt<T>(sg, kRound) * up[j], kRound);
+            } else if (fast_act) {
+              // SiTU in the fast-math forms
+              const float a = 25.0f * tanh_fast(__fdividef(gate[j], 25.0f));
+              const float t4 = 4.0f * tanh_fast(__fdividef(up[j], 4.0f));
+              f[j] = a * (t4 * in_sigmoid_fast(up[j]));
             } else {
               // 25 tanh(a / 25) * (4 tanh(b / 4) * sigmoid(b))
               // (inference/src/int8_linear.rs:54-74)
@@ -297,7 +380,9 @@ __device__ __forceinline__ void act_rot_row(
           load16<T>(x, xrow + col, vec_in, f);
           if constexpr (ACT == kInGeluTanh) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) f[j] = rt<T>(in_gelu_tanh(f[j]), kRound);
+            for (int j = 0; j < 16; ++j) {
+              f[j] = fast_act ? in_gelu_tanh_fast(f[j]) : rt<T>(in_gelu_tanh(f[j]), kRound);
+            }
           } else if constexpr (ACT == kInRmsNorm || ACT == kInRmsModScale || ACT == kInRmsAdaLN) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) sumsq = __fmaf_rn(f[j], f[j], sumsq);
@@ -318,8 +403,19 @@ __device__ __forceinline__ void act_rot_row(
   if constexpr (ACT == kInRmsNorm) {
     // x * rsqrt(mean(x^2) + eps) * w  (int8_linear.cu:1239-1267; ATen's
     // rms_norm forms the same fp32 product and rounds it to T once)
-    const float ss = block_reduce<8>(sumsq, false, red);
-    const float rstd = rsqrtf(ss / static_cast<float>(K) + act_eps);
+    float rstd;
+    if constexpr (ROT) {
+      if (fast_act) {
+        // the reference kernel's summation order and fast-math divide
+        __shared__ float part[1024 + 64];
+        const float ss = sumsq_reference_order<T>(x, xrow, K, static_cast<int>(gridDim.x), part);
+        rstd = rsqrtf(__fdividef(ss, static_cast<float>(K)) + act_eps);
+      } else {
+        rstd = rsqrtf(block_reduce<8>(sumsq, false, red) / static_cast<float>(K) + act_eps);
+      }
+    } else {
+      rstd = rsqrtf(block_reduce<8>(sumsq, false, red) / static_cast<float>(K) + act_eps);
+    }
 #pragma unroll
     for (int i = 0; i < PPT; ++i) {
 #pragma unroll
@@ -500,8 +596,9 @@ __device__ __forceinline__ void act_rot_row(
   // eager: the reference's rotated row is T-typed, so its absmax is T(amax)
   const float s = quant_row_scale<T>(kitchen_mode ? amax : QuantTraits<T>::round_t(amax), kitchen_mode);
   if (threadIdx.x == 0) scales[row] = s;
-  const float div = quant_divisor<T>(s);
+  const float div = quant_divisor<T>(s, kitchen_mode);
   const float recip = __frcp_rn(div);
+  const bool fast_div = kitchen_mode == kScaleKitchenCuda;
 
   // ---- codes: bytes into the team's code buffer at the element's position,
   // then 16 contiguous bytes per thread and group to global memory
@@ -512,7 +609,7 @@ __device__ __forceinline__ void act_rot_row(
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       uint32_t c0, c1;
-      quant_pair<T>(pk(v[i][0][j], v[i][1][j]), div, recip, c0, c1);
+      quant_pair<T>(pk(v[i][0][j], v[i][1][j]), div, recip, c0, c1, fast_div);
       const int e = ROT ? r + 16 * j : 16 * r + j;
       cbuf[e] = static_cast<uint8_t>(c0);
       cbuf[kCodeStride + e] = static_cast<uint8_t>(c1);
@@ -627,7 +724,7 @@ int quantize_act_rot_launch(const void* x, int x_dtype, int64_t rows, int64_t co
                             cudaStream_t stream) {
   if (rows == 0) return 0;
   const int K = static_cast<int>(cols);
-  const int km = scale_mode == W8A8_SCALE_KITCHEN ? 1 : 0;
+  const int km = scale_mode;  // nonzero: kitchen scales (W8A8_SCALE_*)
   const ModArgs mod{mod_scale, mod_shift, mod_group > 0 ? mod_group : 1};
   switch (x_dtype) {
     case W8A8_BF16:

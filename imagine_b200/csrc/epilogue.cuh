@@ -14,9 +14,15 @@ namespace w8a8 {
 //                   y = T(acc * (xs*ws)); y = T(y + bias)         (two roundings)
 //   kDqScaleProduct KSRC backends/triton/quantization.py:861-1018
 //                   y = T(fma(acc, xs*ws, bias))                  (one rounding)
-//   kDqChained      native/comfy-port/kitchen/int8_linear.cu:517-545, 585-708
+//   kDqChained      native/comfy-port/kitchen/int8_linear.cu:669-708 (two-row GEMV)
 //                   y = T(fma(acc*xs, ws, bias))                  (one rounding)
-enum DequantOrder : int { kDqEager = 0, kDqScaleProduct = 1, kDqChained = 2 };
+//   kDqSeparate     native/comfy-port/kitchen/int8_linear.cu:518-543, 586-667
+//                   (stand-alone dequant with a bias, one-row GEMV: the bias
+//                   added in a statement of its own, so not contracted)
+//                   y = T((acc*xs)*ws + bias)                     (three fp32 roundings)
+//                   CUDA-core paths only (dequant_one); the tensor-core GEMM
+//                   epilogues take orders 0-2.
+enum DequantOrder : int { kDqEager = 0, kDqScaleProduct = 1, kDqChained = 2, kDqSeparate = 3 };
 // kActRmsRope: per-head RMSNorm + interleaved RoPE of 128-column heads (the
 // QKV projection's epilogue; GEMM with 256-column tiles and bf16 output only)
 enum OutputAct : int { kActNone = 0, kActGeluTanh = 1, kActRmsRope = 2 };
@@ -137,6 +143,9 @@ __device__ __forceinline__ float dequant_one(float a, float xs_row, float ws_col
   } else if (order == kDqScaleProduct) {
     const float s = __fmul_rn(xs_row, ws_col);
     y = OutTraits<OutT>::round(has_bias ? __fmaf_rn(a, s, bias_col) : __fmul_rn(a, s));
+  } else if (order == kDqSeparate) {
+    const float t = __fmul_rn(__fmul_rn(a, xs_row), ws_col);
+    y = OutTraits<OutT>::round(has_bias ? __fadd_rn(t, bias_col) : t);
   } else {
     const float t = __fmul_rn(a, xs_row);
     y = OutTraits<OutT>::round(has_bias ? __fmaf_rn(t, ws_col, bias_col) : __fmul_rn(t, ws_col));

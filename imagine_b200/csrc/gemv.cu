@@ -91,11 +91,11 @@ __device__ void quantize_rows_to_smem(const T* __restrict__ x, int rows, int K, 
     for (int c = threadIdx.x; c < K; c += kGemvThreads) amax = fmaxf(amax, fabsf(In<T>::f(xr[c])));
     amax = block_max(amax, red);
     const float scale = quant_row_scale<T>(amax, scale_mode);
-    const float div = quant_divisor<T>(scale);
+    const float div = quant_divisor<T>(scale, scale_mode);
     const float recip = __frcp_rn(div);
     if (threadIdx.x == 0) s_scale[m] = scale;
     for (int c = threadIdx.x; c < K; c += kGemvThreads) {
-      const int v = quant_code<T>(In<T>::f(xr[c]), div, recip);
+      const int v = quant_code<T>(In<T>::f(xr[c]), div, recip, scale_mode == kScaleKitchenCuda);
       sq[m * K + c] = static_cast<int8_t>(v);
     }
   }

@@ -139,8 +139,16 @@ void rc_or_throw(int rc) {
   throw std::runtime_error(m);
 }
 
+// Dequant order of the Kitchen kernel each entry stands for
+// (native/comfy-port/kitchen/int8_linear.cu as built, fmad on):
+//   one-row GEMV (586-667) and the stand-alone dequant with a bias (518-543):
+//     (acc*xs)*ws, then + bias in a statement of its own -> SEPARATE;
+//   two-row GEMV (669-708): acc*xs*ws + b in one expression -> CHAINED (FMA);
+//   stand-alone dequant without a bias (545-583): acc*(xs*ws) for a scalar
+//     weight scale and N % 4 == 0 (its vec4 kernel) -> SCALE_PRODUCT, else
+//     (acc*xs)*ws -> CHAINED (no bias: the same two products).
 w8a8_epilogue_t epilogue(const at::Tensor& ws, const at::Tensor* bias, const at::Tensor* resid,
-                         const at::Tensor* rscale, int64_t n) {
+                         const at::Tensor* rscale, int64_t n, int order = W8A8_DQ_CHAINED) {
   w8a8_epilogue_t e{};
   e.ws = ws.data_ptr<float>();
   e.ws_numel = ws.numel();
@@ -148,7 +156,7 @@ w8a8_epilogue_t epilogue(const at::Tensor& ws, const at::Tensor* bias, const at:
   e.residual = resid ? resid->data_ptr() : nullptr;
   e.ldr = n;
   e.residual_scale = rscale ? rscale->data_ptr() : nullptr;
-  e.dequant_order = W8A8_DQ_CHAINED;
+  e.dequant_order = order;
   e.activation = W8A8_ACT_NONE;
   return e;
 }
@@ -167,7 +175,7 @@ int64_t dispatch(const char* name, const Args& a) {
     rows_cols(x, rows, k, ldx);
     rc_or_throw(w8a8_quantize_rowwise(x.data_ptr(), dtype_code(x), rows, k, ldx,
                                       a.tensor(1).data_ptr<int8_t>(), k,
-                                      a.tensor(2).data_ptr<float>(), W8A8_SCALE_KITCHEN,
+                                      a.tensor(2).data_ptr<float>(), W8A8_SCALE_KITCHEN_CUDA,
                                       a.integer(3) ? 1 : 0, static_cast<uint64_t>(a.integer(4)),
                                       stream_of(a.integer(5))));
     return 0;
@@ -179,7 +187,8 @@ int64_t dispatch(const char* name, const Args& a) {
     const at::Tensor& out = a.tensor(5);
     check_ws(ws);
     const int64_t m = q.size(0), k = q.size(1), n = w.size(0);
-    const w8a8_epilogue_t e = epilogue(ws, a.opt_tensor(4), a.opt_tensor(8), a.opt_tensor(9), n);
+    const w8a8_epilogue_t e = epilogue(ws, a.opt_tensor(4), a.opt_tensor(8), a.opt_tensor(9), n,
+                                       m == 2 ? W8A8_DQ_CHAINED : W8A8_DQ_SEPARATE);
     rc_or_throw(w8a8_gemv_dequant(q.data_ptr<int8_t>(), w.data_ptr<int8_t>(),
                                   a.tensor(2).data_ptr<float>(), &e, out.data_ptr(),
                                   static_cast<int>(a.integer(6)), m, n, k,
@@ -216,7 +225,11 @@ int64_t dispatch(const char* name, const Args& a) {
     check_ws(ws);
     const at::Tensor& out = a.tensor(4);
     const int64_t m = acc.size(0), n = acc.size(1);
-    const w8a8_epilogue_t e = epilogue(ws, a.opt_tensor(3), nullptr, nullptr, n);
+    const at::Tensor* bias = a.opt_tensor(3);
+    const int order = bias ? W8A8_DQ_SEPARATE
+                    : (ws.numel() == 1 && n % 4 == 0) ? W8A8_DQ_SCALE_PRODUCT
+                    : W8A8_DQ_CHAINED;
+    const w8a8_epilogue_t e = epilogue(ws, bias, nullptr, nullptr, n, order);
     rc_or_throw(w8a8_dequantize_linear(acc.data_ptr<int32_t>(), a.tensor(1).data_ptr<float>(), &e,
                                        out.data_ptr(), static_cast<int>(a.integer(5)), m, n,
                                        stream_of(a.integer(6))));
@@ -240,16 +253,17 @@ int64_t dispatch(const char* name, const Args& a) {
     int64_t m, k, ldx;
     rows_cols(x, m, k, ldx);
     const int64_t n = w.size(0);
-    const w8a8_epilogue_t e = epilogue(ws, a.opt_tensor(5), a.opt_tensor(14), a.opt_tensor(15), n);
+    const w8a8_epilogue_t e = epilogue(ws, a.opt_tensor(5), a.opt_tensor(14), a.opt_tensor(15), n,
+                                       m == 2 ? W8A8_DQ_CHAINED : W8A8_DQ_SEPARATE);
     if (!convrot && act == 0) {
       rc_or_throw(w8a8_linear_small(x.data_ptr(), dtype_code(x), w.data_ptr<int8_t>(), &e,
-                                    W8A8_SCALE_KITCHEN, q.data_ptr<int8_t>(), xs.data_ptr<float>(),
+                                    W8A8_SCALE_KITCHEN_CUDA, q.data_ptr<int8_t>(), xs.data_ptr<float>(),
                                     out.data_ptr(), code, m, n, k, stream));
     } else {
       rc_or_throw(w8a8_quantize_rowwise_convrot(
           x.data_ptr(), dtype_code(x), m, (act == W8A8_INPUT_ACT_SWIGLU || act == W8A8_INPUT_ACT_SITU) ? k / 2 : k, ldx,
           convrot ? group : 0, act, act_w ? act_w->data_ptr() : nullptr, eps,
-          q.data_ptr<int8_t>(), q.size(-1), xs.data_ptr<float>(), W8A8_SCALE_KITCHEN, stream));
+          q.data_ptr<int8_t>(), q.size(-1), xs.data_ptr<float>(), W8A8_SCALE_KITCHEN_CUDA, stream));
       rc_or_throw(w8a8_gemv_dequant(q.data_ptr<int8_t>(), w.data_ptr<int8_t>(), xs.data_ptr<float>(),
                                     &e, out.data_ptr(), code, m, n, q.size(-1), stream));
     }
@@ -266,7 +280,7 @@ int64_t dispatch(const char* name, const Args& a) {
     rc_or_throw(w8a8_quantize_rowwise_convrot(
         x.data_ptr(), dtype_code(x), rows, q.size(-1), ldx, static_cast<int>(a.integer(3)), act,
         act_w ? act_w->data_ptr() : nullptr, static_cast<float>(a.real(8)), q.data_ptr<int8_t>(),
-        q.size(-1), a.tensor(2).data_ptr<float>(), W8A8_SCALE_KITCHEN, stream_of(a.integer(9))));
+        q.size(-1), a.tensor(2).data_ptr<float>(), W8A8_SCALE_KITCHEN_CUDA, stream_of(a.integer(9))));
     return 0;
   }
   throw NotNative{};

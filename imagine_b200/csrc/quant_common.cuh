@@ -97,12 +97,19 @@ __device__ __forceinline__ float quant_row_scale(float amax, int kitchen_mode) {
   return fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-30f);
 }
 
+// Scale modes (W8A8_SCALE_* of the public header): 0 eager, 1 kitchen,
+// 2 kitchen with the element numerics of the reference's Kitchen CUDA build.
+constexpr int kScaleKitchenCuda = 2;
+
 // Divisor actually applied to the elements: the scale rounded to T, with an
 // exact zero replaced by T's smallest normal (inference/src/eager.rs:94-109).
+// The Kitchen CUDA kernels keep the zero (int8_linear.cu:48-51): a row whose
+// scale rounds to 0 in T (an all-zero f16 row: 1e-30 underflows) divides by
+// zero there, and quant_code reproduces what its clamp makes of that.
 template <typename T>
-__device__ __forceinline__ float quant_divisor(float scale) {
+__device__ __forceinline__ float quant_divisor(float scale, int scale_mode = 0) {
   const float s = QuantTraits<T>::round_t(scale);
-  return s == 0.0f ? QuantTraits<T>::kTiny : s;
+  return (s == 0.0f && scale_mode != kScaleKitchenCuda) ? QuantTraits<T>::kTiny : s;
 }
 
 // One code: clamp(rne(T(x / div)), -128, 127), given recip = RN(1 / div).
@@ -110,9 +117,21 @@ __device__ __forceinline__ float quant_divisor(float scale) {
 // handed to rne_small_int is far inside its exact range.
 __device__ __forceinline__ float div_exact_short(float x, float d, float r);
 
+// With `fast` (the Kitchen CUDA build's numerics, f16 / f32 inputs): the
+// approximate divide that --use_fast_math compiles `x / scale` to, then the
+// reference's clamp(nearbyint(.)) in float, under which a NaN quotient (0 / 0)
+// codes to -128 and +-inf to 127 / -128 (fmaxf returns the non-NaN operand).
+// For bf16 the exact quotient rounds to the same bf16 as any quotient within
+// 2 fp32 ulp (see the W8A8_SCALE_KITCHEN_CUDA note), so bf16 ignores `fast`.
 template <typename T>
-__device__ __forceinline__ int quant_code(float x, float div, float recip) {
+__device__ __forceinline__ int quant_code(float x, float div, float recip, bool fast = false) {
   float y;
+  if constexpr (!std::is_same<T, __nv_bfloat16>::value) {
+    if (fast) {
+      const float t = QuantTraits<T>::round_t(__fdividef(x, div));
+      return static_cast<int>(fminf(127.0f, fmaxf(-128.0f, rintf(t))));
+    }
+  }
   if constexpr (std::is_same<T, float>::value) {
     y = __fmul_rn(x, recip);
     if (!QuantTraits<T>::safe(y)) y = __fdiv_rn(x, div);

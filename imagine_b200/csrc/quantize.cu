@@ -38,11 +38,11 @@ __device__ __forceinline__ uint32_t pcg_hash(uint32_t x) {
 
 template <typename T, bool kStochastic>
 __device__ __forceinline__ int quant_elem(float xv, float div, float recip, int64_t idx,
-                                          uint64_t seed) {
+                                          uint64_t seed, bool fast) {
   if constexpr (!kStochastic) {
-    return quant_code<T>(xv, div, recip);
+    return quant_code<T>(xv, div, recip, fast);
   } else {
-    const float scaled = InTraits<T>::round_t(__fdiv_rn(xv, div));
+    const float scaled = InTraits<T>::round_t(fast ? __fdividef(xv, div) : __fdiv_rn(xv, div));
     const uint64_t key = static_cast<uint64_t>(idx) + seed;
     const uint32_t folded = static_cast<uint32_t>(key) ^ static_cast<uint32_t>(key >> 32);
     const float noise = InTraits<T>::round_t(static_cast<float>(pcg_hash(folded) >> 8) * 0x1.0p-24f);
@@ -131,8 +131,9 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
   }
   const float scale = quant_row_scale<T>(amax, scale_mode);
   if (gt == 0) scales[row] = scale;
-  const float div = quant_divisor<T>(scale);
+  const float div = quant_divisor<T>(scale, scale_mode);
   const float recip = __frcp_rn(div);
+  const bool fast = scale_mode == kScaleKitchenCuda;
   int8_t* qrow = q + static_cast<int64_t>(row) * ldq;
   const int64_t base_idx = static_cast<int64_t>(row) * cols;
 #pragma unroll
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_vec_kernel(
         for (int j = 0; j < 4; ++j) {
           const int c = vi * kPer + w * 4 + j;
           const int qv = quant_elem<T, kStochastic>(InTraits<T>::to_f(e[w * 4 + j]), div, recip,
-                                                    base_idx + c, seed);
+                                                    base_idx + c, seed, fast);
           word |= (static_cast<uint32_t>(qv) & 0xFFu) << (8 * j);
         }
         packed[w] = word;
@@ -193,13 +194,14 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rowwise_scalar_kernel(
   }
   const float scale = quant_row_scale<T>(amax, scale_mode);
   if (threadIdx.x == 0) scales[row] = scale;
-  const float div = quant_divisor<T>(scale);
+  const float div = quant_divisor<T>(scale, scale_mode);
   const float recip = __frcp_rn(div);
+  const bool fast = scale_mode == kScaleKitchenCuda;
   int8_t* qr = q + static_cast<int64_t>(row) * ldq;
   const int64_t base_idx = static_cast<int64_t>(row) * cols;
   for (int c = threadIdx.x; c < cols; c += blockDim.x) {
     qr[c] = static_cast<int8_t>(
-        quant_elem<T, kStochastic>(InTraits<T>::to_f(xr[c]), div, recip, base_idx + c, seed));
+        quant_elem<T, kStochastic>(InTraits<T>::to_f(xr[c]), div, recip, base_idx + c, seed, fast));
   }
 }
 
@@ -465,7 +467,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_modulated_vec_kernel(
   if (!live) return;
   const float scale = quant_row_scale<T>(kitchen ? amax : QuantTraits<T>::round_t(amax), kitchen);
   if (gt == 0) scales[row] = scale;
-  const float div = quant_divisor<T>(scale);
+  const float div = quant_divisor<T>(scale, kitchen);
   const float recip = __frcp_rn(div);
   int8_t* qrow = q + static_cast<int64_t>(row) * ldq;
 #pragma unroll
@@ -481,7 +483,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_modulated_vec_kernel(
         uint32_t word = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int qv = quant_code<T>(elem(v[i], w * 4 + j), div, recip);
+          const int qv = quant_code<T>(elem(v[i], w * 4 + j), div, recip, kitchen == kScaleKitchenCuda);
           word |= (static_cast<uint32_t>(qv) & 0xFFu) << (8 * j);
         }
         packed[w] = word;
@@ -549,7 +551,7 @@ int quantize_modulated_vec_launch(const void* x, int x_dtype, int64_t rows, int6
       (mod_shift && !a16(mod_shift)) || (norm_w && !a16(norm_w))) {
     return -1;
   }
-  const int km = scale_mode == W8A8_SCALE_KITCHEN ? 1 : 0;
+  const int km = scale_mode;  // nonzero: kitchen scales (W8A8_SCALE_*)
   const int64_t g = mod_group > 0 ? mod_group : 1;
   if (x_dtype == W8A8_BF16) {
     return launch_modulated<__nv_bfloat16>(act, x, ldx, mod_scale, mod_shift, norm_w, g, eps, q, ldq,

@@ -21,8 +21,10 @@ import torch
 from . import _native as N
 
 DTYPE_CODE = {torch.float32: N.F32, torch.float16: N.F16, torch.bfloat16: N.BF16}
-DEQUANT = {"eager": N.DQ_EAGER, "scale_product": N.DQ_SCALE_PRODUCT, "chained": N.DQ_CHAINED}
-SCALE_MODE = {"eager": N.SCALE_EAGER, "kitchen": N.SCALE_KITCHEN}
+DEQUANT = {"eager": N.DQ_EAGER, "scale_product": N.DQ_SCALE_PRODUCT, "chained": N.DQ_CHAINED,
+           "separate": N.DQ_SEPARATE}
+SCALE_MODE = {"eager": N.SCALE_EAGER, "kitchen": N.SCALE_KITCHEN,
+              "kitchen_cuda": N.SCALE_KITCHEN_CUDA}
 OUTPUT_ACT = {None: N.ACT_NONE, "none": N.ACT_NONE, "gelu_tanh": N.ACT_GELU_TANH}
 
 

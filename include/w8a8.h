@@ -50,17 +50,33 @@ extern "C" {
 /* ---- row-scale semantics of the INT8 quantiser.
  * EAGER:   max(amax / 127, 1e-30), IEEE divide (inference/src/eager.rs:163-166)
  * KITCHEN: max(min(amax, finite_max) * (1/127), 1e-30), the reference's CUDA
- *          and Triton routes (native/comfy-port/kitchen/int8_linear.cu:206-208) */
+ *          and Triton routes (native/comfy-port/kitchen/int8_linear.cu:206-208),
+ *          elements divided with an IEEE divide (its Triton route's numerics)
+ * KITCHEN_CUDA: KITCHEN scales with the element numerics of the reference's
+ *          Kitchen CUDA kernels as that file is built (--use_fast_math,
+ *          native/comfy-port/CMakeLists.txt:30-36): an approximate divide
+ *          (__fdividef) for f16 / f32 inputs, a divisor that rounds to zero in
+ *          the input type kept (a zero f16 row then codes to -128, as there),
+ *          and the fast-math forms of the fused quantiser's input activations.
+ *          bf16 codes equal KITCHEN's: a quotient of two 8-bit-significand
+ *          values is never within 2 fp32 ulp of a bf16 rounding midpoint. */
 #define W8A8_SCALE_EAGER 0
 #define W8A8_SCALE_KITCHEN 1
+#define W8A8_SCALE_KITCHEN_CUDA 2
 
 /* ---- dequant orders of the INT8 linear epilogue.
  * EAGER:         y = T(acc*(xs*ws)); y = T(y + bias)   (inference/src/int8_linear.rs:244-268)
  * SCALE_PRODUCT: y = T(fma(acc, xs*ws, bias))          (KSRC triton/quantization.py:861-1018)
- * CHAINED:       y = T(fma(acc*xs, ws, bias))          (native/.../int8_linear.cu:517-545) */
+ * CHAINED:       y = T(fma(acc*xs, ws, bias))          (native/.../int8_linear.cu:669-708, two-row GEMV)
+ * SEPARATE:      y = T(((acc*xs)*ws) + bias), three fp32 roundings (native/.../
+ *                int8_linear.cu:518-543 and 586-667: the stand-alone dequant with a
+ *                bias and the one-row GEMV).  Offered by the CUDA-core entry points
+ *                only (w8a8_gemv_dequant, w8a8_linear_small, w8a8_dequantize_linear);
+ *                the tensor-core GEMMs reject it. */
 #define W8A8_DQ_EAGER 0
 #define W8A8_DQ_SCALE_PRODUCT 1
 #define W8A8_DQ_CHAINED 2
+#define W8A8_DQ_SEPARATE 3
 
 /* ---- output activation applied after bias, before the residual */
 #define W8A8_ACT_NONE 0

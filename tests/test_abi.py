@@ -18,7 +18,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert N.LIB.w8a8_abi_version() == 102
+    assert N.LIB.w8a8_abi_version() == 103
 
 
 def test_header_compiles_as_c():
@@ -39,6 +39,9 @@ def test_quantize_rejects_bad_arguments():
     assert rc == N.ERR_VALUE and "dtype" in _err()
     rc = N.LIB.w8a8_quantize_rowwise(None, N.BF16, 1, 4, 4, None, 4, None, 9, 0, 0, None)
     assert rc == N.ERR_VALUE and "scale mode" in _err()
+    rc = N.LIB.w8a8_quantize_rowwise(None, N.BF16, 1, 4, 4, None, 4, None, N.SCALE_KITCHEN_CUDA, 0,
+                                     0, None)
+    assert rc == N.ERR_VALUE and "NULL" in _err()  # mode accepted, then the pointers checked
     rc = N.LIB.w8a8_quantize_rowwise(None, N.BF16, 1, 4, 4, None, 4, None, 0, 0, 0, None)
     assert rc == N.ERR_VALUE and "NULL" in _err()
     # empty input is a no-op success, like the reference launcher's early return
@@ -66,6 +69,13 @@ def test_gemm_rejects_bad_epilogue():
     rc = N.LIB.w8a8_gemm_dequant(None, 16, None, 16, None, ctypes.byref(ep), None, N.BF16, 8, 4, 8,
                                  16, None, None)
     assert rc == N.ERR_VALUE and "dequant order" in _err()
+    # the uncontracted Kitchen order exists on the CUDA-core paths only
+    ep.dequant_order = N.DQ_SEPARATE
+    rc = N.LIB.w8a8_gemm_dequant(None, 16, None, 16, None, ctypes.byref(ep), None, N.BF16, 8, 4, 8,
+                                 16, None, None)
+    assert rc == N.ERR_VALUE and "SEPARATE" in _err()
+    rc = N.LIB.w8a8_dequantize_linear(None, None, ctypes.byref(ep), None, N.BF16, 4, 8, None)
+    assert rc == N.ERR_VALUE and "NULL" in _err()  # order accepted, then the pointers checked
     ep.dequant_order = 0
     rc = N.LIB.w8a8_gemm_dequant(None, 16, None, 16, None, ctypes.byref(ep), None, N.S8, 8, 4, 8,
                                  16, None, None)

@@ -118,7 +118,7 @@ def test_shim_linear_routes_match_c_abi():
         q = torch.empty(m, k, dtype=torch.int8, device=dev)
         xs = torch.empty(m, 1, dtype=torch.float32, device=dev)
         assert _call(lib, "quantize_int8_rowwise", [h.t(x), h.t(q), h.t(xs), B(0), I(0), I(stream)]) == (0, 0)
-        q_ref, xs_ref = W.quantize_int8_rowwise(x, scale_mode="kitchen")
+        q_ref, xs_ref = W.quantize_int8_rowwise(x, scale_mode="kitchen_cuda")
         assert torch.equal(q, q_ref) and torch.equal(xs, xs_ref)
         out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
         rc, res = _call(lib, "cutlass_int8_dequant", [h.t(q), h.t(wq), h.t(xs), h.t(ws), h.t(bias),
@@ -141,7 +141,9 @@ def test_shim_linear_routes_match_c_abi():
         out3 = torch.empty_like(out)
         assert _call(lib, "dequantize_int8_linear", [h.t(acc), h.t(xs), h.t(ws), h.t(bias), h.t(out3),
                                                       I(2), I(stream)])[0] == 0
-        assert torch.equal(out3, out)
+        # with a bias the Kitchen dequant kernel adds it uncontracted
+        assert torch.equal(out3, W.dequantize_int8_linear(acc, xs, ws, bias, torch.bfloat16,
+                                                          dequant="separate"))
         # M = 1 / 2 routes
         x1 = x[:2].contiguous()
         q1 = torch.empty(2, k, dtype=torch.int8, device=dev)
@@ -162,7 +164,7 @@ def test_shim_linear_routes_match_c_abi():
         assert _call(lib, "quantize_int8_rowwise_convrot64",
                      [h.t(x), h.t(qc), h.t(sc), I(256), B(0), I(1), I(0), h.t(empty), F(0.0),
                       I(stream)])[0] == 0
-        qr, sr = W.quantize_int8_rowwise_convrot(x, 256, "gelu_tanh", scale_mode="kitchen")
+        qr, sr = W.quantize_int8_rowwise_convrot(x, 256, "gelu_tanh", scale_mode="kitchen_cuda")
         assert torch.equal(qc, qr) and torch.equal(sc, sr)
         # an argument error comes back as ValueError (-20) with the message
         rc, _ = _call(lib, "quantize_int8_rowwise_convrot64",
