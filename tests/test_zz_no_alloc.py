@@ -1,8 +1,9 @@
 """w8a8_gemm_dequant_splitk_static -- the split-K GEMM on the library's own
 fixed scratch, for callers that cannot allocate -- called through the C ABI
 and checked bit for bit against the entry points that take caller memory,
-on two calls in a row (the second runs on the shared scratch the first one
-used and left behind)."""
+on two calls in a row.  A call that splits clears the part of the shared
+array it uses before launching, so the second call shows that the clear
+makes a used array good again."""
 import ctypes
 
 import pytest
