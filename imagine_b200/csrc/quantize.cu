@@ -11,6 +11,7 @@
 // base are not 16-byte aligned, or that do not fit in registers, take a
 // scalar two-pass path (second pass hits L2).
 #include <cuda_bf16.h>
+#include <algorithm>
 #include <cuda_fp16.h>
 #include <cstdint>
 #include <type_traits>
@@ -493,6 +494,228 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_modulated_vec_kernel(
   }
 }
 
+// Row-loop form of the bf16 modulated quantiser for the modulations whose
+// per-element arithmetic runs on packed pairs (5, 6, and 7 / 8 with eager
+// numerics).  A CTA is one row group of WPR warps; it walks rows blockIdx.x,
+// blockIdx.x + gridDim.x, ..., so a thread always owns the same columns: the
+// bf16 values 1 + s, the shift and the norm weight of those columns are kept
+// in registers (formed again only when a row of another sample comes) instead
+// of being loaded and formed once per row, and the next row's x is loaded
+// while the current one is worked.  The row statistics are summed on packed
+// fp32 pairs.  Per element the operations and their roundings to bf16 are
+// those of quantize_modulated_vec_kernel's paired path (bit-identical for
+// modulation 5; for the others only the order in which the row statistics
+// are summed differs).  Every CTA runs `iters` iterations, rows past the end
+// masked, so its barriers match up.
+template <int WPR, int MAXV, int ACT>
+__global__ void __launch_bounds__(WPR * 32) quantize_modulated_rows_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ msc,
+    const __nv_bfloat16* __restrict__ msh, const __nv_bfloat16* __restrict__ nw, int64_t mgroup,
+    float eps, int8_t* __restrict__ q, int64_t ldq, float* __restrict__ scales, int rows, int cols,
+    int kitchen, int iters) {
+  static_assert(ACT >= 5 && ACT <= 8, "modulations 5-8");
+  constexpr int kThreads = WPR * 32;
+  __shared__ float red[2][WPR];
+  griddep_launch_dependents();  // the GEMM that reads q may start its prologue
+  const int gt = threadIdx.x;
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int nvec = cols / 8;
+  int phase = 0;
+  // sum or max over the CTA; red[] alternates between two halves, so one
+  // barrier per reduction suffices (a half is rewritten only after the next
+  // reduction's barrier, which every reader of it has passed)
+  auto reduce = [&](float v, bool is_max) -> float {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float t = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmaxf(v, t) : __fadd_rn(v, t);
+    }
+    if constexpr (WPR == 1) {
+      return v;
+    } else {
+      if (lane == 0) red[phase][warp] = v;
+      __syncthreads();
+      float r = red[phase][0];
+#pragma unroll
+      for (int w = 1; w < WPR; ++w) r = is_max ? fmaxf(r, red[phase][w]) : __fadd_rn(r, red[phase][w]);
+      phase ^= 1;
+      return r;
+    }
+  };
+  auto unpack2 = [](uint32_t w) -> uint64_t {
+    return pk(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  };
+  auto rne2 = [](uint64_t p) -> uint32_t {  // two RN bf16 roundings, packed
+    const __nv_bfloat162 b = __floats2bfloat162_rn(lo(p), hi(p));
+    return *reinterpret_cast<const uint32_t*>(&b);
+  };
+  auto words = [](const uint4& u, int k) -> uint32_t {
+    return k == 0 ? u.x : k == 1 ? u.y : k == 2 ? u.z : u.w;
+  };
+
+  // per-column constants as bf16 words: 1 + s (rounded), the shift, the norm weight
+  uint32_t one_s[MAXV][4], shw[MAXV][4], nww[MAXV][4];
+  if constexpr (ACT == 6) {
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = gt + i * kThreads;
+      const uint4 wv = vi < nvec ? __ldg(reinterpret_cast<const uint4*>(nw) + vi) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) nww[i][k] = words(wv, k);
+    }
+  }
+  int64_t cur_sample = -1;
+
+  int row = static_cast<int>(blockIdx.x);
+  const int stride = static_cast<int>(gridDim.x);
+  uint4 nx[MAXV];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = gt + i * kThreads;
+    nx[i] = make_uint4(0, 0, 0, 0);
+    if (row < rows && vi < nvec) nx[i] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(row) * ldx) + vi);
+  }
+  const float kf = static_cast<float>(cols);
+  const float inv_k = 1.0f / kf;
+  for (int it = 0; it < iters; ++it, row += stride) {
+    const bool live = row < rows;
+    uint64_t p[MAXV][4];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) p[i][k] = unpack2(words(nx[i], k));
+    }
+    // the next row's x while this one is worked
+    const int nrow = row + stride;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = gt + i * kThreads;
+      if (nrow < rows && vi < nvec) {
+        nx[i] = __ldg(reinterpret_cast<const uint4*>(x + static_cast<int64_t>(nrow) * ldx) + vi);
+      }
+    }
+    // this row's sample constants (uniform over the CTA)
+    if (live) {
+      const int64_t smp = row / mgroup;
+      if (smp != cur_sample) {
+        cur_sample = smp;
+        const int64_t mrow = smp * cols;
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+          const int vi = gt + i * kThreads;
+          uint4 sv = make_uint4(0, 0, 0, 0), hv = make_uint4(0, 0, 0, 0);
+          if (vi < nvec) {
+            sv = __ldg(reinterpret_cast<const uint4*>(msc + mrow) + vi);
+            if constexpr (ACT == 7 || ACT == 8) hv = __ldg(reinterpret_cast<const uint4*>(msh + mrow) + vi);
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            one_s[i][k] = rne2(add2(pk(1.0f, 1.0f), unpack2(words(sv, k))));
+            if constexpr (ACT == 7 || ACT == 8) shw[i][k] = words(hv, k);
+          }
+        }
+      }
+    }
+    // row statistics (columns past the row's end hold zeros and are skipped
+    // where a zero would count)
+    float mean = 0.0f, rstd = 1.0f;
+    if constexpr (ACT == 7) {
+      uint64_t s2 = pk(0.0f, 0.0f);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) s2 = add2(s2, p[i][k]);
+      }
+      mean = reduce(__fadd_rn(lo(s2), hi(s2)), false) * inv_k;
+      const uint64_t mean2 = pk(mean, mean);
+      uint64_t d2 = pk(0.0f, 0.0f);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int vi = gt + i * kThreads;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          p[i][k] = sub2(p[i][k], mean2);  // x - mean, kept for the modulation
+          if (vi < nvec) d2 = fma2(p[i][k], p[i][k], d2);
+        }
+      }
+      rstd = rsqrtf(reduce(__fadd_rn(lo(d2), hi(d2)), false) * inv_k + eps);
+    } else if constexpr (ACT == 6 || ACT == 8) {
+      uint64_t q2 = pk(0.0f, 0.0f);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q2 = fma2(p[i][k], p[i][k], q2);
+      }
+      rstd = rsqrtf(reduce(__fadd_rn(lo(q2), hi(q2)), false) / kf + eps);
+    }
+    // modulated row (bf16 words) and its absmax, as bf16 bit patterns (for
+    // non-negative values the integer order is the value order)
+    const uint64_t rstd2 = pk(rstd, rstd);
+    uint4 ov[MAXV];
+    uint32_t amax_bits = 0;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      uint32_t ow[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint64_t os = unpack2(one_s[i][k]);
+        if constexpr (ACT == 5) {
+          ow[k] = rne2(mul2(p[i][k], os));
+        } else if constexpr (ACT == 6) {
+          const uint64_t nrm = unpack2(rne2(mul2(mul2(p[i][k], rstd2), unpack2(nww[i][k]))));
+          ow[k] = rne2(mul2(nrm, os));
+        } else {
+          // 7: p holds x - mean; 8: mean is 0 and x - 0 is x
+          const uint64_t t = unpack2(rne2(mul2(unpack2(rne2(mul2(p[i][k], rstd2))), os)));
+          ow[k] = rne2(add2(t, unpack2(shw[i][k])));
+        }
+        amax_bits = __vmaxu2(amax_bits, ow[k] & 0x7FFF7FFFu);
+      }
+      ov[i] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    }
+    const uint32_t mb = max(amax_bits & 0xFFFFu, amax_bits >> 16);
+    const float amax = reduce(__uint_as_float(mb << 16), true);
+    if (!live) continue;
+    const float scale = quant_row_scale<__nv_bfloat16>(amax, kitchen);
+    if (gt == 0) scales[row] = scale;
+    const float div = quant_divisor<__nv_bfloat16>(scale, kitchen);
+    const float recip = __frcp_rn(div);
+    int8_t* qrow = q + static_cast<int64_t>(row) * ldq;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = gt + i * kThreads;
+      if (vi < nvec) reinterpret_cast<uint2*>(qrow)[vi] = quant8_bf16(ov[i], div, recip);
+    }
+  }
+}
+
+template <int WPR, int MAXV, int ACT>
+int launch_modulated_rows(const void* x, int64_t ldx, const void* msc, const void* msh,
+                          const void* nw, int64_t mgroup, float eps, int8_t* q, int64_t ldq,
+                          float* scales, int rows, int cols, int kitchen, cudaStream_t stream) {
+  auto kern = quantize_modulated_rows_kernel<WPR, MAXV, ACT>;
+  static int per_sm = 0;  // resident CTAs per SM of this instantiation
+  static int sms = 0;
+  if (per_sm == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WPR * 32, 0) != cudaSuccess ||
+        per_sm < 1) {
+      per_sm = 1;
+      sms = sms > 0 ? sms : 1;
+    }
+  }
+  const int grid = std::max(1, std::min(rows, per_sm * sms));
+  const int iters = (rows + grid - 1) / grid;
+  kern<<<grid, WPR * 32, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(msc),
+      static_cast<const __nv_bfloat16*>(msh), static_cast<const __nv_bfloat16*>(nw), mgroup, eps, q,
+      ldq, scales, rows, cols, kitchen, iters);
+  return 0;
+}
+
 template <typename T, int ACT>
 int launch_modulated_t(const void* x, int64_t ldx, const void* msc, const void* msh,
                        const void* nw, int64_t mgroup, float eps, int8_t* q, int64_t ldq,
@@ -506,6 +729,27 @@ int launch_modulated_t(const void* x, int64_t ldx, const void* msc, const void* 
     }
   }
   if (!wpr) return -1;  // more than 8192 columns: the ConvRot-layout kernel
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if (ACT == 5 || ACT == 6 || !kitchen) {
+      int rc;
+      if (wpr == 4 && nvec <= 4 * 32 * 3) {
+        rc = launch_modulated_rows<4, 3, ACT>(x, ldx, msc, msh, nw, mgroup, eps, q, ldq, scales, rows, cols, kitchen, stream);
+      } else {
+        switch (wpr) {
+          case 1: rc = launch_modulated_rows<1, 4, ACT>(x, ldx, msc, msh, nw, mgroup, eps, q, ldq, scales, rows, cols, kitchen, stream); break;
+          case 2: rc = launch_modulated_rows<2, 4, ACT>(x, ldx, msc, msh, nw, mgroup, eps, q, ldq, scales, rows, cols, kitchen, stream); break;
+          case 4: rc = launch_modulated_rows<4, 4, ACT>(x, ldx, msc, msh, nw, mgroup, eps, q, ldq, scales, rows, cols, kitchen, stream); break;
+          default: rc = launch_modulated_rows<8, 4, ACT>(x, ldx, msc, msh, nw, mgroup, eps, q, ldq, scales, rows, cols, kitchen, stream); break;
+        }
+      }
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) {
+        set_error("modulated quantiser launch failed: %s", cudaGetErrorString(e));
+        return W8A8_ERR_ACCELERATOR;
+      }
+      return rc;
+    }
+  }
   auto go = [&](auto kernel, int rows_per_cta) {
     kernel<<<(rows + rows_per_cta - 1) / rows_per_cta, kQuantThreads, 0, stream>>>(
         static_cast<const T*>(x), ldx, static_cast<const T*>(msc), static_cast<const T*>(msh),
