@@ -46,18 +46,6 @@ namespace w8a8 {
 
 __device__ int g_w8a8_device_error;
 
-int* device_error_word() {
-  static int* addr[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!addr[dev]) {
-    void* a = nullptr;
-    if (cudaGetSymbolAddress(&a, g_w8a8_device_error) != cudaSuccess) return nullptr;
-    addr[dev] = static_cast<int*>(a);
-  }
-  return addr[dev];
-}
-
 int read_and_clear_device_error(cudaStream_t stream, int* value) {
   int v = 0;
   cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_w8a8_device_error, sizeof(int), 0,

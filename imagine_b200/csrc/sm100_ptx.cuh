@@ -25,7 +25,6 @@ enum DeviceError : int {
   kDevTimeoutTmemEmpty = 4, // MMA issuer waited too long for a free accumulator
   kDevBadScaleBlock = 5,    // an MXFP8 scale block outside the caller's buffers
   kDevTimeoutPeer = 6,      // a peer GPU's flag did not arrive (fused all-gather)
-  kDevTimeoutRow = 7,       // a quantiser's bulk row copy did not land
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -9,9 +9,6 @@ namespace w8a8 {
 
 // Device-side error word (one per device, module-scope __device__ variable).
 int read_and_clear_device_error(cudaStream_t stream, int* value);
-// Its device address, for kernels of other translation units (nullptr if the
-// lookup fails; the kernels then record nothing).
-int* device_error_word();
 
 // mode 0: quantise; 1: row absmax only (into `scales`); 2: quantise with the
 // row absmax given in `amax_in`.
