@@ -79,8 +79,11 @@ struct Cfg {
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = (BN / CG) * kBK;  // each CTA of a pair holds half of B
   static constexpr int kStageBytes = kABytes + kBBytes;
-  // MXFP8: one 512-byte block of e8m0 scales for A and BN/128 for B per stage
-  static constexpr int kSFBytes = KIND == 2 ? 512 * (1 + BN / 128) : 0;
+  // MXFP8: one 512-byte block of e8m0 scales for A and BN/128 for B per
+  // stage, the slot rounded up to 1024 bytes so that the staging tiles after
+  // the scale slots keep the 1024-byte alignment their TMA swizzle needs
+  static constexpr int kSFLoadBytes = KIND == 2 ? 512 * (1 + BN / 128) : 0;  // bytes the TMA brings
+  static constexpr int kSFBytes = (kSFLoadBytes + 1023) / 1024 * 1024;          // slot size
   static constexpr int kSFCols = KIND == 2 ? 4 * (1 + BN / 128) : 0;  // TMEM columns per stage
   // one warp's staging tile (split-K stages its int32 partials in 32 x 16
   // halves, which fit the 2-byte outputs' tile)
@@ -97,10 +100,18 @@ struct Cfg {
   static constexpr int kStagesRaw = (kMaxSmem - kFixed) / (kStageBytes + kSFBytes);
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr int kSmemBytes = kFixed + kStages * (kStageBytes + kSFBytes);
-  static constexpr int kSFCol0 = 2 * BN;  // scale factors live after the two accumulators
+  // TMEM accumulators: two of BN columns (the epilogue of one tile overlaps
+  // the MMAs of the next), except MXFP8 at 256 columns, where two would leave
+  // no columns for the scale factors: there three 128-column regions rotate,
+  // tile t taking regions 2t mod 3 and 2t+1 mod 3, and each region goes back
+  // to the MMA warp as soon as the epilogue has copied it to registers, so
+  // the next tile starts once the first half of this one is drained.
+  static constexpr bool kRegions3 = KIND == 2 && BN == 256;
+  static constexpr int kAccCols = kRegions3 ? 3 * 128 : 2 * BN;
+  static constexpr int kSFCol0 = kAccCols;  // scale factors live after the accumulators
   static constexpr uint32_t kTmemCols =
-      (2 * BN + kStages * kSFCols <= 256) ? 256u : 512u;
-  static_assert(2 * BN + kStages * kSFCols <= 512, "TMEM budget exceeded");
+      (kAccCols + kStages * kSFCols <= 256) ? 256u : 512u;
+  static_assert(kAccCols + kStages * kSFCols <= 512, "TMEM budget exceeded");
   static_assert(kStages >= 2, "pipeline needs at least two stages");
   static_assert(kSmemBytes <= kMaxSmem, "shared memory budget exceeded");
 };
@@ -734,8 +745,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sD + C::kDBytes);
   uint64_t* empty = full + C::kStages;
   uint64_t* tfull = empty + C::kStages;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* tempty = tfull + 2;  // two accumulators, or three regions (kRegions3)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 3);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
   volatile int* abortv = abort_flag;
 
@@ -757,8 +768,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&tfull[b], 1);
+    for (int b = 0; b < 2; ++b) mbar_init(&tfull[b], 1);
+    for (int b = 0; b < 3; ++b) {
       mbar_init(&tempty[b], kEpiWarps * CG);  // one arrival per epilogue warp of each CTA
     }
     *abort_flag = 0;
@@ -805,7 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if constexpr (CG == 1) {
             mbar_arrive_expect_tx(&full[s], C::kABytes + (half_unit ? C::kBBytes / 2 : C::kBBytes) +
-                                                C::kSFBytes);
+                                                C::kSFLoadBytes);
             tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kBK, a_row);
             if (half_unit) {
               tma_load_2d(sB + s * C::kBBytes, &tmBh, &full[s], kb * kBK, b_row);
@@ -818,12 +829,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (KIND == 2) {
               // blocked scale layout: 512-byte block (row/128, kb) at
               // ((row/128) * ncb + kb) * 512; blocks outside the buffers the
-              // caller sized from M, N, K are refused (error 5, abort).
+              // caller sized from M, N, K are refused (error 5, abort).  A
+              // 256-column tile whose second half lies wholly past N (no
+              // block of B there) reads the last block again: those columns
+              // are computed but never stored.
               uint8_t* sf = sSF + s * C::kSFBytes;
               const int a_blocks = (M + 127) / 128, b_blocks = (N + 127) / 128;
-              bool in = mb < a_blocks && kb < ep.sf_ncb;
-#pragma unroll
-              for (int j = 0; j < BN / 128; ++j) in = in && (nb * (BN / 128) + j) < b_blocks;
+              const bool in = mb < a_blocks && kb < ep.sf_ncb && nb * (BN / 128) < b_blocks;
               if (!in) {
                 atomicCAS(&g_w8a8_device_error, 0, kDevBadScaleBlock);
                 *abort_flag = 1;
@@ -834,14 +846,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                         &full[s]);
 #pragma unroll
               for (int j = 0; j < BN / 128; ++j) {
+                const int blk = min(nb * (BN / 128) + j, b_blocks - 1);
                 bulk_load(sf + 512 * (1 + j),
-                          ep.sfb + (static_cast<int64_t>(nb * (BN / 128) + j) * ep.sf_ncb + kb) * 512,
+                          ep.sfb + (static_cast<int64_t>(blk) * ep.sf_ncb + kb) * 512,
                           512, &full[s]);
               }
             }
           } else {
             // both CTAs' bytes are counted on the leader's barrier
-            if (leader) mbar_arrive_expect_tx(&full[s], 2 * (C::kStageBytes + C::kSFBytes));
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * (C::kStageBytes + C::kSFLoadBytes));
             const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
             tma_load_2d_pair(sA + s * C::kABytes, &tmA, bar, kb * kBK, a_row);
             tma_load_2d_pair(sB + s * C::kBBytes, &tmB, bar, kb * kBK, b_row);
@@ -874,12 +887,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         (void)id;
         const uint32_t acc = tl & 1u;
         const uint32_t use = tl >> 1;
-        if (!mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abortv, &g_w8a8_device_error,
-                       kDevTimeoutTmemEmpty)) {
-          break;
+        // regions of this tile (kRegions3): slots ja = 2 tl and jb = 2 tl + 1
+        // of the sequence 0, 1, 2, 0, 1, 2, ...; slot j is region j % 3's
+        // (j / 3)-th use, which needs the previous use drained
+        const uint32_t ja = 2u * tl, jb = 2u * tl + 1u;
+        const uint32_t ra = ja % 3u, rb = jb % 3u;
+        if constexpr (C::kRegions3) {
+          if (!mbar_wait(&tempty[ra], ((ja / 3u) & 1u) ^ 1u, abortv, &g_w8a8_device_error,
+                         kDevTimeoutTmemEmpty) ||
+              !mbar_wait(&tempty[rb], ((jb / 3u) & 1u) ^ 1u, abortv, &g_w8a8_device_error,
+                         kDevTimeoutTmemEmpty)) {
+            break;
+          }
+        } else {
+          if (!mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abortv, &g_w8a8_device_error,
+                         kDevTimeoutTmemEmpty)) {
+            break;
+          }
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + (C::kRegions3 ? 128u * ra : acc * BN);
         for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const int s = static_cast<int>(it % C::kStages);
           const uint32_t ph = (it / C::kStages) & 1u;
@@ -902,10 +929,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 #pragma unroll
             for (int k = 0; k < kBK / kUmmaK; ++k) {
-              umma_mx<CG>(d_tmem, smem_desc_k_sw128(a0 + k * kUmmaK),
-                          smem_desc_k_sw128(b0 + k * kUmmaK),
-                          make_idesc_mx(kBM * CG, BN, static_cast<uint32_t>(k)), sf_tmem,
-                          sf_tmem + 4, (kb != kb_lo || k != 0) ? 1u : 0u);
+              const uint32_t accumulate = (kb != kb_lo || k != 0) ? 1u : 0u;
+              if (!C::kRegions3 || rb == ra + 1u) {
+                // the tile's accumulator columns are contiguous: one MMA
+                umma_mx<CG>(d_tmem, smem_desc_k_sw128(a0 + k * kUmmaK),
+                            smem_desc_k_sw128(b0 + k * kUmmaK),
+                            make_idesc_mx(kBM * CG, BN, static_cast<uint32_t>(k)), sf_tmem,
+                            sf_tmem + 4, accumulate);
+              } else {
+                // regions 2 and 0: each 128-column half of B (rows 128 apart,
+                // 16 KB apart in the swizzled stage) into its own region,
+                // with its own block of B scales
+                umma_mx<CG>(tmem_base + 128u * ra, smem_desc_k_sw128(a0 + k * kUmmaK),
+                            smem_desc_k_sw128(b0 + k * kUmmaK),
+                            make_idesc_mx(kBM * CG, 128, static_cast<uint32_t>(k)), sf_tmem,
+                            sf_tmem + 4, accumulate);
+                umma_mx<CG>(tmem_base + 128u * rb, smem_desc_k_sw128(a0 + k * kUmmaK),
+                            smem_desc_k_sw128(b0 + 128 * kBK + k * kUmmaK),
+                            make_idesc_mx(kBM * CG, 128, static_cast<uint32_t>(k)), sf_tmem,
+                            sf_tmem + 8, accumulate);
+              }
             }
           } else {
 #pragma unroll
@@ -1084,6 +1127,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           if (last && lane == 0) *cnt = 0u;
+        }
+        continue;
+      }
+      if constexpr (C::kRegions3) {
+        // chunks 0-3 sit in region ra, 4-7 in region rb: per region, this
+        // warp's two chunks to registers, the region back to the MMA warp,
+        // then their arithmetic
+        static_assert(!SPLIT && CG == 1, "the rotating regions are built for 1-CTA MXFP8");
+        const uint32_t ra = (2u * tl) % 3u, rb = (2u * tl + 1u) % 3u;
+#pragma unroll
+        for (int reg = 0; reg < 2; ++reg) {
+          const uint32_t region = reg == 0 ? ra : rb;
+          uint32_t two[2][32];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int c = half + 2 * (2 * reg + i);
+            if (c < nch && col_base + c * 32 < N) {
+              tmem_ld_32x32b_x32(tmem_base + lane_base + 128u * region + (c % 4) * 32, two[i]);
+            }
+          }
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[region]);
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int ci = 2 * reg + i;
+            const int c = half + 2 * ci;
+            const int col0 = col_base + c * 32;
+            if (c < nch && col0 < N) {
+              finish_chunk<KIND, OutT, ORDER, ACT>(two[i], s_ws + ci * 32, s_bias + ci * 32, xs_row,
+                                                   has_bias, has_resid, ep, grow, col0, row0, M, N,
+                                                   st, &tmD, lane);
+            }
+          }
         }
         continue;
       }
@@ -1368,7 +1446,7 @@ int launch_tc(const GemmArgs& g, const CUtensorMap& ma, const CUtensorMap& mb,
   const int tiles = num_m * num_n;
   const int sms = device_sm_count();
   if (!SPLIT) sk.splits = 1;
-  if (SPLIT || CG != 1 || BN != 256 || sk.half_from > tiles) sk.half_from = tiles;
+  if (SPLIT || CG != 1 || BN != 256 || KIND == 2 || sk.half_from > tiles) sk.half_from = tiles;
   const int64_t all_units = sk.splits > 1 ? static_cast<int64_t>(tiles) * sk.splits
                                           : sk.half_from + 2ll * (tiles - sk.half_from);
   int units = static_cast<int>(
@@ -1705,7 +1783,11 @@ int dispatch_out(const GemmArgs& g, bool tc_ok, const GemmPlan& plan, cudaStream
         return launch_tc<KIND, 128, OutT, O, A, 2>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas,
                                                    stream);
       }
-      return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas, stream);
+      if (bn == 128) {
+        return launch_tc<KIND, 128, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas,
+                                                   stream);
+      }
+      return launch_tc<KIND, 256, OutT, O, A, 1>(g, ma, mb, mbh, md, mw, sk, group_m, max_ctas, stream);
     } else {
       if constexpr (KIND == 0 && !std::is_same<OutT, int32_t>::value) {
         if (splits > 1) {  // split-K runs 128-column tiles
@@ -2065,15 +2147,15 @@ int gemm_launch(const GemmArgs& g_in, cudaStream_t stream) {
     }
   } else if (g.kind == 2) {
     const bool mx_ok = tc_ok && g.K % 32 == 0 && a16(g.sfa) && a16(g.sfb);
-    // 128-column tiles: two 256-column accumulators would fill all 512 TMEM
-    // columns and leave none for the block scales.  One CTA per tile unless
-    // pairs (256 x 128 tiles, each SM loading half of B) are asked for: on
-    // B200 the pairs measured 4-8% slower (5600 x 3072 -> 3072: 93.3 against
-    // 89.1 us; -> 12288: 314 against 292 us; 5600 x 12288 -> 3072: 333
-    // against 306 us).
+    // One CTA per tile, 256 columns (one accumulator, the block scales in the
+    // TMEM columns the second would take) where 256-column tiles fill the SMs,
+    // else 128; CTA pairs (256 x 128 tiles, each SM loading half of B) only
+    // when asked for: on B200 they measured 4-8% slower than 1-CTA 128-column
+    // tiles (5600 x 3072 -> 3072: 93.3 against 89.1 us; -> 12288: 314 against
+    // 292 us; 5600 x 12288 -> 3072: 333 against 306 us).
     GemmPlan mx_plan = plan;
-    mx_plan.bn = 128;
     mx_plan.cg = g.cfg && g.cfg->cta_group ? g.cfg->cta_group : 1;
+    mx_plan.bn = mx_plan.cg == 2 ? 128 : plan.bn;
     switch (g.out_dtype) {
       case W8A8_BF16: return dispatch_out<2, __nv_bfloat16>(g, mx_ok, mx_plan, stream);
       case W8A8_F16: return dispatch_out<2, __half>(g, mx_ok, mx_plan, stream);

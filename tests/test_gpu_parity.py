@@ -503,3 +503,32 @@ def test_mxfp8_linear(m, k, n, cta_group):
     no_device_error()
     ref = O.mxfp8_linear(aq.cpu(), asf.cpu(), wq.cpu(), wsf.cpu(), b, out_dtype=torch.float32)
     assert_rms_close(y, ref)
+
+
+@pytest.mark.parametrize("max_ctas", [0, 3])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("m,k,n", [(300, 3072, 1024), (130, 160, 520), (1000, 1024, 640),
+                                   (777, 512, 2304)])
+def test_mxfp8_linear_256_columns(m, k, n, out_dtype, max_ctas):
+    """256-column MXFP8 tiles: three 128-column TMEM regions rotating over a
+    CTA's tiles (one MMA into contiguous regions, two 128-column MMAs into
+    regions 2 and 0).  max_ctas = 3 makes every CTA run many tiles, so every
+    region assignment and every barrier phase occurs; N tails included."""
+    g = torch.Generator().manual_seed(m + k + n + max_ctas)
+    x = torch.randn(m, k, generator=g)
+    x = torch.where(torch.rand(m, k, generator=g) < 0.01, x * 20, x).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, generator=g) * 0.02).to(out_dtype)
+    aq, asf = W().quantize_mxfp8(x.to(cuda()))
+    wq, wsf = W().quantize_mxfp8(w.to(cuda()))
+    y = W().mxfp8_linear(aq, asf, wq, wsf, b.to(cuda()), out_dtype=out_dtype,
+                         config=(256, 8, max_ctas, 1))
+    no_device_error()
+    ref = O.mxfp8_linear(aq.cpu(), asf.cpu(), wq.cpu(), wsf.cpu(), b, out_dtype=torch.float32)
+    assert_rms_close(y, ref)
+    # the 128-column tiles give the same values (fp32 sums of the same MMAs;
+    # only the tile shape differs)
+    y128 = W().mxfp8_linear(aq, asf, wq, wsf, b.to(cuda()), out_dtype=out_dtype,
+                            config=(128, 8, 0, 1))
+    assert torch.equal(y.view(torch.int16 if out_dtype == torch.bfloat16 else torch.int32),
+                       y128.view(torch.int16 if out_dtype == torch.bfloat16 else torch.int32))
