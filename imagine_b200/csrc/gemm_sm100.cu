@@ -102,10 +102,12 @@ struct Cfg {
   static constexpr int kSmemBytes = kFixed + kStages * (kStageBytes + kSFBytes);
   // TMEM accumulators: two of BN columns (the epilogue of one tile overlaps
   // the MMAs of the next), except MXFP8 at 256 columns, where two would leave
-  // no columns for the scale factors: there three 128-column regions rotate,
-  // tile t taking regions 2t mod 3 and 2t+1 mod 3, and each region goes back
-  // to the MMA warp as soon as the epilogue has copied it to registers, so
-  // the next tile starts once the first half of this one is drained.
+  // no columns for the scale factors: there three 128-column regions, even
+  // tiles in regions 0-1 (columns 0-255), odd tiles in regions 1-2 (columns
+  // 128-383), so every tile is one N = 256 MMA per K step.  Each region goes
+  // back to the MMA warp as soon as the epilogue has copied it to registers,
+  // the shared region 1 first, so the next tile starts once the half of this
+  // one in region 1 is drained.
   static constexpr bool kRegions3 = KIND == 2 && BN == 256;
   static constexpr int kAccCols = kRegions3 ? 3 * 128 : 2 * BN;
   static constexpr int kSFCol0 = kAccCols;  // scale factors live after the accumulators
@@ -887,15 +889,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         (void)id;
         const uint32_t acc = tl & 1u;
         const uint32_t use = tl >> 1;
-        // regions of this tile (kRegions3): slots ja = 2 tl and jb = 2 tl + 1
-        // of the sequence 0, 1, 2, 0, 1, 2, ...; slot j is region j % 3's
-        // (j / 3)-th use, which needs the previous use drained
-        const uint32_t ja = 2u * tl, jb = 2u * tl + 1u;
-        const uint32_t ra = ja % 3u, rb = jb % 3u;
+        // regions of this tile (kRegions3): region 1 (its tl-th use) and
+        // region 0 (even tiles) or 2 (odd tiles), each that region's
+        // (tl / 2)-th use; a use needs the previous one drained
+        const uint32_t r_other = (tl & 1u) ? 2u : 0u;
         if constexpr (C::kRegions3) {
-          if (!mbar_wait(&tempty[ra], ((ja / 3u) & 1u) ^ 1u, abortv, &g_w8a8_device_error,
+          if (!mbar_wait(&tempty[1], (tl & 1u) ^ 1u, abortv, &g_w8a8_device_error,
                          kDevTimeoutTmemEmpty) ||
-              !mbar_wait(&tempty[rb], ((jb / 3u) & 1u) ^ 1u, abortv, &g_w8a8_device_error,
+              !mbar_wait(&tempty[r_other], ((tl >> 1) & 1u) ^ 1u, abortv, &g_w8a8_device_error,
                          kDevTimeoutTmemEmpty)) {
             break;
           }
@@ -906,7 +907,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (C::kRegions3 ? 128u * ra : acc * BN);
+        const uint32_t d_tmem = tmem_base + (C::kRegions3 ? 128u * (tl & 1u) : acc * BN);
         for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const int s = static_cast<int>(it % C::kStages);
           const uint32_t ph = (it / C::kStages) & 1u;
@@ -929,26 +930,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 #pragma unroll
             for (int k = 0; k < kBK / kUmmaK; ++k) {
-              const uint32_t accumulate = (kb != kb_lo || k != 0) ? 1u : 0u;
-              if (!C::kRegions3 || rb == ra + 1u) {
-                // the tile's accumulator columns are contiguous: one MMA
-                umma_mx<CG>(d_tmem, smem_desc_k_sw128(a0 + k * kUmmaK),
-                            smem_desc_k_sw128(b0 + k * kUmmaK),
-                            make_idesc_mx(kBM * CG, BN, static_cast<uint32_t>(k)), sf_tmem,
-                            sf_tmem + 4, accumulate);
-              } else {
-                // regions 2 and 0: each 128-column half of B (rows 128 apart,
-                // 16 KB apart in the swizzled stage) into its own region,
-                // with its own block of B scales
-                umma_mx<CG>(tmem_base + 128u * ra, smem_desc_k_sw128(a0 + k * kUmmaK),
-                            smem_desc_k_sw128(b0 + k * kUmmaK),
-                            make_idesc_mx(kBM * CG, 128, static_cast<uint32_t>(k)), sf_tmem,
-                            sf_tmem + 4, accumulate);
-                umma_mx<CG>(tmem_base + 128u * rb, smem_desc_k_sw128(a0 + k * kUmmaK),
-                            smem_desc_k_sw128(b0 + 128 * kBK + k * kUmmaK),
-                            make_idesc_mx(kBM * CG, 128, static_cast<uint32_t>(k)), sf_tmem,
-                            sf_tmem + 8, accumulate);
-              }
+              umma_mx<CG>(d_tmem, smem_desc_k_sw128(a0 + k * kUmmaK),
+                          smem_desc_k_sw128(b0 + k * kUmmaK),
+                          make_idesc_mx(kBM * CG, BN, static_cast<uint32_t>(k)), sf_tmem,
+                          sf_tmem + 4, (kb != kb_lo || k != 0) ? 1u : 0u);
             }
           } else {
 #pragma unroll
@@ -1131,20 +1116,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       if constexpr (C::kRegions3) {
-        // chunks 0-3 sit in region ra, 4-7 in region rb: per region, this
-        // warp's two chunks to registers, the region back to the MMA warp,
-        // then their arithmetic
-        static_assert(!SPLIT && CG == 1, "the rotating regions are built for 1-CTA MXFP8");
-        const uint32_t ra = (2u * tl) % 3u, rb = (2u * tl + 1u) % 3u;
+        // the tile's columns start at TMEM column 0 (even tiles) or 128 (odd
+        // tiles); chunks 0-3 and 4-7 are its two 128-column regions.  Per
+        // region, region 1 first: this warp's two chunks to registers, the
+        // region back to the MMA warp, then their arithmetic
+        static_assert(!SPLIT && CG == 1, "the shared-region layout is built for 1-CTA MXFP8");
+        const uint32_t col0_tmem = 128u * (tl & 1u);
 #pragma unroll
-        for (int reg = 0; reg < 2; ++reg) {
-          const uint32_t region = reg == 0 ? ra : rb;
+        for (int step = 0; step < 2; ++step) {
+          // group of chunks (0: 0-3, 1: 4-7) in region 1 first
+          const int grp = ((tl & 1u) ? 0 : 1) ^ step;
+          const uint32_t region = (col0_tmem >> 7) + static_cast<uint32_t>(grp);
           uint32_t two[2][32];
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
-            const int c = half + 2 * (2 * reg + i);
+            const int c = half + 2 * (2 * grp + i);
             if (c < nch && col_base + c * 32 < N) {
-              tmem_ld_32x32b_x32(tmem_base + lane_base + 128u * region + (c % 4) * 32, two[i]);
+              tmem_ld_32x32b_x32(tmem_base + lane_base + col0_tmem + c * 32, two[i]);
             }
           }
           tmem_ld_wait();
@@ -1153,7 +1141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(&tempty[region]);
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
-            const int ci = 2 * reg + i;
+            const int ci = 2 * grp + i;
             const int c = half + 2 * ci;
             const int col0 = col_base + c * 32;
             if (c < nch && col0 < N) {
