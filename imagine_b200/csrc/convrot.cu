@@ -264,15 +264,14 @@ template <typename T>
 __device__ __forceinline__ void quant_pair(uint64_t p, float div, float recip, uint32_t& c0,
                                            uint32_t& c1, bool fast) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-    // paired RN conversions; exact quotients by one packed FMA correction
-    // (div_exact_short); rne by adding 1.5 * 2^23
+    // paired RN conversions; bf16(x / d) from the product x RN(1/d), which
+    // rounds to the same bf16 for bf16 x and d (proof at quant8_bf16); rne by
+    // adding 1.5 * 2^23
+    (void)div;
     uint32_t b;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(b) : "f"(hi(p)), "f"(lo(p)));
     const uint64_t xv = pk(__uint_as_float(b << 16), __uint_as_float(b & 0xFFFF0000u));
-    const uint64_t r2 = pk(recip, recip);
-    const uint64_t y0 = mul2(xv, r2);
-    const uint64_t e = fma2(y0, pk(-div, -div), xv);
-    const uint64_t y = fma2(e, r2, y0);
+    const uint64_t y = mul2(xv, pk(recip, recip));
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(b) : "f"(hi(y)), "f"(lo(y)));
     // |quotient| <= 127.75, so only the upper end needs a clamp (-127.75
     // rounds to -128)

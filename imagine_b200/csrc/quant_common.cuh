@@ -6,7 +6,9 @@
 // native/comfy-port/kitchen/int8_linear.cu:47-51).  A divide per element is
 // the dominant cost of a bandwidth-bound kernel.  For bf16/f16 inputs the
 // quotient is computed exactly with one FMA correction (div_exact_short,
-// proof at its definition).  For fp32 inputs it is formed as x * r with
+// proof at its definition); the vectorised bf16 paths need only the product
+// x * RN(1/d), which rounds to the same bf16 (proof at quant8_bf16).  For fp32
+// inputs it is formed as x * r with
 // r = RN(1 / T(scale)):
 //   |x*r - x/s| <= 2^-23 |x/s| (r and the product each round once), i.e. the
 //   product is within 2 ulp of the correctly rounded quotient.
@@ -185,23 +187,28 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
   return r;
 }
 
+// bf16(x / d) for bf16 values x and d (d > 0 finite) from one product with
+// r = RN(1/d): RN(x r) is within 2^-23 |x/d| (relative) of the quotient, while a
+// quotient of two 8-bit significands mx / md lies at least 2^-18 |x/d| from every
+// bf16 rounding midpoint (|mx 2^9 - m md| / (md 2^9) with md < 2^8, and it is
+// never exactly on one: a finite binary expansion of mx / md has at most 8
+// significant bits).  So RN_bf16(RN(x r)) == RN_bf16(x / d) for every such pair;
+// f16 (11-bit significands) leaves no such margin and keeps div_exact_short.
+//
 // Eight codes from one 16-byte vector of bf16 (the hot path of the
-// quantiser): exact quotients (div_exact_short on packed pairs), paired
-// hardware bf16 rounding, rne via the 1.5*2^23 trick (packed), and saturating
-// packs (the clamp to [-128, 127]).
+// quantiser): the product above on packed pairs, paired hardware bf16
+// rounding, rne via the 1.5*2^23 trick (packed), and saturating packs (the
+// clamp to [-128, 127]).
 __device__ __forceinline__ uint2 quant8_bf16(const uint4& v, float div, float recip) {
+  (void)div;
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
   const uint64_t r2 = pk(recip, recip);
-  const uint64_t nd2 = pk(-div, -div);
   const uint64_t magic = pk(12582912.0f, 12582912.0f);
   int q[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint64_t x = pk(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
-    // y0 = RN(x r), e = x - y0 d (exact), y = RN(y0 + e r)
-    const uint64_t y0 = mul2(x, r2);
-    const uint64_t e = fma2(y0, nd2, x);
-    const uint64_t y = fma2(e, r2, y0);
+    const uint64_t y = mul2(x, r2);
     const __nv_bfloat162 b = __floats2bfloat162_rn(lo(y), hi(y));  // .x = lo
     const uint32_t bits = *reinterpret_cast<const uint32_t*>(&b);
     const uint64_t t = add2(pk(__uint_as_float(bits << 16), __uint_as_float(bits & 0xFFFF0000u)), magic);
