@@ -510,10 +510,10 @@ def test_mxfp8_linear(m, k, n, cta_group):
 @pytest.mark.parametrize("m,k,n", [(300, 3072, 1024), (130, 160, 520), (1000, 1024, 640),
                                    (777, 512, 2304)])
 def test_mxfp8_linear_256_columns(m, k, n, out_dtype, max_ctas):
-    """256-column MXFP8 tiles: three 128-column TMEM regions rotating over a
-    CTA's tiles (one MMA into contiguous regions, two 128-column MMAs into
-    regions 2 and 0).  max_ctas = 3 makes every CTA run many tiles, so every
-    region assignment and every barrier phase occurs; N tails included."""
+    """256-column MXFP8 tiles on three 128-column TMEM regions (even tiles in
+    regions 0-1, odd tiles in 1-2, the shared region handed back first).
+    max_ctas = 3 makes every CTA run many tiles, so both placements and every
+    barrier phase occur; N tails included."""
     g = torch.Generator().manual_seed(m + k + n + max_ctas)
     x = torch.randn(m, k, generator=g)
     x = torch.where(torch.rand(m, k, generator=g) < 0.01, x * 20, x).to(torch.bfloat16)
